@@ -1,0 +1,440 @@
+// Hybrid key switching (Han-Ki 2020) for HRotate, hoisted rotations and
+// relinearisation, in the evaluation (NTT) form.
+//
+// For c1 at l limbs, digits D_j = [j*alpha, min((j+1)*alpha, l)), j < beta:
+//   1. xt   = iNTT(c1) * [Qhat_{j,i}^-1]_{q_i}           (scale folded in iNTT)
+//   2. ext_j[t] = sum_{i in D_j} xt_i * [Qhat_{j,i}]_{p_t}, t outside D_j
+//      (fast base conversion), then NTT;  ext_j[t] = c1[t] for t in D_j
+//   3. acc_b[t] = sum_j ext_j[t] * key[j][b][t]         (b = 0, 1)
+//   4. ModDown: z_k = iNTT(acc_b[P_k]) * [Phat_k^-1]_{p_k};
+//      conv_i = NTT(sum_k z_k [Phat_k]_{q_i});
+//      d_b[i] = (acc_b[i] - conv_i) * [P^-1]_{q_i}
+//   5. HRotate: out = (pi_g(c0 + d0), pi_g(d1)); the automorphism is a
+//      gather folded into the ModDown combine.  Relinearisation adds
+//      (d0, d1) of the degree-2 ciphertext instead and uses g = 1.
+// Every key limb (digit, poly, prime) is read by one grid row that covers all
+// ciphertexts of the batch, so a batch sharing a key streams it once.
+#include "b2f_internal.h"
+
+namespace b2f {
+namespace {
+
+constexpr int TPB = 256;
+
+__device__ __forceinline__ uint32_t brv16(uint32_t x) { return __brev(x) >> 16; }
+
+// source evaluation index of output k under X -> X^g (g odd, < 2N)
+__device__ __forceinline__ uint32_t auto_src(uint32_t k, uint32_t g) {
+  uint32_t e = 2 * brv16(k) + 1;
+  uint32_t e2 = (uint32_t)(((uint64_t)e * g) & (2 * kN - 1));
+  return brv16((e2 - 1) >> 1);
+}
+
+// Step 2: fast base conversion of one digit to every target outside it.
+// grid (N/TPB, beta, cts); xt [ct][l][N]; ext [ct][beta][l+K][N]
+__global__ void __launch_bounds__(TPB) modup_conv_kernel(
+    const uint64_t *__restrict__ xt, uint64_t *__restrict__ ext,
+    const ulonglong2 *__restrict__ conv, const uint64_t *__restrict__ primes,
+    int l, int K, int L, int alpha) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int j = blockIdx.y, ct = blockIdx.z;
+  const int beta = gridDim.y, lk = l + K;
+  const int lo = j * alpha, hi = min(lo + alpha, l), w = hi - lo;
+  const uint64_t *src = xt + ((size_t)ct * l + lo) * kN + n;
+  uint64_t xs[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (i < w) xs[i] = src[(size_t)i * kN];
+  uint64_t *dst = ext + ((size_t)ct * beta + j) * lk * kN + n;
+  const ulonglong2 *cj = conv + (size_t)j * lk * alpha;
+  for (int t = 0; t < lk; ++t) {
+    if (t >= lo && t < hi) continue;
+    const uint64_t p = primes[t < l ? t : L + (t - l)], p2 = 2 * p;
+    const ulonglong2 *c = cj + (size_t)t * alpha;
+    uint64_t acc = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < w) {
+        ulonglong2 cc = __ldg(c + i);
+        acc += shoup_lazy(xs[i], cc.x, cc.y, p);
+        acc = acc >= p2 ? acc - p2 : acc;
+      }
+    }
+    dst[(size_t)t * kN] = acc >= p ? acc - p : acc;
+  }
+}
+
+// Step 3: key inner product.  grid (N/TPB, cts, l+K): the slowest grid axis
+// is the target limb so every key limb is reused across the batch in L2.
+__global__ void __launch_bounds__(TPB) key_inner_product_kernel(
+    const uint64_t *__restrict__ c1, long long c1_stride,
+    const uint64_t *__restrict__ ext, const uint64_t *__restrict__ key,
+    uint64_t *__restrict__ acc, const Mod *__restrict__ mods, int l, int K,
+    int L, int alpha, int beta) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int ct = blockIdx.y, t = blockIdx.z;
+  const int lk = l + K, np = L + K;
+  const int gp = t < l ? t : L + (t - l);
+  const Mod M = mods[gp];
+  U128 s0 = {0, 0}, s1 = {0, 0};
+  for (int j = 0; j < beta; ++j) {
+    const int lo = j * alpha, hi = min(lo + alpha, l);
+    uint64_t e;
+    if (t >= lo && t < hi)
+      e = c1[ct * c1_stride + (size_t)t * kN + n];
+    else
+      e = ext[(((size_t)ct * beta + j) * lk + t) * kN + n];
+    const uint64_t *kb = key + ((size_t)j * 2 * np + gp) * kN + n;
+    mac128(s0, e, __ldg(kb));
+    mac128(s1, e, __ldg(kb + (size_t)np * kN));
+  }
+  uint64_t *o = acc + ((size_t)ct * 2 * lk + t) * kN + n;
+  o[0] = reduce128(s0.hi, s0.lo, M);
+  o[(size_t)lk * kN] = reduce128(s1.hi, s1.lo, M);
+}
+
+// Step 4b: convert the P part (coefficient form, pre-scaled) to each q_i.
+// grid (N/TPB, 2, cts); acc [ct][2][l+K][N] -> conv [ct][2][l][N]
+__global__ void __launch_bounds__(TPB) moddown_conv_kernel(
+    const uint64_t *__restrict__ acc, uint64_t *__restrict__ conv_out,
+    const ulonglong2 *__restrict__ md_conv, const uint64_t *__restrict__ primes,
+    int l, int K) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int b = blockIdx.y, ct = blockIdx.z;
+  const int lk = l + K;
+  const uint64_t *z = acc + (((size_t)ct * 2 + b) * lk + l) * kN + n;
+  uint64_t zs[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    if (k < K) zs[k] = z[(size_t)k * kN];
+  uint64_t *o = conv_out + (((size_t)ct * 2 + b) * l) * kN + n;
+  for (int i = 0; i < l; ++i) {
+    const uint64_t q = primes[i], q2 = 2 * q;
+    const ulonglong2 *c = md_conv + (size_t)i * K;
+    uint64_t a = 0;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      if (k < K) {
+        ulonglong2 cc = __ldg(c + k);
+        a += shoup_lazy(zs[k], cc.x, cc.y, q);
+        a = a >= q2 ? a - q2 : a;
+      }
+    }
+    o[(size_t)i * kN] = a >= q ? a - q : a;
+  }
+}
+
+// Step 4c + 5: out_b[i][k] = ((acc_b[i] - conv_b[i]) * P^-1 + add_b[i])[pi_g(k)]
+// grid (N/TPB, l, cts).  add_b may be null (add_stride ignored).
+__global__ void __launch_bounds__(TPB) moddown_combine_kernel(
+    const uint64_t *__restrict__ acc, const uint64_t *__restrict__ conv,
+    const uint64_t *__restrict__ add0, const uint64_t *__restrict__ add1,
+    long long add_stride, uint64_t *__restrict__ out, long long out_stride,
+    const ulonglong2 *__restrict__ pinv, const uint64_t *__restrict__ primes,
+    int l, int K, uint32_t g) {
+  const int k = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, ct = blockIdx.z;
+  const int lk = l + K;
+  const uint32_t src = g == 1 ? (uint32_t)k : auto_src(k, g);
+  const uint64_t q = primes[i];
+  const ulonglong2 pi = pinv[i];
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    const uint64_t a = acc[(((size_t)ct * 2 + b) * lk + i) * kN + src];
+    const uint64_t c = conv[(((size_t)ct * 2 + b) * l + i) * kN + src];
+    uint64_t v = shoup(sub_mod(a, c, q), pi.x, pi.y, q);
+    const uint64_t *add = b ? add1 : add0;
+    if (add) v = add_mod(v, add[ct * add_stride + (size_t)i * kN + src], q);
+    out[ct * out_stride + ((size_t)b * l + i) * kN + k] = v;
+  }
+}
+
+__global__ void __launch_bounds__(TPB) automorphism_kernel(
+    const uint64_t *__restrict__ in, uint64_t *__restrict__ out, uint32_t g) {
+  const int k = blockIdx.x * TPB + threadIdx.x;
+  const size_t limb = blockIdx.y;
+  out[limb * kN + k] = in[limb * kN + auto_src(k, g)];
+}
+
+// ---------------------------------------------------------------------
+// host orchestration
+// ---------------------------------------------------------------------
+struct Scratch {
+  b2f_context *ctx;
+  cudaStream_t s;
+  void *owned = nullptr;
+  char *base = nullptr;
+  size_t used = 0, cap = 0;
+  int init(void *ws, size_t ws_bytes, size_t need) {
+    if (ws) {
+      if (ws_bytes < need) {
+        set_error("workspace too small: %zu bytes given, %zu needed", ws_bytes,
+                  need);
+        return B2F_ERR_ARG;
+      }
+      base = static_cast<char *>(ws);
+      cap = ws_bytes;
+      return B2F_OK;
+    }
+    B2F_CUDA(cudaMallocAsync(&owned, need ? need : 16, s));
+    base = static_cast<char *>(owned);
+    cap = need;
+    return B2F_OK;
+  }
+  uint64_t *take(size_t words) {
+    size_t bytes = (words * 8 + 255) & ~size_t(255);
+    char *p = base + used;
+    used += bytes;
+    return reinterpret_cast<uint64_t *>(p);
+  }
+  ~Scratch() {
+    if (owned) cudaFreeAsync(owned, s);
+  }
+};
+
+inline size_t rnd(size_t words) { return (words * 8 + 255) & ~size_t(255); }
+
+size_t modup_bytes(const b2f_context *ctx, int cts, int l) {
+  const int beta = (l + ctx->alpha - 1) / ctx->alpha;
+  return rnd((size_t)cts * l * kN) + rnd((size_t)cts * beta * (l + ctx->K) * kN);
+}
+size_t moddown_bytes(const b2f_context *ctx, int cts, int l) {
+  return rnd((size_t)cts * 2 * (l + ctx->K) * kN) + rnd((size_t)cts * 2 * l * kN);
+}
+
+// ModUp of c1 (cts ciphertext-strided) into ext; xt is scratch.
+int modup(b2f_context *ctx, const uint64_t *c1, long long c1_stride, int cts,
+          int l, uint64_t *xt, uint64_t *ext, cudaStream_t s) {
+  const LevelTables &T = ctx->levels[l];
+  const int K = ctx->K, lk = l + K, beta = T.beta, alpha = ctx->alpha;
+  // 1. iNTT with the per-digit Qhat^-1 scale: c1 -> xt
+  std::vector<LimbJob> jobs(l);
+  for (int i = 0; i < l; ++i)
+    jobs[i] = LimbJob{(uint32_t)i, (uint32_t)i, (uint16_t)i, (uint16_t)i, 0};
+  const LimbJob *d = job_table(ctx, {1, l}, jobs);
+  if (!d) return B2F_ERR_NOMEM;
+  int rc = launch_ntt(ctx, c1, c1_stride, xt, (long long)l * kN, d, l, cts, 1,
+                      T.modup_scale, s);
+  if (rc) return rc;
+  // 2. base conversion
+  modup_conv_kernel<<<dim3(kN / TPB, beta, cts), TPB, 0, s>>>(
+      xt, ext, T.modup_conv, ctx->d_primes, l, K, ctx->L, alpha);
+  B2F_LAUNCHED("modup_conv_kernel");
+  // 3. NTT of the converted limbs
+  std::vector<LimbJob> fj;
+  for (int j = 0; j < beta; ++j) {
+    int lo = j * alpha, hi = std::min(lo + alpha, l);
+    for (int t = 0; t < lk; ++t) {
+      if (t >= lo && t < hi) continue;
+      uint32_t off = (uint32_t)(j * lk + t);
+      fj.push_back(LimbJob{off, off, (uint16_t)prime_of(ctx, l, t), 0, 0});
+    }
+  }
+  d = job_table(ctx, {2, l}, fj);
+  if (!d) return B2F_ERR_NOMEM;
+  const long long es = (long long)beta * lk * kN;
+  return launch_ntt(ctx, ext, es, ext, es, d, (int)fj.size(), cts, 0, nullptr,
+                    s);
+}
+
+// Inner product with one key and ModDown; writes out (cts x 2 x l limbs).
+int ip_moddown(b2f_context *ctx, const uint64_t *c1, long long c1_stride,
+               const uint64_t *ext, int cts, int l, const uint64_t *key,
+               const uint64_t *add0, const uint64_t *add1,
+               long long add_stride, uint32_t g, uint64_t *out,
+               long long out_stride, uint64_t *acc, uint64_t *conv,
+               cudaStream_t s) {
+  const LevelTables &T = ctx->levels[l];
+  const int K = ctx->K, lk = l + K;
+  key_inner_product_kernel<<<dim3(kN / TPB, cts, lk), TPB, 0, s>>>(
+      c1, c1_stride, ext, key, acc, ctx->d_mod, l, K, ctx->L, ctx->alpha,
+      T.beta);
+  B2F_LAUNCHED("key_inner_product_kernel");
+  // iNTT of the P limbs of both polys, scaled by N^-1 Phat_k^-1
+  std::vector<LimbJob> pj;
+  for (int b = 0; b < 2; ++b)
+    for (int k = 0; k < K; ++k) {
+      uint32_t off = (uint32_t)(b * lk + l + k);
+      pj.push_back(LimbJob{off, off, (uint16_t)(ctx->L + k), (uint16_t)k, 0});
+    }
+  const LimbJob *d = job_table(ctx, {3, l}, pj);
+  if (!d) return B2F_ERR_NOMEM;
+  const long long as = 2LL * lk * kN;
+  int rc = launch_ntt(ctx, acc, as, acc, as, d, 2 * K, cts, 1,
+                      ctx->d_moddown_scale, s);
+  if (rc) return rc;
+  moddown_conv_kernel<<<dim3(kN / TPB, 2, cts), TPB, 0, s>>>(
+      acc, conv, ctx->d_moddown_conv, ctx->d_primes, l, K);
+  B2F_LAUNCHED("moddown_conv_kernel");
+  rc = ntt_polys(ctx, conv, 2 * cts, l, 0, 0, s);
+  if (rc) return rc;
+  moddown_combine_kernel<<<dim3(kN / TPB, l, cts), TPB, 0, s>>>(
+      acc, conv, add0, add1, add_stride, out, out_stride, ctx->d_moddown_pinv,
+      ctx->d_primes, l, K, g);
+  B2F_LAUNCHED("moddown_combine_kernel");
+  return B2F_OK;
+}
+
+int check_level(const b2f_context *ctx, int l, const char *fn) {
+  if (!ctx) {
+    set_error("%s: null context", fn);
+    return B2F_ERR_ARG;
+  }
+  if (l < 1 || l > ctx->L) {
+    set_error("%s: level limbs %d outside [1, %d]", fn, l, ctx->L);
+    return B2F_ERR_ARG;
+  }
+  if (ctx->K < 1 || ctx->K > 16) {
+    set_error("%s: key switching needs 1..16 special primes (K=%d)", fn,
+              ctx->K);
+    return B2F_ERR_UNSUPPORTED;
+  }
+  if (ctx->alpha > 16) {
+    set_error("%s: digits wider than 16 limbs are not supported (alpha=%d)",
+              fn, ctx->alpha);
+    return B2F_ERR_UNSUPPORTED;
+  }
+  return B2F_OK;
+}
+
+bool valid_galois(uint64_t g) { return (g & 1) && g < 2ull * kN; }
+
+}  // namespace
+
+size_t rotate_workspace(const b2f_context *ctx, int cts, int l) {
+  return modup_bytes(ctx, cts, l) + moddown_bytes(ctx, cts, l);
+}
+
+}  // namespace b2f
+
+using namespace b2f;
+
+extern "C" {
+
+size_t b2f_rotate_workspace(const b2f_context *ctx, int num_cts, int l) {
+  if (!ctx || l < 1 || l > ctx->L || num_cts < 0) return 0;
+  return rotate_workspace(ctx, num_cts, l);
+}
+
+int b2f_rotate(b2f_context *ctx, const uint64_t *ct_in, uint64_t *ct_out,
+               int num_cts, int l, uint64_t galois, const uint64_t *key,
+               void *ws, size_t ws_bytes, void *stream) {
+  int rc = check_level(ctx, l, "b2f_rotate");
+  if (rc) return rc;
+  B2F_CHECK_ARG(ct_in && ct_out && key && num_cts >= 0,
+                "b2f_rotate: null argument");
+  B2F_CHECK_ARG(valid_galois(galois), "b2f_rotate: galois element %llu is not "
+                "an odd residue below 2N", (unsigned long long)galois);
+  B2F_CHECK_ARG(ct_in != ct_out, "b2f_rotate: in-place rotation is not supported");
+  if (num_cts == 0) return B2F_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  Scratch sc{ctx, s};
+  if ((rc = sc.init(ws, ws_bytes, rotate_workspace(ctx, num_cts, l)))) return rc;
+  const int beta = ctx->levels[l].beta, lk = l + ctx->K;
+  uint64_t *xt = sc.take((size_t)num_cts * l * kN);
+  uint64_t *ext = sc.take((size_t)num_cts * beta * lk * kN);
+  uint64_t *acc = sc.take((size_t)num_cts * 2 * lk * kN);
+  uint64_t *conv = sc.take((size_t)num_cts * 2 * l * kN);
+  const long long cs = 2LL * l * kN;
+  if ((rc = modup(ctx, ct_in + (size_t)l * kN, cs, num_cts, l, xt, ext, s)))
+    return rc;
+  return ip_moddown(ctx, ct_in + (size_t)l * kN, cs, ext, num_cts, l, key,
+                    ct_in, nullptr, cs, (uint32_t)galois, ct_out, cs, acc, conv,
+                    s);
+}
+
+size_t b2f_relinearize_workspace(const b2f_context *ctx, int num_cts, int l) {
+  if (!ctx || l < 1 || l > ctx->L || num_cts < 0) return 0;
+  return rotate_workspace(ctx, num_cts, l);
+}
+
+int b2f_relinearize(b2f_context *ctx, const uint64_t *ct3_in, uint64_t *ct_out,
+                    int num_cts, int l, const uint64_t *relin_key, void *ws,
+                    size_t ws_bytes, void *stream) {
+  int rc = check_level(ctx, l, "b2f_relinearize");
+  if (rc) return rc;
+  B2F_CHECK_ARG(ct3_in && ct_out && relin_key && num_cts >= 0,
+                "b2f_relinearize: null argument");
+  if (num_cts == 0) return B2F_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  Scratch sc{ctx, s};
+  if ((rc = sc.init(ws, ws_bytes, rotate_workspace(ctx, num_cts, l)))) return rc;
+  const int beta = ctx->levels[l].beta, lk = l + ctx->K;
+  uint64_t *xt = sc.take((size_t)num_cts * l * kN);
+  uint64_t *ext = sc.take((size_t)num_cts * beta * lk * kN);
+  uint64_t *acc = sc.take((size_t)num_cts * 2 * lk * kN);
+  uint64_t *conv = sc.take((size_t)num_cts * 2 * l * kN);
+  const long long s3 = 3LL * l * kN;
+  const uint64_t *d2 = ct3_in + 2 * (size_t)l * kN;
+  if ((rc = modup(ctx, d2, s3, num_cts, l, xt, ext, s))) return rc;
+  return ip_moddown(ctx, d2, s3, ext, num_cts, l, relin_key, ct3_in,
+                    ct3_in + (size_t)l * kN, s3, 1u, ct_out, 2LL * l * kN, acc,
+                    conv, s);
+}
+
+size_t b2f_modup_workspace(const b2f_context *ctx, int l) {
+  if (!ctx || l < 1 || l > ctx->L) return 0;
+  return rnd((size_t)l * kN);
+}
+
+int b2f_modup(b2f_context *ctx, const uint64_t *ct, int l, uint64_t *ext,
+              void *ws, size_t ws_bytes, void *stream) {
+  int rc = check_level(ctx, l, "b2f_modup");
+  if (rc) return rc;
+  B2F_CHECK_ARG(ct && ext, "b2f_modup: null argument");
+  cudaStream_t s = (cudaStream_t)stream;
+  Scratch sc{ctx, s};
+  if ((rc = sc.init(ws, ws_bytes, b2f_modup_workspace(ctx, l)))) return rc;
+  uint64_t *xt = sc.take((size_t)l * kN);
+  return modup(ctx, ct + (size_t)l * kN, 2LL * l * kN, 1, l, xt, ext, s);
+}
+
+size_t b2f_rotate_hoisted_workspace(const b2f_context *ctx, int l) {
+  if (!ctx || l < 1 || l > ctx->L) return 0;
+  return moddown_bytes(ctx, 1, l);
+}
+
+int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
+                       const uint64_t *ext, int count, const uint64_t *galois,
+                       const uint64_t *const *keys, uint64_t *out, void *ws,
+                       size_t ws_bytes, void *stream) {
+  int rc = check_level(ctx, l, "b2f_rotate_hoisted");
+  if (rc) return rc;
+  B2F_CHECK_ARG(ct && ext && out && count >= 0 && (count == 0 || (galois && keys)),
+                "b2f_rotate_hoisted: null argument");
+  for (int r = 0; r < count; ++r) {
+    B2F_CHECK_ARG(keys[r], "b2f_rotate_hoisted: key %d is null", r);
+    B2F_CHECK_ARG(valid_galois(galois[r]),
+                  "b2f_rotate_hoisted: bad galois element %llu",
+                  (unsigned long long)galois[r]);
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  Scratch sc{ctx, s};
+  if ((rc = sc.init(ws, ws_bytes, moddown_bytes(ctx, 1, l)))) return rc;
+  const int lk = l + ctx->K;
+  uint64_t *acc = sc.take((size_t)2 * lk * kN);
+  uint64_t *conv = sc.take((size_t)2 * l * kN);
+  const long long cs = 2LL * l * kN;
+  for (int r = 0; r < count; ++r) {
+    rc = ip_moddown(ctx, ct + (size_t)l * kN, cs, ext, 1, l, keys[r], ct,
+                    nullptr, cs, (uint32_t)galois[r], out + (size_t)r * cs, cs,
+                    acc, conv, s);
+    if (rc) return rc;
+  }
+  return B2F_OK;
+}
+
+int b2f_automorphism(b2f_context *ctx, const uint64_t *in, uint64_t *out,
+                     int num_polys, int limbs, uint64_t galois, void *stream) {
+  B2F_CHECK_ARG(ctx && in && out && num_polys >= 0 && limbs >= 0,
+                "b2f_automorphism: bad argument");
+  B2F_CHECK_ARG(valid_galois(galois), "b2f_automorphism: bad galois element");
+  B2F_CHECK_ARG(in != out, "b2f_automorphism: in-place is not supported");
+  if (!num_polys || !limbs) return B2F_OK;
+  automorphism_kernel<<<dim3(kN / TPB, num_polys * limbs), TPB, 0,
+                        (cudaStream_t)stream>>>(in, out, (uint32_t)galois);
+  B2F_LAUNCHED("automorphism_kernel");
+  return B2F_OK;
+}
+
+}  // extern "C"

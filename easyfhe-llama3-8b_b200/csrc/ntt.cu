@@ -1,0 +1,382 @@
+// Batched negacyclic NTT / inverse NTT for N = 2^16 on sm_100a.
+//
+// One thread-block cluster of 8 CTAs owns one limb (2^16 words = 512 KiB):
+// the limb is read from HBM once and written once, and everything in between
+// stays on chip.  Forward (Cooley-Tukey, natural order in, bit-reversed out):
+//   1. each CTA loads 1024 columns x 8 rows (row stride 8192) straight from
+//      HBM and runs stages 0-2 as radix-8 butterflies in registers;
+//   2. each column's 8 outputs are scattered to the 8 CTAs of the cluster
+//      through distributed shared memory, so CTA r then holds the contiguous
+//      block [8192 r, 8192 (r+1));
+//   3. stages 3-15 run in three register passes of 4 stages over shared
+//      memory (radix-16 per thread, 512 threads x 16 words); the last stage
+//      pairs neighbouring words and uses a warp shuffle;
+//   4. the block is staged through shared memory and written with 16-byte
+//      coalesced stores.
+// The inverse (Gentleman-Sande, bit-reversed in, natural out) runs the same
+// steps backwards and folds N^-1 (times an optional per-limb constant) into
+// the final stage.  Butterflies use Harvey's lazy reduction: forward values
+// live in [0, 4q), inverse values in [0, 2q), outputs are fully reduced.
+// Shared memory holds the block with two pad words per 32 so that every
+// pass is free of bank conflicts.
+#include <cooperative_groups.h>
+
+#include "b2f_internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace b2f {
+namespace {
+
+constexpr int CL = 8;                       // CTAs per cluster = per limb
+constexpr int BLK = kN / CL;                // 8192 words per CTA
+constexpr int NT = 512;                     // threads per CTA
+constexpr int SMEM_WORDS = BLK + 2 * (BLK / 32);
+constexpr int SMEM_BYTES = SMEM_WORDS * 8;  // 69632
+
+__device__ __forceinline__ int pad(int l) { return l + ((l >> 5) << 1); }
+
+struct NttParams {
+  const uint64_t *in;
+  uint64_t *out;
+  const LimbJob *jobs;
+  long long in_stride, out_stride;
+  const ulonglong2 *tw;      // [prime][N]
+  const uint64_t *primes;
+  const ulonglong2 *scales;  // inverse only
+  int jobs_per_item;
+};
+
+__device__ __forceinline__ ulonglong2 ldtw(const ulonglong2 *tw, int idx) {
+  return __ldg(tw + idx);
+}
+
+// twiddle index of stage s for global element j: 2^s + j / 2^(16-s)
+__device__ __forceinline__ int tw_index(int s, int j) {
+  return (1 << s) + (j >> (kLogN - s));
+}
+
+__device__ __forceinline__ void ct_bfly(uint64_t &x, uint64_t &y, ulonglong2 w,
+                                        uint64_t q, uint64_t q2) {
+  uint64_t u = x >= q2 ? x - q2 : x;
+  uint64_t t = y * w.x - __umul64hi(y, w.y) * q;
+  x = u + t;
+  y = u - t + q2;
+}
+
+__device__ __forceinline__ void gs_bfly(uint64_t &x, uint64_t &y, ulonglong2 w,
+                                        uint64_t q, uint64_t q2) {
+  uint64_t u = x + y;
+  u = u >= q2 ? u - q2 : u;
+  uint64_t t = x - y + q2;
+  x = u;
+  y = t * w.x - __umul64hi(t, w.y) * q;
+}
+
+// Four CT stages s0..s0+3 on 16 registers whose element index is
+// j(k) = base + k * stride.
+__device__ __forceinline__ void ct_pass(uint64_t (&x)[16], const ulonglong2 *tw,
+                                        int s0, int base, int stride,
+                                        uint64_t q, uint64_t q2) {
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int d = 8 >> s;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      if (k & d) continue;
+      ulonglong2 w = ldtw(tw, tw_index(s0 + s, base + k * stride));
+      ct_bfly(x[k], x[k + d], w, q, q2);
+    }
+  }
+}
+
+__device__ __forceinline__ void gs_pass(uint64_t (&x)[16], const ulonglong2 *tw,
+                                        int s0, int base, int stride,
+                                        uint64_t q, uint64_t q2) {
+  // stages s0+3 down to s0
+#pragma unroll
+  for (int s = 3; s >= 0; --s) {
+    const int d = 8 >> s;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      if (k & d) continue;
+      ulonglong2 w = ldtw(tw, tw_index(s0 + s, base + k * stride));
+      gs_bfly(x[k], x[k + d], w, q, q2);
+    }
+  }
+}
+
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 1)
+    ntt_fwd_kernel(NttParams P) {
+  extern __shared__ __align__(16) uint64_t buf[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int tid = threadIdx.x;
+  const long long job_id = blockIdx.x / CL;
+  const long long item = job_id / P.jobs_per_item;
+  const LimbJob job = P.jobs[job_id % P.jobs_per_item];
+  const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
+  uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
+  const uint64_t q = P.primes[job.prime], q2 = 2 * q;
+  const ulonglong2 *tw = P.tw + (size_t)job.prime * kN;
+
+  uint64_t x[16];
+  const int c0 = rank * 1024 + 2 * tid;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + c0 + k * BLK);
+    x[k] = v.x;
+    x[8 + k] = v.y;
+  }
+  // stages 0..2 on the 8 rows of both columns
+  {
+    const ulonglong2 w1 = ldtw(tw, 1), w2 = ldtw(tw, 2), w3 = ldtw(tw, 3);
+    const ulonglong2 w4 = ldtw(tw, 4), w5 = ldtw(tw, 5), w6 = ldtw(tw, 6),
+                     w7 = ldtw(tw, 7);
+#pragma unroll
+    for (int h = 0; h < 16; h += 8) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) ct_bfly(x[h + k], x[h + k + 4], w1, q, q2);
+      ct_bfly(x[h + 0], x[h + 2], w2, q, q2);
+      ct_bfly(x[h + 1], x[h + 3], w2, q, q2);
+      ct_bfly(x[h + 4], x[h + 6], w3, q, q2);
+      ct_bfly(x[h + 5], x[h + 7], w3, q, q2);
+      ct_bfly(x[h + 0], x[h + 1], w4, q, q2);
+      ct_bfly(x[h + 2], x[h + 3], w5, q, q2);
+      ct_bfly(x[h + 4], x[h + 5], w6, q, q2);
+      ct_bfly(x[h + 6], x[h + 7], w7, q, q2);
+    }
+  }
+  cluster.sync();  // every CTA of the cluster is resident
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    uint64_t *remote = cluster.map_shared_rank(buf, k);
+    *reinterpret_cast<ulonglong2 *>(remote + pad(c0)) =
+        make_ulonglong2(x[k], x[8 + k]);
+  }
+  cluster.sync();
+
+  const int jb = rank * BLK;
+  // pass A: stages 3-6, l = tid + 512 k
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = buf[pad(tid + 512 * k)];
+  ct_pass(x, tw, 3, jb + tid, 512, q, q2);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) buf[pad(tid + 512 * k)] = x[k];
+  __syncthreads();
+  // pass B: stages 7-10, l = (tid/32)*512 + tid%32 + 32 k
+  const int lb = (tid >> 5) * 512 + (tid & 31);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = buf[pad(lb + 32 * k)];
+  ct_pass(x, tw, 7, jb + lb, 32, q, q2);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) buf[pad(lb + 32 * k)] = x[k];
+  __syncthreads();
+  // pass C: stages 11-14 in registers, stage 15 across lane pairs
+  const int lc = (tid >> 1) * 32 + (tid & 1);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = buf[pad(lc + 2 * k)];
+  ct_pass(x, tw, 11, jb + lc, 2, q, q2);
+  const bool odd = tid & 1;
+  const int je = jb + (tid >> 1) * 32;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    uint64_t mine = x[k];
+    uint64_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+    uint64_t X = odd ? other : mine, Y = odd ? mine : other;
+    ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * k));
+    uint64_t u = X >= q2 ? X - q2 : X;
+    uint64_t t = Y * w.x - __umul64hi(Y, w.y) * q;
+    uint64_t r = odd ? u - t + q2 : u + t;
+    r = r >= q2 ? r - q2 : r;
+    x[k] = r >= q ? r - q : r;
+  }
+  // stage through shared memory for coalesced 16-byte stores
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 16; ++k) buf[pad(lc + 2 * k)] = x[k];
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int idx = 2 * (tid + NT * r);
+    ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(buf + pad(idx));
+    *reinterpret_cast<ulonglong2 *>(o + jb + idx) = v;
+  }
+}
+
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 1)
+    ntt_inv_kernel(NttParams P) {
+  extern __shared__ __align__(16) uint64_t buf[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int tid = threadIdx.x;
+  const long long job_id = blockIdx.x / CL;
+  const long long item = job_id / P.jobs_per_item;
+  const LimbJob job = P.jobs[job_id % P.jobs_per_item];
+  const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
+  uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
+  const uint64_t q = P.primes[job.prime], q2 = 2 * q;
+  const ulonglong2 *tw = P.tw + (size_t)job.prime * kN;
+  const int jb = rank * BLK;
+
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int idx = 2 * (tid + NT * r);
+    ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + jb + idx);
+    *reinterpret_cast<ulonglong2 *>(buf + pad(idx)) = v;
+  }
+  __syncthreads();
+
+  uint64_t x[16];
+  // pass C: stage 15 across lane pairs, then stages 14-11
+  const int lc = (tid >> 1) * 32 + (tid & 1);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = buf[pad(lc + 2 * k)];
+  const bool odd = tid & 1;
+  const int je = jb + (tid >> 1) * 32;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    uint64_t mine = x[k];
+    uint64_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+    uint64_t X = odd ? other : mine, Y = odd ? mine : other;
+    if (odd) {
+      ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * k));
+      uint64_t t = X - Y + q2;
+      x[k] = t * w.x - __umul64hi(t, w.y) * q;
+    } else {
+      uint64_t u = X + Y;
+      x[k] = u >= q2 ? u - q2 : u;
+    }
+  }
+  gs_pass(x, tw, 11, jb + lc, 2, q, q2);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) buf[pad(lc + 2 * k)] = x[k];
+  __syncthreads();
+  // pass B: stages 10-7
+  const int lb = (tid >> 5) * 512 + (tid & 31);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = buf[pad(lb + 32 * k)];
+  gs_pass(x, tw, 7, jb + lb, 32, q, q2);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) buf[pad(lb + 32 * k)] = x[k];
+  __syncthreads();
+  // pass A: stages 6-3
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = buf[pad(tid + 512 * k)];
+  gs_pass(x, tw, 3, jb + tid, 512, q, q2);
+  cluster.sync();  // every CTA has finished reading its own block
+  // word l of block `rank` is row `rank` of column l, owned by CTA l/1024
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int l = tid + 512 * k;
+    uint64_t *remote = cluster.map_shared_rank(buf, l >> 10);
+    remote[rank * 1024 + (l & 1023)] = x[k];
+  }
+  cluster.sync();
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(buf + k * 1024 + 2 * tid);
+    x[k] = v.x;
+    x[8 + k] = v.y;
+  }
+  const ulonglong2 w1 = ldtw(tw, 1), w2 = ldtw(tw, 2), w3 = ldtw(tw, 3);
+  const ulonglong2 w4 = ldtw(tw, 4), w5 = ldtw(tw, 5), w6 = ldtw(tw, 6),
+                   w7 = ldtw(tw, 7);
+  const ulonglong2 sc = P.scales[job.scale_idx];
+  const int c0 = rank * 1024 + 2 * tid;
+#pragma unroll
+  for (int h = 0; h < 16; h += 8) {
+    gs_bfly(x[h + 0], x[h + 1], w4, q, q2);
+    gs_bfly(x[h + 2], x[h + 3], w5, q, q2);
+    gs_bfly(x[h + 4], x[h + 5], w6, q, q2);
+    gs_bfly(x[h + 6], x[h + 7], w7, q, q2);
+    gs_bfly(x[h + 0], x[h + 2], w2, q, q2);
+    gs_bfly(x[h + 1], x[h + 3], w2, q, q2);
+    gs_bfly(x[h + 4], x[h + 6], w3, q, q2);
+    gs_bfly(x[h + 5], x[h + 7], w3, q, q2);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) gs_bfly(x[h + k], x[h + k + 4], w1, q, q2);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint64_t r = x[h + k] * sc.x - __umul64hi(x[h + k], sc.y) * q;
+      x[h + k] = r >= q ? r - q : r;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    *reinterpret_cast<ulonglong2 *>(o + c0 + k * BLK) =
+        make_ulonglong2(x[k], x[8 + k]);
+}
+
+}  // namespace
+
+int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
+               uint64_t *out, long long out_stride, const LimbJob *jobs,
+               int jobs_per_item, int items, int inverse,
+               const ulonglong2 *scales, cudaStream_t s) {
+  if (items <= 0 || jobs_per_item <= 0) return B2F_OK;
+  static unsigned configured = 0;  // one bit per device
+  const unsigned bit = 1u << (ctx->device & 31);
+  if (!(configured & bit)) {
+    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SMEM_BYTES));
+    B2F_CUDA(cudaFuncSetAttribute(ntt_inv_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SMEM_BYTES));
+    configured |= bit;
+  }
+  NttParams P;
+  P.in = in;
+  P.out = out;
+  P.in_stride = in_stride;
+  P.out_stride = out_stride;
+  P.jobs = jobs;
+  P.tw = inverse ? ctx->d_tw_inv : ctx->d_tw_fwd;
+  P.primes = ctx->d_primes;
+  P.scales = scales ? scales : ctx->d_ninv;
+  P.jobs_per_item = jobs_per_item;
+  const long long blocks = (long long)items * jobs_per_item * CL;
+  if (blocks > 0x7fffffffLL) {
+    set_error("launch_ntt: batch too large (%lld limbs)", blocks / CL);
+    return B2F_ERR_ARG;
+  }
+  if (inverse)
+    ntt_inv_kernel<<<(unsigned)blocks, NT, SMEM_BYTES, s>>>(P);
+  else
+    ntt_fwd_kernel<<<(unsigned)blocks, NT, SMEM_BYTES, s>>>(P);
+  B2F_LAUNCHED("ntt kernel launch");
+  return B2F_OK;
+}
+
+int ntt_polys(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
+              int p_limbs, int inverse, cudaStream_t s) {
+  const int limbs = q_limbs + p_limbs;
+  std::vector<int> key = {0, q_limbs, p_limbs};
+  std::vector<LimbJob> jobs(limbs);
+  for (int i = 0; i < limbs; ++i) {
+    int pi = prime_of(ctx, q_limbs, i);
+    jobs[i] = LimbJob{(uint32_t)i, (uint32_t)i, (uint16_t)pi, (uint16_t)pi};
+  }
+  const LimbJob *d = job_table(ctx, key, jobs);
+  if (!d) return B2F_ERR_NOMEM;
+  const long long st = (long long)limbs * kN;
+  return launch_ntt(ctx, data, st, data, st, d, limbs, num_polys, inverse,
+                    nullptr, s);
+}
+
+}  // namespace b2f
+
+using namespace b2f;
+
+extern "C" int b2f_ntt(b2f_context *ctx, uint64_t *data, int num_polys,
+                       int q_limbs, int p_limbs, int inverse, void *stream) {
+  B2F_CHECK_ARG(ctx && data, "b2f_ntt: null argument");
+  B2F_CHECK_ARG(num_polys >= 0 && q_limbs >= 0 && q_limbs <= ctx->L &&
+                    p_limbs >= 0 && p_limbs <= ctx->K && q_limbs + p_limbs > 0,
+                "b2f_ntt: bad limb counts q=%d p=%d (L=%d K=%d)", q_limbs,
+                p_limbs, ctx->L, ctx->K);
+  B2F_CHECK_ARG(((uintptr_t)data & 15) == 0, "b2f_ntt: data must be 16-byte aligned");
+  return ntt_polys(ctx, data, num_polys, q_limbs, p_limbs, inverse,
+                   (cudaStream_t)stream);
+}

@@ -1,0 +1,339 @@
+// Level management, limb-wise arithmetic and the baby-step/giant-step
+// plaintext x ciphertext multiply-accumulate.
+#include "b2f_internal.h"
+
+namespace b2f {
+size_t rotate_workspace(const b2f_context *ctx, int cts, int l);
+namespace {
+
+constexpr int TPB = 256;
+constexpr int GMAX = 8;  // giants accumulated per MAC pass
+
+__device__ __forceinline__ uint32_t brv16(uint32_t x) { return __brev(x) >> 16; }
+
+// rescale step 2: centred lift of the last limb (coefficient form) to q_i
+// grid (N/TPB, l-1, polys)
+__global__ void __launch_bounds__(TPB) rescale_lift_kernel(
+    const uint64_t *__restrict__ last, uint64_t *__restrict__ lifted,
+    const uint64_t *__restrict__ primes, const uint64_t *__restrict__ qlast_mod,
+    int l, uint64_t q_last) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, p = blockIdx.z;
+  const uint64_t v = last[(size_t)p * kN + n];
+  const uint64_t qi = primes[i];
+  uint64_t r = v % qi;
+  if (v > (q_last - 1) / 2) r = sub_mod(r, qlast_mod[i], qi);
+  lifted[((size_t)p * (l - 1) + i) * kN + n] = r;
+}
+
+// rescale step 4: out = (in - lifted) * q_last^-1
+__global__ void __launch_bounds__(TPB) rescale_combine_kernel(
+    const uint64_t *__restrict__ in, const uint64_t *__restrict__ lifted,
+    uint64_t *__restrict__ out, const uint64_t *__restrict__ primes,
+    const ulonglong2 *__restrict__ inv, int l) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, p = blockIdx.z;
+  const uint64_t q = primes[i];
+  const ulonglong2 w = inv[i];
+  const uint64_t a = in[((size_t)p * l + i) * kN + n];
+  const uint64_t b = lifted[((size_t)p * (l - 1) + i) * kN + n];
+  out[((size_t)p * (l - 1) + i) * kN + n] = shoup(sub_mod(a, b, q), w.x, w.y, q);
+}
+
+// grid (N/TPB, l, polys)
+__global__ void __launch_bounds__(TPB) elementwise_kernel(
+    int op, const uint64_t *__restrict__ a, const uint64_t *__restrict__ b,
+    uint64_t *__restrict__ out, const Mod *__restrict__ mods, int l,
+    int b_polys) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, p = blockIdx.z;
+  const size_t ia = ((size_t)p * l + i) * kN + n;
+  const size_t ib = ((size_t)(b_polys == 1 ? 0 : p) * l + i) * kN + n;
+  const Mod M = mods[i];
+  const uint64_t x = a[ia], y = b[ib];
+  uint64_t r;
+  if (op == 0)
+    r = add_mod(x, y, M.q);
+  else if (op == 1)
+    r = sub_mod(x, y, M.q);
+  else
+    r = mul_mod(x, y, M);
+  out[ia] = r;
+}
+
+__global__ void __launch_bounds__(TPB) mul_i_kernel(
+    const uint64_t *__restrict__ a, uint64_t *__restrict__ out,
+    const ulonglong2 *__restrict__ factor, const uint64_t *__restrict__ primes,
+    int l, int negative) {
+  const int k = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, p = blockIdx.z;
+  const size_t idx = ((size_t)p * l + i) * kN + k;
+  const uint64_t q = primes[i];
+  const ulonglong2 w = factor[i];
+  const uint32_t e = 2 * brv16(k) + 1;
+  // evaluation at psi^e of X^(N/2) is omega^e, omega = psi^(N/2) (order 4)
+  const bool minus = ((e & 3) == 3) != (negative != 0);
+  uint64_t r = shoup(a[idx], w.x, w.y, q);
+  out[idx] = (minus && r) ? q - r : r;
+}
+
+struct ScalarArgs {
+  ulonglong2 mul[64];
+  uint64_t add[64];
+  int has_mul, has_add, add_poly;
+};
+
+__global__ void __launch_bounds__(TPB) scalar_kernel(
+    const uint64_t *__restrict__ a, uint64_t *__restrict__ out,
+    const uint64_t *__restrict__ primes, int l, ScalarArgs S) {
+  const int k = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, p = blockIdx.z;
+  const size_t idx = ((size_t)p * l + i) * kN + k;
+  const uint64_t q = primes[i];
+  uint64_t r = a[idx];
+  if (S.has_mul) r = shoup(r, S.mul[i].x, S.mul[i].y, q);
+  if (S.has_add && (S.add_poly < 0 || S.add_poly == p)) r = add_mod(r, S.add[i], q);
+  out[idx] = r;
+}
+
+// out[ct][g] (2 polys, l limbs) = sum_b pt[g0+g][b] * babies[ct][b]
+// grid (N/TPB, l, cts); up to GMAX giants per launch.
+__global__ void __launch_bounds__(TPB) mac_kernel(
+    const uint64_t *__restrict__ babies, int baby_count,
+    const uint64_t *__restrict__ pts, int g0, int G, int l,
+    uint64_t *__restrict__ out, int out_giants, const Mod *__restrict__ mods) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, ct = blockIdx.z;
+  const Mod M = mods[i];
+  const size_t limb = (size_t)i * kN + n;
+  const size_t ct_words = 2 * (size_t)l * kN, pt_words = (size_t)l * kN;
+  const uint64_t *bb = babies + (size_t)ct * baby_count * ct_words + limb;
+  U128 acc[GMAX][2];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) acc[g][0] = acc[g][1] = U128{0, 0};
+  for (int b = 0; b < baby_count; ++b) {
+    const uint64_t c0 = bb[(size_t)b * ct_words];
+    const uint64_t c1 = bb[(size_t)b * ct_words + pt_words];
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      if (g < G) {
+        const uint64_t w =
+            __ldg(pts + ((size_t)(g0 + g) * baby_count + b) * pt_words + limb);
+        mac128(acc[g][0], c0, w);
+        mac128(acc[g][1], c1, w);
+      }
+    }
+    // keep the 128-bit sums far from overflow for long baby runs
+    if ((b & 31) == 31) {
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g)
+        if (g < G) {
+          acc[g][0] = U128{reduce128(acc[g][0].hi, acc[g][0].lo, M), 0};
+          acc[g][1] = U128{reduce128(acc[g][1].hi, acc[g][1].lo, M), 0};
+        }
+    }
+  }
+  uint64_t *o = out + ((size_t)ct * out_giants + g0) * ct_words + limb;
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g)
+    if (g < G) {
+      o[(size_t)g * ct_words] = reduce128(acc[g][0].hi, acc[g][0].lo, M);
+      o[(size_t)g * ct_words + pt_words] = reduce128(acc[g][1].hi, acc[g][1].lo, M);
+    }
+}
+
+int launch_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
+               const uint64_t *pts, int giant_count, int l, uint64_t *out,
+               int cts, cudaStream_t s) {
+  for (int g0 = 0; g0 < giant_count; g0 += GMAX) {
+    const int G = std::min(GMAX, giant_count - g0);
+    mac_kernel<<<dim3(kN / TPB, l, cts), TPB, 0, s>>>(
+        babies, baby_count, pts, g0, G, l, out, giant_count, ctx->d_mod);
+    B2F_LAUNCHED("mac_kernel");
+  }
+  return B2F_OK;
+}
+
+}  // namespace
+}  // namespace b2f
+
+using namespace b2f;
+
+extern "C" {
+
+size_t b2f_rescale_workspace(const b2f_context *ctx, int num_polys, int l) {
+  if (!ctx || l < 2 || num_polys < 0) return 0;
+  return ((size_t)num_polys * kN + (size_t)num_polys * (l - 1) * kN) * 8 + 512;
+}
+
+int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
+                int num_polys, int l, void *ws, size_t ws_bytes, void *stream) {
+  B2F_CHECK_ARG(ctx && in && out && num_polys >= 0, "b2f_rescale: null argument");
+  B2F_CHECK_ARG(l >= 2 && l <= ctx->L, "b2f_rescale: needs 2..%d limbs, got %d",
+                ctx->L, l);
+  B2F_CHECK_ARG(in != out, "b2f_rescale: in-place rescale is not supported");
+  if (!num_polys) return B2F_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t need = b2f_rescale_workspace(ctx, num_polys, l);
+  void *owned = nullptr;
+  if (!ws) {
+    B2F_CUDA(cudaMallocAsync(&owned, need, s));
+    ws = owned;
+  } else {
+    B2F_CHECK_ARG(ws_bytes >= need, "b2f_rescale: workspace %zu < %zu", ws_bytes,
+                  need);
+  }
+  uint64_t *last = static_cast<uint64_t *>(ws);
+  uint64_t *lifted = last + (size_t)num_polys * kN;
+  const LevelTables &T = ctx->levels[l];
+  int rc;
+  {
+    std::vector<LimbJob> j = {
+        LimbJob{(uint32_t)(l - 1), 0u, (uint16_t)(l - 1), (uint16_t)(l - 1), 0}};
+    const LimbJob *d = job_table(ctx, {4, l}, j);
+    rc = d ? launch_ntt(ctx, in, (long long)l * kN, last, kN, d, 1, num_polys, 1,
+                        nullptr, s)
+           : B2F_ERR_NOMEM;
+  }
+  if (!rc) {
+    rescale_lift_kernel<<<dim3(kN / TPB, l - 1, num_polys), TPB, 0, s>>>(
+        last, lifted, ctx->d_primes, T.rescale_qlast, l, ctx->primes[l - 1]);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = cuda_status(e, "rescale_lift_kernel");
+  }
+  if (!rc) rc = ntt_polys(ctx, lifted, num_polys, l - 1, 0, 0, s);
+  if (!rc) {
+    rescale_combine_kernel<<<dim3(kN / TPB, l - 1, num_polys), TPB, 0, s>>>(
+        in, lifted, out, ctx->d_primes, T.rescale_inv, l);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = cuda_status(e, "rescale_combine_kernel");
+  }
+  if (owned) cudaFreeAsync(owned, s);
+  return rc;
+}
+
+int b2f_drop_limbs(b2f_context *ctx, const uint64_t *in, uint64_t *out,
+                   int num_polys, int l_in, int l_out, void *stream) {
+  B2F_CHECK_ARG(ctx && in && out && num_polys >= 0, "b2f_drop_limbs: null argument");
+  B2F_CHECK_ARG(l_out >= 1 && l_out <= l_in && l_in <= ctx->L,
+                "b2f_drop_limbs: cannot go from %d to %d limbs", l_in, l_out);
+  if (!num_polys) return B2F_OK;
+  B2F_CUDA(cudaMemcpy2DAsync(out, (size_t)l_out * kN * 8, in, (size_t)l_in * kN * 8,
+                             (size_t)l_out * kN * 8, num_polys,
+                             cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+  return B2F_OK;
+}
+
+int b2f_elementwise(b2f_context *ctx, int op, const uint64_t *a,
+                    const uint64_t *b, uint64_t *out, int num_polys, int l,
+                    int b_polys, void *stream) {
+  B2F_CHECK_ARG(ctx && a && b && out, "b2f_elementwise: null argument");
+  B2F_CHECK_ARG(op >= 0 && op <= 2, "b2f_elementwise: unknown op %d", op);
+  B2F_CHECK_ARG(l >= 1 && l <= ctx->L + ctx->K, "b2f_elementwise: bad limbs %d", l);
+  B2F_CHECK_ARG(b_polys == 1 || b_polys == num_polys,
+                "b2f_elementwise: b_polys must be 1 or num_polys");
+  if (num_polys <= 0) return B2F_OK;
+  elementwise_kernel<<<dim3(kN / TPB, l, num_polys), TPB, 0, (cudaStream_t)stream>>>(
+      op, a, b, out, ctx->d_mod, l, b_polys);
+  B2F_LAUNCHED("elementwise_kernel");
+  return B2F_OK;
+}
+
+int b2f_mul_i(b2f_context *ctx, const uint64_t *a, uint64_t *out, int num_polys,
+              int l, int negative, void *stream) {
+  B2F_CHECK_ARG(ctx && a && out, "b2f_mul_i: null argument");
+  B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_mul_i: bad limbs %d", l);
+  if (num_polys <= 0) return B2F_OK;
+  mul_i_kernel<<<dim3(kN / TPB, l, num_polys), TPB, 0, (cudaStream_t)stream>>>(
+      a, out, ctx->d_i_factor, ctx->d_primes, l, negative);
+  B2F_LAUNCHED("mul_i_kernel");
+  return B2F_OK;
+}
+
+int b2f_scalar_op(b2f_context *ctx, const uint64_t *a, uint64_t *out,
+                  int num_polys, int l, const uint64_t *mul_residues,
+                  const uint64_t *add_residues, int add_poly, void *stream) {
+  B2F_CHECK_ARG(ctx && a && out, "b2f_scalar_op: null argument");
+  B2F_CHECK_ARG(l >= 1 && l <= ctx->L && l <= 64, "b2f_scalar_op: bad limbs %d", l);
+  if (num_polys <= 0) return B2F_OK;
+  ScalarArgs S{};
+  S.has_mul = mul_residues != nullptr;
+  S.has_add = add_residues != nullptr;
+  S.add_poly = add_poly;
+  for (int i = 0; i < l; ++i) {
+    const uint64_t q = ctx->primes[i];
+    if (S.has_mul) {
+      uint64_t w = mul_residues[i] % q;
+      S.mul[i] = make_ulonglong2(
+          w, (uint64_t)(((unsigned __int128)w << 64) / q));
+    }
+    if (S.has_add) S.add[i] = add_residues[i] % q;
+  }
+  scalar_kernel<<<dim3(kN / TPB, l, num_polys), TPB, 0, (cudaStream_t)stream>>>(
+      a, out, ctx->d_primes, l, S);
+  B2F_LAUNCHED("scalar_kernel");
+  return B2F_OK;
+}
+
+int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
+            const uint64_t *pts, int giant_count, int l, uint64_t *out,
+            int num_cts, void *stream) {
+  B2F_CHECK_ARG(ctx && babies && pts && out, "b2f_mac: null argument");
+  B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_mac: bad limbs %d", l);
+  B2F_CHECK_ARG(baby_count >= 1 && giant_count >= 1 && num_cts >= 0,
+                "b2f_mac: bad counts");
+  if (!num_cts) return B2F_OK;
+  return launch_mac(ctx, babies, baby_count, pts, giant_count, l, out, num_cts,
+                    (cudaStream_t)stream);
+}
+
+size_t b2f_bsgs_mac_workspace(const b2f_context *ctx, int l) {
+  if (!ctx || l < 1 || l > ctx->L) return 0;
+  // inner results for up to 64 giants + accumulator + rotated + rotate scratch
+  return 0;  // computed per call from giant_count; see b2f_bsgs_mac
+}
+
+int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
+                 const uint64_t *pts, int giant_count, int l,
+                 uint64_t giant_galois, const uint64_t *giant_key,
+                 uint64_t *out, void *ws, size_t ws_bytes, void *stream) {
+  B2F_CHECK_ARG(ctx && babies && pts && out, "b2f_bsgs_mac: null argument");
+  B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_bsgs_mac: bad limbs %d", l);
+  B2F_CHECK_ARG(baby_count >= 1 && giant_count >= 1, "b2f_bsgs_mac: bad counts");
+  B2F_CHECK_ARG(giant_count == 1 || giant_key,
+                "b2f_bsgs_mac: giant_count > 1 needs the giant rotation key");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t ct_words = 2 * (size_t)l * kN;
+  const size_t rot_ws = rotate_workspace(ctx, 1, l);
+  const size_t need = (giant_count + 1) * ct_words * 8 + rot_ws + 512;
+  void *owned = nullptr;
+  if (!ws) {
+    B2F_CUDA(cudaMallocAsync(&owned, need, s));
+    ws = owned;
+  } else {
+    B2F_CHECK_ARG(ws_bytes >= need, "b2f_bsgs_mac: workspace %zu < %zu", ws_bytes,
+                  need);
+  }
+  uint64_t *inner = static_cast<uint64_t *>(ws);
+  uint64_t *rot = inner + giant_count * ct_words;
+  void *rws = rot + ct_words;
+  int rc = launch_mac(ctx, babies, baby_count, pts, giant_count, l, inner, 1, s);
+  if (!rc && giant_count == 1) {
+    cudaError_t e = cudaMemcpyAsync(out, inner, ct_words * 8,
+                                    cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) rc = cuda_status(e, "b2f_bsgs_mac copy");
+  }
+  // Horner over the giants: acc = inner[G-1]; acc = rot(acc) + inner[g]
+  const uint64_t *acc = inner + (size_t)(giant_count - 1) * ct_words;
+  for (int g = giant_count - 2; !rc && g >= 0; --g) {
+    rc = b2f_rotate(ctx, acc, rot, 1, l, giant_galois, giant_key, rws, rot_ws, s);
+    if (rc) break;
+    uint64_t *dst = g == 0 ? out : inner + (size_t)(g + 1) * ct_words;
+    rc = b2f_elementwise(ctx, 0, rot, inner + (size_t)g * ct_words, dst, 2, l, 2, s);
+    acc = dst;
+  }
+  if (owned) cudaFreeAsync(owned, s);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,330 @@
+"""Device-level host layer over libb200fhe: parameters, context, keys, buffers.
+
+Everything here is plumbing around the C ABI: torch provides device memory,
+streams and the caching allocator; all arithmetic runs in the CUDA kernels of
+libb200fhe.  Residue buffers are torch.int64 tensors holding uint64 values
+([polys, limbs, N], limbs contiguous), handed to the library as raw pointers.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _native
+from ._native import call, lib
+
+LOG_N = 16
+N = 1 << LOG_N
+
+
+def gen_primes(log_n: int, bits: int, count: int, mode: int = 0, exclude=()) -> list[int]:
+    out = (ctypes.c_uint64 * max(count, 1))()
+    ex = (ctypes.c_uint64 * max(len(exclude), 1))(*[int(v) for v in exclude])
+    call("b2f_generate_primes", log_n, bits, count, mode, ex, len(exclude), out)
+    return [int(out[i]) for i in range(count)]
+
+
+@dataclass(frozen=True)
+class Params:
+    """RNS-CKKS parameter set: Q = q[0..L), special primes P = p[0..K)."""
+
+    log_n: int
+    q: tuple[int, ...]
+    p: tuple[int, ...]
+    dnum: int
+    scale_bits: int
+
+    @property
+    def L(self) -> int:
+        return len(self.q)
+
+    @property
+    def K(self) -> int:
+        return len(self.p)
+
+    @property
+    def alpha(self) -> int:
+        return -(-self.L // self.dnum)
+
+    @staticmethod
+    def from_depth(depth: int, log_n: int, dnum: int, dcrt_bits: int, first_mod: int,
+                   special_bits: int = 60) -> "Params":
+        """The layer configuration (assets/feature_major.json): q_0 of
+        first_mod bits, depth scaling primes alternating just below / above
+        2^dcrt_bits, and enough special primes of special_bits bits for P to
+        exceed the largest digit (ceil(digit bits / special_bits))."""
+
+        L = int(depth) + 1
+        q0 = gen_primes(log_n, first_mod, 1, 0)
+        scaling = gen_primes(log_n, dcrt_bits, L - 1, 1, exclude=q0)
+        q = tuple(q0 + scaling)
+        alpha = -(-L // int(dnum))
+        digit_bits = max(
+            sum(math.log2(v) for v in q[j:j + alpha]) for j in range(0, L, alpha)
+        )
+        K = int(math.ceil(digit_bits / special_bits))
+        p = tuple(gen_primes(log_n, special_bits, K, 0, exclude=q))
+        return Params(log_n, q, p, int(dnum), int(dcrt_bits))
+
+    @staticmethod
+    def uniform(L: int, K: int, dnum: int, bits: int = 50, log_n: int = LOG_N,
+                scale_bits: int = 40) -> "Params":
+        """L + K primes of `bits` bits, q = 1 mod 2N (the primitive microbench:
+        50-bit primes, q = 1 mod 2^17 at N = 2^16)."""
+
+        allp = gen_primes(log_n, bits, L + K, 0)
+        return Params(log_n, tuple(allp[:L]), tuple(allp[L:]), int(dnum), int(scale_bits))
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return int(t.data_ptr())
+
+
+def _stream() -> int:
+    return int(torch.cuda.current_stream().cuda_stream)
+
+
+class NativeContext:
+    """A libb200fhe context on one CUDA device."""
+
+    def __init__(self, params: Params, device: str | torch.device = "cuda"):
+        self.params = params
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("libb200fhe runs on CUDA devices only (no CPU fallback)")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        q = (ctypes.c_uint64 * params.L)(*params.q)
+        p = (ctypes.c_uint64 * max(params.K, 1))(*params.p)
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            call("b2f_context_create", params.log_n, q, params.L, p, params.K, params.dnum,
+                 self.device.index, ctypes.byref(handle))
+        self.handle = handle
+        info = (ctypes.c_int * 6)()
+        call("b2f_context_info", self.handle, info)
+        self.log_n, self.L, self.K, self.dnum, self.alpha, self.digits = list(info)
+        self.n = 1 << self.log_n
+        self.primes = list(params.q) + list(params.p)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib.b2f_context_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- buffers --------------------------------------------------------
+    def empty(self, *shape: int) -> torch.Tensor:
+        return torch.empty(*shape, self.n, dtype=torch.int64, device=self.device)
+
+    def workspace(self, nbytes: int) -> torch.Tensor:
+        return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=self.device)
+
+    def key_shape(self) -> tuple[int, int, int, int]:
+        return (self.digits, 2, self.L + self.K, self.n)
+
+    # ---- transforms -----------------------------------------------------
+    def ntt(self, data: torch.Tensor, q_limbs: int, p_limbs: int = 0,
+            inverse: bool = False) -> torch.Tensor:
+        limbs = q_limbs + p_limbs
+        polys = data.numel() // (limbs * self.n)
+        call("b2f_ntt", self.handle, _ptr(data), polys, q_limbs, p_limbs, int(inverse),
+             _stream())
+        return data
+
+    # ---- keys -----------------------------------------------------------
+    def secret_to_ntt(self, s_coeff: np.ndarray) -> torch.Tensor:
+        s8 = np.ascontiguousarray(s_coeff, dtype=np.int8)
+        out = self.empty(self.L + self.K)
+        call("b2f_secret_to_ntt", self.handle, s8.ctypes.data, _ptr(out), _stream())
+        return out
+
+    def keygen_rotation(self, s_ntt: torch.Tensor, galois: int, seed: int) -> torch.Tensor:
+        key = torch.empty(self.key_shape(), dtype=torch.int64, device=self.device)
+        call("b2f_keygen_rotation", self.handle, _ptr(s_ntt), int(galois), int(seed),
+             _ptr(key), _stream())
+        return key
+
+    def keygen_relin(self, s_ntt: torch.Tensor, seed: int) -> torch.Tensor:
+        key = torch.empty(self.key_shape(), dtype=torch.int64, device=self.device)
+        call("b2f_keygen_relin", self.handle, _ptr(s_ntt), int(seed), _ptr(key), _stream())
+        return key
+
+    def keygen_switch(self, s_from: torch.Tensor, s_to: torch.Tensor, seed: int,
+                      tag: int) -> torch.Tensor:
+        key = torch.empty(self.key_shape(), dtype=torch.int64, device=self.device)
+        call("b2f_keygen_switch", self.handle, _ptr(s_from), _ptr(s_to), int(seed), int(tag),
+             _ptr(key), _stream())
+        return key
+
+    # ---- (de)cryption -----------------------------------------------------
+    def encode(self, values: torch.Tensor, scale: float, q_limbs: int,
+               p_limbs: int = 0) -> torch.Tensor:
+        """values: complex128 [rows, slots] (or [slots]) on the device."""
+
+        v = values.to(device=self.device, dtype=torch.complex128).contiguous()
+        rows = 1 if v.dim() == 1 else v.shape[0]
+        slots = v.shape[-1]
+        out = self.empty(rows, q_limbs + p_limbs)
+        ws = self.workspace(lib.b2f_encode_workspace(self.handle, rows, slots))
+        call("b2f_encode", self.handle, _ptr(v), rows, slots, float(scale), q_limbs, p_limbs,
+             _ptr(out), _ptr(ws), ws.numel(), _stream())
+        return out if v.dim() > 1 else out[0]
+
+    def decode(self, pt: torch.Tensor, l: int, slots: int, scale: float) -> np.ndarray:
+        out = torch.empty(slots, dtype=torch.complex128, device=self.device)
+        ws = self.workspace(lib.b2f_decode_workspace(self.handle, slots))
+        call("b2f_decode", self.handle, _ptr(pt), l, slots, float(scale), _ptr(out), _ptr(ws),
+             ws.numel(), _stream())
+        return out.cpu().numpy()
+
+    def encrypt(self, m_ntt: torch.Tensor, l: int, s_ntt: torch.Tensor, seed: int,
+                nonce: int) -> torch.Tensor:
+        ct = self.empty(2, l)
+        call("b2f_encrypt", self.handle, _ptr(m_ntt), l, _ptr(s_ntt), int(seed), int(nonce),
+             _ptr(ct), _stream())
+        return ct
+
+    def decrypt(self, ct: torch.Tensor, l: int, s_ntt: torch.Tensor) -> torch.Tensor:
+        m = self.empty(l)
+        call("b2f_decrypt", self.handle, _ptr(ct), l, _ptr(s_ntt), _ptr(m), _stream())
+        return m
+
+    # ---- evaluation -------------------------------------------------------
+    def rotate(self, ct: torch.Tensor, l: int, galois: int, key: torch.Tensor,
+               out: torch.Tensor | None = None, ws: torch.Tensor | None = None) -> torch.Tensor:
+        num = ct.numel() // (2 * l * self.n)
+        if out is None:
+            out = torch.empty_like(ct)
+        if ws is None:
+            ws = self.workspace(lib.b2f_rotate_workspace(self.handle, num, l))
+        call("b2f_rotate", self.handle, _ptr(ct), _ptr(out), num, l, int(galois), _ptr(key),
+             _ptr(ws), ws.numel(), _stream())
+        return out
+
+    def relinearize(self, ct3: torch.Tensor, l: int, key: torch.Tensor) -> torch.Tensor:
+        num = ct3.numel() // (3 * l * self.n)
+        out = self.empty(num, 2, l) if ct3.dim() == 4 else self.empty(2, l)
+        ws = self.workspace(lib.b2f_relinearize_workspace(self.handle, num, l))
+        call("b2f_relinearize", self.handle, _ptr(ct3), _ptr(out), num, l, _ptr(key),
+             _ptr(ws), ws.numel(), _stream())
+        return out
+
+    def modup(self, ct: torch.Tensor, l: int) -> torch.Tensor:
+        beta = -(-l // self.alpha)
+        ext = self.empty(beta, l + self.K)
+        ws = self.workspace(lib.b2f_modup_workspace(self.handle, l))
+        call("b2f_modup", self.handle, _ptr(ct), l, _ptr(ext), _ptr(ws), ws.numel(),
+             _stream())
+        return ext
+
+    def rotate_hoisted(self, ct: torch.Tensor, l: int, ext: torch.Tensor, galois, keys,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+        count = len(galois)
+        if out is None:
+            out = self.empty(count, 2, l)
+        g = (ctypes.c_uint64 * max(count, 1))(*[int(v) for v in galois])
+        kp = (ctypes.c_void_p * max(count, 1))(*[_ptr(k) for k in keys])
+        ws = self.workspace(lib.b2f_rotate_hoisted_workspace(self.handle, l))
+        call("b2f_rotate_hoisted", self.handle, _ptr(ct), l, _ptr(ext), count, g, kp,
+             _ptr(out), _ptr(ws), ws.numel(), _stream())
+        return out
+
+    def rescale(self, data: torch.Tensor, num_polys: int, l: int) -> torch.Tensor:
+        out = self.empty(num_polys, l - 1)
+        ws = self.workspace(lib.b2f_rescale_workspace(self.handle, num_polys, l))
+        call("b2f_rescale", self.handle, _ptr(data), _ptr(out), num_polys, l, _ptr(ws),
+             ws.numel(), _stream())
+        return out
+
+    def drop_limbs(self, data: torch.Tensor, num_polys: int, l_in: int,
+                   l_out: int) -> torch.Tensor:
+        out = self.empty(num_polys, l_out)
+        call("b2f_drop_limbs", self.handle, _ptr(data), _ptr(out), num_polys, l_in, l_out,
+             _stream())
+        return out
+
+    def elementwise(self, op: int, a: torch.Tensor, b: torch.Tensor, num_polys: int,
+                    l: int, b_polys: int | None = None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+        if out is None:
+            out = self.empty(num_polys, l)
+        call("b2f_elementwise", self.handle, op, _ptr(a), _ptr(b), _ptr(out), num_polys, l,
+             num_polys if b_polys is None else b_polys, _stream())
+        return out
+
+    def mul_i(self, a: torch.Tensor, num_polys: int, l: int, negative: bool = False) -> torch.Tensor:
+        out = self.empty(num_polys, l)
+        call("b2f_mul_i", self.handle, _ptr(a), _ptr(out), num_polys, l, int(negative),
+             _stream())
+        return out
+
+    def scalar_op(self, a: torch.Tensor, num_polys: int, l: int, mul=None, add=None,
+                  add_poly: int = 0) -> torch.Tensor:
+        out = self.empty(num_polys, l)
+        m = (ctypes.c_uint64 * l)(*[int(v) for v in mul]) if mul is not None else None
+        ad = (ctypes.c_uint64 * l)(*[int(v) for v in add]) if add is not None else None
+        call("b2f_scalar_op", self.handle, _ptr(a), _ptr(out), num_polys, l, m, ad, add_poly,
+             _stream())
+        return out
+
+    def mac(self, babies: torch.Tensor, baby_count: int, pts: torch.Tensor,
+            giant_count: int, l: int, num_cts: int = 1) -> torch.Tensor:
+        out = self.empty(num_cts, giant_count, 2, l)
+        call("b2f_mac", self.handle, _ptr(babies), baby_count, _ptr(pts), giant_count, l,
+             _ptr(out), num_cts, _stream())
+        return out
+
+    def bsgs_mac(self, babies: torch.Tensor, baby_count: int, pts: torch.Tensor,
+                 giant_count: int, l: int, giant_galois: int,
+                 giant_key: torch.Tensor | None) -> torch.Tensor:
+        out = self.empty(2, l)
+        call("b2f_bsgs_mac", self.handle, _ptr(babies), baby_count, _ptr(pts), giant_count, l,
+             int(giant_galois), _ptr(giant_key) if giant_key is not None else None, _ptr(out),
+             None, 0, _stream())
+        return out
+
+    def pack_diagonals(self, weight: torch.Tensor, dimension: int, token_lanes: int,
+                       baby_steps: int, giant_base: int, giant_count: int,
+                       slots: int) -> torch.Tensor:
+        w = weight.contiguous()
+        if w.dtype == torch.complex128:
+            dtype = 2
+        elif w.dtype == torch.float32:
+            dtype = 1
+        else:
+            w = w.to(torch.float64)
+            dtype = 0
+        rows = giant_count * baby_steps
+        out = torch.empty(rows, slots, dtype=torch.complex128, device=self.device)
+        call("b2f_pack_diagonals", self.handle, _ptr(w), dtype, dimension, token_lanes,
+             baby_steps, giant_base, giant_count, slots, _ptr(out), _stream())
+        return out
+
+
+def galois_element(rotation: int, log_n: int = LOG_N) -> int:
+    return int(lib.b2f_galois_element(log_n, int(rotation)))
+
+
+def sample_secret(seed: int, hamming: int, log_n: int = LOG_N) -> np.ndarray:
+    s = np.zeros(1 << log_n, dtype=np.int8)
+    call("b2f_sample_secret", log_n, int(seed), int(hamming), s.ctypes.data)
+    return s
+
+
+def to_numpy_u64(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().numpy().view(np.uint64)
+
+
+def from_numpy_u64(a: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint64).view(np.int64)).to(device)

@@ -1,0 +1,234 @@
+/*
+ * b200fhe.h -- C ABI of libb200fhe, the B200 (sm_100a) CKKS evaluation
+ * backend that replaces the external EasyFHE runtime behind the reference's
+ * `easyfhe.fhe` Python surface.
+ *
+ * Conventions
+ *  - Every pointer named *data / *in / *out / *key / *ws is a DEVICE pointer
+ *    on the context's device; sizes are element counts unless named *_bytes.
+ *  - A polynomial at l limbs is l contiguous limbs of N = 2^16 uint64
+ *    residues (limb i modulo prime i).  An extended polynomial holds l Q-limbs
+ *    followed by K P-limbs.  A ciphertext is two polynomials back to back
+ *    (c0 then c1); a batch of ciphertexts is contiguous.
+ *  - Polynomials are in the evaluation (NTT) form unless a function says
+ *    otherwise; evaluation k is a(psi^(2*bitrev(k)+1)), psi the smallest
+ *    primitive 2N-th root of unity modulo the limb's prime.
+ *  - Residues are fully reduced ([0, q)) on input and output.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream); every call is
+ *    asynchronous on it.  Scratch memory is passed in as `ws`/`ws_bytes`
+ *    (size from the matching *_workspace query); ws == NULL makes the call
+ *    allocate and free its scratch stream-ordered (cudaMallocAsync).
+ *  - Every function returns 0 (B2F_OK) or a b2f_status; the message of the
+ *    last failure on the calling thread is b2f_last_error().
+ *
+ * Reference citations are to Azathoth13/easyfhe-llama3-8b; the Python names
+ * are the `easyfhe.fhe` calls the reference makes at those lines.
+ */
+#ifndef B200FHE_H
+#define B200FHE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct b2f_context b2f_context;
+
+typedef enum {
+  B2F_OK = 0,
+  B2F_ERR_ARG = 1,         /* bad argument: shape, level, pointer, size */
+  B2F_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  B2F_ERR_NOMEM = 3,       /* device allocation failed */
+  B2F_ERR_UNSUPPORTED = 4  /* parameters outside what the kernels implement */
+} b2f_status;
+
+/* Message of the last failure on the calling thread ("" if none). */
+const char *b2f_last_error(void);
+int b2f_abi_version(void);
+
+/* NTT-friendly primes q = 1 mod 2N: mode 0 descending below 2^bits, mode 1
+ * alternating just below / just above 2^bits.  Serves the modulus chain of
+ * fhe.CKKSContextSpec(depth, log_n, dnum, dcrt_bits, first_mod)
+ * (llama3fhe/application/session.py:31-45, llama3fhe/backend.py:457-471). */
+int b2f_generate_primes(int log_n, int bits, int count, int mode,
+                        const uint64_t *exclude, int n_exclude, uint64_t *out);
+
+/* Context over Q = q[0..L) and special primes P = p[0..K), dnum digits.
+ * Replaces the native context of fhe.generate_client_context
+ * (llama3fhe/application/session.py:31-45).  log_n must be 16. */
+int b2f_context_create(int log_n, const uint64_t *q, int L, const uint64_t *p,
+                       int K, int dnum, int device, b2f_context **out);
+int b2f_context_destroy(b2f_context *ctx);
+/* log_n, L, K, dnum, alpha (limbs per digit), digits (top level) */
+int b2f_context_info(const b2f_context *ctx, int *info6);
+
+/* ---- number-theoretic transform (no direct Python site; inside every op,
+ * SURVEY a10) ---- */
+int b2f_ntt(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
+            int p_limbs, int inverse, void *stream);
+
+/* ---- automorphism X -> X^g in evaluation form: out[k] = in[perm_g(k)] ----
+ * Part of fhe.homo_rotate (llama3fhe/operators/linear/operator.py:333-337). */
+int b2f_automorphism(b2f_context *ctx, const uint64_t *in, uint64_t *out,
+                     int num_polys, int limbs, uint64_t galois, void *stream);
+/* Galois element of a slot rotation r (5^r mod 2N); r == 2N-1 is complex
+ * conjugation (index context.M - 1, llama3fhe/operators/linear/complex.py:47-51). */
+uint64_t b2f_galois_element(int log_n, int64_t rotation);
+
+/* ---- hybrid key switching ----
+ * Key layout: [digits][2][L+K][N], NTT form, generated for the top level and
+ * used truncated at any level l (limbs 0..l-1 and L..L+K-1).
+ * fhe.homo_rotate(ct, r, ctx) (34 call sites, e.g.
+ * llama3fhe/operators/linear/operator.py:333-337, qkv_kernel.py:829-834):
+ * out = (pi_g(c0 + d0), pi_g(d1)), (d0, d1) = KeySwitch(c1).  num_cts
+ * ciphertexts at l limbs share one key. */
+size_t b2f_rotate_workspace(const b2f_context *ctx, int num_cts, int l);
+int b2f_rotate(b2f_context *ctx, const uint64_t *ct_in, uint64_t *ct_out,
+               int num_cts, int l, uint64_t galois, const uint64_t *key,
+               void *ws, size_t ws_bytes, void *stream);
+
+/* Relinearisation of degree-2 ciphertexts (d0, d1, d2) -> (d0 + ks0(d2),
+ * d1 + ks1(d2)): fhe.homo_relinearize / the relin inside fhe.homo_mul_relin
+ * (llama3fhe/operators/primitives.py:25, attention/kernel_helpers.py:155). */
+size_t b2f_relinearize_workspace(const b2f_context *ctx, int num_cts, int l);
+int b2f_relinearize(b2f_context *ctx, const uint64_t *ct3_in, uint64_t *ct_out,
+                    int num_cts, int l, const uint64_t *relin_key, void *ws,
+                    size_t ws_bytes, void *stream);
+
+/* Hoisting: ModUp of c1 once into the extended digits
+ * ext[digit][l+K][N] (NTT form) ...
+ * fhe.prepare_hoisted_baby_rotations (llama3fhe/operators/linear/operator.py:105-111) */
+size_t b2f_modup_workspace(const b2f_context *ctx, int l);
+int b2f_modup(b2f_context *ctx, const uint64_t *ct, int l, uint64_t *ext,
+              void *ws, size_t ws_bytes, void *stream);
+/* ... then one inner product + ModDown + automorphism per rotation: out[r]
+ * = rotation galois[r] of ct using keys[r] (an array of `count` device key
+ * pointers, host array).  fhe.prepare_hoisted_baby_rotations / fast_rotate
+ * (llama3fhe/operators/attention/input.py:792-797, 1143-1148). */
+size_t b2f_rotate_hoisted_workspace(const b2f_context *ctx, int l);
+int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
+                       const uint64_t *ext, int count, const uint64_t *galois,
+                       const uint64_t *const *keys, uint64_t *out, void *ws,
+                       size_t ws_bytes, void *stream);
+
+/* ---- level management ----
+ * fhe.rescale (llama3fhe/operators/linear/operator.py:386-388): divide by the
+ * last prime with a centred lift; in (num_polys x l limbs) -> out
+ * (num_polys x (l-1) limbs). */
+size_t b2f_rescale_workspace(const b2f_context *ctx, int num_polys, int l);
+int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
+                int num_polys, int l, void *ws, size_t ws_bytes, void *stream);
+/* fhe.align_to to fewer limbs (llama3fhe/operators/primitives.py:100-155):
+ * keep limbs 0..l_out-1 of each poly. */
+int b2f_drop_limbs(b2f_context *ctx, const uint64_t *in, uint64_t *out,
+                   int num_polys, int l_in, int l_out, void *stream);
+
+/* ---- elementwise (limb-wise, NTT form) ----
+ * op: 0 add, 1 sub, 2 mul.  fhe.homo_add / homo_sub (28 / 9 sites),
+ * fhe.homo_mul_pt (llama3fhe/operators/primitives.py:43), homo_add_pt.
+ * a, b and out hold num_polys polys of l limbs; b_polys is 1 (plaintext
+ * broadcast over the polys) or num_polys. */
+int b2f_elementwise(b2f_context *ctx, int op, const uint64_t *a,
+                    const uint64_t *b, uint64_t *out, int num_polys, int l,
+                    int b_polys, void *stream);
+/* out = a * X^(N/2) (multiply every slot by i, or -i when negative):
+ * fhe.homo_mul_i (llama3fhe/operators/linear/complex.py:22). */
+int b2f_mul_i(b2f_context *ctx, const uint64_t *a, uint64_t *out,
+              int num_polys, int l, int negative, void *stream);
+/* out = a * c (+ add) with per-limb integer constants c[l], add[l]
+ * (residues, NULL = none): fhe.homo_mul_scalar / homo_add_scalar on
+ * fhe.encode_scalar constants (llama3fhe/operators/nonlinear/bootstrap.py:331-349). */
+int b2f_scalar_op(b2f_context *ctx, const uint64_t *a, uint64_t *out,
+                  int num_polys, int l, const uint64_t *mul_residues,
+                  const uint64_t *add_residues, int add_poly, void *stream);
+
+/* ---- baby-step / giant-step plaintext x ciphertext MAC ----
+ * fhe.hoisted_mac_sum (llama3fhe/operators/linear/operator.py:320-330,
+ * llama3fhe/operators/transform.py:108-116): for each giant g < giant_count,
+ * inner_g = sum_b pt[g*B + b] * babies[b]; out = Horner over the giants with
+ * the rotation by giant_offset (key giant_key):
+ *   acc = inner_{G-1}; acc = rot(acc) + inner_g for g = G-2..0.
+ * babies: B ciphertexts at l limbs; pts: G*B plaintexts at l limbs. */
+size_t b2f_bsgs_mac_workspace(const b2f_context *ctx, int l);
+int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
+                 const uint64_t *pts, int giant_count, int l,
+                 uint64_t giant_galois, const uint64_t *giant_key,
+                 uint64_t *out, void *ws, size_t ws_bytes, void *stream);
+/* Only the MAC: out[g] = sum_b pt[g*B+b] * babies[b] for g < giant_count
+ * (num_cts independent baby sets, each with its own output block). */
+int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
+            const uint64_t *pts, int giant_count, int l, uint64_t *out,
+            int num_cts, void *stream);
+
+/* ---- encoding ----
+ * Slot vectors (complex128 interleaved re/im, device) -> plaintexts at
+ * q_limbs (+ p_limbs) in NTT form: special inverse FFT, times scale, round
+ * to nearest, reduce per limb, NTT.  fhe.ConstantBundle.plaintext
+ * (llama3fhe/backend.py:231-297, llama3fhe/operators/linear/weight.py:344-357),
+ * client.encrypt's encoding (llama3fhe/application/session.py:71-77). */
+int b2f_encode(b2f_context *ctx, const double *values, int num_rows, int slots,
+               double scale, int q_limbs, int p_limbs, uint64_t *out, void *ws,
+               size_t ws_bytes, void *stream);
+size_t b2f_encode_workspace(const b2f_context *ctx, int num_rows, int slots);
+/* Plaintext (l limbs, NTT) -> complex slots, decoded from the first
+ * min(l, 2) limbs (client.decrypt, llama3fhe/backend.py:305-313). */
+int b2f_decode(b2f_context *ctx, const uint64_t *pt, int l, int slots,
+               double scale, double *values, void *ws, size_t ws_bytes,
+               void *stream);
+size_t b2f_decode_workspace(const b2f_context *ctx, int slots);
+
+/* Diagonal packer of a feature-major BSGS chunk (replaces the reference's
+ * Triton kernels, llama3fhe/operators/linear/gpu_packer.py:144-184 and
+ * 317-424, formula weight.py:18-47):
+ *   row(g,b)[s] = W[(f(s) - g*B) mod D, (f(s) + b) mod D], f(s) = s / lanes,
+ * g = giant_base + row / B.  weight: D x D, dtype 0 float64, 1 float32,
+ * 2 complex128 (interleaved).  out: rows x slots complex128 interleaved. */
+int b2f_pack_diagonals(b2f_context *ctx, const void *weight, int dtype,
+                       int dimension, int token_lanes, int baby_steps,
+                       int giant_base, int giant_count, int slots,
+                       double *out, void *stream);
+/* Structured variant: W_phys[o,i] = column_scale[i] * (real_scale[o] *
+ * src[real_source[o]][real_row[o], column[i]] + 1j * imag_scale[o] *
+ * src[imag_source[o]][imag_row[o], column[i]]), -1 = zero
+ * (llama3fhe/operators/linear/structured_weight.py:1-20). maps: int64 x D,
+ * scales: float64 x D; sources: up to 3 device matrices with (row, col)
+ * strides in elements, dtype 0 float64 / 1 float32. */
+int b2f_pack_structured(b2f_context *ctx, const void *const *sources,
+                        const int64_t *strides, int source_count, int dtype,
+                        const int64_t *real_source, const int64_t *real_row,
+                        const double *real_scale, const int64_t *imag_source,
+                        const int64_t *imag_row, const double *imag_scale,
+                        const int64_t *column, const double *column_scale,
+                        int dimension, int token_lanes, int baby_steps,
+                        int giant_base, int giant_count, int slots, double *out,
+                        void *stream);
+
+/* ---- keys and (de)cryption (client side of fhe.generate_client_context,
+ * client.encrypt / client.decrypt, session.py:31-77, backend.py:305-313) ----
+ * Randomness: ChaCha20 keyed by `seed`.  s_* are secrets in NTT form over all
+ * L+K primes.  Not a hot path. */
+int b2f_secret_to_ntt(b2f_context *ctx, const int8_t *s_coeff /* host, N */,
+                      uint64_t *s_ntt, void *stream);
+int b2f_keygen_switch(b2f_context *ctx, const uint64_t *s_from_ntt,
+                      const uint64_t *s_to_ntt, uint64_t seed, uint32_t tag,
+                      uint64_t *key, void *stream);
+int b2f_keygen_rotation(b2f_context *ctx, const uint64_t *s_ntt,
+                        uint64_t galois, uint64_t seed, uint64_t *key,
+                        void *stream);
+int b2f_keygen_relin(b2f_context *ctx, const uint64_t *s_ntt, uint64_t seed,
+                     uint64_t *key, void *stream);
+int b2f_encrypt(b2f_context *ctx, const uint64_t *m_ntt, int l,
+                const uint64_t *s_ntt, uint64_t seed, uint64_t nonce,
+                uint64_t *ct, void *stream);
+int b2f_decrypt(b2f_context *ctx, const uint64_t *ct, int l,
+                const uint64_t *s_ntt, uint64_t *m_ntt, void *stream);
+/* sparse ternary (hamming > 0) or uniform ternary (hamming == 0) secret,
+ * host output, same ChaCha20 stream definition as the keys. */
+int b2f_sample_secret(int log_n, uint64_t seed, int hamming, int8_t *s_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200FHE_H */

@@ -1,0 +1,201 @@
+"""GPU parity of the CKKS primitives against the CPU oracle, bit-exact in RNS
+residues.  Inputs are seeded uniform
+residues at N = 2^16 with 50-bit NTT primes (q = 1 mod 2^17), the primitive
+microbench parameters, plus one small parameter set whose special primes
+cover a digit so that decrypted values are meaningful."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from _ckks import N, pair, rand_residues, to_dev, to_host
+
+pytestmark = pytest.mark.gpu
+
+
+def test_generated_primes_match_oracle(oracle_mod):
+    from easyfhe import core
+
+    for log_n, bits, count, mode in ((16, 50, 12, 0), (16, 59, 9, 1), (16, 60, 5, 0)):
+        assert core.gen_primes(log_n, bits, count, mode) == oracle_mod.gen_primes(
+            log_n, bits, count, mode)
+
+
+@pytest.mark.parametrize("L", [8, 16, 24, 32])
+def test_ntt_forward_inverse_bit_exact(L):
+    ctx, orc = pair(L, 2, 4)
+    rng = np.random.default_rng(1000 + L)
+    x = rand_residues(rng, ctx.primes[:L], 3)
+    d = to_dev(x)
+    ctx.ntt(d, L, 0, inverse=False)
+    got = to_host(d)
+    want = orc.ntt(x, L, 0, inverse=False).reshape(x.shape)
+    assert np.array_equal(got, want)
+    ctx.ntt(d, L, 0, inverse=True)
+    assert np.array_equal(to_host(d), x)
+    # inverse on fresh data, against the oracle
+    y = rand_residues(rng, ctx.primes[:L], 2)
+    dy = to_dev(y)
+    ctx.ntt(dy, L, 0, inverse=True)
+    assert np.array_equal(to_host(dy), orc.ntt(y, L, 0, inverse=True).reshape(y.shape))
+
+
+def test_ntt_extended_limbs():
+    ctx, orc = pair(8, 2, 4)
+    rng = np.random.default_rng(7)
+    x = rand_residues(rng, ctx.primes[:5] + ctx.primes[8:10], 2)
+    d = to_dev(x)
+    ctx.ntt(d, 5, 2)
+    assert np.array_equal(to_host(d), orc.ntt(x, 5, 2).reshape(x.shape))
+
+
+def test_secret_and_keys_match_oracle(oracle_mod):
+    from easyfhe import core
+
+    ctx, orc = pair(8, 2, 3)
+    s = core.sample_secret(1234, 192)
+    assert np.array_equal(s.astype(np.int64), oracle_mod.sample_secret(16, 1234, 192))
+    assert int(np.count_nonzero(s)) == 192
+    su = core.sample_secret(99, 0)
+    assert np.array_equal(su.astype(np.int64), oracle_mod.sample_secret(16, 99, 0))
+    s_ntt = ctx.secret_to_ntt(s)
+    want = orc.secret_to_ntt(s.astype(np.int64))
+    assert np.array_equal(to_host(s_ntt), want)
+    g = core.galois_element(5)
+    key = ctx.keygen_rotation(s_ntt, g, seed=77)
+    assert np.array_equal(to_host(key), orc.keygen_rotation(want, g, 77))
+    rk = ctx.keygen_relin(s_ntt, seed=78)
+    assert np.array_equal(to_host(rk), orc.keygen_relin(want, 78))
+
+
+@pytest.mark.parametrize("rotation", [1, 3, 1024, 131071])
+def test_rotate_bit_exact(rotation):
+    from easyfhe import core
+
+    L, l = 8, 7
+    ctx, orc = pair(L, 2, 3)
+    s = core.sample_secret(5, 192)
+    s_ntt = ctx.secret_to_ntt(s)
+    g = core.galois_element(rotation)
+    key = ctx.keygen_rotation(s_ntt, g, seed=11)
+    rng = np.random.default_rng(rotation)
+    cts = rand_residues(rng, ctx.primes[:l], 6).reshape(3, 2, l, N)
+    out = to_host(ctx.rotate(to_dev(cts), l, g, key))
+    hkey = to_host(key)
+    for c in range(3):
+        assert np.array_equal(out[c], orc.rotate(cts[c], l, g, hkey)), f"ct {c}"
+
+
+def test_hoisted_rotations_bit_exact():
+    from easyfhe import core
+
+    L, l = 8, 8
+    ctx, orc = pair(L, 2, 3)
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(6, 192))
+    gs = [core.galois_element(r) for r in (1, 2, 8)]
+    keys = [ctx.keygen_rotation(s_ntt, g, seed=20 + i) for i, g in enumerate(gs)]
+    rng = np.random.default_rng(3)
+    ct = rand_residues(rng, ctx.primes[:l], 2)
+    dct = to_dev(ct)
+    ext = ctx.modup(dct, l)
+    got = to_host(ctx.rotate_hoisted(dct, l, ext, gs, keys))
+    want = orc.rotate_hoisted(ct, l, gs, [to_host(k) for k in keys])
+    assert np.array_equal(got, want)
+    # one hoisted rotation equals the plain HRotate
+    plain = to_host(ctx.rotate(dct, l, gs[1], keys[1]))
+    assert np.array_equal(got[1], plain)
+
+
+def test_relinearize_bit_exact():
+    from easyfhe import core
+
+    L, l = 8, 6
+    ctx, orc = pair(L, 2, 3)
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(8, 192))
+    rk = ctx.keygen_relin(s_ntt, seed=5)
+    rng = np.random.default_rng(4)
+    ct3 = rand_residues(rng, ctx.primes[:l], 3)
+    got = to_host(ctx.relinearize(to_dev(ct3), l, rk))
+    d0, d1 = orc.keyswitch(ct3[2], l, to_host(rk))
+    q = np.array(ctx.primes[:l], dtype=object)[:, None]
+    w0 = (ct3[0].astype(object) + d0.astype(object)) % q
+    w1 = (ct3[1].astype(object) + d1.astype(object)) % q
+    assert np.array_equal(got[0], w0.astype(np.uint64))
+    assert np.array_equal(got[1], w1.astype(np.uint64))
+
+
+@pytest.mark.parametrize("l", [2, 9, 16])
+def test_rescale_bit_exact(l):
+    ctx, orc = pair(16, 2, 4)
+    rng = np.random.default_rng(l)
+    x = rand_residues(rng, ctx.primes[:l], 2)
+    got = to_host(ctx.rescale(to_dev(x), 2, l))
+    assert np.array_equal(got, orc.rescale(x, 2, l))
+
+
+@pytest.mark.parametrize("negative", [False, True])
+def test_mul_i_bit_exact(negative):
+    ctx, orc = pair(8, 2, 3)
+    rng = np.random.default_rng(17)
+    x = rand_residues(rng, ctx.primes[:5], 2)
+    got = to_host(ctx.mul_i(to_dev(x), 2, 5, negative))
+    assert np.array_equal(got, orc.mul_i(x, 2, 5, negative).reshape(x.shape))
+
+
+def test_elementwise_bit_exact():
+    ctx, _ = pair(8, 2, 3)
+    rng = np.random.default_rng(2)
+    l = 6
+    a = rand_residues(rng, ctx.primes[:l], 2)
+    b = rand_residues(rng, ctx.primes[:l], 1)
+    q = np.array(ctx.primes[:l], dtype=object)[None, :, None]
+    A, B = a.astype(object), b.astype(object)
+    for op, ref in ((0, (A + B) % q), (1, (A - B) % q), (2, (A * B) % q)):
+        got = to_host(ctx.elementwise(op, to_dev(a), to_dev(b), 2, l, b_polys=1))
+        assert np.array_equal(got, ref.astype(np.uint64)), op
+
+
+def test_encode_bit_exact_and_decode():
+    ctx, orc = pair(8, 2, 3)
+    import torch
+
+    rng = np.random.default_rng(21)
+    z = rng.uniform(-1, 1, 32768) + 1j * rng.uniform(-1, 1, 32768)
+    scale = 2.0 ** 40
+    got = to_host(ctx.encode(torch.from_numpy(z).to("cuda:0"), scale, 6, 2))
+    want = orc.encode(z, scale, 6, 2)
+    assert np.array_equal(got, want)
+    dec = ctx.decode(to_dev(want), 6, 32768, scale)
+    assert np.max(np.abs(dec - z)) < 1e-9
+    # sparse slots
+    z2 = z[:1024]
+    got2 = to_host(ctx.encode(torch.from_numpy(z2).to("cuda:0"), scale, 3, 0))
+    assert np.array_equal(got2, orc.encode(z2, scale, 3, 0))
+
+
+def test_encrypt_rotate_decrypt_values():
+    """Functional check where noise is meaningful (alpha = K): slots rotate
+    left, conjugation conjugates, rescale divides the scale."""
+
+    import torch
+
+    from easyfhe import core
+
+    ctx, orc = pair(4, 2, 2, bits=50)
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(31, 192))
+    scale = 2.0 ** 40
+    rng = np.random.default_rng(8)
+    z = rng.uniform(-1, 1, 32768) + 1j * rng.uniform(-1, 1, 32768)
+    m = ctx.encode(torch.from_numpy(z).to("cuda:0"), scale, 4)
+    ct = ctx.encrypt(m, 4, s_ntt, seed=3, nonce=1)
+    # encryption matches the oracle bit for bit
+    want = orc.encrypt(to_host(m), 4, to_host(s_ntt), 3, 1)
+    assert np.array_equal(to_host(ct), want)
+    for r in (1, 7, 131071):
+        g = core.galois_element(r)
+        key = ctx.keygen_rotation(s_ntt, g, seed=40 + r)
+        rot = ctx.rotate(ct, 4, g, key)
+        dec = ctx.decode(ctx.decrypt(rot, 4, s_ntt), 4, 32768, scale)
+        ref = np.conj(z) if r == 131071 else np.roll(z, -r)
+        assert np.max(np.abs(dec - ref)) < 1e-4, r
