@@ -9,10 +9,12 @@
 //      through distributed shared memory, so CTA r then holds the contiguous
 //      block [8192 r, 8192 (r+1));
 //   3. stages 3-15 run in three register passes of 4 stages over shared
-//      memory (radix-16 per thread, 512 threads x 16 words); the last stage
-//      pairs neighbouring words and uses a warp shuffle;
-//   4. the block is staged through shared memory and written with 16-byte
-//      coalesced stores.
+//      memory (radix-16 per thread, 512 threads x 16 words, two CTAs per
+//      SM); the second and third passes of a warp touch only its own
+//      512-word segment, so they exchange data under __syncwarp; the last
+//      stage pairs neighbouring words across lanes tid, tid^1 (shuffle);
+//   4. each warp stages its segment through shared memory and writes it
+//      with 16-byte coalesced stores.
 // The inverse (Gentleman-Sande, bit-reversed in, natural out) runs the same
 // steps backwards and folds N^-1 (times an optional per-limb constant) into
 // the final stage.  Butterflies use Harvey's lazy reduction: forward values
@@ -30,10 +32,12 @@ namespace {
 
 constexpr int CL = 8;                       // CTAs per cluster = per limb
 constexpr int BLK = kN / CL;                // 8192 words per CTA
-constexpr int NT = 512;                     // threads per CTA
+constexpr int NT = 512;                     // threads per CTA, 16 words each
+constexpr int SEG = 512;                    // words owned by one warp in B/C
 constexpr int SMEM_WORDS = BLK + 2 * (BLK / 32);
 constexpr int SMEM_BYTES = SMEM_WORDS * 8;  // 69632
 
+// two pad words per 32 keep every pass free of shared-memory bank conflicts
 __device__ __forceinline__ int pad(int l) { return l + ((l >> 5) << 1); }
 
 struct NttParams {
@@ -56,6 +60,7 @@ __device__ __forceinline__ int tw_index(int s, int j) {
   return (1 << s) + (j >> (kLogN - s));
 }
 
+// forward butterfly, values in [0, 4q): (x, y) -> (x + w y, x - w y)
 __device__ __forceinline__ void ct_bfly(uint64_t &x, uint64_t &y, ulonglong2 w,
                                         uint64_t q, uint64_t q2) {
   uint64_t u = x >= q2 ? x - q2 : x;
@@ -64,6 +69,7 @@ __device__ __forceinline__ void ct_bfly(uint64_t &x, uint64_t &y, ulonglong2 w,
   y = u - t + q2;
 }
 
+// inverse butterfly, values in [0, 2q): (x, y) -> (x + y, (x - y) w)
 __device__ __forceinline__ void gs_bfly(uint64_t &x, uint64_t &y, ulonglong2 w,
                                         uint64_t q, uint64_t q2) {
   uint64_t u = x + y;
@@ -73,19 +79,20 @@ __device__ __forceinline__ void gs_bfly(uint64_t &x, uint64_t &y, ulonglong2 w,
   y = t * w.x - __umul64hi(t, w.y) * q;
 }
 
-// Four CT stages s0..s0+3 on 16 registers whose element index is
-// j(k) = base + k * stride.
+// Four CT stages s0..s0+3 on 16 registers with element index
+// j(k) = base + k * stride; at local stage t the pairs are (k, k + d),
+// d = 8 >> t, and each block of 2d registers shares one twiddle.
 __device__ __forceinline__ void ct_pass(uint64_t (&x)[16], const ulonglong2 *tw,
                                         int s0, int base, int stride,
                                         uint64_t q, uint64_t q2) {
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const int d = 8 >> s;
+  for (int t = 0; t < 4; ++t) {
+    const int d = 8 >> t;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      if (k & d) continue;
-      ulonglong2 w = ldtw(tw, tw_index(s0 + s, base + k * stride));
-      ct_bfly(x[k], x[k + d], w, q, q2);
+    for (int blk = 0; blk < 16; blk += 2 * d) {
+      const ulonglong2 w = ldtw(tw, tw_index(s0 + t, base + blk * stride));
+#pragma unroll
+      for (int k = blk; k < blk + d; ++k) ct_bfly(x[k], x[k + d], w, q, q2);
     }
   }
 }
@@ -93,25 +100,43 @@ __device__ __forceinline__ void ct_pass(uint64_t (&x)[16], const ulonglong2 *tw,
 __device__ __forceinline__ void gs_pass(uint64_t (&x)[16], const ulonglong2 *tw,
                                         int s0, int base, int stride,
                                         uint64_t q, uint64_t q2) {
-  // stages s0+3 down to s0
 #pragma unroll
-  for (int s = 3; s >= 0; --s) {
-    const int d = 8 >> s;
+  for (int t = 3; t >= 0; --t) {
+    const int d = 8 >> t;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      if (k & d) continue;
-      ulonglong2 w = ldtw(tw, tw_index(s0 + s, base + k * stride));
-      gs_bfly(x[k], x[k + d], w, q, q2);
+    for (int blk = 0; blk < 16; blk += 2 * d) {
+      const ulonglong2 w = ldtw(tw, tw_index(s0 + t, base + blk * stride));
+#pragma unroll
+      for (int k = blk; k < blk + d; ++k) gs_bfly(x[k], x[k + d], w, q, q2);
     }
   }
 }
 
-__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 1)
+template <int STRIDE>
+__device__ __forceinline__ void load16(uint64_t (&x)[16], const uint64_t *buf, int l) {
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = buf[pad(l + STRIDE * k)];
+}
+template <int STRIDE>
+__device__ __forceinline__ void store16(const uint64_t (&x)[16], uint64_t *buf, int l) {
+#pragma unroll
+  for (int k = 0; k < 16; ++k) buf[pad(l + STRIDE * k)] = x[k];
+}
+
+// Passes over a CTA's block (element l = base + stride k):
+//   A: stages 3-6,   base tid,                        stride 512 (CTA-wide)
+//   B: stages 7-10,  base (tid/32)*512 + tid%32,      stride 32
+//   C: stages 11-14, base (tid/2)*32 + tid%2,         stride 2, then stage 15
+//      across lanes tid, tid^1.
+// Warp w touches only words [512 w, 512 w + 512) in B and C, so the B <-> C
+// exchange and the output staging need only warp synchronisation.
+
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     ntt_fwd_kernel(NttParams P) {
   extern __shared__ __align__(16) uint64_t buf[];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long job_id = blockIdx.x / CL;
   const long long item = job_id / P.jobs_per_item;
   const LimbJob job = P.jobs[job_id % P.jobs_per_item];
@@ -121,18 +146,16 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 1)
   const ulonglong2 *tw = P.tw + (size_t)job.prime * kN;
 
   uint64_t x[16];
+  // stages 0-2 on columns c0, c0+1 (rows k at stride 8192), straight from HBM
   const int c0 = rank * 1024 + 2 * tid;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + c0 + k * BLK);
+    const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + c0 + k * BLK);
     x[k] = v.x;
     x[8 + k] = v.y;
   }
-  // stages 0..2 on the 8 rows of both columns
   {
     const ulonglong2 w1 = ldtw(tw, 1), w2 = ldtw(tw, 2), w3 = ldtw(tw, 3);
-    const ulonglong2 w4 = ldtw(tw, 4), w5 = ldtw(tw, 5), w6 = ldtw(tw, 6),
-                     w7 = ldtw(tw, 7);
 #pragma unroll
     for (int h = 0; h < 16; h += 8) {
 #pragma unroll
@@ -141,75 +164,67 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 1)
       ct_bfly(x[h + 1], x[h + 3], w2, q, q2);
       ct_bfly(x[h + 4], x[h + 6], w3, q, q2);
       ct_bfly(x[h + 5], x[h + 7], w3, q, q2);
-      ct_bfly(x[h + 0], x[h + 1], w4, q, q2);
-      ct_bfly(x[h + 2], x[h + 3], w5, q, q2);
-      ct_bfly(x[h + 4], x[h + 5], w6, q, q2);
-      ct_bfly(x[h + 6], x[h + 7], w7, q, q2);
+#pragma unroll
+      for (int k = 0; k < 8; k += 2)
+        ct_bfly(x[h + k], x[h + k + 1], ldtw(tw, 4 + k / 2), q, q2);
     }
   }
-  cluster.sync();  // every CTA of the cluster is resident
+  // every CTA of the cluster is resident before its shared memory is written;
+  // nothing needs publishing yet, so the arrive is relaxed
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n"
+               "barrier.cluster.wait.aligned;\n" ::: "memory");
+  // row k of every column belongs to block k
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    uint64_t *remote = cluster.map_shared_rank(buf, k);
-    *reinterpret_cast<ulonglong2 *>(remote + pad(c0)) =
+  for (int k = 0; k < 8; ++k)
+    *reinterpret_cast<ulonglong2 *>(cluster.map_shared_rank(buf, k) + pad(c0)) =
         make_ulonglong2(x[k], x[8 + k]);
-  }
   cluster.sync();
 
   const int jb = rank * BLK;
-  // pass A: stages 3-6, l = tid + 512 k
-#pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = buf[pad(tid + 512 * k)];
+  load16<512>(x, buf, tid);
   ct_pass(x, tw, 3, jb + tid, 512, q, q2);
-#pragma unroll
-  for (int k = 0; k < 16; ++k) buf[pad(tid + 512 * k)] = x[k];
+  store16<512>(x, buf, tid);
   __syncthreads();
-  // pass B: stages 7-10, l = (tid/32)*512 + tid%32 + 32 k
-  const int lb = (tid >> 5) * 512 + (tid & 31);
-#pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = buf[pad(lb + 32 * k)];
+  const int lb = warp * SEG + lane;
+  load16<32>(x, buf, lb);
   ct_pass(x, tw, 7, jb + lb, 32, q, q2);
-#pragma unroll
-  for (int k = 0; k < 16; ++k) buf[pad(lb + 32 * k)] = x[k];
-  __syncthreads();
-  // pass C: stages 11-14 in registers, stage 15 across lane pairs
+  store16<32>(x, buf, lb);
+  __syncwarp();
   const int lc = (tid >> 1) * 32 + (tid & 1);
-#pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = buf[pad(lc + 2 * k)];
+  load16<2>(x, buf, lc);
   ct_pass(x, tw, 11, jb + lc, 2, q, q2);
   const bool odd = tid & 1;
   const int je = jb + (tid >> 1) * 32;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
-    uint64_t mine = x[k];
-    uint64_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
-    uint64_t X = odd ? other : mine, Y = odd ? mine : other;
-    ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * k));
-    uint64_t u = X >= q2 ? X - q2 : X;
-    uint64_t t = Y * w.x - __umul64hi(Y, w.y) * q;
+    const uint64_t mine = x[k];
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+    const uint64_t X = odd ? other : mine, Y = odd ? mine : other;
+    const ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * k));
+    const uint64_t u = X >= q2 ? X - q2 : X;
+    const uint64_t t = Y * w.x - __umul64hi(Y, w.y) * q;
     uint64_t r = odd ? u - t + q2 : u + t;
     r = r >= q2 ? r - q2 : r;
     x[k] = r >= q ? r - q : r;
   }
-  // stage through shared memory for coalesced 16-byte stores
-  __syncthreads();
+  // each lane rewrites the words it read in pass C, then the warp writes its
+  // 512-word segment with coalesced 16-byte stores
+  store16<2>(x, buf, lc);
+  __syncwarp();
 #pragma unroll
-  for (int k = 0; k < 16; ++k) buf[pad(lc + 2 * k)] = x[k];
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int idx = 2 * (tid + NT * r);
-    ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(buf + pad(idx));
-    *reinterpret_cast<ulonglong2 *>(o + jb + idx) = v;
+  for (int r = 0; r < SEG / 64; ++r) {
+    const int idx = warp * SEG + 2 * (lane + 32 * r);
+    *reinterpret_cast<ulonglong2 *>(o + jb + idx) =
+        *reinterpret_cast<const ulonglong2 *>(buf + pad(idx));
   }
 }
 
-__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 1)
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     ntt_inv_kernel(NttParams P) {
   extern __shared__ __align__(16) uint64_t buf[];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long job_id = blockIdx.x / CL;
   const long long item = job_id / P.jobs_per_item;
   const LimbJob job = P.jobs[job_id % P.jobs_per_item];
@@ -219,77 +234,66 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 1)
   const ulonglong2 *tw = P.tw + (size_t)job.prime * kN;
   const int jb = rank * BLK;
 
+  // each warp stages its own 512-word segment
 #pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int idx = 2 * (tid + NT * r);
-    ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + jb + idx);
-    *reinterpret_cast<ulonglong2 *>(buf + pad(idx)) = v;
+  for (int r = 0; r < SEG / 64; ++r) {
+    const int idx = warp * SEG + 2 * (lane + 32 * r);
+    *reinterpret_cast<ulonglong2 *>(buf + pad(idx)) =
+        *reinterpret_cast<const ulonglong2 *>(a + jb + idx);
   }
-  __syncthreads();
+  __syncwarp();
 
   uint64_t x[16];
-  // pass C: stage 15 across lane pairs, then stages 14-11
   const int lc = (tid >> 1) * 32 + (tid & 1);
-#pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = buf[pad(lc + 2 * k)];
+  load16<2>(x, buf, lc);
   const bool odd = tid & 1;
   const int je = jb + (tid >> 1) * 32;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
-    uint64_t mine = x[k];
-    uint64_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
-    uint64_t X = odd ? other : mine, Y = odd ? mine : other;
+    const uint64_t mine = x[k];
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+    const uint64_t X = odd ? other : mine, Y = odd ? mine : other;
     if (odd) {
-      ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * k));
-      uint64_t t = X - Y + q2;
+      const ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * k));
+      const uint64_t t = X - Y + q2;
       x[k] = t * w.x - __umul64hi(t, w.y) * q;
     } else {
-      uint64_t u = X + Y;
+      const uint64_t u = X + Y;
       x[k] = u >= q2 ? u - q2 : u;
     }
   }
   gs_pass(x, tw, 11, jb + lc, 2, q, q2);
-#pragma unroll
-  for (int k = 0; k < 16; ++k) buf[pad(lc + 2 * k)] = x[k];
-  __syncthreads();
-  // pass B: stages 10-7
-  const int lb = (tid >> 5) * 512 + (tid & 31);
-#pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = buf[pad(lb + 32 * k)];
+  store16<2>(x, buf, lc);
+  __syncwarp();
+  const int lb = warp * SEG + lane;
+  load16<32>(x, buf, lb);
   gs_pass(x, tw, 7, jb + lb, 32, q, q2);
-#pragma unroll
-  for (int k = 0; k < 16; ++k) buf[pad(lb + 32 * k)] = x[k];
+  store16<32>(x, buf, lb);
   __syncthreads();
-  // pass A: stages 6-3
-#pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = buf[pad(tid + 512 * k)];
+  load16<512>(x, buf, tid);
   gs_pass(x, tw, 3, jb + tid, 512, q, q2);
   cluster.sync();  // every CTA has finished reading its own block
   // word l of block `rank` is row `rank` of column l, owned by CTA l/1024
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     const int l = tid + 512 * k;
-    uint64_t *remote = cluster.map_shared_rank(buf, l >> 10);
-    remote[rank * 1024 + (l & 1023)] = x[k];
+    cluster.map_shared_rank(buf, l >> 10)[rank * 1024 + (l & 1023)] = x[k];
   }
   cluster.sync();
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(buf + k * 1024 + 2 * tid);
+    const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(buf + k * 1024 + 2 * tid);
     x[k] = v.x;
     x[8 + k] = v.y;
   }
   const ulonglong2 w1 = ldtw(tw, 1), w2 = ldtw(tw, 2), w3 = ldtw(tw, 3);
-  const ulonglong2 w4 = ldtw(tw, 4), w5 = ldtw(tw, 5), w6 = ldtw(tw, 6),
-                   w7 = ldtw(tw, 7);
   const ulonglong2 sc = P.scales[job.scale_idx];
   const int c0 = rank * 1024 + 2 * tid;
 #pragma unroll
   for (int h = 0; h < 16; h += 8) {
-    gs_bfly(x[h + 0], x[h + 1], w4, q, q2);
-    gs_bfly(x[h + 2], x[h + 3], w5, q, q2);
-    gs_bfly(x[h + 4], x[h + 5], w6, q, q2);
-    gs_bfly(x[h + 6], x[h + 7], w7, q, q2);
+#pragma unroll
+    for (int k = 0; k < 8; k += 2)
+      gs_bfly(x[h + k], x[h + k + 1], ldtw(tw, 4 + k / 2), q, q2);
     gs_bfly(x[h + 0], x[h + 2], w2, q, q2);
     gs_bfly(x[h + 1], x[h + 3], w2, q, q2);
     gs_bfly(x[h + 4], x[h + 6], w3, q, q2);
@@ -298,14 +302,13 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 1)
     for (int k = 0; k < 4; ++k) gs_bfly(x[h + k], x[h + k + 4], w1, q, q2);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      uint64_t r = x[h + k] * sc.x - __umul64hi(x[h + k], sc.y) * q;
+      const uint64_t r = x[h + k] * sc.x - __umul64hi(x[h + k], sc.y) * q;
       x[h + k] = r >= q ? r - q : r;
     }
   }
 #pragma unroll
   for (int k = 0; k < 8; ++k)
-    *reinterpret_cast<ulonglong2 *>(o + c0 + k * BLK) =
-        make_ulonglong2(x[k], x[8 + k]);
+    *reinterpret_cast<ulonglong2 *>(o + c0 + k * BLK) = make_ulonglong2(x[k], x[8 + k]);
 }
 
 }  // namespace

@@ -1,0 +1,783 @@
+"""``easyfhe.fhe`` -- the CKKS evaluation surface llama3fhe calls, on libb200fhe.
+
+Names, argument meanings, ownership and error types follow the reference's
+call sites (SURVEY section 8(b) lists them; each function cites one).  Every
+operation runs in the CUDA kernels of libb200fhe on the current torch stream;
+Python only validates levels and bookkeeps ciphertext state.
+
+Ciphertexts are torch.int64 tensors [polys, limbs, N] of uint64 residues in
+the evaluation (NTT) form, with a CipherState(cur_limbs, scale_degree,
+scaling_factor).  Scale management is FIXEDMANUAL: scale_at(l) is
+2^dcrt_bits at every level, rescale divides the tracked scaling factor by
+the dropped prime (rescale_divisor_at), align_to drops limbs and keeps it.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+import sys
+from dataclasses import dataclass, field
+from typing import Any, Iterable
+
+import numpy as np
+import torch
+
+from . import core
+from .core import N, NativeContext, Params, galois_element, sample_secret
+
+# ---------------------------------------------------------------------------
+# states, specs
+# ---------------------------------------------------------------------------
+
+
+@dataclass(frozen=True)
+class CipherState:
+    """(cur_limbs, scale_degree, scaling_factor), as the reference builds it
+    (llama3fhe/backend.py:248-254; primitives.py:130-134 uses .replace)."""
+
+    cur_limbs: int
+    scale_degree: int = 1
+    scaling_factor: float | None = None
+
+    def replace(self, **changes) -> "CipherState":
+        return dataclasses.replace(self, **changes)
+
+
+@dataclass(frozen=True)
+class CKKSContextSpec:
+    """fhe.CKKSContextSpec(depth, log_n, dnum, dcrt_bits, first_mod,
+    secret_key_dist, scale_mode, rescale_policy, rotations, auto_load_keys)
+    (llama3fhe/application/session.py:31-45)."""
+
+    depth: int
+    log_n: int
+    dnum: int
+    dcrt_bits: int
+    first_mod: int
+    secret_key_dist: str = "SPARSE_TERNARY"
+    scale_mode: str = "fixed"
+    rescale_policy: str = "manual"
+    rotations: tuple = ()
+    auto_load_keys: bool = True
+    seed: int = 0x5EEDB200
+    hamming_weight: int = 192
+    special_bits: int = 60
+    relin_key: bool = True
+
+
+# ---------------------------------------------------------------------------
+# context, client, ciphertexts, plaintexts
+# ---------------------------------------------------------------------------
+
+
+class Context:
+    """Evaluation context: primes, device tables and evaluation keys."""
+
+    def __init__(self, spec: CKKSContextSpec, params: Params, device: str):
+        if str(spec.scale_mode).lower() != "fixed":
+            raise NotImplementedError("only scale_mode='fixed' is implemented")
+        self.spec = spec
+        self.params = params
+        self.native = NativeContext(params, device)
+        self.device = str(self.native.device)
+        self.logN = params.log_n
+        self.N = 1 << self.logN
+        self.M = 2 * self.N
+        self.L = params.L
+        self.K = params.K
+        self.max_slots = self.N // 2
+        self.rotation_keys: dict[int, torch.Tensor] = {}
+        self.relin_key: torch.Tensor | None = None
+        self._ws: dict[str, torch.Tensor] = {}
+
+    def scale_at(self, cur_limbs: int) -> float:
+        return float(2.0 ** int(self.spec.dcrt_bits))
+
+    def rescale_divisor_at(self, cur_limbs: int) -> float:
+        """Prime removed by the rescale that lands on cur_limbs."""
+
+        return float(self.params.q[int(cur_limbs)])
+
+    def clear_cuda_rotation_cache(self) -> None:
+        """Keys stay resident in HBM (llama3fhe/operators/nonlinear/bootstrap.py:191-215
+        evicts EasyFHE's cache to make room; 180 GB needs no eviction)."""
+
+    def rotation_key(self, rotation: int) -> tuple[int, torch.Tensor]:
+        g = galois_element(int(rotation), self.logN)
+        key = self.rotation_keys.get(g)
+        if key is None:
+            raise ValueError(
+                f"no rotation key for index {rotation} (galois {g}); the context "
+                "rotation set must include every rotation used")
+        return g, key
+
+    def workspace(self, name: str, nbytes: int) -> torch.Tensor:
+        """A reusable scratch buffer (one per name; single-stream use)."""
+
+        buf = self._ws.get(name)
+        if buf is None or buf.numel() < nbytes:
+            buf = self.native.workspace(nbytes)
+            self._ws[name] = buf
+        return buf
+
+
+class Ciphertext:
+    """A (batch of) ciphertext(s): data [polys, limbs, N] or
+    [batch, polys, limbs, N]."""
+
+    __slots__ = ("data", "state", "slots", "is_ext", "context")
+
+    def __init__(self, data: torch.Tensor, state: CipherState, slots: int,
+                 context: Context, is_ext: bool = False):
+        self.data = data
+        self.state = state
+        self.slots = int(slots)
+        self.context = context
+        self.is_ext = bool(is_ext)
+
+    @property
+    def batch_size(self) -> int:
+        return 1 if self.data.dim() == 3 else int(self.data.shape[0])
+
+    @property
+    def polys(self) -> int:
+        return int(self.data.shape[-3])
+
+    @property
+    def cv(self) -> list[torch.Tensor]:
+        return [self.data.select(-3, p) for p in range(self.polys)]
+
+    def deep_copy(self) -> "Ciphertext":
+        return Ciphertext(self.data.clone(), self.state, self.slots, self.context,
+                          self.is_ext)
+
+    def cipher_like(self, cv, slots: int | None = None,
+                    batch_size: int | None = None) -> "Ciphertext":
+        data = torch.stack([torch.as_tensor(c) for c in cv], dim=-3).contiguous()
+        return Ciphertext(data, self.state, self.slots if slots is None else slots,
+                          self.context, self.is_ext)
+
+    def release(self) -> None:
+        self.data = None
+
+
+class Plaintext:
+    """Encoded plaintext(s): data [rows, limbs, N] (ext: l Q-limbs + K)."""
+
+    __slots__ = ("data", "state", "slots", "is_ext", "rows")
+
+    def __init__(self, data: torch.Tensor, state: CipherState, slots: int, is_ext: bool):
+        self.data = data
+        self.state = state
+        self.slots = int(slots)
+        self.is_ext = bool(is_ext)
+        self.rows = int(data.shape[0]) if data.dim() == 3 else 1
+
+    def q_part(self, limbs: int) -> torch.Tensor:
+        """[rows, limbs, N] view of the Q limbs (contiguous when not ext)."""
+
+        d = self.data if self.data.dim() == 3 else self.data.unsqueeze(0)
+        if d.shape[1] == limbs:
+            return d
+        return d[:, :limbs].contiguous()
+
+    def release(self) -> None:
+        self.data = None
+
+
+class Client:
+    """Holds the secret key; client.encrypt / client.decrypt
+    (llama3fhe/application/session.py:71-77, llama3fhe/backend.py:305-313)."""
+
+    def __init__(self, context: Context, secret: np.ndarray, seed: int):
+        self.context = context
+        self._s_ntt = context.native.secret_to_ntt(secret)
+        self._seed = int(seed)
+        self._nonce = 0
+
+    def encode(self, values, slots: int, cur_limbs: int, scaling_factor: float,
+               ext: bool = False) -> torch.Tensor:
+        v = torch.as_tensor(np.asarray(values)).reshape(-1)
+        if v.numel() > slots:
+            raise ValueError(f"{v.numel()} values do not fit {slots} slots")
+        z = torch.zeros(slots, dtype=torch.complex128)
+        z[: v.numel()] = v.to(torch.complex128)
+        return self.context.native.encode(z.to(self.context.device), scaling_factor,
+                                          cur_limbs, self.context.K if ext else 0)
+
+    def encrypt(self, values, device=None, slots: int | None = None,
+                cur_limbs: int | None = None, scaling_factor: float | None = None):
+        ctx = self.context
+        slots = ctx.max_slots if slots is None else int(slots)
+        cur_limbs = ctx.L if cur_limbs is None else int(cur_limbs)
+        scale = ctx.scale_at(cur_limbs) if scaling_factor is None else float(scaling_factor)
+        m = self.encode(values, slots, cur_limbs, scale)
+        self._nonce += 1
+        data = ctx.native.encrypt(m, cur_limbs, self._s_ntt, self._seed, self._nonce)
+        return Ciphertext(data, CipherState(cur_limbs, 1, scale), slots, ctx)
+
+    def decrypt(self, cipher: Ciphertext) -> np.ndarray:
+        """Real parts of the slots (float64)."""
+
+        return self.decrypt_complex(cipher).real.copy()
+
+    def decrypt_complex(self, cipher: Ciphertext) -> np.ndarray:
+        ctx = self.context
+        if cipher.is_ext:
+            raise ValueError("decrypt needs a non-extended ciphertext")
+        l = int(cipher.state.cur_limbs)
+        data = cipher.data
+        if cipher.polys == 3:
+            data = homo_relinearize(cipher, ctx).data
+        m = ctx.native.decrypt(data, l, self._s_ntt)
+        scale = float(cipher.state.scaling_factor or ctx.scale_at(l))
+        return ctx.native.decode(m, l, cipher.slots, scale)
+
+
+def generate_client_context(spec: CKKSContextSpec, device: str = "cuda"):
+    """fhe.generate_client_context (llama3fhe/application/session.py:31-45):
+    primes, device tables, secret key, relinearisation and rotation keys."""
+
+    if int(spec.log_n) != core.LOG_N:
+        raise NotImplementedError("libb200fhe kernels are built for log_n = 16")
+    params = Params.from_depth(spec.depth, spec.log_n, spec.dnum, spec.dcrt_bits,
+                               spec.first_mod, special_bits=spec.special_bits)
+    ctx = Context(spec, params, device)
+    dist = str(spec.secret_key_dist).upper()
+    hamming = int(spec.hamming_weight) if dist.startswith("SPARSE") else 0
+    secret = sample_secret(int(spec.seed), hamming, spec.log_n)
+    client = Client(ctx, secret, int(spec.seed) ^ 0xC1)
+    s = client._s_ntt
+    if spec.relin_key:
+        ctx.relin_key = ctx.native.keygen_relin(s, int(spec.seed) ^ 0xE1)
+    for r in sorted({int(v) for v in spec.rotations}):
+        g = galois_element(r, spec.log_n)
+        if g != 1 and g not in ctx.rotation_keys:
+            ctx.rotation_keys[g] = ctx.native.keygen_rotation(s, g, int(spec.seed) ^ g)
+    return client, ctx
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+
+def _ctx_of(context) -> Context:
+    c = getattr(context, "context", context)
+    if not isinstance(c, Context):
+        raise TypeError(f"expected an easyfhe.fhe.Context, got {type(context)!r}")
+    return c
+
+
+def _limbs(ct) -> int:
+    return int(ct.state.cur_limbs)
+
+
+def _drop(ct: Ciphertext, target: int) -> Ciphertext:
+    l = _limbs(ct)
+    if target == l:
+        return ct
+    if target > l or target < 1:
+        raise ValueError(f"cannot align {l} limbs to {target}")
+    polys = ct.polys * ct.batch_size
+    data = ct.context.native.drop_limbs(ct.data, polys, l, target)
+    shape = list(ct.data.shape)
+    shape[-2] = target
+    return Ciphertext(data.view(shape), ct.state.replace(cur_limbs=target), ct.slots,
+                      ct.context, ct.is_ext)
+
+
+def _match(a: Ciphertext, b: Ciphertext) -> tuple[Ciphertext, Ciphertext]:
+    la, lb = _limbs(a), _limbs(b)
+    if la > lb:
+        a = _drop(a, lb)
+    elif lb > la:
+        b = _drop(b, la)
+    return a, b
+
+
+def _check_scales(a: Ciphertext, b, what: str) -> None:
+    if int(a.state.scale_degree) != int(b.state.scale_degree):
+        raise ValueError(f"{what}: scale degrees differ ({a.state.scale_degree} vs "
+                         f"{b.state.scale_degree})")
+
+
+def _new(data: torch.Tensor, like: Ciphertext, state: CipherState | None = None) -> Ciphertext:
+    return Ciphertext(data, like.state if state is None else state, like.slots, like.context,
+                      like.is_ext)
+
+
+def _polys_total(ct: Ciphertext) -> int:
+    return ct.polys * ct.batch_size
+
+
+# ---------------------------------------------------------------------------
+# additive ops
+# ---------------------------------------------------------------------------
+
+
+def _addsub(op: int, a: Ciphertext, b: Ciphertext, context) -> Ciphertext:
+    ctx = _ctx_of(context)
+    a, b = _match(a, b)
+    _check_scales(a, b, "homo_add" if op == 0 else "homo_sub")
+    if a.polys != b.polys:
+        if a.polys < b.polys:
+            a = _pad_polys(a, b.polys)
+        else:
+            b = _pad_polys(b, a.polys)
+    l = _limbs(a)
+    out = ctx.native.elementwise(op, a.data, b.data, _polys_total(a), l)
+    return _new(out.view(a.data.shape), a)
+
+
+def _pad_polys(ct: Ciphertext, polys: int) -> Ciphertext:
+    extra = torch.zeros((polys - ct.polys,) + tuple(ct.data.shape[-2:]), dtype=ct.data.dtype,
+                        device=ct.data.device)
+    return _new(torch.cat([ct.data, extra], dim=0), ct)
+
+
+def homo_add(a: Ciphertext, b: Ciphertext, context) -> Ciphertext:
+    """a + b (28 call sites, e.g. llama3fhe/operators/linear/operator.py:345-351)."""
+
+    return _addsub(0, a, b, context)
+
+
+def homo_sub(a: Ciphertext, b: Ciphertext, context) -> Ciphertext:
+    """a - b (llama3fhe/operators/linear/complex.py:60-62)."""
+
+    return _addsub(1, a, b, context)
+
+
+def homo_add_pt(ct: Ciphertext, pt: Plaintext, context) -> Ciphertext:
+    """ct + pt, pt added to c0."""
+
+    ctx = _ctx_of(context)
+    l = _limbs(ct)
+    p = pt.q_part(l) if _pt_limbs(pt) >= l else None
+    if p is None:
+        raise ValueError("plaintext has fewer limbs than the ciphertext")
+    out = ct.data.clone()
+    ctx.native.elementwise(0, ct.data[0], p[0], 1, l, out=out[0])
+    return _new(out, ct)
+
+
+def _pt_limbs(pt: Plaintext) -> int:
+    limbs = int(pt.data.shape[-2])
+    return limbs - pt.context_k if getattr(pt, "context_k", None) else int(pt.state.cur_limbs)
+
+
+def homo_mul_pt(ct: Ciphertext, pt: Plaintext, context) -> Ciphertext:
+    """ct * pt (llama3fhe/operators/primitives.py:40-49); scale degree adds."""
+
+    ctx = _ctx_of(context)
+    l = _limbs(ct)
+    if int(pt.state.cur_limbs) < l:
+        raise ValueError(f"plaintext at {pt.state.cur_limbs} limbs, ciphertext at {l}")
+    p = pt.q_part(l)[0]
+    out = ctx.native.elementwise(2, ct.data, p, _polys_total(ct), l, b_polys=1)
+    state = ct.state.replace(
+        scale_degree=int(ct.state.scale_degree) + int(pt.state.scale_degree),
+        scaling_factor=float(ct.state.scaling_factor) * float(pt.state.scaling_factor))
+    return _new(out.view(ct.data.shape), ct, state)
+
+
+def homo_mul_i(ct: Ciphertext, context, negative: bool = False) -> Ciphertext:
+    """Multiply every slot by i (or -i): the monomial X^(N/2), no key
+    (llama3fhe/operators/linear/complex.py:22; attention/codec.py:42)."""
+
+    ctx = _ctx_of(context)
+    out = ctx.native.mul_i(ct.data, _polys_total(ct), _limbs(ct), bool(negative))
+    return _new(out.view(ct.data.shape), ct)
+
+
+# ---------------------------------------------------------------------------
+# scalars
+# ---------------------------------------------------------------------------
+
+
+@dataclass(frozen=True)
+class EncodedScalar:
+    residues: tuple[int, ...]
+    state: CipherState
+    value: float
+
+
+def encode_scalar(value, cur_limbs: int, scale_degree: int = 1, scaling_factor=None,
+                  context=None, mode: str = "double") -> EncodedScalar:
+    """fhe.encode_scalar(v, cur_limbs, scale_degree, scaling_factor | mode,
+    context) (llama3fhe/operators/nonlinear/bootstrap.py:331-349,
+    polynomial.py:41-47): the constant round(v * scale^degree) in RNS."""
+
+    ctx = _ctx_of(context)
+    cur_limbs = int(cur_limbs)
+    if str(mode) == "integer":
+        integer = int(value)
+        scale = 1.0
+        degree = 0
+    else:
+        degree = int(scale_degree)
+        scale = float(scaling_factor if scaling_factor is not None
+                      else ctx.scale_at(cur_limbs)) if degree else 1.0
+        x = float(value) * (scale if degree else 1.0)
+        if not math.isfinite(x):
+            raise ValueError("encoded scalar overflows")
+        integer = int(round(x))
+    residues = tuple(integer % q for q in ctx.params.q[:cur_limbs])
+    return EncodedScalar(residues, CipherState(cur_limbs, degree, scale), float(value))
+
+
+def _enc_for(ct: Ciphertext, enc: EncodedScalar) -> tuple[int, ...]:
+    l = _limbs(ct)
+    if len(enc.residues) < l:
+        raise ValueError(f"scalar encoded for {len(enc.residues)} limbs, cipher has {l}")
+    return enc.residues[:l]
+
+
+def homo_mul_scalar(ct: Ciphertext, enc: EncodedScalar, context) -> Ciphertext:
+    """ct * scalar without rescale (llama3fhe/operators/nonlinear/bootstrap.py:338)."""
+
+    ctx = _ctx_of(context)
+    l = _limbs(ct)
+    out = ctx.native.scalar_op(ct.data, _polys_total(ct), l, mul=_enc_for(ct, enc))
+    state = ct.state.replace(
+        scale_degree=int(ct.state.scale_degree) + int(enc.state.scale_degree),
+        scaling_factor=float(ct.state.scaling_factor) * float(enc.state.scaling_factor))
+    return _new(out.view(ct.data.shape), ct, state)
+
+
+def homo_mul_scalar_rescale(ct: Ciphertext, enc: EncodedScalar, context) -> Ciphertext:
+    """ct * scalar, rescaled (llama3fhe/operators/norm/refresh.py:28-30)."""
+
+    return rescale(homo_mul_scalar(ct, enc, context), context)
+
+
+def homo_add_scalar(ct: Ciphertext, enc: EncodedScalar, context) -> Ciphertext:
+    """ct + scalar, added to c0 (llama3fhe/operators/nonlinear/polynomial.py:84-88)."""
+
+    ctx = _ctx_of(context)
+    l = _limbs(ct)
+    out = ctx.native.scalar_op(ct.data, _polys_total(ct), l, add=_enc_for(ct, enc),
+                               add_poly=0 if ct.batch_size == 1 else -1)
+    if ct.batch_size != 1:
+        raise NotImplementedError("homo_add_scalar on a ciphertext batch")
+    return _new(out.view(ct.data.shape), ct)
+
+
+# ---------------------------------------------------------------------------
+# levels
+# ---------------------------------------------------------------------------
+
+
+def rescale(ct: Ciphertext, context) -> Ciphertext:
+    """Divide by the last prime (57 sites; llama3fhe/operators/linear/operator.py:386-388)."""
+
+    ctx = _ctx_of(context)
+    l = _limbs(ct)
+    if l < 2:
+        raise ValueError("rescale needs at least two limbs")
+    out = ctx.native.rescale(ct.data, _polys_total(ct), l)
+    shape = list(ct.data.shape)
+    shape[-2] = l - 1
+    state = ct.state.replace(
+        cur_limbs=l - 1,
+        scale_degree=max(1, int(ct.state.scale_degree) - 1),
+        scaling_factor=float(ct.state.scaling_factor) / ctx.rescale_divisor_at(l - 1))
+    return _new(out.view(shape), ct, state)
+
+
+def align_to(ct: Ciphertext, state: CipherState, context) -> Ciphertext:
+    """Scale-preserving modulus drop to state.cur_limbs; returns ct itself when
+    nothing changes (llama3fhe/operators/primitives.py:100-155)."""
+
+    _ctx_of(context)
+    target = int(state.cur_limbs)
+    if target == _limbs(ct):
+        return ct
+    if target > _limbs(ct):
+        raise ValueError(f"cannot raise {_limbs(ct)} limbs to {target}")
+    return _drop(ct, target)
+
+
+# ---------------------------------------------------------------------------
+# rotations and multiplication
+# ---------------------------------------------------------------------------
+
+
+def homo_rotate(ct: Ciphertext, rotation: int, context) -> Ciphertext:
+    """Left rotation of the slots by `rotation` (M - 1: conjugation) with hybrid
+    key switching (34 sites, e.g. llama3fhe/operators/linear/operator.py:333-337)."""
+
+    ctx = _ctx_of(context)
+    if ct.is_ext:
+        raise ValueError("homo_rotate needs a non-extended ciphertext")
+    if ct.polys != 2:
+        raise ValueError("homo_rotate needs a relinearised ciphertext")
+    g = galois_element(int(rotation), ctx.logN)
+    if g == 1:
+        return ct.deep_copy()
+    _, key = ctx.rotation_key(int(rotation))
+    l = _limbs(ct)
+    out = ctx.native.rotate(ct.data, l, g, key)
+    return _new(out, ct)
+
+
+def homo_mul_no_relin(a: Ciphertext, b: Ciphertext, context) -> Ciphertext:
+    """Tensor product (d0, d1, d2) (llama3fhe/operators/attention/qk.py:399)."""
+
+    ctx = _ctx_of(context)
+    a, b = _match(a, b)
+    if a.polys != 2 or b.polys != 2:
+        raise ValueError("homo_mul_no_relin needs degree-1 ciphertexts")
+    l = _limbs(a)
+    nat = ctx.native
+    shape = (3,) + tuple(a.data.shape[-2:])
+    out = nat.empty(3, l).view(shape)
+    nat.elementwise(2, a.data[0], b.data[0], 1, l, out=out[0])
+    nat.elementwise(2, a.data[1], b.data[1], 1, l, out=out[2])
+    t = nat.elementwise(2, a.data[0], b.data[1], 1, l)
+    u = nat.elementwise(2, a.data[1], b.data[0], 1, l)
+    nat.elementwise(0, t, u, 1, l, out=out[1])
+    state = a.state.replace(
+        scale_degree=int(a.state.scale_degree) + int(b.state.scale_degree),
+        scaling_factor=float(a.state.scaling_factor) * float(b.state.scaling_factor))
+    return _new(out, a, state)
+
+
+def homo_relinearize(ct: Ciphertext, context) -> Ciphertext:
+    """(d0, d1, d2) -> (d0, d1) + KeySwitch_{s^2 -> s}(d2)
+    (llama3fhe/operators/attention/kernel_helpers.py:155)."""
+
+    ctx = _ctx_of(context)
+    if ct.polys == 2:
+        return ct.deep_copy()
+    if ctx.relin_key is None:
+        raise ValueError("context has no relinearisation key")
+    l = _limbs(ct)
+    out = ctx.native.relinearize(ct.data, l, ctx.relin_key)
+    return _new(out, ct)
+
+
+def homo_mul_relin(a: Ciphertext, b: Ciphertext, context) -> Ciphertext:
+    """a * b, relinearised (llama3fhe/operators/primitives.py:21-31)."""
+
+    return homo_relinearize(homo_mul_no_relin(a, b, context), context)
+
+
+def homo_mul_relin_rescale_postop(left: Ciphertext, right: Ciphertext, context,
+                                  apply_double: bool = False, sub=None,
+                                  scalar: EncodedScalar | None = None) -> Ciphertext:
+    """rescale(relin(l * r)), then optionally times 2, minus `sub`, plus `scalar`
+    (llama3fhe/operators/nonlinear/polynomial.py:108-159)."""
+
+    out = rescale(homo_mul_relin(left, right, context), context)
+    if apply_double:
+        out = homo_add(out, out, context)
+    if sub is not None:
+        out = homo_sub(out, align_to(sub, out.state, context), context)
+    if scalar is not None:
+        out = homo_add_scalar(out, scalar, context)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# baby-step / giant-step
+# ---------------------------------------------------------------------------
+
+
+class BabyRotations(tuple):
+    """Hoisted baby rotations of one ciphertext: block 0 is a Ciphertext batch
+    [B, 2, l, N] (baby b = rotation by baby_offsets[b]); iterable like the
+    reference's block tuple (llama3fhe/operators/linear/operator.py:119-122)."""
+
+    offsets: tuple[int, ...] = ()
+
+
+def prepare_hoisted_baby_rotations(ct: Ciphertext, baby_offsets, context,
+                                   strategy: str = "normal",
+                                   baby_anchor_step: int = -1) -> BabyRotations:
+    """One ModUp of c1, then one key inner product + ModDown per baby offset
+    (llama3fhe/operators/linear/operator.py:105-111)."""
+
+    ctx = _ctx_of(context)
+    offsets = tuple(int(v) for v in baby_offsets)
+    l = _limbs(ct)
+    nat = ctx.native
+    out = nat.empty(len(offsets), 2, l)
+    rot_idx, gal, keys = [], [], []
+    for b, off in enumerate(offsets):
+        g = galois_element(off, ctx.logN)
+        if g == 1:
+            out[b].copy_(ct.data)
+        else:
+            _, key = ctx.rotation_key(off)
+            rot_idx.append(b)
+            gal.append(g)
+            keys.append(key)
+    if rot_idx:
+        ext = nat.modup(ct.data, l)
+        res = nat.rotate_hoisted(ct.data, l, ext, gal, keys)
+        idx = torch.tensor(rot_idx, device=out.device)
+        out.index_copy_(0, idx, res)
+    block = Ciphertext(out, ct.state, ct.slots, ctx)
+    babies = BabyRotations((block,))
+    babies.offsets = offsets
+    return babies
+
+
+def hoisted_mac_sum(ct: Ciphertext, baby_offsets, plaintexts: Plaintext, giant_offset: int,
+                    giant_count: int, context, strategy: str = "normal",
+                    baby_anchor_step: int = -1, baby_rotations=None) -> Ciphertext:
+    """sum_{g<G} rot_{g*giant_offset}(sum_b pt[g*B+b] * rot_{baby_offsets[b]}(ct)),
+    Horner over the giants with the one giant key
+    (llama3fhe/operators/linear/operator.py:320-330, transform.py:108-116).
+    The result is at the input level with scale degree 2; the caller rescales."""
+
+    ctx = _ctx_of(context)
+    offsets = tuple(int(v) for v in baby_offsets)
+    B, G = len(offsets), int(giant_count)
+    l = _limbs(ct)
+    if baby_rotations is None:
+        baby_rotations = prepare_hoisted_baby_rotations(ct, offsets, ctx, strategy,
+                                                        baby_anchor_step)
+    block = tuple(baby_rotations)[0]
+    if int(block.state.cur_limbs) != l:
+        raise ValueError("baby rotations were prepared at a different level")
+    if plaintexts.rows < G * B:
+        raise ValueError(f"{plaintexts.rows} plaintext rows < giants*babies = {G * B}")
+    pts = plaintexts.q_part(l)
+    if G > 1:
+        gg, gkey = ctx.rotation_key(int(giant_offset))
+    else:
+        gg, gkey = 1, None
+    out = ctx.native.bsgs_mac(block.data, B, pts, G, l, gg, gkey)
+    state = ct.state.replace(
+        scale_degree=int(ct.state.scale_degree) + int(plaintexts.state.scale_degree),
+        scaling_factor=float(ct.state.scaling_factor) * float(plaintexts.state.scaling_factor))
+    return Ciphertext(out, state, ct.slots, ctx)
+
+
+# ---------------------------------------------------------------------------
+# constants
+# ---------------------------------------------------------------------------
+
+
+class PackedRaw:
+    """Slot values already packed: [rows, slots] or [slots] (llama3fhe/backend.py:282)."""
+
+    def __init__(self, tensor):
+        self.tensor = tensor
+
+
+class UnpackedRaw:
+    """Raw weight plus the packer that lays out its diagonals
+    (llama3fhe/operators/linear/weight.py:309-310)."""
+
+    def __init__(self, source, packer):
+        self.source = source
+        self.packer = packer
+
+
+class ConstantBundle:
+    """Named constant vectors encoded on demand at a requested state
+    (llama3fhe/backend.py:231-297, llama3fhe/operators/linear/weight.py:344-357).
+    cache_mode 'plain'/'both' keeps the encoded plaintexts; 'middle' keeps the
+    packed slot values; 'none' keeps nothing."""
+
+    _MODES = {"none", "middle", "plain", "both"}
+
+    def __init__(self, vectors: dict, cache_mode: str = "none"):
+        if str(cache_mode) not in self._MODES:
+            raise ValueError(f"cache_mode must be one of {sorted(self._MODES)}")
+        self.vectors = dict(vectors)
+        self.cache_mode = str(cache_mode)
+        self._middle: dict[Any, torch.Tensor] = {}
+        self._plain: dict[Any, Plaintext] = {}
+        self._stats = {"middle_hits": 0, "middle_misses": 0, "plain_hits": 0,
+                       "plain_misses": 0}
+
+    def set_cache_mode(self, mode: str) -> None:
+        if str(mode) not in self._MODES:
+            raise ValueError(f"cache_mode must be one of {sorted(self._MODES)}")
+        self.cache_mode = str(mode)
+
+    def _slots_values(self, name: str, slots: int, context: Context) -> torch.Tensor:
+        key = (name, slots)
+        if key in self._middle:
+            self._stats["middle_hits"] += 1
+            return self._middle[key]
+        self._stats["middle_misses"] += 1
+        raw = self.vectors[name]
+        if isinstance(raw, UnpackedRaw):
+            values = raw.packer(raw.source, slots, context)
+        elif isinstance(raw, PackedRaw):
+            values = raw.tensor
+        else:
+            values = raw
+        t = torch.as_tensor(values)
+        if t.device.type != "cuda":
+            t = t.to(context.device)
+        t = t.to(torch.complex128)
+        if t.dim() == 1:
+            t = t.unsqueeze(0)
+        if t.shape[-1] != slots:
+            if t.shape[-1] > slots:
+                raise ValueError(f"{t.shape[-1]} values do not fit {slots} slots")
+            pad = torch.zeros(t.shape[0], slots - t.shape[-1], dtype=t.dtype, device=t.device)
+            t = torch.cat([t, pad], dim=1)
+        if self.cache_mode in ("middle", "both"):
+            self._middle[key] = t
+        return t
+
+    def plaintext(self, name: str, state: CipherState | None = None, slots: int | None = None,
+                  context=None, is_ext: bool = False, cache: bool = False) -> Plaintext:
+        ctx = _ctx_of(context)
+        slots = ctx.max_slots if slots is None else int(slots)
+        state = state or CipherState(ctx.L, 1, ctx.scale_at(ctx.L))
+        l = int(state.cur_limbs)
+        scale = float(state.scaling_factor if state.scaling_factor is not None
+                      else ctx.scale_at(l))
+        key = (name, slots, l, scale, bool(is_ext))
+        if key in self._plain:
+            self._stats["plain_hits"] += 1
+            return self._plain[key]
+        self._stats["plain_misses"] += 1
+        values = self._slots_values(name, slots, ctx)
+        data = ctx.native.encode(values, scale, l, ctx.K if is_ext else 0)
+        pt = Plaintext(data, CipherState(l, int(state.scale_degree or 1), scale), slots,
+                       bool(is_ext))
+        if self.cache_mode in ("plain", "both") and cache is not False:
+            self._plain[key] = pt
+        return pt
+
+    def cache_info(self) -> dict:
+        mb = sum(int(t.numel() * t.element_size()) for t in self._middle.values())
+        pb = sum(int(p.data.numel() * 8) for p in self._plain.values() if p.data is not None)
+        return {"middle_entries": len(self._middle), "plain_entries": len(self._plain),
+                "middle_bytes": mb, "plain_bytes": pb, "total_bytes": mb + pb, **self._stats}
+
+    def clear_cache(self) -> None:
+        self._middle.clear()
+        self._plain.clear()
+
+
+# ---------------------------------------------------------------------------
+# not yet on the native path (attention batch ops): fail loudly
+# ---------------------------------------------------------------------------
+
+
+def _pending(name: str, site: str):
+    def fn(*args, **kwargs):
+        raise NotImplementedError(
+            f"fhe.{name} ({site}) is not implemented on libb200fhe yet")
+
+    fn.__name__ = name
+    return fn
+
+
+fast_rotate = _pending("fast_rotate", "llama3fhe/operators/attention/input.py:792-797")
+pack_cipher_batch = _pending("pack_cipher_batch", "llama3fhe/operators/attention/input.py:810")
+unpack_cipher_batch = _pending("unpack_cipher_batch", "llama3fhe/operators/attention/input.py:798")
+grouped_pairwise_mac = _pending("grouped_pairwise_mac",
+                                "llama3fhe/operators/attention/input.py:814-819")
+moddown_from_ext = _pending("moddown_from_ext", "llama3fhe/operators/attention/input.py:821")
