@@ -337,3 +337,103 @@ int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Rescale that allocates nothing (b2f_rescale_noalloc).
+//
+// For callers that cannot allocate device memory: a process whose HBM is
+// owned by another allocator (a framework that reserved the device up front
+// and hands out only its own blocks), or a step with a fixed memory budget
+// that may not call cudaMalloc/cudaMallocAsync.  The scratch lives in a
+// file-scope __device__ array instead; every GPU that loads this library
+// holds it (16 MiB) until the process exits.
+// ---------------------------------------------------------------------------
+namespace b2f {
+namespace {
+
+// scratch: the last limb of every poly (num_polys N words) followed by its
+// lift to the other primes (num_polys (l-1) N words)
+constexpr size_t kNoAllocBytes = 16u << 20;
+constexpr size_t kNoAllocWords = kNoAllocBytes / sizeof(uint64_t);
+__device__ __align__(256) uint64_t g_noalloc_scratch[kNoAllocWords];
+// NTT job tables of the two transforms: row 0 the last limb, row 1 limbs
+// 0..l-2 (l <= 64)
+__device__ __align__(256) LimbJob g_noalloc_jobs[2][64];
+
+struct NoAllocDevice {
+  bool ready = false;
+  uint64_t *scratch = nullptr;
+  LimbJob *jobs = nullptr;
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[64];
+
+__global__ void noalloc_jobs_kernel(LimbJob *jobs, int l) {
+  const int i = threadIdx.x;
+  if (i == 0)
+    jobs[0] = LimbJob{(uint32_t)(l - 1), 0u, (uint16_t)(l - 1), (uint16_t)(l - 1), 0};
+  if (i < l - 1) jobs[64 + i] = LimbJob{(uint32_t)i, (uint32_t)i, (uint16_t)i, (uint16_t)i, 0};
+}
+
+// The host-side names of the arrays above are stand-ins, not device
+// addresses: look the addresses up once per device, with that device
+// current, and hand those to the kernels.
+int noalloc_setup(const b2f_context *ctx, NoAllocDevice **out) {
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  NoAllocDevice &d = g_noalloc_dev[ctx->device & 63];
+  if (!d.ready) {
+    int prev = 0;
+    B2F_CUDA(cudaGetDevice(&prev));
+    if (prev != ctx->device) B2F_CUDA(cudaSetDevice(ctx->device));
+    cudaError_t e1 = cudaGetSymbolAddress((void **)&d.scratch, g_noalloc_scratch);
+    cudaError_t e2 = cudaGetSymbolAddress((void **)&d.jobs, g_noalloc_jobs);
+    if (prev != ctx->device) cudaSetDevice(prev);
+    if (e1 != cudaSuccess) return cuda_status(e1, "cudaGetSymbolAddress(scratch)");
+    if (e2 != cudaSuccess) return cuda_status(e2, "cudaGetSymbolAddress(jobs)");
+    d.ready = true;
+  }
+  *out = &d;
+  return B2F_OK;
+}
+
+}  // namespace
+}  // namespace b2f
+
+extern "C" int b2f_rescale_noalloc(b2f_context *ctx, const uint64_t *in,
+                                   uint64_t *out, int num_polys, int l,
+                                   void *stream) {
+  B2F_CHECK_ARG(ctx && in && out && num_polys >= 0,
+                "b2f_rescale_noalloc: null argument");
+  B2F_CHECK_ARG(l >= 2 && l <= ctx->L && l <= 64,
+                "b2f_rescale_noalloc: needs 2..%d limbs, got %d", ctx->L, l);
+  B2F_CHECK_ARG(in != out, "b2f_rescale_noalloc: in-place rescale is not supported");
+  const size_t need = (size_t)num_polys * l * kN;
+  B2F_CHECK_ARG(need <= kNoAllocWords,
+                "b2f_rescale_noalloc: %d polys x %d limbs need %zu bytes of scratch, "
+                "more than its fixed %zu (num_polys * l must be <= %zu)",
+                num_polys, l, need * 8, kNoAllocBytes, kNoAllocWords / kN);
+  if (!num_polys) return B2F_OK;
+  NoAllocDevice *d = nullptr;
+  int rc = noalloc_setup(ctx, &d);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  uint64_t *last = d->scratch;
+  uint64_t *lifted = last + (size_t)num_polys * kN;
+  const LevelTables &T = ctx->levels[l];
+  noalloc_jobs_kernel<<<1, 64, 0, s>>>(d->jobs, l);
+  B2F_LAUNCHED("noalloc_jobs_kernel");
+  rc = launch_ntt(ctx, in, (long long)l * kN, last, kN, d->jobs, 1, num_polys, 1,
+                  nullptr, s);
+  if (rc) return rc;
+  rescale_lift_kernel<<<dim3(kN / TPB, l - 1, num_polys), TPB, 0, s>>>(
+      last, lifted, ctx->d_primes, T.rescale_qlast, l, ctx->primes[l - 1]);
+  B2F_LAUNCHED("rescale_lift_kernel");
+  const long long ls = (long long)(l - 1) * kN;
+  rc = launch_ntt(ctx, lifted, ls, lifted, ls, d->jobs + 64, l - 1, num_polys, 0,
+                  nullptr, s);
+  if (rc) return rc;
+  rescale_combine_kernel<<<dim3(kN / TPB, l - 1, num_polys), TPB, 0, s>>>(
+      in, lifted, out, ctx->d_primes, T.rescale_inv, l);
+  B2F_LAUNCHED("rescale_combine_kernel");
+  return B2F_OK;
+}

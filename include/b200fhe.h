@@ -120,6 +120,17 @@ int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
 size_t b2f_rescale_workspace(const b2f_context *ctx, int num_polys, int l);
 int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
                 int num_polys, int l, void *ws, size_t ws_bytes, void *stream);
+/* Same result as b2f_rescale, bit for bit, with no device allocation: for
+ * callers that cannot allocate device memory (their HBM is owned by another
+ * allocator, or the step runs under a fixed memory budget).  No counterpart
+ * in the reference.  Scratch is a fixed 16 MiB array in device memory that
+ * every GPU loading this library holds until exit; num_polys * l must be
+ * <= 32 (e.g. one ciphertext at up to 16 limbs), larger requests fail with
+ * B2F_ERR_ARG.  The first call on a device looks up that device's array
+ * address; make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU (other streams, other threads) race. */
+int b2f_rescale_noalloc(b2f_context *ctx, const uint64_t *in, uint64_t *out,
+                        int num_polys, int l, void *stream);
 /* fhe.align_to to fewer limbs (llama3fhe/operators/primitives.py:100-155):
  * keep limbs 0..l_out-1 of each poly. */
 int b2f_drop_limbs(b2f_context *ctx, const uint64_t *in, uint64_t *out,
