@@ -350,21 +350,18 @@ def homo_sub(a: Ciphertext, b: Ciphertext, context) -> Ciphertext:
 
 
 def homo_add_pt(ct: Ciphertext, pt: Plaintext, context) -> Ciphertext:
-    """ct + pt, pt added to c0."""
+    """ct + pt, the plaintext added to c0."""
 
     ctx = _ctx_of(context)
     l = _limbs(ct)
-    p = pt.q_part(l) if _pt_limbs(pt) >= l else None
-    if p is None:
-        raise ValueError("plaintext has fewer limbs than the ciphertext")
+    if int(pt.state.cur_limbs) < l:
+        raise ValueError(f"plaintext at {pt.state.cur_limbs} limbs, ciphertext at {l}")
+    if int(pt.state.scale_degree) != int(ct.state.scale_degree):
+        raise ValueError("homo_add_pt: scale degrees differ")
+    p = pt.q_part(l)[0]
     out = ct.data.clone()
-    ctx.native.elementwise(0, ct.data[0], p[0], 1, l, out=out[0])
+    ctx.native.elementwise(0, ct.data[0], p, 1, l, out=out[0])
     return _new(out, ct)
-
-
-def _pt_limbs(pt: Plaintext) -> int:
-    limbs = int(pt.data.shape[-2])
-    return limbs - pt.context_k if getattr(pt, "context_k", None) else int(pt.state.cur_limbs)
 
 
 def homo_mul_pt(ct: Ciphertext, pt: Plaintext, context) -> Ciphertext:
