@@ -156,6 +156,26 @@ __global__ void __launch_bounds__(TPB) automorphism_kernel(
   out[limb * kN + k] = in[limb * kN + auto_src(k, g)];
 }
 
+// Extended-basis rotation output (double hoisting): for every limb t of
+// Q_l u P, out0[t][k] = (t < l ? [P]_{q_t} c0[t] : 0)[src] + acc0[t][src],
+// out1[t][k] = acc1[t][src], src = pi_g(k); with acc == null (g = 1) the
+// output is (P c0, P c1).  grid (N/TPB, l+K, 2)
+__global__ void __launch_bounds__(TPB) ext_combine_kernel(
+    const uint64_t *__restrict__ acc, const uint64_t *__restrict__ ct,
+    uint64_t *__restrict__ out, const Mod *__restrict__ mods,
+    const uint64_t *__restrict__ pmod, int l, int K, int L, uint32_t g) {
+  const int k = blockIdx.x * TPB + threadIdx.x;
+  const int t = blockIdx.y, b = blockIdx.z;
+  const int lk = l + K;
+  const uint32_t src = g == 1 ? (uint32_t)k : auto_src(k, g);
+  const Mod M = mods[t < l ? t : L + (t - l)];
+  uint64_t v = 0;
+  if (t < l && (acc == nullptr || b == 0))
+    v = mul_mod(pmod[t], ct[((size_t)b * l + t) * kN + src], M);
+  if (acc) v = add_mod(v, acc[((size_t)b * lk + t) * kN + src], M.q);
+  out[((size_t)b * lk + t) * kN + k] = v;
+}
+
 // ---------------------------------------------------------------------
 // host orchestration
 // ---------------------------------------------------------------------
@@ -421,6 +441,93 @@ int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
                     acc, conv, s);
     if (rc) return rc;
   }
+  return B2F_OK;
+}
+
+size_t b2f_rotate_hoisted_ext_workspace(const b2f_context *ctx, int l) {
+  if (!ctx || l < 1 || l > ctx->L) return 0;
+  return rnd((size_t)2 * (l + ctx->K) * kN);
+}
+
+int b2f_rotate_hoisted_ext(b2f_context *ctx, const uint64_t *ct, int l,
+                           const uint64_t *ext, int count, const uint64_t *galois,
+                           const uint64_t *const *keys, uint64_t *out, void *ws,
+                           size_t ws_bytes, void *stream) {
+  int rc = check_level(ctx, l, "b2f_rotate_hoisted_ext");
+  if (rc) return rc;
+  B2F_CHECK_ARG(ct && out && count >= 0 && (count == 0 || galois),
+                "b2f_rotate_hoisted_ext: null argument");
+  bool need_ext = false;
+  for (int r = 0; r < count; ++r) {
+    B2F_CHECK_ARG(valid_galois(galois[r]),
+                  "b2f_rotate_hoisted_ext: bad galois element %llu",
+                  (unsigned long long)galois[r]);
+    if (galois[r] != 1) {
+      B2F_CHECK_ARG(keys && keys[r], "b2f_rotate_hoisted_ext: key %d is null", r);
+      need_ext = true;
+    }
+  }
+  B2F_CHECK_ARG(!need_ext || ext, "b2f_rotate_hoisted_ext: ModUp digits are null");
+  cudaStream_t s = (cudaStream_t)stream;
+  Scratch sc{ctx, s};
+  if ((rc = sc.init(ws, ws_bytes, b2f_rotate_hoisted_ext_workspace(ctx, l)))) return rc;
+  const int K = ctx->K, lk = l + K;
+  uint64_t *acc = sc.take((size_t)2 * lk * kN);
+  const LevelTables &T = ctx->levels[l];
+  for (int r = 0; r < count; ++r) {
+    uint64_t *o = out + (size_t)r * 2 * lk * kN;
+    const uint64_t *a = nullptr;
+    if (galois[r] != 1) {
+      key_inner_product_kernel<<<dim3(kN / TPB, 1, lk), TPB, 0, s>>>(
+          ct + (size_t)l * kN, 0, ext, keys[r], acc, ctx->d_mod, l, K, ctx->L,
+          ctx->alpha, T.beta);
+      B2F_LAUNCHED("key_inner_product_kernel");
+      a = acc;
+    }
+    ext_combine_kernel<<<dim3(kN / TPB, lk, 2), TPB, 0, s>>>(
+        a, ct, o, ctx->d_mod, ctx->d_pmod, l, K, ctx->L, (uint32_t)galois[r]);
+    B2F_LAUNCHED("ext_combine_kernel");
+  }
+  return B2F_OK;
+}
+
+size_t b2f_moddown_ext_workspace(const b2f_context *ctx, int num_cts, int l) {
+  if (!ctx || l < 1 || l > ctx->L || num_cts < 0) return 0;
+  return moddown_bytes(ctx, num_cts, l);
+}
+
+int b2f_moddown_ext(b2f_context *ctx, const uint64_t *in, int num_cts, int l,
+                    uint64_t *out, void *ws, size_t ws_bytes, void *stream) {
+  int rc = check_level(ctx, l, "b2f_moddown_ext");
+  if (rc) return rc;
+  B2F_CHECK_ARG(in && out && num_cts >= 0, "b2f_moddown_ext: null argument");
+  if (!num_cts) return B2F_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  Scratch sc{ctx, s};
+  if ((rc = sc.init(ws, ws_bytes, moddown_bytes(ctx, num_cts, l)))) return rc;
+  const int K = ctx->K, lk = l + K;
+  uint64_t *pcoef = sc.take((size_t)num_cts * 2 * lk * kN);  // P limbs only
+  uint64_t *conv = sc.take((size_t)num_cts * 2 * l * kN);
+  std::vector<LimbJob> pj;
+  for (int b = 0; b < 2; ++b)
+    for (int k = 0; k < K; ++k) {
+      uint32_t off = (uint32_t)(b * lk + l + k);
+      pj.push_back(LimbJob{off, off, (uint16_t)(ctx->L + k), (uint16_t)k, 0});
+    }
+  const LimbJob *d = job_table(ctx, {3, l}, pj);
+  if (!d) return B2F_ERR_NOMEM;
+  const long long as = 2LL * lk * kN;
+  if ((rc = launch_ntt(ctx, in, as, pcoef, as, d, 2 * K, num_cts, 1,
+                       ctx->d_moddown_scale, s)))
+    return rc;
+  moddown_conv_kernel<<<dim3(kN / TPB, 2, num_cts), TPB, 0, s>>>(
+      pcoef, conv, ctx->d_moddown_conv, ctx->d_primes, l, K);
+  B2F_LAUNCHED("moddown_conv_kernel");
+  if ((rc = ntt_polys(ctx, conv, 2 * num_cts, l, 0, 0, s))) return rc;
+  moddown_combine_kernel<<<dim3(kN / TPB, l, num_cts), TPB, 0, s>>>(
+      in, conv, nullptr, nullptr, 0, out, 2LL * l * kN, ctx->d_moddown_pinv,
+      ctx->d_primes, l, K, 1u);
+  B2F_LAUNCHED("moddown_combine_kernel");
   return B2F_OK;
 }
 

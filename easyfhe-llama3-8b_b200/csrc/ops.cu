@@ -142,6 +142,34 @@ __global__ void __launch_bounds__(TPB) mac_kernel(
     }
 }
 
+// out[g] = sum over i in group g of ct[i] * pt[i]; cts [count][2][limbs],
+// pts rows of pt_stride limbs (the first `limbs` used).  grid (N/TPB, limbs,
+// groups); limb t is prime t < q_limbs ? t : L + t - q_limbs.
+__global__ void __launch_bounds__(TPB) pairwise_mac_kernel(
+    const uint64_t *__restrict__ cts, const uint64_t *__restrict__ pts,
+    uint64_t *__restrict__ out, int per_group, int limbs, int q_limbs,
+    int pt_stride, int L, const Mod *__restrict__ mods) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int t = blockIdx.y, g = blockIdx.z;
+  const Mod M = mods[t < q_limbs ? t : L + (t - q_limbs)];
+  const size_t ct_words = 2 * (size_t)limbs * kN;
+  U128 a0 = {0, 0}, a1 = {0, 0};
+  for (int j = 0; j < per_group; ++j) {
+    const size_t i = (size_t)g * per_group + j;
+    const uint64_t w = __ldg(pts + (i * pt_stride + t) * kN + n);
+    const uint64_t *c = cts + i * ct_words + (size_t)t * kN + n;
+    mac128(a0, c[0], w);
+    mac128(a1, c[(size_t)limbs * kN], w);
+    if ((j & 31) == 31) {
+      a0 = U128{reduce128(a0.hi, a0.lo, M), 0};
+      a1 = U128{reduce128(a1.hi, a1.lo, M), 0};
+    }
+  }
+  uint64_t *o = out + (size_t)g * ct_words + (size_t)t * kN + n;
+  o[0] = reduce128(a0.hi, a0.lo, M);
+  o[(size_t)limbs * kN] = reduce128(a1.hi, a1.lo, M);
+}
+
 int launch_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
                const uint64_t *pts, int giant_count, int l, uint64_t *out,
                int cts, cudaStream_t s) {
@@ -285,6 +313,23 @@ int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
   if (!num_cts) return B2F_OK;
   return launch_mac(ctx, babies, baby_count, pts, giant_count, l, out, num_cts,
                     (cudaStream_t)stream);
+}
+
+int b2f_pairwise_mac(b2f_context *ctx, const uint64_t *cts, const uint64_t *pts,
+                     int count, int groups, int q_limbs, int p_limbs,
+                     int pt_limb_stride, uint64_t *out, void *stream) {
+  B2F_CHECK_ARG(ctx && cts && pts && out, "b2f_pairwise_mac: null argument");
+  B2F_CHECK_ARG(count >= 1 && groups >= 1 && count % groups == 0,
+                "b2f_pairwise_mac: %d pairs do not split into %d groups", count, groups);
+  B2F_CHECK_ARG(q_limbs >= 1 && q_limbs <= ctx->L && p_limbs >= 0 && p_limbs <= ctx->K,
+                "b2f_pairwise_mac: bad limbs q=%d p=%d", q_limbs, p_limbs);
+  const int limbs = q_limbs + p_limbs;
+  B2F_CHECK_ARG(pt_limb_stride >= limbs, "b2f_pairwise_mac: plaintext rows of %d limbs "
+                "are shorter than %d", pt_limb_stride, limbs);
+  pairwise_mac_kernel<<<dim3(kN / TPB, limbs, groups), TPB, 0, (cudaStream_t)stream>>>(
+      cts, pts, out, count / groups, limbs, q_limbs, pt_limb_stride, ctx->L, ctx->d_mod);
+  B2F_LAUNCHED("pairwise_mac_kernel");
+  return B2F_OK;
 }
 
 size_t b2f_bsgs_mac_workspace(const b2f_context *ctx, int l) {

@@ -51,6 +51,12 @@ _SIGS = {
     "b2f_rotate_hoisted_workspace": (_size, [_vp, _int]),
     "b2f_rotate_hoisted": (_int, [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _size,
                                   _vp]),
+    "b2f_rotate_hoisted_ext_workspace": (_size, [_vp, _int]),
+    "b2f_rotate_hoisted_ext": (_int, [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp,
+                                      _size, _vp]),
+    "b2f_moddown_ext_workspace": (_size, [_vp, _int, _int]),
+    "b2f_moddown_ext": (_int, [_vp, _vp, _int, _int, _vp, _vp, _size, _vp]),
+    "b2f_pairwise_mac": (_int, [_vp, _vp, _vp, _int, _int, _int, _int, _int, _vp, _vp]),
     "b2f_rescale_workspace": (_size, [_vp, _int, _int]),
     "b2f_rescale": (_int, [_vp, _vp, _vp, _int, _int, _vp, _size, _vp]),
     "b2f_rescale_noalloc": (_int, [_vp, _vp, _vp, _int, _int, _vp]),

@@ -240,6 +240,33 @@ class NativeContext:
              _ptr(out), _ptr(ws), ws.numel(), _stream())
         return out
 
+    def rotate_hoisted_ext(self, ct: torch.Tensor, l: int, ext: torch.Tensor | None, galois,
+                           keys) -> torch.Tensor:
+        count = len(galois)
+        out = self.empty(count, 2, l + self.K)
+        g = (ctypes.c_uint64 * max(count, 1))(*[int(v) for v in galois])
+        kp = (ctypes.c_void_p * max(count, 1))(*[_ptr(k) if k is not None else None
+                                                  for k in keys])
+        ws = self.workspace(lib.b2f_rotate_hoisted_ext_workspace(self.handle, l))
+        call("b2f_rotate_hoisted_ext", self.handle, _ptr(ct), l,
+             _ptr(ext) if ext is not None else None, count, g, kp, _ptr(out), _ptr(ws),
+             ws.numel(), _stream())
+        return out
+
+    def moddown_ext(self, data: torch.Tensor, num_cts: int, l: int) -> torch.Tensor:
+        out = self.empty(num_cts, 2, l)
+        ws = self.workspace(lib.b2f_moddown_ext_workspace(self.handle, num_cts, l))
+        call("b2f_moddown_ext", self.handle, _ptr(data), num_cts, l, _ptr(out), _ptr(ws),
+             ws.numel(), _stream())
+        return out
+
+    def pairwise_mac(self, cts: torch.Tensor, pts: torch.Tensor, count: int, groups: int,
+                     q_limbs: int, p_limbs: int, pt_limb_stride: int) -> torch.Tensor:
+        out = self.empty(groups, 2, q_limbs + p_limbs)
+        call("b2f_pairwise_mac", self.handle, _ptr(cts), _ptr(pts), count, groups, q_limbs,
+             p_limbs, pt_limb_stride, _ptr(out), _stream())
+        return out
+
     def rescale(self, data: torch.Tensor, num_polys: int, l: int) -> torch.Tensor:
         out = self.empty(num_polys, l - 1)
         ws = self.workspace(lib.b2f_rescale_workspace(self.handle, num_polys, l))

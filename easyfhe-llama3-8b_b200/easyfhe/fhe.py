@@ -174,6 +174,22 @@ class Plaintext:
         self.is_ext = bool(is_ext)
         self.rows = int(data.shape[0]) if data.dim() == 3 else 1
 
+    @property
+    def batch_size(self) -> int:
+        return self.rows
+
+    @property
+    def cv(self) -> list[torch.Tensor]:
+        return [self.data if self.data.dim() == 3 else self.data.unsqueeze(0)]
+
+    def cipher_like(self, cv, slots: int | None = None,
+                    batch_size: int | None = None) -> "Plaintext":
+        """A plaintext batch over cv[0] (rows sliced by the caller,
+        llama3fhe/operators/attention/input.py:1108-1115)."""
+
+        return Plaintext(cv[0], self.state, self.slots if slots is None else slots,
+                         self.is_ext)
+
     def q_part(self, limbs: int) -> torch.Tensor:
         """[rows, limbs, N] view of the Q limbs (contiguous when not ext)."""
 
@@ -759,22 +775,101 @@ class ConstantBundle:
 
 
 # ---------------------------------------------------------------------------
-# not yet on the native path (attention batch ops): fail loudly
+# extended-basis batches (double hoisting): attention input layout
 # ---------------------------------------------------------------------------
 
 
-def _pending(name: str, site: str):
-    def fn(*args, **kwargs):
-        raise NotImplementedError(
-            f"fhe.{name} ({site}) is not implemented on libb200fhe yet")
+def fast_rotate(ct: Ciphertext, offsets, context, output_ext: bool = False) -> Ciphertext:
+    """Hoisted rotations of ct by every offset as one batch [count, 2, limbs, N].
+    output_ext=True leaves them in the extended basis Q_l u P (P times the
+    rotation, before ModDown) for grouped_pairwise_mac + moddown_from_ext
+    (llama3fhe/operators/attention/input.py:792-797, 1143-1148)."""
 
-    fn.__name__ = name
-    return fn
+    ctx = _ctx_of(context)
+    offsets = tuple(int(v) for v in offsets)
+    if not offsets:
+        raise ValueError("fast_rotate needs at least one offset")
+    if not output_ext:
+        block = tuple(prepare_hoisted_baby_rotations(ct, offsets, ctx))[0]
+        return block
+    l = _limbs(ct)
+    gal, keys = [], []
+    for off in offsets:
+        g = galois_element(off, ctx.logN)
+        gal.append(g)
+        keys.append(None if g == 1 else ctx.rotation_key(off)[1])
+    ext = ctx.native.modup(ct.data, l) if any(g != 1 for g in gal) else None
+    out = ctx.native.rotate_hoisted_ext(ct.data, l, ext, gal, keys)
+    return Ciphertext(out, ct.state, ct.slots, ctx, is_ext=True)
 
 
-fast_rotate = _pending("fast_rotate", "llama3fhe/operators/attention/input.py:792-797")
-pack_cipher_batch = _pending("pack_cipher_batch", "llama3fhe/operators/attention/input.py:810")
-unpack_cipher_batch = _pending("unpack_cipher_batch", "llama3fhe/operators/attention/input.py:798")
-grouped_pairwise_mac = _pending("grouped_pairwise_mac",
-                                "llama3fhe/operators/attention/input.py:814-819")
-moddown_from_ext = _pending("moddown_from_ext", "llama3fhe/operators/attention/input.py:821")
+def unpack_cipher_batch(batch: Ciphertext) -> tuple[Ciphertext, ...]:
+    """The items of a batch as borrowed views (llama3fhe/operators/attention/input.py:798)."""
+
+    if batch.data.dim() == 3:
+        return (batch,)
+    return tuple(Ciphertext(batch.data[i], batch.state, batch.slots, batch.context,
+                            batch.is_ext) for i in range(batch.batch_size))
+
+
+def pack_cipher_batch(items: Iterable[Ciphertext]) -> Ciphertext:
+    """One contiguous batch of same-shape ciphertexts
+    (llama3fhe/operators/attention/input.py:810-813, 1142)."""
+
+    items = tuple(items)
+    if not items:
+        raise ValueError("pack_cipher_batch needs at least one ciphertext")
+    first = items[0]
+    for it in items:
+        if it.data.shape[-2:] != first.data.shape[-2:] or it.is_ext != first.is_ext:
+            raise ValueError("pack_cipher_batch: items differ in limbs or basis")
+    data = torch.stack([it.data if it.data.dim() == 3 else it.data.squeeze(0)
+                        for it in items]).contiguous()
+    return Ciphertext(data, first.state, first.slots, first.context, first.is_ext)
+
+
+def grouped_pairwise_mac(batch: Ciphertext, plaintexts: Plaintext, groups: int,
+                         context) -> Ciphertext:
+    """sum_i batch[i] * plaintexts[i] in `groups` consecutive groups; extended
+    batches multiply extended plaintexts over Q_l u P and stay extended
+    (llama3fhe/operators/attention/input.py:814-819, 1274-1279)."""
+
+    ctx = _ctx_of(context)
+    groups = int(groups)
+    count = batch.batch_size
+    data = batch.data if batch.data.dim() == 4 else batch.data.unsqueeze(0)
+    if plaintexts.rows < count:
+        raise ValueError(f"{plaintexts.rows} plaintext rows for {count} ciphertexts")
+    l = _limbs(batch)
+    pts = plaintexts.cv[0]
+    pt_limbs = int(pts.shape[1])
+    if batch.is_ext:
+        if not plaintexts.is_ext:
+            raise ValueError("an extended batch needs extended plaintexts")
+        q_limbs, p_limbs = l, ctx.K
+        if pt_limbs != l + ctx.K or int(plaintexts.state.cur_limbs) != l:
+            raise ValueError("extended plaintexts are not at the batch's level")
+    else:
+        q_limbs, p_limbs = l, 0
+        if int(plaintexts.state.cur_limbs) < l:
+            raise ValueError("plaintexts are below the batch's level")
+    out = ctx.native.pairwise_mac(data, pts, count, groups, q_limbs, p_limbs, pt_limbs)
+    state = batch.state.replace(
+        scale_degree=int(batch.state.scale_degree) + int(plaintexts.state.scale_degree),
+        scaling_factor=float(batch.state.scaling_factor) * float(plaintexts.state.scaling_factor))
+    res = out[0] if groups == 1 else out
+    return Ciphertext(res, state, batch.slots, ctx, batch.is_ext)
+
+
+def moddown_from_ext(ct: Ciphertext, context) -> Ciphertext:
+    """ModDown of an extended (batch of) ciphertext(s) to Q_l
+    (llama3fhe/operators/attention/input.py:821-826)."""
+
+    ctx = _ctx_of(context)
+    if not ct.is_ext:
+        return ct.deep_copy()
+    l = _limbs(ct)
+    data = ct.data if ct.data.dim() == 4 else ct.data.unsqueeze(0)
+    out = ctx.native.moddown_ext(data, data.shape[0], l)
+    res = out[0] if ct.data.dim() == 3 else out
+    return Ciphertext(res, ct.state, ct.slots, ctx, False)

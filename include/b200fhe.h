@@ -113,6 +113,22 @@ int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
                        const uint64_t *const *keys, uint64_t *out, void *ws,
                        size_t ws_bytes, void *stream);
 
+/* Hoisted rotations left in the extended basis (double hoisting): out[r]
+ * (2 polys x (l+K) limbs, Q limbs then P limbs) = (pi_g(P c0 + acc0),
+ * pi_g(acc1)), P times the rotation before ModDown; galois 1 gives (P c0,
+ * P c1) and needs no key.  fhe.fast_rotate(ct, offsets, ctx, output_ext=True)
+ * (llama3fhe/operators/attention/input.py:792-797, 1143-1148). */
+size_t b2f_rotate_hoisted_ext_workspace(const b2f_context *ctx, int l);
+int b2f_rotate_hoisted_ext(b2f_context *ctx, const uint64_t *ct, int l,
+                           const uint64_t *ext, int count, const uint64_t *galois,
+                           const uint64_t *const *keys, uint64_t *out, void *ws,
+                           size_t ws_bytes, void *stream);
+/* ModDown of num_cts extended ciphertexts (2 x (l+K) limbs) to l limbs:
+ * fhe.moddown_from_ext (llama3fhe/operators/attention/input.py:821-826). */
+size_t b2f_moddown_ext_workspace(const b2f_context *ctx, int num_cts, int l);
+int b2f_moddown_ext(b2f_context *ctx, const uint64_t *in, int num_cts, int l,
+                    uint64_t *out, void *ws, size_t ws_bytes, void *stream);
+
 /* ---- level management ----
  * fhe.rescale (llama3fhe/operators/linear/operator.py:386-388): divide by the
  * last prime with a centred lift; in (num_polys x l limbs) -> out
@@ -167,6 +183,14 @@ int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
                  const uint64_t *pts, int giant_count, int l,
                  uint64_t giant_galois, const uint64_t *giant_key,
                  uint64_t *out, void *ws, size_t ws_bytes, void *stream);
+/* out[g] = sum_{i in group g} ct[i] * pt[i] over q_limbs Q limbs and p_limbs
+ * P limbs (extended ciphertexts and plaintexts), count pairs split into
+ * `groups` consecutive groups; plaintext rows are pt_limb_stride limbs apart.
+ * fhe.grouped_pairwise_mac(batch, plaintexts, groups, ctx)
+ * (llama3fhe/operators/attention/input.py:814-819, 1274-1279). */
+int b2f_pairwise_mac(b2f_context *ctx, const uint64_t *cts, const uint64_t *pts,
+                     int count, int groups, int q_limbs, int p_limbs,
+                     int pt_limb_stride, uint64_t *out, void *stream);
 /* Only the MAC: out[g] = sum_b pt[g*B+b] * babies[b] for g < giant_count
  * (num_cts independent baby sets, each with its own output block). */
 int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,

@@ -603,6 +603,61 @@ void orc_rotate_hoisted(const orc_ctx *c, const uint64_t *ct, int l,
   free(ext);
 }
 
+/* Hoisted rotations left in the extended basis Q_l u P (double hoisting,
+ * Bossuat et al. 2021): out[r] = (pi_g(P c0 + acc0), pi_g(acc1)) over l+K
+ * limbs, i.e. P times the rotated ciphertext before ModDown.  A rotation with
+ * galois element 1 is (P c0, P c1) with no key switch. */
+void orc_rotate_hoisted_ext(const orc_ctx *c, const uint64_t *ct, int l,
+                            int count, const uint64_t *galois,
+                            const uint64_t *const *keys, uint64_t *out) {
+  const uint64_t n = c->n;
+  const int lk = l + c->K;
+  int beta;
+  uint64_t *ext = modup(c, ct + (uint64_t)l * n, l, &beta);
+  uint64_t *acc0 = (uint64_t *)malloc(8 * n * lk), *acc1 = (uint64_t *)malloc(8 * n * lk);
+  int32_t *perm = (int32_t *)malloc(4 * n);
+  for (int r = 0; r < count; r++) {
+    uint64_t *o0 = out + (uint64_t)r * 2 * lk * n, *o1 = o0 + (uint64_t)lk * n;
+    if (galois[r] == 1) {
+      for (int t = 0; t < lk; t++) {
+        uint64_t q = c->primes[ext_prime(c, l, t)];
+        uint64_t pm = 1;
+        for (int k = 0; k < c->K; k++) pm = mulmod(pm, c->primes[c->L + k] % q, q);
+        for (uint64_t x = 0; x < n; x++) {
+          o0[t * n + x] = t < l ? mulmod(pm, ct[t * n + x], q) : 0;
+          o1[t * n + x] = t < l ? mulmod(pm, ct[((uint64_t)l + t) * n + x], q) : 0;
+        }
+      }
+      continue;
+    }
+    key_inner_product(c, ext, l, beta, keys[r], acc0, acc1);
+    for (int t = 0; t < l; t++) {
+      uint64_t q = c->primes[t];
+      uint64_t pm = 1;
+      for (int k = 0; k < c->K; k++) pm = mulmod(pm, c->primes[c->L + k] % q, q);
+      for (uint64_t x = 0; x < n; x++)
+        acc0[t * n + x] = addmod(acc0[t * n + x], mulmod(pm, ct[t * n + x], q), q);
+    }
+    orc_automorphism_perm(c->log_n, galois[r], perm);
+    for (int t = 0; t < lk; t++) {
+      apply_perm(acc0 + (uint64_t)t * n, o0 + (uint64_t)t * n, perm, n);
+      apply_perm(acc1 + (uint64_t)t * n, o1 + (uint64_t)t * n, perm, n);
+    }
+  }
+  free(perm);
+  free(acc0);
+  free(acc1);
+  free(ext);
+}
+
+/* ModDown of num_polys extended polys (l+K limbs each) to l limbs. */
+void orc_moddown(const orc_ctx *c, const uint64_t *in, int num_polys, int l,
+                 uint64_t *out) {
+  const uint64_t n = c->n;
+  for (int p = 0; p < num_polys; p++)
+    moddown(c, in + (uint64_t)p * (l + c->K) * n, l, out + (uint64_t)p * l * n);
+}
+
 /* ------------------------------------------------------------------ */
 /* rescale, multiply by i                                               */
 /* ------------------------------------------------------------------ */

@@ -84,6 +84,11 @@ void orc_rotate(const orc_ctx *ctx, const uint64_t *ct, int l, uint64_t g,
 void orc_rotate_hoisted(const orc_ctx *ctx, const uint64_t *ct, int l,
                         int count, const uint64_t *galois,
                         const uint64_t *const *keys, uint64_t *out);
+void orc_rotate_hoisted_ext(const orc_ctx *ctx, const uint64_t *ct, int l,
+                            int count, const uint64_t *galois,
+                            const uint64_t *const *keys, uint64_t *out);
+void orc_moddown(const orc_ctx *ctx, const uint64_t *in, int num_polys, int l,
+                 uint64_t *out);
 void orc_rescale(const orc_ctx *ctx, const uint64_t *in, int num_polys, int l,
                  uint64_t *out);
 void orc_mul_i(const orc_ctx *ctx, uint64_t *data, int num_polys, int l,

@@ -67,6 +67,10 @@ def lib():
                                  _u64p]
         L.orc_rotate_hoisted.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int,
                                          _u64p, ctypes.POINTER(_u64p), _u64p]
+        L.orc_rotate_hoisted_ext.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int,
+                                             ctypes.c_int, _u64p, ctypes.POINTER(_u64p),
+                                             _u64p]
+        L.orc_moddown.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p]
         L.orc_rescale.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p]
         L.orc_mul_i.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.orc_sample_secret.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int, _i64p]
@@ -205,6 +209,20 @@ class Oracle:
         keys = [_u64(k) for k in keys]
         arr = (_u64p * count)(*[_p(k) for k in keys])
         lib().orc_rotate_hoisted(self._h, _p(_u64(ct)), l, count, _p(g), arr, _p(out))
+        return out
+
+    def rotate_hoisted_ext(self, ct: np.ndarray, l: int, galois, keys) -> np.ndarray:
+        count = len(galois)
+        out = np.zeros((count, 2, l + self.K, self.n), dtype=np.uint64)
+        g = _u64(galois)
+        keys = [_u64(k) if k is not None else np.zeros(1, dtype=np.uint64) for k in keys]
+        arr = (_u64p * count)(*[_p(k) for k in keys])
+        lib().orc_rotate_hoisted_ext(self._h, _p(_u64(ct)), l, count, _p(g), arr, _p(out))
+        return out
+
+    def moddown(self, data: np.ndarray, num_polys: int, l: int) -> np.ndarray:
+        out = np.zeros((num_polys, l, self.n), dtype=np.uint64)
+        lib().orc_moddown(self._h, _p(_u64(data)), num_polys, l, _p(out))
         return out
 
     def rescale(self, data: np.ndarray, num_polys: int, l: int) -> np.ndarray:
