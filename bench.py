@@ -208,12 +208,10 @@ def main() -> None:
         if world > 1:
             dist.barrier(device_ids=[local])
 
+    from easyfhe import shard
+
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(x, dev)
 
     launches_per_rotate = 8  # iNTT, ModUp conv, NTT, inner product, iNTT(P), conv, NTT, combine
 
