@@ -40,6 +40,25 @@ __global__ void __launch_bounds__(TPB) rescale_combine_kernel(
   out[((size_t)p * (l - 1) + i) * kN + n] = shoup(sub_mod(a, b, q), w.x, w.y, q);
 }
 
+// ModRaise step 2: limb 0 of every poly holds coefficients mod q_0; write
+// their centred lift modulo q_t into limbs t = 1 .. l_out-1.
+// grid (N/TPB, l_out-1, polys)
+__global__ void __launch_bounds__(TPB) modraise_lift_kernel(
+    uint64_t *__restrict__ data, const uint64_t *__restrict__ primes, int l_out) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int t = blockIdx.y + 1, p = blockIdx.z;
+  const uint64_t q0 = primes[0], qt = primes[t];
+  const uint64_t v = data[(size_t)p * l_out * kN + n];
+  uint64_t r;
+  if (v > (q0 - 1) / 2) {
+    const uint64_t m = (q0 - v) % qt;
+    r = m ? qt - m : 0;
+  } else {
+    r = v % qt;
+  }
+  data[((size_t)p * l_out + t) * kN + n] = r;
+}
+
 // grid (N/TPB, l, polys)
 __global__ void __launch_bounds__(TPB) elementwise_kernel(
     int op, const uint64_t *__restrict__ a, const uint64_t *__restrict__ b,
@@ -238,6 +257,27 @@ int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
   }
   if (owned) cudaFreeAsync(owned, s);
   return rc;
+}
+
+int b2f_modraise(b2f_context *ctx, const uint64_t *in, int num_polys, int l_out,
+                 uint64_t *out, void *stream) {
+  B2F_CHECK_ARG(ctx && in && out && num_polys >= 0, "b2f_modraise: null argument");
+  B2F_CHECK_ARG(l_out >= 1 && l_out <= ctx->L, "b2f_modraise: bad target limbs %d", l_out);
+  B2F_CHECK_ARG(in != out, "b2f_modraise: in-place ModRaise is not supported");
+  if (!num_polys) return B2F_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  std::vector<LimbJob> j = {LimbJob{0u, 0u, 0, 0, 0}};
+  const LimbJob *d = job_table(ctx, {6}, j);
+  if (!d) return B2F_ERR_NOMEM;
+  int rc = launch_ntt(ctx, in, kN, out, (long long)l_out * kN, d, 1, num_polys, 1,
+                      nullptr, s);
+  if (rc) return rc;
+  if (l_out > 1) {
+    modraise_lift_kernel<<<dim3(kN / TPB, l_out - 1, num_polys), TPB, 0, s>>>(
+        out, ctx->d_primes, l_out);
+    B2F_LAUNCHED("modraise_lift_kernel");
+  }
+  return ntt_polys(ctx, out, num_polys, l_out, 0, 0, s);
 }
 
 int b2f_drop_limbs(b2f_context *ctx, const uint64_t *in, uint64_t *out,

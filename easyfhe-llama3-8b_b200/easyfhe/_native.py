@@ -60,6 +60,7 @@ _SIGS = {
     "b2f_rescale_workspace": (_size, [_vp, _int, _int]),
     "b2f_rescale": (_int, [_vp, _vp, _vp, _int, _int, _vp, _size, _vp]),
     "b2f_rescale_noalloc": (_int, [_vp, _vp, _vp, _int, _int, _vp]),
+    "b2f_modraise": (_int, [_vp, _vp, _int, _int, _vp, _vp]),
     "b2f_drop_limbs": (_int, [_vp, _vp, _vp, _int, _int, _int, _vp]),
     "b2f_elementwise": (_int, [_vp, _int, _vp, _vp, _vp, _int, _int, _int, _vp]),
     "b2f_mul_i": (_int, [_vp, _vp, _vp, _int, _int, _int, _vp]),

@@ -274,6 +274,11 @@ class NativeContext:
              ws.numel(), _stream())
         return out
 
+    def modraise(self, data: torch.Tensor, num_polys: int, l_out: int) -> torch.Tensor:
+        out = self.empty(num_polys, l_out)
+        call("b2f_modraise", self.handle, _ptr(data), num_polys, l_out, _ptr(out), _stream())
+        return out
+
     def drop_limbs(self, data: torch.Tensor, num_polys: int, l_in: int,
                    l_out: int) -> torch.Tensor:
         out = self.empty(num_polys, l_out)

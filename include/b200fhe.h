@@ -147,6 +147,12 @@ int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
  * calls that overlap on the GPU (other streams, other threads) race. */
 int b2f_rescale_noalloc(b2f_context *ctx, const uint64_t *in, uint64_t *out,
                         int num_polys, int l, void *stream);
+/* ModRaise of bootstrapping: num_polys polys at one limb (q_0, NTT form)
+ * -> l_out limbs: the coefficients' centred lift modulo every prime, NTT
+ * form (bs.bootstrap, mode "modraise_first": llama3fhe/model.py:45,
+ * llama3fhe/operators/nonlinear/bootstrap.py:370). */
+int b2f_modraise(b2f_context *ctx, const uint64_t *in, int num_polys, int l_out,
+                 uint64_t *out, void *stream);
 /* fhe.align_to to fewer limbs (llama3fhe/operators/primitives.py:100-155):
  * keep limbs 0..l_out-1 of each poly. */
 int b2f_drop_limbs(b2f_context *ctx, const uint64_t *in, uint64_t *out,

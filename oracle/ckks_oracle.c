@@ -690,6 +690,28 @@ void orc_rescale(const orc_ctx *c, const uint64_t *in, int num_polys, int l,
   }
 }
 
+/* ModRaise: polys at one limb (q_0, NTT form) -> l_out limbs, each limb the
+ * centred lift of the q_0 coefficients (NTT form). */
+void orc_modraise(const orc_ctx *c, const uint64_t *in, int num_polys, int l_out,
+                  uint64_t *out) {
+  const uint64_t n = c->n, q0 = c->primes[0];
+  uint64_t *coef = (uint64_t *)malloc(8 * n);
+  for (int p = 0; p < num_polys; p++) {
+    memcpy(coef, in + (uint64_t)p * n, 8 * n);
+    orc_ntt_inverse(c, coef, 0);
+    uint64_t *o = out + (uint64_t)p * l_out * n;
+    for (int t = 0; t < l_out; t++) {
+      uint64_t qt = c->primes[t];
+      for (uint64_t x = 0; x < n; x++) {
+        uint64_t v = coef[x];
+        o[(uint64_t)t * n + x] = v > (q0 - 1) / 2 ? (qt - (q0 - v) % qt) % qt : v % qt;
+      }
+    }
+    orc_poly_ntt(c, o, 1, l_out, 0, 0);
+  }
+  free(coef);
+}
+
 /* times X^(N/2): evaluation at psi^e is multiplied by psi^(e*N/2) */
 void orc_mul_i(const orc_ctx *c, uint64_t *data, int num_polys, int l,
                int negative) {

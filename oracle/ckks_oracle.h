@@ -91,6 +91,8 @@ void orc_moddown(const orc_ctx *ctx, const uint64_t *in, int num_polys, int l,
                  uint64_t *out);
 void orc_rescale(const orc_ctx *ctx, const uint64_t *in, int num_polys, int l,
                  uint64_t *out);
+void orc_modraise(const orc_ctx *ctx, const uint64_t *in, int num_polys,
+                  int l_out, uint64_t *out);
 void orc_mul_i(const orc_ctx *ctx, uint64_t *data, int num_polys, int l,
                int negative);
 

@@ -72,6 +72,7 @@ def lib():
                                              _u64p]
         L.orc_moddown.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p]
         L.orc_rescale.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p]
+        L.orc_modraise.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p]
         L.orc_mul_i.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.orc_sample_secret.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int, _i64p]
         L.orc_secret_to_ntt.argtypes = [ctypes.c_void_p, _i64p, _u64p]
@@ -228,6 +229,11 @@ class Oracle:
     def rescale(self, data: np.ndarray, num_polys: int, l: int) -> np.ndarray:
         out = np.zeros((num_polys, l - 1, self.n), dtype=np.uint64)
         lib().orc_rescale(self._h, _p(_u64(data)), num_polys, l, _p(out))
+        return out
+
+    def modraise(self, data: np.ndarray, num_polys: int, l_out: int) -> np.ndarray:
+        out = np.zeros((num_polys, l_out, self.n), dtype=np.uint64)
+        lib().orc_modraise(self._h, _p(_u64(data)), num_polys, l_out, _p(out))
         return out
 
     def mul_i(self, data: np.ndarray, num_polys: int, l: int, negative=False) -> np.ndarray:
