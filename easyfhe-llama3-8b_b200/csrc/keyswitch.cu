@@ -21,6 +21,19 @@ namespace {
 
 constexpr int TPB = 256;
 
+// Per-item key pointers and galois elements of one launch, passed by value.
+// With shared != 0 every item uses entry 0 (a batch sharing one key); hoisted
+// rotations of one ciphertext use one entry per rotation.
+constexpr int kMaxItems = 64;
+struct ItemKeys {
+  const uint64_t *key[kMaxItems];
+  uint32_t g[kMaxItems];
+  int16_t pos[kMaxItems];  // output slot of item i (per-item mode only)
+  int shared;
+  __host__ __device__ int at(int i) const { return shared ? 0 : i; }
+  __host__ __device__ int out(int i) const { return shared ? i : pos[i]; }
+};
+
 __device__ __forceinline__ uint32_t brv16(uint32_t x) { return __brev(x) >> 16; }
 
 // source evaluation index of output k under X -> X^g (g odd, < 2N)
@@ -64,11 +77,13 @@ __global__ void __launch_bounds__(TPB) modup_conv_kernel(
   }
 }
 
-// Step 3: key inner product.  grid (N/TPB, cts, l+K): the slowest grid axis
-// is the target limb so every key limb is reused across the batch in L2.
+// Step 3: key inner product.  grid (N/TPB, items, l+K): the slowest grid
+// axis is the target limb, so a key limb shared by a batch, or an ext limb
+// shared by the hoisted rotations of one ciphertext (ext_stride = 0, c1_stride
+// = 0), is reused across the items in L2.
 __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
     const uint64_t *__restrict__ c1, long long c1_stride,
-    const uint64_t *__restrict__ ext, const uint64_t *__restrict__ key,
+    const uint64_t *__restrict__ ext, long long ext_stride, const ItemKeys items,
     uint64_t *__restrict__ acc, const Mod *__restrict__ mods, int l, int K,
     int L, int alpha, int beta) {
   const int n = blockIdx.x * TPB + threadIdx.x;
@@ -76,6 +91,7 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
   const int lk = l + K, np = L + K;
   const int gp = t < l ? t : L + (t - l);
   const Mod M = mods[gp];
+  const uint64_t *__restrict__ key = items.key[items.at(ct)];
   U128 s0 = {0, 0}, s1 = {0, 0};
   for (int j = 0; j < beta; ++j) {
     const int lo = j * alpha, hi = min(lo + alpha, l);
@@ -83,7 +99,7 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
     if (t >= lo && t < hi)
       e = c1[ct * c1_stride + (size_t)t * kN + n];
     else
-      e = ext[(((size_t)ct * beta + j) * lk + t) * kN + n];
+      e = ext[ct * ext_stride + ((size_t)j * lk + t) * kN + n];
     const uint64_t *kb = key + ((size_t)j * 2 * np + gp) * kN + n;
     mac128(s0, e, __ldg(kb));
     mac128(s1, e, __ldg(kb + (size_t)np * kN));
@@ -125,16 +141,17 @@ __global__ void __launch_bounds__(TPB) moddown_conv_kernel(
 }
 
 // Step 4c + 5: out_b[i][k] = ((acc_b[i] - conv_b[i]) * P^-1 + add_b[i])[pi_g(k)]
-// grid (N/TPB, l, cts).  add_b may be null (add_stride ignored).
+// grid (N/TPB, l, items), g per item.  add_b may be null (add_stride ignored).
 __global__ void __launch_bounds__(TPB) moddown_combine_kernel(
     const uint64_t *__restrict__ acc, const uint64_t *__restrict__ conv,
     const uint64_t *__restrict__ add0, const uint64_t *__restrict__ add1,
     long long add_stride, uint64_t *__restrict__ out, long long out_stride,
     const ulonglong2 *__restrict__ pinv, const uint64_t *__restrict__ primes,
-    int l, int K, uint32_t g) {
+    int l, int K, const ItemKeys items) {
   const int k = blockIdx.x * TPB + threadIdx.x;
   const int i = blockIdx.y, ct = blockIdx.z;
   const int lk = l + K;
+  const uint32_t g = items.g[items.at(ct)];
   const uint32_t src = g == 1 ? (uint32_t)k : auto_src(k, g);
   const uint64_t q = primes[i];
   const ulonglong2 pi = pinv[i];
@@ -145,7 +162,7 @@ __global__ void __launch_bounds__(TPB) moddown_combine_kernel(
     uint64_t v = shoup(sub_mod(a, c, q), pi.x, pi.y, q);
     const uint64_t *add = b ? add1 : add0;
     if (add) v = add_mod(v, add[ct * add_stride + (size_t)i * kN + src], q);
-    out[ct * out_stride + ((size_t)b * l + i) * kN + k] = v;
+    out[items.out(ct) * out_stride + ((size_t)b * l + i) * kN + k] = v;
   }
 }
 
@@ -158,22 +175,30 @@ __global__ void __launch_bounds__(TPB) automorphism_kernel(
 
 // Extended-basis rotation output (double hoisting): for every limb t of
 // Q_l u P, out0[t][k] = (t < l ? [P]_{q_t} c0[t] : 0)[src] + acc0[t][src],
-// out1[t][k] = acc1[t][src], src = pi_g(k); with acc == null (g = 1) the
-// output is (P c0, P c1).  grid (N/TPB, l+K, 2)
+// out1[t][k] = acc1[t][src], src = pi_g(k); an item without a key (g = 1)
+// has no acc and its output is (P c0, P c1).  grid (N/TPB, l+K, 2 items);
+// item r reads acc slot slot[r] (-1: none).
+struct ExtItems {
+  uint32_t g[kMaxItems];
+  int16_t slot[kMaxItems];
+};
 __global__ void __launch_bounds__(TPB) ext_combine_kernel(
     const uint64_t *__restrict__ acc, const uint64_t *__restrict__ ct,
     uint64_t *__restrict__ out, const Mod *__restrict__ mods,
-    const uint64_t *__restrict__ pmod, int l, int K, int L, uint32_t g) {
+    const uint64_t *__restrict__ pmod, int l, int K, int L, const ExtItems items) {
   const int k = blockIdx.x * TPB + threadIdx.x;
-  const int t = blockIdx.y, b = blockIdx.z;
+  const int t = blockIdx.y, b = blockIdx.z & 1, r = blockIdx.z >> 1;
   const int lk = l + K;
+  const uint32_t g = items.g[r];
+  const int slot = items.slot[r];
   const uint32_t src = g == 1 ? (uint32_t)k : auto_src(k, g);
   const Mod M = mods[t < l ? t : L + (t - l)];
+  const uint64_t *a = slot >= 0 ? acc + (size_t)slot * 2 * lk * kN : nullptr;
   uint64_t v = 0;
-  if (t < l && (acc == nullptr || b == 0))
+  if (t < l && (a == nullptr || b == 0))
     v = mul_mod(pmod[t], ct[((size_t)b * l + t) * kN + src], M);
-  if (acc) v = add_mod(v, acc[((size_t)b * lk + t) * kN + src], M.q);
-  out[((size_t)b * lk + t) * kN + k] = v;
+  if (a) v = add_mod(v, a[((size_t)b * lk + t) * kN + src], M.q);
+  out[(((size_t)r * 2 + b) * lk + t) * kN + k] = v;
 }
 
 // ---------------------------------------------------------------------
@@ -259,16 +284,15 @@ int modup(b2f_context *ctx, const uint64_t *c1, long long c1_stride, int cts,
 
 // Inner product with one key and ModDown; writes out (cts x 2 x l limbs).
 int ip_moddown(b2f_context *ctx, const uint64_t *c1, long long c1_stride,
-               const uint64_t *ext, int cts, int l, const uint64_t *key,
-               const uint64_t *add0, const uint64_t *add1,
-               long long add_stride, uint32_t g, uint64_t *out,
-               long long out_stride, uint64_t *acc, uint64_t *conv,
-               cudaStream_t s) {
+               const uint64_t *ext, long long ext_stride, int cts, int l,
+               const ItemKeys &items, const uint64_t *add0, const uint64_t *add1,
+               long long add_stride, uint64_t *out, long long out_stride,
+               uint64_t *acc, uint64_t *conv, cudaStream_t s) {
   const LevelTables &T = ctx->levels[l];
   const int K = ctx->K, lk = l + K;
   key_inner_product_kernel<<<dim3(kN / TPB, cts, lk), TPB, 0, s>>>(
-      c1, c1_stride, ext, key, acc, ctx->d_mod, l, K, ctx->L, ctx->alpha,
-      T.beta);
+      c1, c1_stride, ext, ext_stride, items, acc, ctx->d_mod, l, K, ctx->L,
+      ctx->alpha, T.beta);
   B2F_LAUNCHED("key_inner_product_kernel");
   // iNTT of the P limbs of both polys, scaled by N^-1 Phat_k^-1
   std::vector<LimbJob> pj;
@@ -290,7 +314,7 @@ int ip_moddown(b2f_context *ctx, const uint64_t *c1, long long c1_stride,
   if (rc) return rc;
   moddown_combine_kernel<<<dim3(kN / TPB, l, cts), TPB, 0, s>>>(
       acc, conv, add0, add1, add_stride, out, out_stride, ctx->d_moddown_pinv,
-      ctx->d_primes, l, K, g);
+      ctx->d_primes, l, K, items);
   B2F_LAUNCHED("moddown_combine_kernel");
   return B2F_OK;
 }
@@ -358,9 +382,13 @@ int b2f_rotate(b2f_context *ctx, const uint64_t *ct_in, uint64_t *ct_out,
   const long long cs = 2LL * l * kN;
   if ((rc = modup(ctx, ct_in + (size_t)l * kN, cs, num_cts, l, xt, ext, s)))
     return rc;
-  return ip_moddown(ctx, ct_in + (size_t)l * kN, cs, ext, num_cts, l, key,
-                    ct_in, nullptr, cs, (uint32_t)galois, ct_out, cs, acc, conv,
-                    s);
+  ItemKeys it{};
+  it.key[0] = key;
+  it.g[0] = (uint32_t)galois;
+  it.shared = 1;
+  return ip_moddown(ctx, ct_in + (size_t)l * kN, cs, ext,
+                    (long long)beta * lk * kN, num_cts, l, it, ct_in, nullptr,
+                    cs, ct_out, cs, acc, conv, s);
 }
 
 size_t b2f_relinearize_workspace(const b2f_context *ctx, int num_cts, int l) {
@@ -387,9 +415,13 @@ int b2f_relinearize(b2f_context *ctx, const uint64_t *ct3_in, uint64_t *ct_out,
   const long long s3 = 3LL * l * kN;
   const uint64_t *d2 = ct3_in + 2 * (size_t)l * kN;
   if ((rc = modup(ctx, d2, s3, num_cts, l, xt, ext, s))) return rc;
-  return ip_moddown(ctx, d2, s3, ext, num_cts, l, relin_key, ct3_in,
-                    ct3_in + (size_t)l * kN, s3, 1u, ct_out, 2LL * l * kN, acc,
-                    conv, s);
+  ItemKeys it{};
+  it.key[0] = relin_key;
+  it.g[0] = 1u;
+  it.shared = 1;
+  return ip_moddown(ctx, d2, s3, ext, (long long)beta * lk * kN, num_cts, l, it,
+                    ct3_in, ct3_in + (size_t)l * kN, s3, ct_out, 2LL * l * kN,
+                    acc, conv, s);
 }
 
 size_t b2f_modup_workspace(const b2f_context *ctx, int l) {
@@ -409,9 +441,9 @@ int b2f_modup(b2f_context *ctx, const uint64_t *ct, int l, uint64_t *ext,
   return modup(ctx, ct + (size_t)l * kN, 2LL * l * kN, 1, l, xt, ext, s);
 }
 
-size_t b2f_rotate_hoisted_workspace(const b2f_context *ctx, int l) {
-  if (!ctx || l < 1 || l > ctx->L) return 0;
-  return moddown_bytes(ctx, 1, l);
+size_t b2f_rotate_hoisted_workspace(const b2f_context *ctx, int count, int l) {
+  if (!ctx || l < 1 || l > ctx->L || count < 0) return 0;
+  return moddown_bytes(ctx, std::max(1, std::min(count, kMaxItems)), l);
 }
 
 int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
@@ -420,33 +452,58 @@ int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
                        size_t ws_bytes, void *stream) {
   int rc = check_level(ctx, l, "b2f_rotate_hoisted");
   if (rc) return rc;
-  B2F_CHECK_ARG(ct && ext && out && count >= 0 && (count == 0 || (galois && keys)),
+  B2F_CHECK_ARG(ct && out && count >= 0 && (count == 0 || (galois && keys)),
                 "b2f_rotate_hoisted: null argument");
+  bool need_ext = false;
   for (int r = 0; r < count; ++r) {
-    B2F_CHECK_ARG(keys[r], "b2f_rotate_hoisted: key %d is null", r);
     B2F_CHECK_ARG(valid_galois(galois[r]),
                   "b2f_rotate_hoisted: bad galois element %llu",
                   (unsigned long long)galois[r]);
+    if (galois[r] != 1) {
+      B2F_CHECK_ARG(keys[r], "b2f_rotate_hoisted: key %d is null", r);
+      need_ext = true;
+    }
   }
+  B2F_CHECK_ARG(!need_ext || ext, "b2f_rotate_hoisted: ModUp digits are null");
   cudaStream_t s = (cudaStream_t)stream;
   Scratch sc{ctx, s};
-  if ((rc = sc.init(ws, ws_bytes, moddown_bytes(ctx, 1, l)))) return rc;
+  if ((rc = sc.init(ws, ws_bytes, b2f_rotate_hoisted_workspace(ctx, count, l))))
+    return rc;
   const int lk = l + ctx->K;
-  uint64_t *acc = sc.take((size_t)2 * lk * kN);
-  uint64_t *conv = sc.take((size_t)2 * l * kN);
+  const int chunk = std::max(1, std::min(count, kMaxItems));
+  uint64_t *acc = sc.take((size_t)chunk * 2 * lk * kN);
+  uint64_t *conv = sc.take((size_t)chunk * 2 * l * kN);
   const long long cs = 2LL * l * kN;
+  // identity items are copies; the others go through the key switch in
+  // groups of up to kMaxItems, one launch sequence per group
+  std::vector<int> keyed;
   for (int r = 0; r < count; ++r) {
-    rc = ip_moddown(ctx, ct + (size_t)l * kN, cs, ext, 1, l, keys[r], ct,
-                    nullptr, cs, (uint32_t)galois[r], out + (size_t)r * cs, cs,
-                    acc, conv, s);
+    if (galois[r] == 1) {
+      B2F_CUDA(cudaMemcpyAsync(out + (size_t)r * cs, ct, cs * 8,
+                               cudaMemcpyDeviceToDevice, s));
+    } else {
+      keyed.push_back(r);
+    }
+  }
+  for (size_t p = 0; p < keyed.size(); p += kMaxItems) {
+    const int n = (int)std::min<size_t>(kMaxItems, keyed.size() - p);
+    ItemKeys it{};
+    it.shared = 0;
+    for (int i = 0; i < n; ++i) {
+      it.key[i] = keys[keyed[p + i]];
+      it.g[i] = (uint32_t)galois[keyed[p + i]];
+      it.pos[i] = (int16_t)(keyed[p + i] - keyed[p]);
+    }
+    rc = ip_moddown(ctx, ct + (size_t)l * kN, 0, ext, 0, n, l, it, ct, nullptr,
+                    0, out + (size_t)keyed[p] * cs, cs, acc, conv, s);
     if (rc) return rc;
   }
   return B2F_OK;
 }
 
-size_t b2f_rotate_hoisted_ext_workspace(const b2f_context *ctx, int l) {
-  if (!ctx || l < 1 || l > ctx->L) return 0;
-  return rnd((size_t)2 * (l + ctx->K) * kN);
+size_t b2f_rotate_hoisted_ext_workspace(const b2f_context *ctx, int count, int l) {
+  if (!ctx || l < 1 || l > ctx->L || count < 0) return 0;
+  return rnd((size_t)std::max(1, std::min(count, kMaxItems)) * 2 * (l + ctx->K) * kN);
 }
 
 int b2f_rotate_hoisted_ext(b2f_context *ctx, const uint64_t *ct, int l,
@@ -470,22 +527,34 @@ int b2f_rotate_hoisted_ext(b2f_context *ctx, const uint64_t *ct, int l,
   B2F_CHECK_ARG(!need_ext || ext, "b2f_rotate_hoisted_ext: ModUp digits are null");
   cudaStream_t s = (cudaStream_t)stream;
   Scratch sc{ctx, s};
-  if ((rc = sc.init(ws, ws_bytes, b2f_rotate_hoisted_ext_workspace(ctx, l)))) return rc;
+  if ((rc = sc.init(ws, ws_bytes, b2f_rotate_hoisted_ext_workspace(ctx, count, l))))
+    return rc;
   const int K = ctx->K, lk = l + K;
-  uint64_t *acc = sc.take((size_t)2 * lk * kN);
+  const int chunk = std::max(1, std::min(count, kMaxItems));
+  uint64_t *acc = sc.take((size_t)chunk * 2 * lk * kN);
   const LevelTables &T = ctx->levels[l];
-  for (int r = 0; r < count; ++r) {
-    uint64_t *o = out + (size_t)r * 2 * lk * kN;
-    const uint64_t *a = nullptr;
-    if (galois[r] != 1) {
-      key_inner_product_kernel<<<dim3(kN / TPB, 1, lk), TPB, 0, s>>>(
-          ct + (size_t)l * kN, 0, ext, keys[r], acc, ctx->d_mod, l, K, ctx->L,
+  for (int p = 0; p < count; p += kMaxItems) {
+    const int n = std::min(kMaxItems, count - p);
+    ItemKeys it{};
+    ExtItems ex{};
+    int keyed = 0;
+    for (int i = 0; i < n; ++i) {
+      ex.g[i] = (uint32_t)galois[p + i];
+      ex.slot[i] = -1;
+      if (galois[p + i] != 1) {
+        it.key[keyed] = keys[p + i];
+        ex.slot[i] = (int16_t)keyed++;
+      }
+    }
+    if (keyed) {
+      key_inner_product_kernel<<<dim3(kN / TPB, keyed, lk), TPB, 0, s>>>(
+          ct + (size_t)l * kN, 0, ext, 0, it, acc, ctx->d_mod, l, K, ctx->L,
           ctx->alpha, T.beta);
       B2F_LAUNCHED("key_inner_product_kernel");
-      a = acc;
     }
-    ext_combine_kernel<<<dim3(kN / TPB, lk, 2), TPB, 0, s>>>(
-        a, ct, o, ctx->d_mod, ctx->d_pmod, l, K, ctx->L, (uint32_t)galois[r]);
+    ext_combine_kernel<<<dim3(kN / TPB, lk, 2 * n), TPB, 0, s>>>(
+        acc, ct, out + (size_t)p * 2 * lk * kN, ctx->d_mod, ctx->d_pmod, l, K,
+        ctx->L, ex);
     B2F_LAUNCHED("ext_combine_kernel");
   }
   return B2F_OK;
@@ -526,7 +595,7 @@ int b2f_moddown_ext(b2f_context *ctx, const uint64_t *in, int num_cts, int l,
   if ((rc = ntt_polys(ctx, conv, 2 * num_cts, l, 0, 0, s))) return rc;
   moddown_combine_kernel<<<dim3(kN / TPB, l, num_cts), TPB, 0, s>>>(
       in, conv, nullptr, nullptr, 0, out, 2LL * l * kN, ctx->d_moddown_pinv,
-      ctx->d_primes, l, K, 1u);
+      ctx->d_primes, l, K, ItemKeys{{}, {1u}, {}, 1});
   B2F_LAUNCHED("moddown_combine_kernel");
   return B2F_OK;
 }

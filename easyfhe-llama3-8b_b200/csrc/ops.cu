@@ -59,6 +59,26 @@ __global__ void __launch_bounds__(TPB) modraise_lift_kernel(
   data[((size_t)p * l_out + t) * kN + n] = r;
 }
 
+// Tensor product of ciphertext pairs: (a0 b0, a0 b1 + a1 b0, a1 b1), the
+// middle term accumulated in 128 bits and reduced once.  grid (N/TPB, l, cts)
+__global__ void __launch_bounds__(TPB) tensor_kernel(
+    const uint64_t *__restrict__ a, const uint64_t *__restrict__ b,
+    uint64_t *__restrict__ out, const Mod *__restrict__ mods, int l) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, ct = blockIdx.z;
+  const size_t lim = (size_t)l * kN, off = (size_t)i * kN + n;
+  const size_t in = (size_t)ct * 2 * lim + off;
+  const Mod M = mods[i];
+  const uint64_t a0 = a[in], a1 = a[in + lim], b0 = b[in], b1 = b[in + lim];
+  U128 mid = {0, 0};
+  mac128(mid, a0, b1);
+  mac128(mid, a1, b0);
+  const size_t o = (size_t)ct * 3 * lim + off;
+  out[o] = mul_mod(a0, b0, M);
+  out[o + lim] = reduce128(mid.hi, mid.lo, M);
+  out[o + 2 * lim] = mul_mod(a1, b1, M);
+}
+
 // grid (N/TPB, l, polys)
 __global__ void __launch_bounds__(TPB) elementwise_kernel(
     int op, const uint64_t *__restrict__ a, const uint64_t *__restrict__ b,
@@ -111,7 +131,9 @@ __global__ void __launch_bounds__(TPB) scalar_kernel(
   const uint64_t q = primes[i];
   uint64_t r = a[idx];
   if (S.has_mul) r = shoup(r, S.mul[i].x, S.mul[i].y, q);
-  if (S.has_add && (S.add_poly < 0 || S.add_poly == p)) r = add_mod(r, S.add[i], q);
+  const bool add_here = S.add_poly == -1 || S.add_poly == p ||
+                        (S.add_poly == -2 && (p & 1) == 0);
+  if (S.has_add && add_here) r = add_mod(r, S.add[i], q);
   out[idx] = r;
 }
 
@@ -318,11 +340,25 @@ int b2f_mul_i(b2f_context *ctx, const uint64_t *a, uint64_t *out, int num_polys,
   return B2F_OK;
 }
 
+int b2f_tensor(b2f_context *ctx, const uint64_t *a, const uint64_t *b,
+               uint64_t *out, int num_cts, int l, void *stream) {
+  B2F_CHECK_ARG(ctx && a && b && out && num_cts >= 0, "b2f_tensor: null argument");
+  B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_tensor: bad limbs %d", l);
+  B2F_CHECK_ARG(out != a && out != b, "b2f_tensor: output overlaps an input");
+  if (!num_cts) return B2F_OK;
+  tensor_kernel<<<dim3(kN / TPB, l, num_cts), TPB, 0, (cudaStream_t)stream>>>(
+      a, b, out, ctx->d_mod, l);
+  B2F_LAUNCHED("tensor_kernel");
+  return B2F_OK;
+}
+
 int b2f_scalar_op(b2f_context *ctx, const uint64_t *a, uint64_t *out,
                   int num_polys, int l, const uint64_t *mul_residues,
                   const uint64_t *add_residues, int add_poly, void *stream) {
   B2F_CHECK_ARG(ctx && a && out, "b2f_scalar_op: null argument");
   B2F_CHECK_ARG(l >= 1 && l <= ctx->L && l <= 64, "b2f_scalar_op: bad limbs %d", l);
+  B2F_CHECK_ARG(add_poly >= -2 && add_poly < num_polys,
+                "b2f_scalar_op: add_poly %d outside [-2, %d)", add_poly, num_polys);
   if (num_polys <= 0) return B2F_OK;
   ScalarArgs S{};
   S.has_mul = mul_residues != nullptr;

@@ -48,10 +48,10 @@ _SIGS = {
     "b2f_relinearize": (_int, [_vp, _vp, _vp, _int, _int, _vp, _vp, _size, _vp]),
     "b2f_modup_workspace": (_size, [_vp, _int]),
     "b2f_modup": (_int, [_vp, _vp, _int, _vp, _vp, _size, _vp]),
-    "b2f_rotate_hoisted_workspace": (_size, [_vp, _int]),
+    "b2f_rotate_hoisted_workspace": (_size, [_vp, _int, _int]),
     "b2f_rotate_hoisted": (_int, [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _size,
                                   _vp]),
-    "b2f_rotate_hoisted_ext_workspace": (_size, [_vp, _int]),
+    "b2f_rotate_hoisted_ext_workspace": (_size, [_vp, _int, _int]),
     "b2f_rotate_hoisted_ext": (_int, [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp,
                                       _size, _vp]),
     "b2f_moddown_ext_workspace": (_size, [_vp, _int, _int]),
@@ -65,6 +65,7 @@ _SIGS = {
     "b2f_elementwise": (_int, [_vp, _int, _vp, _vp, _vp, _int, _int, _int, _vp]),
     "b2f_mul_i": (_int, [_vp, _vp, _vp, _int, _int, _int, _vp]),
     "b2f_scalar_op": (_int, [_vp, _vp, _vp, _int, _int, _vp, _vp, _int, _vp]),
+    "b2f_tensor": (_int, [_vp, _vp, _vp, _vp, _int, _int, _vp]),
     "b2f_bsgs_mac_workspace": (_size, [_vp, _int]),
     "b2f_bsgs_mac": (_int, [_vp, _vp, _int, _vp, _int, _int, _u64, _vp, _vp, _vp, _size,
                             _vp]),

@@ -73,10 +73,17 @@ class Requirements:
 
 @dataclass(frozen=True)
 class _Plan:
+    """Offsets (g B + b) step, g in giants (from gmin), b < B.  The babies are
+    the hoisted rotations by (gmin B + b) step, so the Horner chain over the
+    giants 0 .. G-1 needs no final rotation by gmin B step."""
+
     step: int
     babies: int
     giants: tuple
     gmin: int
+
+    def baby_offsets(self) -> tuple:
+        return tuple((self.gmin * self.babies + b) * self.step for b in range(self.babies))
 
 
 def _check(spec: BootstrapSpec, log_n: int) -> None:
@@ -108,12 +115,11 @@ def requirements(specs, log_n: int) -> Requirements:
     for spec in specs:
         _check(spec, log_n)
         cts, stc = _level_plans(int(log_n), int(spec.log_slots), spec.level_budget)
+        slots = 1 << int(spec.log_slots)
         for _, plan in cts + stc:
-            rots.update(b * plan.step for b in range(1, plan.babies))
+            rots.update(o % slots for o in plan.baby_offsets() if o % slots)
             if len(plan.giants) > 1:
                 rots.add(plan.babies * plan.step)
-            if plan.gmin:
-                rots.add(plan.gmin * plan.babies * plan.step)
     return Requirements(tuple(sorted(rots)))
 
 
@@ -156,8 +162,9 @@ class Program:
 
 
 def level_rows(diags: dict, plan: _Plan, slots: int) -> np.ndarray:
-    """Row g*B + b (g over plan.giants, from gmin) = D_{(gB+b) step} rotated
-    by -g B step, so the Horner giant rotations put every term back."""
+    """Row (g - gmin) B + b (g over plan.giants) = D_{(gB+b) step} rotated by
+    -(g - gmin) B step: with babies rot_{(gmin B + b) step}(ct), the Horner
+    giant rotations put every term back."""
 
     rows = []
     for g in plan.giants:
@@ -166,7 +173,7 @@ def level_rows(diags: dict, plan: _Plan, slots: int) -> np.ndarray:
             d = diags.get(o)
             if d is None:
                 d = np.zeros(slots, dtype=np.complex128)
-            rows.append(np.roll(d, g * plan.babies * plan.step))
+            rows.append(np.roll(d, (g - plan.gmin) * plan.babies * plan.step))
     return np.array(rows)
 
 
@@ -218,12 +225,11 @@ def generate(context, spec: BootstrapSpec) -> Program:
 
 def _linear(ct: fhe.Ciphertext, level: _Level, ctx: fhe.Context) -> fhe.Ciphertext:
     p = level.plan
-    offsets = tuple(b * p.step for b in range(p.babies))
+    slots = int(ct.slots)
+    offsets = tuple(o % slots for o in p.baby_offsets())
     babies = fhe.prepare_hoisted_baby_rotations(ct, offsets, ctx)
     acc = fhe.hoisted_mac_sum(ct, offsets, level.pts, p.babies * p.step, len(p.giants), ctx,
                               baby_rotations=babies)
-    if p.gmin:
-        acc = fhe.homo_rotate(acc, p.gmin * p.babies * p.step, ctx)
     return fhe.rescale(acc, ctx)
 
 
@@ -405,9 +411,9 @@ def bootstrap(ct: fhe.Ciphertext, context, program: Program) -> fhe.Ciphertext:
     conj = fhe.homo_rotate(y, ctx.M - 1, ctx)
     x_re = fhe.homo_add(y, conj, ctx)
     x_im = fhe.homo_mul_i(fhe.homo_sub(y, conj, ctx), ctx, negative=True)
-    # 4. EvalMod
-    s_re = _evalmod(x_re, program.cheb, delta, ctx)
-    s_im = _evalmod(x_im, program.cheb, delta, ctx)
+    # 4. EvalMod on both parts as one batch of two ciphertexts
+    both = _evalmod(fhe.pack_cipher_batch((x_re, x_im)), program.cheb, delta, ctx)
+    s_re, s_im = fhe.unpack_cipher_batch(both)
     # 5. recombine and SlotToCoeff
     z = fhe.homo_add(s_re, fhe.homo_mul_i(s_im, ctx), ctx)
     for level in program.stc:

@@ -234,9 +234,11 @@ class NativeContext:
         if out is None:
             out = self.empty(count, 2, l)
         g = (ctypes.c_uint64 * max(count, 1))(*[int(v) for v in galois])
-        kp = (ctypes.c_void_p * max(count, 1))(*[_ptr(k) for k in keys])
-        ws = self.workspace(lib.b2f_rotate_hoisted_workspace(self.handle, l))
-        call("b2f_rotate_hoisted", self.handle, _ptr(ct), l, _ptr(ext), count, g, kp,
+        kp = (ctypes.c_void_p * max(count, 1))(*[_ptr(k) if k is not None else None
+                                                  for k in keys])
+        ws = self.workspace(lib.b2f_rotate_hoisted_workspace(self.handle, count, l))
+        call("b2f_rotate_hoisted", self.handle, _ptr(ct), l,
+             _ptr(ext) if ext is not None else None, count, g, kp,
              _ptr(out), _ptr(ws), ws.numel(), _stream())
         return out
 
@@ -247,7 +249,7 @@ class NativeContext:
         g = (ctypes.c_uint64 * max(count, 1))(*[int(v) for v in galois])
         kp = (ctypes.c_void_p * max(count, 1))(*[_ptr(k) if k is not None else None
                                                   for k in keys])
-        ws = self.workspace(lib.b2f_rotate_hoisted_ext_workspace(self.handle, l))
+        ws = self.workspace(lib.b2f_rotate_hoisted_ext_workspace(self.handle, count, l))
         call("b2f_rotate_hoisted_ext", self.handle, _ptr(ct), l,
              _ptr(ext) if ext is not None else None, count, g, kp, _ptr(out), _ptr(ws),
              ws.numel(), _stream())
@@ -293,6 +295,11 @@ class NativeContext:
             out = self.empty(num_polys, l)
         call("b2f_elementwise", self.handle, op, _ptr(a), _ptr(b), _ptr(out), num_polys, l,
              num_polys if b_polys is None else b_polys, _stream())
+        return out
+
+    def tensor(self, a: torch.Tensor, b: torch.Tensor, num_cts: int, l: int) -> torch.Tensor:
+        out = self.empty(num_cts, 3, l)
+        call("b2f_tensor", self.handle, _ptr(a), _ptr(b), _ptr(out), num_cts, l, _stream())
         return out
 
     def mul_i(self, a: torch.Tensor, num_polys: int, l: int, negative: bool = False) -> torch.Tensor:

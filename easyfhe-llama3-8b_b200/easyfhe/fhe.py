@@ -470,10 +470,10 @@ def homo_add_scalar(ct: Ciphertext, enc: EncodedScalar, context) -> Ciphertext:
 
     ctx = _ctx_of(context)
     l = _limbs(ct)
+    if ct.batch_size != 1 and ct.polys != 2:
+        raise NotImplementedError("homo_add_scalar on a batch of degree-2 ciphertexts")
     out = ctx.native.scalar_op(ct.data, _polys_total(ct), l, add=_enc_for(ct, enc),
-                               add_poly=0 if ct.batch_size == 1 else -1)
-    if ct.batch_size != 1:
-        raise NotImplementedError("homo_add_scalar on a ciphertext batch")
+                               add_poly=0 if ct.batch_size == 1 else -2)
     return _new(out.view(ct.data.shape), ct)
 
 
@@ -542,15 +542,12 @@ def homo_mul_no_relin(a: Ciphertext, b: Ciphertext, context) -> Ciphertext:
     a, b = _match(a, b)
     if a.polys != 2 or b.polys != 2:
         raise ValueError("homo_mul_no_relin needs degree-1 ciphertexts")
+    if a.batch_size != b.batch_size:
+        raise ValueError(f"homo_mul_no_relin: batches of {a.batch_size} and {b.batch_size}")
     l = _limbs(a)
-    nat = ctx.native
-    shape = (3,) + tuple(a.data.shape[-2:])
-    out = nat.empty(3, l).view(shape)
-    nat.elementwise(2, a.data[0], b.data[0], 1, l, out=out[0])
-    nat.elementwise(2, a.data[1], b.data[1], 1, l, out=out[2])
-    t = nat.elementwise(2, a.data[0], b.data[1], 1, l)
-    u = nat.elementwise(2, a.data[1], b.data[0], 1, l)
-    nat.elementwise(0, t, u, 1, l, out=out[1])
+    out = ctx.native.tensor(a.data, b.data, a.batch_size, l)
+    out = out.view((3,) + tuple(a.data.shape[-2:]) if a.data.dim() == 3
+                   else (a.batch_size, 3) + tuple(a.data.shape[-2:]))
     state = a.state.replace(
         scale_degree=int(a.state.scale_degree) + int(b.state.scale_degree),
         scaling_factor=float(a.state.scaling_factor) * float(b.state.scaling_factor))
@@ -616,22 +613,13 @@ def prepare_hoisted_baby_rotations(ct: Ciphertext, baby_offsets, context,
     offsets = tuple(int(v) for v in baby_offsets)
     l = _limbs(ct)
     nat = ctx.native
-    out = nat.empty(len(offsets), 2, l)
-    rot_idx, gal, keys = [], [], []
-    for b, off in enumerate(offsets):
+    gal, keys = [], []
+    for off in offsets:
         g = galois_element(off, ctx.logN)
-        if g == 1:
-            out[b].copy_(ct.data)
-        else:
-            _, key = ctx.rotation_key(off)
-            rot_idx.append(b)
-            gal.append(g)
-            keys.append(key)
-    if rot_idx:
-        ext = nat.modup(ct.data, l)
-        res = nat.rotate_hoisted(ct.data, l, ext, gal, keys)
-        idx = torch.tensor(rot_idx, device=out.device)
-        out.index_copy_(0, idx, res)
+        gal.append(g)
+        keys.append(None if g == 1 else ctx.rotation_key(off)[1])
+    ext = nat.modup(ct.data, l) if any(g != 1 for g in gal) else None
+    out = nat.rotate_hoisted(ct.data, l, ext, gal, keys)
     block = Ciphertext(out, ct.state, ct.slots, ctx)
     babies = BabyRotations((block,))
     babies.offsets = offsets

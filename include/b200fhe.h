@@ -103,11 +103,13 @@ int b2f_relinearize(b2f_context *ctx, const uint64_t *ct3_in, uint64_t *ct_out,
 size_t b2f_modup_workspace(const b2f_context *ctx, int l);
 int b2f_modup(b2f_context *ctx, const uint64_t *ct, int l, uint64_t *ext,
               void *ws, size_t ws_bytes, void *stream);
-/* ... then one inner product + ModDown + automorphism per rotation: out[r]
- * = rotation galois[r] of ct using keys[r] (an array of `count` device key
- * pointers, host array).  fhe.prepare_hoisted_baby_rotations / fast_rotate
+/* ... then the inner product + ModDown + automorphism of every rotation:
+ * out[r] = rotation galois[r] of ct using keys[r] (an array of `count` device
+ * key pointers, host array); galois 1 copies ct and needs no key (ext may be
+ * null when every item is galois 1).  Rotations run in groups of up to 64
+ * per launch sequence.  fhe.prepare_hoisted_baby_rotations / fast_rotate
  * (llama3fhe/operators/attention/input.py:792-797, 1143-1148). */
-size_t b2f_rotate_hoisted_workspace(const b2f_context *ctx, int l);
+size_t b2f_rotate_hoisted_workspace(const b2f_context *ctx, int count, int l);
 int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
                        const uint64_t *ext, int count, const uint64_t *galois,
                        const uint64_t *const *keys, uint64_t *out, void *ws,
@@ -118,7 +120,7 @@ int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
  * pi_g(acc1)), P times the rotation before ModDown; galois 1 gives (P c0,
  * P c1) and needs no key.  fhe.fast_rotate(ct, offsets, ctx, output_ext=True)
  * (llama3fhe/operators/attention/input.py:792-797, 1143-1148). */
-size_t b2f_rotate_hoisted_ext_workspace(const b2f_context *ctx, int l);
+size_t b2f_rotate_hoisted_ext_workspace(const b2f_context *ctx, int count, int l);
 int b2f_rotate_hoisted_ext(b2f_context *ctx, const uint64_t *ct, int l,
                            const uint64_t *ext, int count, const uint64_t *galois,
                            const uint64_t *const *keys, uint64_t *out, void *ws,
@@ -170,9 +172,16 @@ int b2f_elementwise(b2f_context *ctx, int op, const uint64_t *a,
  * fhe.homo_mul_i (llama3fhe/operators/linear/complex.py:22). */
 int b2f_mul_i(b2f_context *ctx, const uint64_t *a, uint64_t *out,
               int num_polys, int l, int negative, void *stream);
+/* Tensor product of num_cts ciphertext pairs at l limbs (NTT form): out[c]
+ * (3 polys) = (a0 b0, a0 b1 + a1 b0, a1 b1).  fhe.homo_mul_no_relin
+ * (llama3fhe/operators/attention/qk.py:399, primitives.py:21-31). */
+int b2f_tensor(b2f_context *ctx, const uint64_t *a, const uint64_t *b,
+               uint64_t *out, int num_cts, int l, void *stream);
 /* out = a * c (+ add) with per-limb integer constants c[l], add[l]
- * (residues, NULL = none): fhe.homo_mul_scalar / homo_add_scalar on
- * fhe.encode_scalar constants (llama3fhe/operators/nonlinear/bootstrap.py:331-349). */
+ * (residues, NULL = none); add goes to poly add_poly, to every poly (-1) or
+ * to c0 of every ciphertext of a batch of 2-poly ciphertexts (-2):
+ * fhe.homo_mul_scalar / homo_add_scalar on fhe.encode_scalar constants
+ * (llama3fhe/operators/nonlinear/bootstrap.py:331-349). */
 int b2f_scalar_op(b2f_context *ctx, const uint64_t *a, uint64_t *out,
                   int num_polys, int l, const uint64_t *mul_residues,
                   const uint64_t *add_residues, int add_poly, void *stream);

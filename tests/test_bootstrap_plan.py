@@ -38,12 +38,12 @@ def test_dft_levels_match_oracle_fft(oracle_mod, log_n, budget):
 
 def _bsgs_apply(rows, plan, x):
     B, step = plan.babies, plan.step
-    babies = [np.roll(x, -b * step) for b in range(B)]
+    babies = [np.roll(x, -o) for o in plan.baby_offsets()]
     acc = None
     for gi in range(len(plan.giants) - 1, -1, -1):  # Horner over giants
         inner = sum(rows[gi * B + b] * babies[b] for b in range(B))
         acc = inner if acc is None else np.roll(acc, -B * step) + inner
-    return np.roll(acc, -plan.gmin * B * step)
+    return acc
 
 
 def test_bsgs_rows_reproduce_levels():
@@ -69,9 +69,9 @@ def test_requirements_cover_every_rotation():
     assert 131071 in rots and spec.depth == 18
     cts, stc = bs._level_plans(16, 15, (4, 4))
     for _, p in cts + stc:
-        for b in range(1, p.babies):
-            assert b * p.step in rots
-        assert p.babies * p.step in rots and p.gmin * p.babies * p.step in rots
+        for o in p.baby_offsets():
+            assert o % 32768 == 0 or o % 32768 in rots
+        assert p.babies * p.step in rots
 
 
 def test_bootstrap_pipeline_on_clear_slots(oracle_mod):

@@ -107,6 +107,53 @@ def test_hoisted_rotations_bit_exact():
     assert np.array_equal(got[1], plain)
 
 
+def test_hoisted_rotations_identity_items_and_groups():
+    """Identity items (galois 1, no key) anywhere in the list are copies, and
+    more than 64 rotations run as several launch groups."""
+
+    from easyfhe import core
+
+    L, l = 4, 4
+    ctx, orc = pair(L, 1, 2)
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(12, 192))
+    base = [core.galois_element(r) for r in (1, 3, 5)]
+    keys3 = [ctx.keygen_rotation(s_ntt, g, seed=40 + i) for i, g in enumerate(base)]
+    rng = np.random.default_rng(13)
+    ct = rand_residues(rng, ctx.primes[:l], 2)
+    dct = to_dev(ct)
+    ext = ctx.modup(dct, l)
+    gs, keys = [], []
+    for r in range(70):
+        if r in (0, 33, 64):
+            gs.append(1)
+            keys.append(None)
+        else:
+            gs.append(base[r % 3])
+            keys.append(keys3[r % 3])
+    got = to_host(ctx.rotate_hoisted(dct, l, ext, gs, keys))
+    hk = [to_host(k) for k in keys3]
+    want3 = orc.rotate_hoisted(ct, l, base, hk)
+    for r in range(70):
+        want = ct if gs[r] == 1 else want3[r % 3]
+        assert np.array_equal(got[r], want), f"item {r}"
+
+
+def test_tensor_product_bit_exact():
+    ctx, _ = pair(8, 2, 3)
+    l, cts = 3, 2
+    rng = np.random.default_rng(14)
+    a = rand_residues(rng, ctx.primes[:l], 2 * cts).reshape(cts, 2, l, N)
+    b = rand_residues(rng, ctx.primes[:l], 2 * cts).reshape(cts, 2, l, N)
+    got = to_host(ctx.tensor(to_dev(a), to_dev(b), cts, l)).reshape(cts, 3, l, N)
+    q = np.array(ctx.primes[:l], dtype=object)[:, None]
+    A, B = a.astype(object), b.astype(object)
+    for c in range(cts):
+        want = [(A[c, 0] * B[c, 0]) % q, (A[c, 0] * B[c, 1] + A[c, 1] * B[c, 0]) % q,
+                (A[c, 1] * B[c, 1]) % q]
+        for p in range(3):
+            assert np.array_equal(got[c, p], want[p].astype(np.uint64)), (c, p)
+
+
 def test_relinearize_bit_exact():
     from easyfhe import core
 
