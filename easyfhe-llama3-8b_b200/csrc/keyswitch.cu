@@ -43,16 +43,34 @@ __device__ __forceinline__ uint32_t auto_src(uint32_t k, uint32_t g) {
   return brv16((e2 - 1) >> 1);
 }
 
+// Base conversions: Shoup products with the constant's precomputed
+// quotient, summed lazily in [0, 2p).  A block row covers `tper` targets;
+// small launches (one ciphertext) split the targets over more blocks so the
+// grid still fills the GPU, large batches keep one row per digit so each
+// input word is read once.
+inline int conv_split(int rows, int targets) {
+  const int want = 2048;  // ~14 blocks of 256 threads per SM
+  const int have = rows * (kN / 256);
+  if (have >= want) return targets;
+  const int chunks = std::min(targets, (want + have - 1) / have);
+  return (targets + chunks - 1) / chunks;
+}
+
 // Step 2: fast base conversion of one digit to every target outside it.
-// grid (N/TPB, beta, cts); xt [ct][l][N]; ext [ct][beta][l+K][N]
+// grid (N/TPB, beta * ceil((l+K)/tper), cts); xt [ct][l][N];
+// ext [ct][beta][l+K][N]
 __global__ void __launch_bounds__(TPB) modup_conv_kernel(
     const uint64_t *__restrict__ xt, uint64_t *__restrict__ ext,
     const ulonglong2 *__restrict__ conv, const uint64_t *__restrict__ primes,
-    int l, int K, int L, int alpha) {
+    int l, int K, int L, int alpha, int tper) {
   const int n = blockIdx.x * TPB + threadIdx.x;
-  const int j = blockIdx.y, ct = blockIdx.z;
-  const int beta = gridDim.y, lk = l + K;
+  const int lk = l + K, tchunks = (lk + tper - 1) / tper;
+  const int j = blockIdx.y / tchunks, tc = blockIdx.y % tchunks;
+  const int ct = blockIdx.z;
+  const int beta = gridDim.y / tchunks;
   const int lo = j * alpha, hi = min(lo + alpha, l), w = hi - lo;
+  const int t0 = tc * tper, t1 = min(t0 + tper, lk);
+  if (t0 >= lo && t1 <= hi) return;  // the whole chunk lies in the digit
   const uint64_t *src = xt + ((size_t)ct * l + lo) * kN + n;
   uint64_t xs[16];
 #pragma unroll
@@ -60,7 +78,7 @@ __global__ void __launch_bounds__(TPB) modup_conv_kernel(
     if (i < w) xs[i] = src[(size_t)i * kN];
   uint64_t *dst = ext + ((size_t)ct * beta + j) * lk * kN + n;
   const ulonglong2 *cj = conv + (size_t)j * lk * alpha;
-  for (int t = 0; t < lk; ++t) {
+  for (int t = t0; t < t1; ++t) {
     if (t >= lo && t < hi) continue;
     const uint64_t p = primes[t < l ? t : L + (t - l)], p2 = 2 * p;
     const ulonglong2 *c = cj + (size_t)t * alpha;
@@ -93,16 +111,32 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
   const Mod M = mods[gp];
   const uint64_t *__restrict__ key = items.key[items.at(ct)];
   U128 s0 = {0, 0}, s1 = {0, 0};
-  for (int j = 0; j < beta; ++j) {
+  // digits in groups of four: all loads of a group are issued before its
+  // multiplies, so each thread keeps 12 memory requests in flight
+  auto digit = [&](int j) -> const uint64_t * {
     const int lo = j * alpha, hi = min(lo + alpha, l);
-    uint64_t e;
-    if (t >= lo && t < hi)
-      e = c1[ct * c1_stride + (size_t)t * kN + n];
-    else
-      e = ext[ct * ext_stride + ((size_t)j * lk + t) * kN + n];
-    const uint64_t *kb = key + ((size_t)j * 2 * np + gp) * kN + n;
-    mac128(s0, e, __ldg(kb));
-    mac128(s1, e, __ldg(kb + (size_t)np * kN));
+    return (t >= lo && t < hi) ? c1 + ct * c1_stride + (size_t)t * kN + n
+                               : ext + ct * ext_stride + ((size_t)j * lk + t) * kN + n;
+  };
+  const size_t kstep = (size_t)2 * np * kN;
+  const uint64_t *kb = key + (size_t)gp * kN + n;
+  for (int j = 0; j < beta; j += 4) {
+    uint64_t e[4], k0[4], k1[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (j + u < beta) {
+        e[u] = *digit(j + u);
+        k0[u] = __ldg(kb + (j + u) * kstep);
+        k1[u] = __ldg(kb + (j + u) * kstep + (size_t)np * kN);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (j + u < beta) {
+        mac128(s0, e[u], k0[u]);
+        mac128(s1, e[u], k1[u]);
+      }
+    }
   }
   uint64_t *o = acc + ((size_t)ct * 2 * lk + t) * kN + n;
   o[0] = reduce128(s0.hi, s0.lo, M);
@@ -110,13 +144,15 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
 }
 
 // Step 4b: convert the P part (coefficient form, pre-scaled) to each q_i.
-// grid (N/TPB, 2, cts); acc [ct][2][l+K][N] -> conv [ct][2][l][N]
+// grid (N/TPB, 2 * ceil(l/tper), cts); acc [ct][2][l+K][N] -> conv [ct][2][l][N]
 __global__ void __launch_bounds__(TPB) moddown_conv_kernel(
     const uint64_t *__restrict__ acc, uint64_t *__restrict__ conv_out,
     const ulonglong2 *__restrict__ md_conv, const uint64_t *__restrict__ primes,
-    int l, int K) {
+    int l, int K, int tper) {
   const int n = blockIdx.x * TPB + threadIdx.x;
-  const int b = blockIdx.y, ct = blockIdx.z;
+  const int ichunks = (l + tper - 1) / tper;
+  const int b = blockIdx.y / ichunks, ic = blockIdx.y % ichunks;
+  const int ct = blockIdx.z;
   const int lk = l + K;
   const uint64_t *z = acc + (((size_t)ct * 2 + b) * lk + l) * kN + n;
   uint64_t zs[16];
@@ -124,7 +160,8 @@ __global__ void __launch_bounds__(TPB) moddown_conv_kernel(
   for (int k = 0; k < 16; ++k)
     if (k < K) zs[k] = z[(size_t)k * kN];
   uint64_t *o = conv_out + (((size_t)ct * 2 + b) * l) * kN + n;
-  for (int i = 0; i < l; ++i) {
+  const int i1 = min((ic + 1) * tper, l);
+  for (int i = ic * tper; i < i1; ++i) {
     const uint64_t q = primes[i], q2 = 2 * q;
     const ulonglong2 *c = md_conv + (size_t)i * K;
     uint64_t a = 0;
@@ -262,8 +299,10 @@ int modup(b2f_context *ctx, const uint64_t *c1, long long c1_stride, int cts,
                       T.modup_scale, s);
   if (rc) return rc;
   // 2. base conversion
-  modup_conv_kernel<<<dim3(kN / TPB, beta, cts), TPB, 0, s>>>(
-      xt, ext, T.modup_conv, ctx->d_primes, l, K, ctx->L, alpha);
+  const int tper = conv_split(beta * cts, lk);
+  const int tchunks = (lk + tper - 1) / tper;
+  modup_conv_kernel<<<dim3(kN / TPB, beta * tchunks, cts), TPB, 0, s>>>(
+      xt, ext, T.modup_conv, ctx->d_primes, l, K, ctx->L, alpha, tper);
   B2F_LAUNCHED("modup_conv_kernel");
   // 3. NTT of the converted limbs
   std::vector<LimbJob> fj;
@@ -307,8 +346,10 @@ int ip_moddown(b2f_context *ctx, const uint64_t *c1, long long c1_stride,
   int rc = launch_ntt(ctx, acc, as, acc, as, d, 2 * K, cts, 1,
                       ctx->d_moddown_scale, s);
   if (rc) return rc;
-  moddown_conv_kernel<<<dim3(kN / TPB, 2, cts), TPB, 0, s>>>(
-      acc, conv, ctx->d_moddown_conv, ctx->d_primes, l, K);
+  const int tper = conv_split(2 * cts, l);
+  moddown_conv_kernel<<<dim3(kN / TPB, 2 * ((l + tper - 1) / tper), cts), TPB, 0,
+                        s>>>(acc, conv, ctx->d_moddown_conv, ctx->d_primes, l, K,
+                             tper);
   B2F_LAUNCHED("moddown_conv_kernel");
   rc = ntt_polys(ctx, conv, 2 * cts, l, 0, 0, s);
   if (rc) return rc;
@@ -589,8 +630,10 @@ int b2f_moddown_ext(b2f_context *ctx, const uint64_t *in, int num_cts, int l,
   if ((rc = launch_ntt(ctx, in, as, pcoef, as, d, 2 * K, num_cts, 1,
                        ctx->d_moddown_scale, s)))
     return rc;
-  moddown_conv_kernel<<<dim3(kN / TPB, 2, num_cts), TPB, 0, s>>>(
-      pcoef, conv, ctx->d_moddown_conv, ctx->d_primes, l, K);
+  const int tper = conv_split(2 * num_cts, l);
+  moddown_conv_kernel<<<dim3(kN / TPB, 2 * ((l + tper - 1) / tper), num_cts), TPB,
+                        0, s>>>(pcoef, conv, ctx->d_moddown_conv, ctx->d_primes,
+                                l, K, tper);
   B2F_LAUNCHED("moddown_conv_kernel");
   if ((rc = ntt_polys(ctx, conv, 2 * num_cts, l, 0, 0, s))) return rc;
   moddown_combine_kernel<<<dim3(kN / TPB, l, num_cts), TPB, 0, s>>>(

@@ -138,34 +138,50 @@ __global__ void __launch_bounds__(TPB) scalar_kernel(
 }
 
 // out[ct][g] (2 polys, l limbs) = sum_b pt[g0+g][b] * babies[ct][b]
-// grid (N/TPB, l, cts); up to GMAX giants per launch.
+// grid (N/TPB, l, cts); up to GMAX giants per launch.  The plaintext rows are
+// read once and dominate the traffic, so the babies are taken two at a time
+// with every load of the pair issued before its multiplies.
 __global__ void __launch_bounds__(TPB) mac_kernel(
     const uint64_t *__restrict__ babies, int baby_count,
     const uint64_t *__restrict__ pts, int g0, int G, int l,
     uint64_t *__restrict__ out, int out_giants, const Mod *__restrict__ mods) {
+  constexpr int BU = 2;
   const int n = blockIdx.x * TPB + threadIdx.x;
   const int i = blockIdx.y, ct = blockIdx.z;
   const Mod M = mods[i];
   const size_t limb = (size_t)i * kN + n;
   const size_t ct_words = 2 * (size_t)l * kN, pt_words = (size_t)l * kN;
   const uint64_t *bb = babies + (size_t)ct * baby_count * ct_words + limb;
+  const uint64_t *pp = pts + (size_t)g0 * baby_count * pt_words + limb;
   U128 acc[GMAX][2];
 #pragma unroll
   for (int g = 0; g < GMAX; ++g) acc[g][0] = acc[g][1] = U128{0, 0};
-  for (int b = 0; b < baby_count; ++b) {
-    const uint64_t c0 = bb[(size_t)b * ct_words];
-    const uint64_t c1 = bb[(size_t)b * ct_words + pt_words];
+  for (int b = 0; b < baby_count; b += BU) {
+    uint64_t c0[BU], c1[BU], w[BU][GMAX];
 #pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      if (g < G) {
-        const uint64_t w =
-            __ldg(pts + ((size_t)(g0 + g) * baby_count + b) * pt_words + limb);
-        mac128(acc[g][0], c0, w);
-        mac128(acc[g][1], c1, w);
+    for (int u = 0; u < BU; ++u) {
+      if (b + u < baby_count) {
+        c0[u] = bb[(size_t)(b + u) * ct_words];
+        c1[u] = bb[(size_t)(b + u) * ct_words + pt_words];
+#pragma unroll
+        for (int g = 0; g < GMAX; ++g)
+          if (g < G) w[u][g] = __ldg(pp + ((size_t)g * baby_count + b + u) * pt_words);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < BU; ++u) {
+      if (b + u < baby_count) {
+#pragma unroll
+        for (int g = 0; g < GMAX; ++g) {
+          if (g < G) {
+            mac128(acc[g][0], c0[u], w[u][g]);
+            mac128(acc[g][1], c1[u], w[u][g]);
+          }
+        }
       }
     }
     // keep the 128-bit sums far from overflow for long baby runs
-    if ((b & 31) == 31) {
+    if (((b + BU) & 31) == 0) {
 #pragma unroll
       for (int g = 0; g < GMAX; ++g)
         if (g < G) {
