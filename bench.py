@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -43,14 +44,20 @@ def parse():
     ap.add_argument("--limbs", type=int, default=24)
     ap.add_argument("--dnum", type=int, default=3)
     ap.add_argument("--special", type=int, default=2)
-    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="ciphertexts per rank (hrotate 32, bootstrap 16, linear 16)")
     ap.add_argument("--rotation", type=int, default=1)
-    ap.add_argument("--workload", default="hrotate", choices=["hrotate", "ntt"],
-                    help="ntt: only the NTT kernel loop (for profiling)")
+    ap.add_argument("--workload", default="hrotate",
+                    choices=["hrotate", "ntt", "bootstrap", "linear"],
+                    help="ntt: only the NTT kernel loop (for profiling); bootstrap: "
+                         "BASELINE configs[3]; linear: BASELINE configs[2]")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=6,
                     help="rotations timed on the CPU oracle")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.batch is None:
+        a.batch = {"hrotate": 32, "ntt": 32, "bootstrap": 16, "linear": 16}[a.workload]
+    return a
 
 
 def config(a) -> dict:
@@ -167,6 +174,249 @@ def run_reference(a) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) -> None:
+    """full-slot bootstrapping at the layer parameters
+    (logN 16, depth 37, dnum 5, 59/60-bit primes, BootstrapSpec(15, (4, 4),
+    19)) of `batch` ciphertexts per rank with uniform complex slots in
+    [-1, 1]^2.  One step bootstraps every ciphertext of the batch once."""
+
+    import numpy as np
+    import torch
+
+    from easyfhe import fhe
+    from easyfhe.bs import openfhe as bs
+
+    dev = ctx_dev
+    spec = bs.BootstrapSpec(log_slots=15, level_budget=(4, 4), output_levels=19)
+    rots = bs.requirements((spec,), 16).rotations
+    client, ctx = fhe.generate_client_context(
+        fhe.CKKSContextSpec(depth=37, log_n=16, dnum=5, dcrt_bits=59, first_mod=60,
+                            rotations=rots, seed=11 + rank), dev)
+    program = bs.generate(ctx, spec)
+    rng = np.random.default_rng(77 + rank)
+    n = ctx.max_slots
+    zs = [rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n) for _ in range(a.batch)]
+    cts = [client.encrypt(z, slots=n, cur_limbs=2, scaling_factor=ctx.scale_at(2))
+           for z in zs]
+    stream = torch.cuda.current_stream()
+
+    def step(inputs):
+        return [bs.bootstrap(c, ctx, program) for c in inputs]
+
+    for _ in range(a.warmup):
+        outs = step(cts)
+    torch.cuda.synchronize()
+    clocks = Clocks(dev.index or 0, not a.no_clocks)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(a.steps):
+        outs = step(cts)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    err = max(float(np.max(np.abs(client.decrypt_complex(o) - z))) for o, z in zip(outs, zs))
+
+    # end to end: pinned host limbs in, bootstrap, refreshed limbs back out
+    host_in = [c.data.cpu().pin_memory() for c in cts]
+    host_out = [torch.empty(o.data.shape, dtype=torch.int64, pin_memory=True) for o in outs]
+    dev_in = [torch.empty_like(c.data) for c in cts]
+    e2e_steps = max(1, min(a.steps, 3))
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        ins = []
+        for h, d, c in zip(host_in, dev_in, cts):
+            d.copy_(h, non_blocking=True)
+            ins.append(fhe.Ciphertext(d, c.state, c.slots, ctx))
+        res = step(ins)
+        for h, o in zip(host_out, res):
+            h.copy_(o.data, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    if rank == 0:
+        unit = "bootstraps/s"
+        line = {
+            "metric": "bootstraps/s (full-slot CKKS bootstrapping, BASELINE configs[3])",
+            "value": world * a.batch / (ms / 1e3), "unit": unit, "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u64", "data": "synthetic",
+            "config": {"workload": (f"bootstrap N=2^16 depth 37 dnum 5 59/60-bit, "
+                                    f"BootstrapSpec(15, (4, 4), 19), batch={a.batch} "
+                                    "ciphertexts/rank at 2 limbs"),
+                       "batch_per_rank": a.batch,
+                       "l2": "working set (keys 29 x up to 230 MiB) larger than L2; no flush"},
+            "ms_per_bootstrap": ms / a.batch,
+            "precision_bits": -math.log2(err) if err > 0 else None,
+            "max_abs_error": err,
+            "output_limbs": int(outs[0].state.cur_limbs),
+            "roofline": None,
+            "cpu_baseline": None,
+            "note": "the CPU oracle has no bootstrap; cpu_baseline and the kernel roofline "
+                    "are reported on the hrotate line",
+            "e2e": {"value": world * a.batch / (e2e_ms / 1e3), "unit": unit,
+                    "h2d_bytes_per_step": sum(h.numel() * 8 for h in host_in),
+                    "d2h_bytes_per_step": sum(h.numel() * 8 for h in host_out)},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
+    """the QKV-shaped 4096 -> 4096 feature-major BSGS
+    linear at l = 13 with the reference's production plan (B = 64 babies at
+    offsets 8 b, giant offset 512, 8 chunks of 512 plaintext rows,
+    llama3fhe/operators/linear/config.py:163-317), QuaRot-like synthetic
+    weight W = G H (G ~ N(0, 1/sqrt(4096)), H a random-sign Hadamard /
+    sqrt(4096)).  The 4096 diagonals are packed and encoded once (timed
+    separately); one step runs LinearOperator.apply's call sequence
+    (operator.py:320-394) on `batch` token-shard ciphertexts per rank."""
+
+    import numpy as np
+    import torch
+
+    from easyfhe import fhe
+
+    D, lanes, B, rows_per_chunk, level = 4096, 8, 64, 512, 13
+    slots = 32768
+    chunk_giants = rows_per_chunk // B
+    G = D // B
+    chunks = [(base, min(chunk_giants, G - base)) for base in range(0, G, chunk_giants)]
+    giant_offset = B * lanes
+    offsets = tuple(b * lanes for b in range(B))
+    rotations = set(offsets[1:]) | {giant_offset} | {b * giant_offset for b, _ in chunks if b}
+    client, ctx = fhe.generate_client_context(
+        fhe.CKKSContextSpec(depth=37, log_n=16, dnum=5, dcrt_bits=59, first_mod=60,
+                            rotations=tuple(sorted(rotations)), seed=21 + rank), dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    Gm = torch.randn(D, D, dtype=torch.float64, device=dev, generator=gen) / math.sqrt(D)
+    H = torch.ones(1, 1, dtype=torch.float64, device=dev)
+    while H.shape[0] < D:
+        H = torch.cat([torch.cat([H, H], 1), torch.cat([H, -H], 1)], 0)
+    signs = torch.randint(0, 2, (D,), device=dev, generator=gen).to(torch.float64) * 2 - 1
+    W = (Gm @ (H * signs[None, :])) / math.sqrt(D)
+    del Gm, H
+    scale = ctx.scale_at(level)
+    # pack + encode every diagonal once at the working level (timed)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    pts = []
+    for base, count in chunks:
+        vals = ctx.native.pack_diagonals(W, D, lanes, B, base, count, slots)
+        data = ctx.native.encode(vals, scale, level)
+        pts.append(fhe.Plaintext(data, fhe.CipherState(level, 1, scale), slots, False))
+        del vals
+    torch.cuda.synchronize()
+    encode_s = time.perf_counter() - t0
+    rng = np.random.default_rng(5 + rank)
+    tokens = [rng.normal(0, 1, (lanes, D)) for _ in range(a.batch)]
+
+    def layout(t):
+        return np.ascontiguousarray(t.T).reshape(-1)  # feature f at slots [8 f, 8 f + 8)
+
+    cts = [client.encrypt(layout(t), slots=slots, cur_limbs=level, scaling_factor=scale)
+           for t in tokens]
+    stream = torch.cuda.current_stream()
+
+    def apply(ct):
+        babies = fhe.prepare_hoisted_baby_rotations(ct, offsets, ctx)
+        acc = None
+        for (base, count), pt in zip(chunks, pts):
+            r = fhe.hoisted_mac_sum(ct, offsets, pt, giant_offset, count, ctx,
+                                    baby_rotations=babies)
+            if base:
+                r = fhe.homo_rotate(r, base * giant_offset, ctx)
+            acc = r if acc is None else fhe.homo_add(acc, r, ctx)
+        return fhe.rescale(acc, ctx)
+
+    def step(inputs):
+        return [apply(c) for c in inputs]
+
+    for _ in range(a.warmup):
+        outs = step(cts)
+    torch.cuda.synchronize()
+    clocks = Clocks(dev.index or 0, not a.no_clocks)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(a.steps):
+        outs = step(cts)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    Wn = W.cpu().numpy()
+    err = max(float(np.max(np.abs(client.decrypt(o) - layout(t @ Wn.T))))
+              for o, t in zip(outs[:2], tokens[:2]))
+
+    host_in = [c.data.cpu().pin_memory() for c in cts]
+    host_out = [torch.empty(o.data.shape, dtype=torch.int64, pin_memory=True) for o in outs]
+    dev_in = [torch.empty_like(c.data) for c in cts]
+    e2e_steps = max(1, min(a.steps, 3))
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        ins = []
+        for h, d, c in zip(host_in, dev_in, cts):
+            d.copy_(h, non_blocking=True)
+            ins.append(fhe.Ciphertext(d, c.state, c.slots, ctx))
+        res = step(ins)
+        for h, o in zip(host_out, res):
+            h.copy_(o.data, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    if rank == 0:
+        peaks = {}
+        try:
+            peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        except Exception:
+            pass
+        hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+        # SURVEY-style algorithmic bytes: every plaintext once per ciphertext
+        # (one hoisted_mac_sum call per ciphertext, as the reference calls it),
+        # babies and outputs once
+        lim = N * 8
+        alg = a.batch * (D * level * lim + B * 2 * level * lim + 2 * level * lim)
+        unit = "ciphertexts/s"
+        line = {
+            "metric": "linear-block ciphertexts/s (QKV-shaped 4096x4096 BSGS, BASELINE configs[2])",
+            "value": world * a.batch / (ms / 1e3), "unit": unit, "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u64", "data": "synthetic",
+            "config": {"workload": (f"QKV-shaped linear D=4096 l={level} B=64 G=64 in 8 chunks, "
+                                    f"{a.batch} token-shard ciphertexts/rank, depth 37 dnum 5"),
+                       "batch_per_rank": a.batch,
+                       "l2": "plaintexts 26 GiB > L2; no flush"},
+            "pt_x_ct_per_s": world * a.batch * D / (ms / 1e3),
+            "encode_rows_per_s": D / encode_s,
+            "max_abs_error": err,
+            "roofline": {"bound": "hbm", "kernel": "whole step", "achieved":
+                         alg / (ms / 1e3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": alg / (ms / 1e3) / 1e9 / hbm_peak, "traffic": None},
+            "cpu_baseline": None,
+            "note": "cpu_baseline is reported on the hrotate line",
+            "e2e": {"value": world * a.batch / (e2e_ms / 1e3), "unit": unit,
+                    "h2d_bytes_per_step": sum(h.numel() * 8 for h in host_in),
+                    "d2h_bytes_per_step": sum(h.numel() * 8 for h in host_out)},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     a = parse()
     if a.impl == "reference":
@@ -189,6 +439,26 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
+    from easyfhe import shard
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        return shard.max_over_ranks(x, dev)
+
+    if a.workload == "bootstrap":
+        run_bootstrap(a, dev, rank, world, barrier, max_over_ranks)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    if a.workload == "linear":
+        run_linear(a, dev, rank, world, barrier, max_over_ranks)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
     params = core.Params.uniform(a.limbs, a.special, a.dnum, bits=50)
     ctx = core.NativeContext(params, dev)
     l, C = a.limbs, a.batch
@@ -203,15 +473,6 @@ def main() -> None:
     out = torch.empty_like(ct)
     ws = ctx.workspace(core.lib.b2f_rotate_workspace(ctx.handle, C, l))
     stream = torch.cuda.current_stream()
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local])
-
-    from easyfhe import shard
-
-    def max_over_ranks(x: float) -> float:
-        return shard.max_over_ranks(x, dev)
 
     launches_per_rotate = 8  # iNTT, ModUp conv, NTT, inner product, iNTT(P), conv, NTT, combine
 
