@@ -49,16 +49,59 @@ struct LimbJob {
 };
 
 // Constants of the hybrid key switch at one level (l Q-limbs).
+// Constants to reduce a value below 2^80 modulo p (2^33 < p < 2^62):
+// mu = floor(2^64 / p) (fits 32 bits), r = 2^64 mod p, rs its Shoup quotient.
+struct Red79 {
+  uint64_t p, r, rs, mu;
+};
+
 struct LevelTables {
   int l = 0, beta = 0;
   // per Q limb i < l: N^-1 * [Qhat_{j(i),i}^-1] mod q_i (Shoup pair)
   ulonglong2 *modup_scale = nullptr;
   // [beta][l+K][alpha]: [Qhat_{j,i}] mod p_t (Shoup pair w.r.t. p_t)
   ulonglong2 *modup_conv = nullptr;
+  // the same conversions as byte-split tensor-core operands: per digit j a
+  // u8 matrix of conv_rows(l+K-width_j) x conv_kpad(alpha) (conv_bytes)
+  uint8_t *modup_bytes = nullptr;
+  size_t modup_bytes_stride = 0;  // bytes per digit
   // rescale: for i < l-1, [q_{l-1}^-1] mod q_i and [q_{l-1}] mod q_i
   ulonglong2 *rescale_inv = nullptr;
   uint64_t *rescale_qlast = nullptr;
 };
+
+// Byte-split operands of a base conversion out_t = sum_{i<w} x_i c_{t,i} mod
+// p_t (t < T) for the u8 tensor-core path: x_i = sum_a x_{i,a} 2^(8a), and
+// row (group G, tile m, r) of the constant matrix, r < 16, holds for target
+// t = 8G + (r & 7) and output byte b = 2m + (r >> 3) the bytes b of
+// c_{t,i} 2^(8a) mod p_t at column k = 8i + a.  Then
+// sum_b 2^(8b) sum_k A[row(t,b)][k] x_bytes[k] = sum_i c_{t,i} x_i (mod p_t),
+// and the four 16-row tiles of a group give one thread every byte position
+// of its outputs.
+inline int conv_wpad(int w) { return w <= 4 ? 4 : (w <= 8 ? 8 : 16); }
+inline int conv_kpad(int w) { return 8 * conv_wpad(w); }
+inline int conv_groups(int T) { return (T + 7) / 8; }
+inline size_t conv_rows(int T) { return (size_t)conv_groups(T) * 64; }
+// c(t, i) gives c_{t,i} (t < T, i < w) and p(t) the target prime; rows are
+// kp >= conv_kpad(w) bytes (zero beyond 8 w)
+template <class C, class Pm>
+void conv_bytes(uint8_t *A, int T, int w, int kp, C c, Pm p) {
+  for (size_t r = 0; r < conv_rows(T); ++r) {
+    const int G = (int)(r / 64), m = (int)(r % 64) / 16, rr = (int)(r % 16);
+    const int t = 8 * G + (rr & 7), b = 2 * m + (rr >> 3);
+    for (int k = 0; k < kp; ++k) {
+      const int i = k / 8, a = k % 8;
+      uint8_t v = 0;
+      if (t < T && i < w) {
+        const uint64_t pt = p(t);
+        const uint64_t shifted =
+            (uint64_t)(((unsigned __int128)(c(t, i) % pt) << (8 * a)) % pt);
+        v = (uint8_t)(shifted >> (8 * b));
+      }
+      A[r * kp + k] = v;
+    }
+  }
+}
 
 }  // namespace b2f
 
@@ -72,12 +115,14 @@ struct b2f_context {
   // device tables
   uint64_t *d_primes = nullptr;       // L+K
   b2f::Mod *d_mod = nullptr;          // L+K Barrett constants
+  b2f::Red79 *d_red79 = nullptr;      // L+K constants of reduce79
   ulonglong2 *d_tw_fwd = nullptr;     // (L+K) x N  (psi^bitrev(k), Shoup)
   ulonglong2 *d_tw_inv = nullptr;     // (L+K) x N
   ulonglong2 *d_ninv = nullptr;       // L+K: N^-1
   ulonglong2 *d_i_factor = nullptr;   // L+K: psi^(N/2) (multiply by i)
   ulonglong2 *d_moddown_scale = nullptr;  // K: N^-1 * [Phat_k^-1] mod p_k
   ulonglong2 *d_moddown_conv = nullptr;   // L x K: [Phat_k] mod q_i
+  uint8_t *d_moddown_bytes = nullptr;     // the same, byte split (conv_bytes)
   ulonglong2 *d_moddown_pinv = nullptr;   // L: [P^-1] mod q_i
   uint64_t *d_pmod = nullptr;             // L: [P] mod q_i
   std::vector<b2f::LevelTables> levels;   // index l = 1..L

@@ -154,6 +154,17 @@ static int build_tables(b2f_context *ctx) {
   int rc;
   if ((rc = upload(ctx, &ctx->d_primes, P))) return rc;
   if ((rc = upload(ctx, &ctx->d_mod, mods))) return rc;
+  {
+    std::vector<Red79> red(P.size());
+    for (size_t i = 0; i < P.size(); ++i) {
+      const uint64_t q = P[i];
+      const unsigned __int128 two64 = (unsigned __int128)1 << 64;
+      const uint64_t r = (uint64_t)(two64 % q);
+      red[i] = Red79{q, r, (uint64_t)(((unsigned __int128)r << 64) / q),
+                     (uint64_t)(two64 / q)};
+    }
+    if ((rc = upload(ctx, &ctx->d_red79, red))) return rc;
+  }
   if ((rc = upload(ctx, &ctx->d_tw_fwd, twf))) return rc;
   if ((rc = upload(ctx, &ctx->d_tw_inv, twi))) return rc;
   if ((rc = upload(ctx, &ctx->d_ninv, ninv))) return rc;
@@ -180,6 +191,14 @@ static int build_tables(b2f_context *ctx) {
   }
   if ((rc = upload(ctx, &ctx->d_moddown_scale, md_scale))) return rc;
   if ((rc = upload(ctx, &ctx->d_moddown_conv, md_conv))) return rc;
+  if (K) {
+    std::vector<uint8_t> mdb(conv_rows(L) * conv_kpad(K));
+    conv_bytes(
+        mdb.data(), L, K, conv_kpad(K),
+        [&](int t, int k) { return md_conv[(size_t)t * K + k].x; },
+        [&](int t) { return P[t]; });
+    if ((rc = upload(ctx, &ctx->d_moddown_bytes, mdb))) return rc;
+  }
   if ((rc = upload(ctx, &ctx->d_moddown_pinv, md_pinv))) return rc;
   if ((rc = upload(ctx, &ctx->d_pmod, pmod))) return rc;
 
@@ -211,6 +230,27 @@ static int build_tables(b2f_context *ctx) {
     }
     if ((rc = upload(ctx, &T.modup_scale, scale))) return rc;
     if ((rc = upload(ctx, &T.modup_conv, conv))) return rc;
+    {
+      // targets of digit j: limbs t < l+K outside [lo, hi), in order
+      const int lk = l + K;
+      T.modup_bytes_stride = conv_rows(lk) * conv_kpad(alpha);
+      std::vector<uint8_t> mb(T.modup_bytes_stride * T.beta);
+      for (int j = 0; j < T.beta; ++j) {
+        const int lo = j * alpha, hi = std::min(lo + alpha, l), w = hi - lo;
+        auto tgt = [&](int tau) { return tau < lo ? tau : tau + w; };
+        conv_bytes(
+            mb.data() + (size_t)j * T.modup_bytes_stride, lk - w, w,
+            conv_kpad(alpha),
+            [&](int tau, int i) {
+              return conv[((size_t)j * lk + tgt(tau)) * alpha + i].x;
+            },
+            [&](int tau) {
+              const int t = tgt(tau);
+              return P[t < l ? t : L + (t - l)];
+            });
+      }
+      if ((rc = upload(ctx, &T.modup_bytes, mb))) return rc;
+    }
     std::vector<ulonglong2> rinv(l > 1 ? l - 1 : 1);
     std::vector<uint64_t> rq(l > 1 ? l - 1 : 1);
     for (int i = 0; i + 1 < l; ++i) {
@@ -318,9 +358,10 @@ int b2f_context_create(int log_n, const uint64_t *q, int L, const uint64_t *p,
   B2F_CHECK_ARG(L + K <= 64, "b2f_context_create: at most 64 primes");
   for (int i = 0; i < L + K; ++i) {
     uint64_t v = i < L ? q[i] : p[i - L];
-    B2F_CHECK_ARG(v < (1ull << 61) && v % (2ull << log_n) == 1 && h_is_prime(v),
+    B2F_CHECK_ARG(v < (1ull << 61) && v > (1ull << 33) &&
+                      v % (2ull << log_n) == 1 && h_is_prime(v),
                   "b2f_context_create: prime %d (%llu) is not an NTT prime "
-                  "below 2^61", i, (unsigned long long)v);
+                  "in (2^33, 2^61)", i, (unsigned long long)v);
   }
   B2F_CUDA(cudaSetDevice(device));
   auto *ctx = new b2f_context();

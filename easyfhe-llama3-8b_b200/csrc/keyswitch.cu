@@ -95,6 +95,241 @@ __global__ void __launch_bounds__(TPB) modup_conv_kernel(
   }
 }
 
+// ---------------------------------------------------------------------
+// Base conversion on the u8 tensor cores (mma.sync m16n8k32, s32
+// accumulate).  The input words are their own byte matrix: coefficient n's
+// limbs x_0..x_{w-1} stored as consecutive 64-bit words are the bytes
+// x_{i,a} at k = 8 i + a of column n.  The constant matrix (conv_bytes)
+// puts, for each group of 8 targets, output byte 2m in rows 0-7 and byte
+// 2m+1 in rows 8-15 of tile m, so after the four tiles the thread holding
+// row g has all eight byte sums of target 8G+g for its two columns:
+// V = sum_b C_b 2^(8b) < 2^79, reduced once (Barrett).  Exact: the residue
+// equals sum_i x_i c_{t,i} mod p_t, as the Shoup kernels compute it.
+// ---------------------------------------------------------------------
+constexpr int CNB = 256;  // coefficients (= threads) per conversion block
+
+__device__ __forceinline__ void mma_u8(int (&c)[4], uint32_t a0, uint32_t a1,
+                                       uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+inline size_t conv_mma_smem(int kp, int T) {
+  const int stride = kp / 4 + 4;  // words; = 4 mod 8 keeps fragment loads conflict free
+  return ((size_t)CNB + conv_rows(T)) * stride * 4;
+}
+
+// a * b mod 2^64 and floor(a * b / 2^64) for a 32-bit b
+__device__ __forceinline__ uint64_t mul_lo_32(uint64_t a, uint32_t b) {
+  return (uint64_t)(uint32_t)a * b + (((uint64_t)(uint32_t)(a >> 32) * b) << 32);
+}
+__device__ __forceinline__ uint64_t mul_hi_32(uint64_t a, uint32_t b) {
+  return ((uint64_t)(uint32_t)(a >> 32) * b + (((uint64_t)(uint32_t)a * b) >> 32)) >> 32;
+}
+
+// (hi 2^64 + lo) mod p for hi < 2^16: lo by Barrett with the 32-bit
+// mu = floor(2^64/p) (quotient short by at most one, remainder < 2p), hi by
+// a Shoup product with 2^64 mod p (< 2p); both lazily, then two
+// conditional subtractions.
+__device__ __forceinline__ uint64_t reduce79(uint64_t hi, uint64_t lo, const Red79 &R) {
+  const uint64_t p = R.p;
+  const uint64_t qe = mul_hi_32(lo, (uint32_t)R.mu);
+  uint64_t r0 = lo - mul_lo_32(p, (uint32_t)qe);
+  const uint32_t h = (uint32_t)hi;
+  const uint64_t y1 = mul_lo_32(R.r, h) - mul_lo_32(p, (uint32_t)mul_hi_32(R.rs, h));
+  uint64_t v = r0 + y1;  // < 4p
+  v = v >= 2 * p ? v - 2 * p : v;
+  return v >= p ? v - p : v;
+}
+
+// out(t): limb pointer of target t < T; red(t): its reduce79 constants.
+// x: limb 0 of the w input limbs; the block converts coefficients
+// [n0, n0 + CNB).  KW = 32-bit words per operand row (kp / 4).
+template <int KW, class Out, class Rd>
+__device__ __forceinline__ void conv_mma_block(const uint64_t *__restrict__ x,
+                                               int w,
+                                               const uint8_t *__restrict__ A,
+                                               int T, Out out, Rd red, int n0) {
+  constexpr int ST = KW + 4;
+  extern __shared__ __align__(16) uint32_t csm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, tq = lane & 3;
+  const int groups = (T + 7) / 8;
+  uint32_t *Xs = csm;
+  uint32_t *As = csm + CNB * ST;
+  const uint4 *Ag = reinterpret_cast<const uint4 *>(A);
+  const int quads = groups * 64 * (KW / 4);  // 16-byte pieces of A
+  for (int idx = tid; idx < quads; idx += CNB) {
+    const uint4 v = __ldg(Ag + idx);
+    uint32_t *d = As + (idx / (KW / 4)) * ST + (idx % (KW / 4)) * 4;
+    d[0] = v.x;
+    d[1] = v.y;
+    d[2] = v.z;
+    d[3] = v.w;
+  }
+#pragma unroll
+  for (int i = 0; i < KW / 2; ++i) {
+    const uint64_t v = i < w ? x[(size_t)i * kN + n0 + tid] : 0;
+    Xs[tid * ST + 2 * i] = (uint32_t)v;
+    Xs[tid * ST + 2 * i + 1] = (uint32_t)(v >> 32);
+  }
+  __syncthreads();
+  // the warp's four n-tiles: B fragments stay in registers for every group
+  uint32_t bf[4][KW / 4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const uint32_t *xr = Xs + ((warp * 4 + u) * 8 + g) * ST + tq;
+#pragma unroll
+    for (int kk = 0; kk < KW / 8; ++kk) {
+      bf[u][2 * kk] = xr[8 * kk];
+      bf[u][2 * kk + 1] = xr[8 * kk + 4];
+    }
+  }
+  const uint32_t *ag = As + g * ST + tq;
+  for (int G = 0; G < groups; ++G, ag += 64 * ST) {
+    // A fragments of the group's four tiles, reused by the four n-tiles
+    uint32_t af[4][KW / 8][4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+#pragma unroll
+      for (int kk = 0; kk < KW / 8; ++kk) {
+        const uint32_t *ar = ag + m * 16 * ST + 8 * kk;
+        af[m][kk][0] = ar[0];
+        af[m][kk][1] = ar[8 * ST];
+        af[m][kk][2] = ar[4];
+        af[m][kk][3] = ar[8 * ST + 4];
+      }
+    const int t = 8 * G + g;
+    const bool live = t < T;
+    Red79 R{};
+    uint64_t *obase = nullptr;
+    if (live) {
+      R = red(t);
+      obase = out(t) + n0 + 2 * tq;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      int acc[4][4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0;
+#pragma unroll
+      for (int kk = 0; kk < KW / 8; ++kk)
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+          mma_u8(acc[m], af[m][kk][0], af[m][kk][1], af[m][kk][2], af[m][kk][3],
+                 bf[u][2 * kk], bf[u][2 * kk + 1]);
+      if (live) {
+        uint64_t *o = obase + (warp * 4 + u) * 8;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint64_t lo4 = 0, hi4 = 0;  // byte sums 0-3 and 4-7
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            lo4 += (uint64_t)(uint32_t)acc[m][c] << (16 * m);
+            lo4 += (uint64_t)(uint32_t)acc[m][2 + c] << (16 * m + 8);
+            hi4 += (uint64_t)(uint32_t)acc[m + 2][c] << (16 * m);
+            hi4 += (uint64_t)(uint32_t)acc[m + 2][2 + c] << (16 * m + 8);
+          }
+          const uint64_t lo = lo4 + (hi4 << 32);
+          const uint64_t hi = (hi4 >> 32) + (lo < lo4);
+          o[c] = reduce79(hi, lo, R);
+        }
+      }
+    }
+  }
+}
+
+// ModUp step 2 on tensor cores.  grid (N/CNB, beta, cts)
+template <int KW>
+__global__ void __launch_bounds__(CNB) modup_conv_mma_kernel(
+    const uint64_t *__restrict__ xt, uint64_t *__restrict__ ext,
+    const uint8_t *__restrict__ bytes, size_t bytes_stride,
+    const Red79 *__restrict__ reds, int l, int K, int L, int alpha) {
+  const int j = blockIdx.y, ct = blockIdx.z, beta = gridDim.y, lk = l + K;
+  const int lo = j * alpha, hi = min(lo + alpha, l), w = hi - lo;
+  uint64_t *dst = ext + ((size_t)ct * beta + j) * lk * kN;
+  conv_mma_block<KW>(
+      xt + ((size_t)ct * l + lo) * kN, w, bytes + j * bytes_stride, lk - w,
+      [=](int tau) { return dst + (size_t)(tau < lo ? tau : tau + w) * kN; },
+      [=](int tau) {
+        const int t = tau < lo ? tau : tau + w;
+        return reds[t < l ? t : L + (t - l)];
+      },
+      blockIdx.x * CNB);
+}
+
+// ModDown step 4b on tensor cores.  grid (N/CNB, 2, cts)
+template <int KW>
+__global__ void __launch_bounds__(CNB) moddown_conv_mma_kernel(
+    const uint64_t *__restrict__ acc, uint64_t *__restrict__ conv_out,
+    const uint8_t *__restrict__ bytes, const Red79 *__restrict__ reds, int l,
+    int K) {
+  const int b = blockIdx.y, ct = blockIdx.z, lk = l + K;
+  uint64_t *o = conv_out + (((size_t)ct * 2 + b) * l) * kN;
+  conv_mma_block<KW>(
+      acc + (((size_t)ct * 2 + b) * lk + l) * kN, K, bytes, l,
+      [=](int t) { return o + (size_t)t * kN; }, [=](int t) { return reds[t]; },
+      blockIdx.x * CNB);
+}
+
+template <class Kern>
+int set_smem(Kern k, size_t bytes) {
+  if (bytes > 48 * 1024)
+    B2F_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)bytes));
+  return B2F_OK;
+}
+
+int launch_modup_conv(b2f_context *ctx, const uint64_t *xt, uint64_t *ext, int l,
+                      int cts, cudaStream_t s) {
+  const LevelTables &T = ctx->levels[l];
+  const int K = ctx->K, lk = l + K, kp = conv_kpad(ctx->alpha);
+  const size_t sm = conv_mma_smem(kp, lk);
+  const dim3 grid(kN / CNB, T.beta, cts);
+  int rc;
+#define B2F_MODUP(KWV)                                                        \
+  if ((rc = set_smem(modup_conv_mma_kernel<KWV>, sm))) return rc;             \
+  modup_conv_mma_kernel<KWV><<<grid, CNB, sm, s>>>(                           \
+      xt, ext, T.modup_bytes, T.modup_bytes_stride, ctx->d_red79, l, K, ctx->L, \
+      ctx->alpha);
+  if (kp == 32) {
+    B2F_MODUP(8)
+  } else if (kp == 64) {
+    B2F_MODUP(16)
+  } else {
+    B2F_MODUP(32)
+  }
+#undef B2F_MODUP
+  B2F_LAUNCHED("modup_conv_mma_kernel");
+  return B2F_OK;
+}
+
+int launch_moddown_conv(b2f_context *ctx, const uint64_t *acc, uint64_t *conv,
+                        int l, int cts, cudaStream_t s) {
+  const int K = ctx->K, kp = conv_kpad(K);
+  const size_t sm = conv_mma_smem(kp, l);
+  const dim3 grid(kN / CNB, 2, cts);
+  int rc;
+#define B2F_MODDOWN(KWV)                                                \
+  if ((rc = set_smem(moddown_conv_mma_kernel<KWV>, sm))) return rc;     \
+  moddown_conv_mma_kernel<KWV><<<grid, CNB, sm, s>>>(acc, conv, ctx->d_moddown_bytes, \
+                                                     ctx->d_red79, l, K);
+  if (kp == 32) {
+    B2F_MODDOWN(8)
+  } else if (kp == 64) {
+    B2F_MODDOWN(16)
+  } else {
+    B2F_MODDOWN(32)
+  }
+#undef B2F_MODDOWN
+  B2F_LAUNCHED("moddown_conv_mma_kernel");
+  return B2F_OK;
+}
+
 // Step 3: key inner product.  grid (N/TPB, items, l+K): the slowest grid
 // axis is the target limb, so a key limb shared by a batch, or an ext limb
 // shared by the hoisted rotations of one ciphertext (ext_stride = 0, c1_stride
@@ -299,11 +534,7 @@ int modup(b2f_context *ctx, const uint64_t *c1, long long c1_stride, int cts,
                       T.modup_scale, s);
   if (rc) return rc;
   // 2. base conversion
-  const int tper = conv_split(beta * cts, lk);
-  const int tchunks = (lk + tper - 1) / tper;
-  modup_conv_kernel<<<dim3(kN / TPB, beta * tchunks, cts), TPB, 0, s>>>(
-      xt, ext, T.modup_conv, ctx->d_primes, l, K, ctx->L, alpha, tper);
-  B2F_LAUNCHED("modup_conv_kernel");
+  if ((rc = launch_modup_conv(ctx, xt, ext, l, cts, s))) return rc;
   // 3. NTT of the converted limbs
   std::vector<LimbJob> fj;
   for (int j = 0; j < beta; ++j) {
@@ -346,11 +577,7 @@ int ip_moddown(b2f_context *ctx, const uint64_t *c1, long long c1_stride,
   int rc = launch_ntt(ctx, acc, as, acc, as, d, 2 * K, cts, 1,
                       ctx->d_moddown_scale, s);
   if (rc) return rc;
-  const int tper = conv_split(2 * cts, l);
-  moddown_conv_kernel<<<dim3(kN / TPB, 2 * ((l + tper - 1) / tper), cts), TPB, 0,
-                        s>>>(acc, conv, ctx->d_moddown_conv, ctx->d_primes, l, K,
-                             tper);
-  B2F_LAUNCHED("moddown_conv_kernel");
+  if ((rc = launch_moddown_conv(ctx, acc, conv, l, cts, s))) return rc;
   rc = ntt_polys(ctx, conv, 2 * cts, l, 0, 0, s);
   if (rc) return rc;
   moddown_combine_kernel<<<dim3(kN / TPB, l, cts), TPB, 0, s>>>(
@@ -630,11 +857,7 @@ int b2f_moddown_ext(b2f_context *ctx, const uint64_t *in, int num_cts, int l,
   if ((rc = launch_ntt(ctx, in, as, pcoef, as, d, 2 * K, num_cts, 1,
                        ctx->d_moddown_scale, s)))
     return rc;
-  const int tper = conv_split(2 * num_cts, l);
-  moddown_conv_kernel<<<dim3(kN / TPB, 2 * ((l + tper - 1) / tper), num_cts), TPB,
-                        0, s>>>(pcoef, conv, ctx->d_moddown_conv, ctx->d_primes,
-                                l, K, tper);
-  B2F_LAUNCHED("moddown_conv_kernel");
+  if ((rc = launch_moddown_conv(ctx, pcoef, conv, l, num_cts, s))) return rc;
   if ((rc = ntt_polys(ctx, conv, 2 * num_cts, l, 0, 0, s))) return rc;
   moddown_combine_kernel<<<dim3(kN / TPB, l, num_cts), TPB, 0, s>>>(
       in, conv, nullptr, nullptr, 0, out, 2LL * l * kN, ctx->d_moddown_pinv,
