@@ -12,7 +12,10 @@ Chen-Chillotti-Song 2019 ordering):
   0. pre-scale: multiply by 2^-k and rescale (the input carries at least two
      limbs), so the message part of t / q_0 is at most 2^-(k+1);
   1. ModRaise: drop to q_0 and lift the coefficients to all L primes:
-     t = Delta u 2^-k + q_0 I;
+     t = Delta u 2^-k + q_0 I; a sparse message (n = 2^log_slots < N/2 slots,
+     coefficients on Z[X^gap], gap = N / 2n) is then projected back onto
+     that subring by SubSum, t <- t + rot_{n 2^i}(t) for i < log2(gap),
+     which multiplies it by gap (1/gap is folded into step 2);
   2. CoeffToSlot: the encoder's inverse butterfly stages (len = n .. 2)
      merged into level_budget[0] levels, times Delta / (q_0 2 (K+1)): the slots
      hold (t_j + i t_{j+n}) / (2 q_0 (K+1)) in bit-reversed order;
@@ -89,9 +92,8 @@ class _Plan:
 def _check(spec: BootstrapSpec, log_n: int) -> None:
     if str(spec.mode) != "modraise_first":
         raise NotImplementedError(f"bootstrap mode {spec.mode!r} is not implemented")
-    if int(spec.log_slots) != int(log_n) - 1:
-        raise NotImplementedError("only full-slot bootstrapping (log_slots = log_n - 1) "
-                                  "is implemented")
+    if not 1 <= int(spec.log_slots) <= int(log_n) - 1:
+        raise ValueError(f"log_slots {spec.log_slots} outside [1, {int(log_n) - 1}]")
     b1, b2 = (int(v) for v in spec.level_budget)
     if not (1 <= b1 <= spec.log_slots and 1 <= b2 <= spec.log_slots):
         raise ValueError(f"level budget {spec.level_budget} outside [1, log_slots]")
@@ -114,6 +116,7 @@ def requirements(specs, log_n: int) -> Requirements:
     rots = {(2 << int(log_n)) - 1}  # conjugation, index M - 1
     for spec in specs:
         _check(spec, log_n)
+        rots.update(_subsum_rotations(spec, log_n))
         cts, stc = _level_plans(int(log_n), int(spec.log_slots), spec.level_budget)
         slots = 1 << int(spec.log_slots)
         for _, plan in cts + stc:
@@ -121,6 +124,19 @@ def requirements(specs, log_n: int) -> Requirements:
             if len(plan.giants) > 1:
                 rots.add(plan.babies * plan.step)
     return Requirements(tuple(sorted(rots)))
+
+
+def _gap(spec: BootstrapSpec, log_n: int) -> int:
+    """Replication factor of a sparse message: (N/2) / slots."""
+
+    return (1 << (int(log_n) - 1)) // spec.slots
+
+
+def _subsum_rotations(spec: BootstrapSpec, log_n: int) -> list[int]:
+    """Rotations n 2^i (i < log2 gap) of the SubSum of a sparse bootstrap."""
+
+    gap = _gap(spec, log_n)
+    return [spec.slots << i for i in range(gap.bit_length() - 1)]
 
 
 class _Constants:
@@ -201,7 +217,8 @@ def generate(context, spec: BootstrapSpec) -> Program:
                          f"limbs, the program leaves {out_limbs}")
     delta = ctx.scale_at(L)
     q0 = float(ctx.params.q[0])
-    alpha = delta / (q0 * 2.0 * (K_RANGE + 1))
+    # the SubSum of a sparse message multiplies it by the gap (N/2)/slots
+    alpha = delta / (q0 * 2.0 * (K_RANGE + 1) * _gap(spec, ctx.logN))
     beta = q0 * 2.0 ** PRESCALE_BITS / (2.0 * math.pi * delta)
     cts, stc = _level_plans(ctx.logN, int(spec.log_slots), spec.level_budget, alpha, beta)
     slots = spec.slots
@@ -404,6 +421,10 @@ def bootstrap(ct: fhe.Ciphertext, context, program: Program) -> fhe.Ciphertext:
     # read t + q_0 I at the scale the CoeffToSlot factor alpha assumes
     delta = ctx.scale_at(ctx.L)
     y = fhe.Ciphertext(raised, fhe.CipherState(ctx.L, 1, delta), x.slots, ctx)
+    # 1b. sparse messages: SubSum (trace onto Z[X^gap]) keeps the subring
+    # coefficients of t = Delta u 2^-k + q_0 I, times the gap (folded into alpha)
+    for r in _subsum_rotations(spec, ctx.logN):
+        y = fhe.homo_add(y, fhe.homo_rotate(y, r, ctx), ctx)
     # 2. CoeffToSlot
     for level in program.cts:
         y = _linear(y, level, ctx)

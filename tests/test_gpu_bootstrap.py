@@ -104,3 +104,49 @@ def test_meta_bts_two_pass_correction():
     print(f"Meta-BTS: one pass 2^{np.log2(e1):.1f}, two passes 2^{np.log2(e2):.1f}")
     assert e1 < 2.0 ** -17
     assert e2 < 2.0 ** -28  # 2^-35 measured on B200: the correction adds ~16 bits
+
+
+@functools.lru_cache(maxsize=None)
+def _program_context():
+    """One context with the keys of a deep (3, 3) full-slot program and a
+    sparse (slim, 2^7 slots) program (llama3fhe/operators/nonlinear/
+    bootstrap.py:60-85, model.py:49-57)."""
+
+    from easyfhe import fhe
+    from easyfhe.bs import openfhe as bs
+
+    deep = bs.BootstrapSpec(log_slots=15, level_budget=(3, 3), output_levels=21)
+    slim = bs.BootstrapSpec(log_slots=7, level_budget=(4, 4), output_levels=19)
+    rots = bs.requirements((deep, slim), 16).rotations
+    client, ctx = fhe.generate_client_context(
+        fhe.CKKSContextSpec(depth=37, log_n=16, dnum=5, dcrt_bits=59, first_mod=60,
+                            rotations=rots, seed=7), "cuda:0")
+    return client, ctx, bs.generate(ctx, deep), bs.generate(ctx, slim)
+
+
+def test_bootstrap_deep_program():
+    from easyfhe.bs import openfhe as bs
+
+    client, ctx, deep, _ = _program_context()
+    rng = np.random.default_rng(63)
+    z = rng.uniform(-1, 1, ctx.max_slots) + 1j * rng.uniform(-1, 1, ctx.max_slots)
+    out = bs.bootstrap(_encrypt(client, ctx, z, 2), ctx, deep)
+    assert out.state.cur_limbs == 22  # depth 16 at (3, 3): output_levels 21
+    err = np.max(np.abs(client.decrypt_complex(out) - z))
+    print(f"deep (3, 3) bootstrap: max error 2^{np.log2(err):.1f}")
+    assert err < 2.0 ** -17
+
+
+def test_bootstrap_sparse_slots():
+    from easyfhe.bs import openfhe as bs
+
+    client, ctx, _, slim = _program_context()
+    n = slim.spec.slots
+    rng = np.random.default_rng(64)
+    z = rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)
+    ct = client.encrypt(z, slots=n, cur_limbs=2, scaling_factor=ctx.scale_at(2))
+    out = bs.bootstrap(ct, ctx, slim)
+    assert out.slots == n and out.state.cur_limbs == 20
+    err = np.max(np.abs(client.decrypt_complex(out) - z))
+    print(f"sparse (2^7 slots) bootstrap: max error 2^{np.log2(err):.1f}")
+    assert err < 2.0 ** -17
