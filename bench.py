@@ -52,6 +52,9 @@ def parse():
                     help="ntt: only the NTT kernel loop (for profiling); bootstrap: "
                          "BASELINE configs[3]; linear: BASELINE configs[2]")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--per-ct", action="store_true",
+                    help="bootstrap/linear: one ciphertext per call (the reference's "
+                         "calling pattern) instead of one batched call")
     ap.add_argument("--cpu-sample", type=int, default=6,
                     help="rotations timed on the CPU oracle")
     a = ap.parse_args()
@@ -201,7 +204,10 @@ def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) ->
     stream = torch.cuda.current_stream()
 
     def step(inputs):
-        return [bs.bootstrap(c, ctx, program) for c in inputs]
+        if a.per_ct:
+            return [bs.bootstrap(c, ctx, program) for c in inputs]
+        out = bs.bootstrap(fhe.pack_cipher_batch(inputs), ctx, program)
+        return list(fhe.unpack_cipher_batch(out))
 
     for _ in range(a.warmup):
         outs = step(cts)
@@ -252,6 +258,7 @@ def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) ->
                                     f"BootstrapSpec(15, (4, 4), 19), batch={a.batch} "
                                     "ciphertexts/rank at 2 limbs"),
                        "batch_per_rank": a.batch,
+                       "calls": "one per ciphertext" if a.per_ct else "one batched call",
                        "l2": "working set (keys 29 x up to 230 MiB) larger than L2; no flush"},
             "ms_per_bootstrap": ms / a.batch,
             "precision_bits": -math.log2(err) if err > 0 else None,
@@ -327,6 +334,7 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
     stream = torch.cuda.current_stream()
 
     def apply(ct):
+        # LinearOperator.apply's call sequence; ct may be a ciphertext batch
         babies = fhe.prepare_hoisted_baby_rotations(ct, offsets, ctx)
         acc = None
         for (base, count), pt in zip(chunks, pts):
@@ -338,7 +346,9 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
         return fhe.rescale(acc, ctx)
 
     def step(inputs):
-        return [apply(c) for c in inputs]
+        if a.per_ct:
+            return [apply(c) for c in inputs]
+        return list(fhe.unpack_cipher_batch(apply(fhe.pack_cipher_batch(inputs))))
 
     for _ in range(a.warmup):
         outs = step(cts)
@@ -385,11 +395,13 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
         except Exception:
             pass
         hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-        # SURVEY-style algorithmic bytes: every plaintext once per ciphertext
-        # (one hoisted_mac_sum call per ciphertext, as the reference calls it),
-        # babies and outputs once
+        # algorithmic bytes: the plaintext rows once per call (once per
+        # ciphertext when called per ciphertext, as the reference does; once
+        # per batch otherwise), babies and outputs once
         lim = N * 8
-        alg = a.batch * (D * level * lim + B * 2 * level * lim + 2 * level * lim)
+        pt_reads = a.batch if a.per_ct else 1
+        alg = (pt_reads * D * level * lim
+               + a.batch * (B * 2 * level * lim + 2 * level * lim))
         unit = "ciphertexts/s"
         line = {
             "metric": "linear-block ciphertexts/s (QKV-shaped 4096x4096 BSGS, BASELINE configs[2])",
@@ -400,6 +412,7 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
             "config": {"workload": (f"QKV-shaped linear D=4096 l={level} B=64 G=64 in 8 chunks, "
                                     f"{a.batch} token-shard ciphertexts/rank, depth 37 dnum 5"),
                        "batch_per_rank": a.batch,
+                       "calls": "one per ciphertext" if a.per_ct else "one batched call",
                        "l2": "plaintexts 26 GiB > L2; no flush"},
             "pt_x_ct_per_s": world * a.batch * D / (ms / 1e3),
             "encode_rows_per_s": D / encode_s,

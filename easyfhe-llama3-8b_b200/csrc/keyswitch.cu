@@ -25,13 +25,21 @@ constexpr int TPB = 256;
 // With shared != 0 every item uses entry 0 (a batch sharing one key); hoisted
 // rotations of one ciphertext use one entry per rotation.
 constexpr int kMaxItems = 64;
+// In per-item mode item i is rotation i % per of ciphertext i / per (the
+// ciphertext indexes c1, ext and c0; out_ct_stride and pos[] place the result).
 struct ItemKeys {
   const uint64_t *key[kMaxItems];
   uint32_t g[kMaxItems];
-  int16_t pos[kMaxItems];  // output slot of item i (per-item mode only)
+  int16_t pos[kMaxItems];  // output slot of rotation r within its ciphertext
   int shared;
-  __host__ __device__ int at(int i) const { return shared ? 0 : i; }
-  __host__ __device__ int out(int i) const { return shared ? i : pos[i]; }
+  int per = 1;             // rotations per ciphertext (per-item mode)
+  long long out_ct_stride; // words between ciphertexts' outputs (per-item mode)
+  __host__ __device__ int at(int i) const { return shared ? 0 : i % per; }
+  __host__ __device__ int ct(int i) const { return shared ? i : i / per; }
+  __host__ __device__ long long out(int i, long long stride) const {
+    return shared ? (long long)i * stride
+                  : ct(i) * out_ct_stride + (long long)pos[i % per] * stride;
+  }
 };
 
 __device__ __forceinline__ uint32_t brv16(uint32_t x) { return __brev(x) >> 16; }
@@ -340,11 +348,11 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
     uint64_t *__restrict__ acc, const Mod *__restrict__ mods, int l, int K,
     int L, int alpha, int beta) {
   const int n = blockIdx.x * TPB + threadIdx.x;
-  const int ct = blockIdx.y, t = blockIdx.z;
+  const int it = blockIdx.y, t = blockIdx.z, ct = items.ct(it);
   const int lk = l + K, np = L + K;
   const int gp = t < l ? t : L + (t - l);
   const Mod M = mods[gp];
-  const uint64_t *__restrict__ key = items.key[items.at(ct)];
+  const uint64_t *__restrict__ key = items.key[items.at(it)];
   U128 s0 = {0, 0}, s1 = {0, 0};
   // digits in groups of four: all loads of a group are issued before its
   // multiplies, so each thread keeps 12 memory requests in flight
@@ -373,7 +381,7 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
       }
     }
   }
-  uint64_t *o = acc + ((size_t)ct * 2 * lk + t) * kN + n;
+  uint64_t *o = acc + ((size_t)it * 2 * lk + t) * kN + n;
   o[0] = reduce128(s0.hi, s0.lo, M);
   o[(size_t)lk * kN] = reduce128(s1.hi, s1.lo, M);
 }
@@ -421,20 +429,20 @@ __global__ void __launch_bounds__(TPB) moddown_combine_kernel(
     const ulonglong2 *__restrict__ pinv, const uint64_t *__restrict__ primes,
     int l, int K, const ItemKeys items) {
   const int k = blockIdx.x * TPB + threadIdx.x;
-  const int i = blockIdx.y, ct = blockIdx.z;
+  const int i = blockIdx.y, it = blockIdx.z, ct = items.ct(it);
   const int lk = l + K;
-  const uint32_t g = items.g[items.at(ct)];
+  const uint32_t g = items.g[items.at(it)];
   const uint32_t src = g == 1 ? (uint32_t)k : auto_src(k, g);
   const uint64_t q = primes[i];
   const ulonglong2 pi = pinv[i];
 #pragma unroll
   for (int b = 0; b < 2; ++b) {
-    const uint64_t a = acc[(((size_t)ct * 2 + b) * lk + i) * kN + src];
-    const uint64_t c = conv[(((size_t)ct * 2 + b) * l + i) * kN + src];
+    const uint64_t a = acc[(((size_t)it * 2 + b) * lk + i) * kN + src];
+    const uint64_t c = conv[(((size_t)it * 2 + b) * l + i) * kN + src];
     uint64_t v = shoup(sub_mod(a, c, q), pi.x, pi.y, q);
     const uint64_t *add = b ? add1 : add0;
     if (add) v = add_mod(v, add[ct * add_stride + (size_t)i * kN + src], q);
-    out[items.out(ct) * out_stride + ((size_t)b * l + i) * kN + k] = v;
+    out[items.out(it, out_stride) + ((size_t)b * l + i) * kN + k] = v;
   }
 }
 
@@ -692,35 +700,54 @@ int b2f_relinearize(b2f_context *ctx, const uint64_t *ct3_in, uint64_t *ct_out,
                     acc, conv, s);
 }
 
+size_t b2f_modup_batch_workspace(const b2f_context *ctx, int num_cts, int l) {
+  if (!ctx || l < 1 || l > ctx->L || num_cts < 0) return 0;
+  return rnd((size_t)std::max(num_cts, 1) * l * kN);
+}
+
+int b2f_modup_batch(b2f_context *ctx, const uint64_t *ct, int num_cts, int l,
+                    uint64_t *ext, void *ws, size_t ws_bytes, void *stream) {
+  int rc = check_level(ctx, l, "b2f_modup");
+  if (rc) return rc;
+  B2F_CHECK_ARG(ct && ext && num_cts >= 0, "b2f_modup: null argument");
+  if (!num_cts) return B2F_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  Scratch sc{ctx, s};
+  if ((rc = sc.init(ws, ws_bytes, b2f_modup_batch_workspace(ctx, num_cts, l))))
+    return rc;
+  uint64_t *xt = sc.take((size_t)num_cts * l * kN);
+  return modup(ctx, ct + (size_t)l * kN, 2LL * l * kN, num_cts, l, xt, ext, s);
+}
+
 size_t b2f_modup_workspace(const b2f_context *ctx, int l) {
-  if (!ctx || l < 1 || l > ctx->L) return 0;
-  return rnd((size_t)l * kN);
+  return b2f_modup_batch_workspace(ctx, 1, l);
 }
 
 int b2f_modup(b2f_context *ctx, const uint64_t *ct, int l, uint64_t *ext,
               void *ws, size_t ws_bytes, void *stream) {
-  int rc = check_level(ctx, l, "b2f_modup");
-  if (rc) return rc;
-  B2F_CHECK_ARG(ct && ext, "b2f_modup: null argument");
-  cudaStream_t s = (cudaStream_t)stream;
-  Scratch sc{ctx, s};
-  if ((rc = sc.init(ws, ws_bytes, b2f_modup_workspace(ctx, l)))) return rc;
-  uint64_t *xt = sc.take((size_t)l * kN);
-  return modup(ctx, ct + (size_t)l * kN, 2LL * l * kN, 1, l, xt, ext, s);
+  return b2f_modup_batch(ctx, ct, 1, l, ext, ws, ws_bytes, stream);
+}
+
+size_t b2f_rotate_hoisted_batch_workspace(const b2f_context *ctx, int num_cts,
+                                          int count, int l) {
+  if (!ctx || l < 1 || l > ctx->L || count < 0 || num_cts < 0) return 0;
+  const long long items = std::max(1LL, (long long)num_cts * std::max(count, 1));
+  return moddown_bytes(ctx, (int)std::min<long long>(items, kMaxItems), l);
 }
 
 size_t b2f_rotate_hoisted_workspace(const b2f_context *ctx, int count, int l) {
-  if (!ctx || l < 1 || l > ctx->L || count < 0) return 0;
-  return moddown_bytes(ctx, std::max(1, std::min(count, kMaxItems)), l);
+  return b2f_rotate_hoisted_batch_workspace(ctx, 1, count, l);
 }
 
-int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
-                       const uint64_t *ext, int count, const uint64_t *galois,
-                       const uint64_t *const *keys, uint64_t *out, void *ws,
-                       size_t ws_bytes, void *stream) {
+int b2f_rotate_hoisted_batch(b2f_context *ctx, const uint64_t *ct, int num_cts,
+                             int l, const uint64_t *ext, int count,
+                             const uint64_t *galois, const uint64_t *const *keys,
+                             uint64_t *out, void *ws, size_t ws_bytes,
+                             void *stream) {
   int rc = check_level(ctx, l, "b2f_rotate_hoisted");
   if (rc) return rc;
-  B2F_CHECK_ARG(ct && out && count >= 0 && (count == 0 || (galois && keys)),
+  B2F_CHECK_ARG(ct && out && count >= 0 && num_cts >= 0 &&
+                    (count == 0 || (galois && keys)),
                 "b2f_rotate_hoisted: null argument");
   bool need_ext = false;
   for (int r = 0; r < count; ++r) {
@@ -733,40 +760,61 @@ int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
     }
   }
   B2F_CHECK_ARG(!need_ext || ext, "b2f_rotate_hoisted: ModUp digits are null");
+  if (!num_cts || !count) return B2F_OK;
   cudaStream_t s = (cudaStream_t)stream;
   Scratch sc{ctx, s};
-  if ((rc = sc.init(ws, ws_bytes, b2f_rotate_hoisted_workspace(ctx, count, l))))
+  if ((rc = sc.init(ws, ws_bytes,
+                    b2f_rotate_hoisted_batch_workspace(ctx, num_cts, count, l))))
     return rc;
   const int lk = l + ctx->K;
-  const int chunk = std::max(1, std::min(count, kMaxItems));
-  uint64_t *acc = sc.take((size_t)chunk * 2 * lk * kN);
-  uint64_t *conv = sc.take((size_t)chunk * 2 * l * kN);
-  const long long cs = 2LL * l * kN;
-  // identity items are copies; the others go through the key switch in
-  // groups of up to kMaxItems, one launch sequence per group
+  const long long items_max =
+      std::min<long long>((long long)num_cts * count, kMaxItems);
+  uint64_t *acc = sc.take((size_t)items_max * 2 * lk * kN);
+  uint64_t *conv = sc.take((size_t)items_max * 2 * l * kN);
+  const long long cs = 2LL * l * kN;                 // one ciphertext
+  const long long ocs = (long long)count * cs;       // one ciphertext's outputs
+  const long long es = (long long)ctx->levels[l].beta * lk * kN;
+  // identity items are copies; the keyed rotations go through the key switch
+  // in launch groups of up to kMaxItems (rotations x ciphertexts)
   std::vector<int> keyed;
   for (int r = 0; r < count; ++r) {
     if (galois[r] == 1) {
-      B2F_CUDA(cudaMemcpyAsync(out + (size_t)r * cs, ct, cs * 8,
-                               cudaMemcpyDeviceToDevice, s));
+      for (int c = 0; c < num_cts; ++c)
+        B2F_CUDA(cudaMemcpyAsync(out + c * ocs + (size_t)r * cs, ct + c * cs,
+                                 cs * 8, cudaMemcpyDeviceToDevice, s));
     } else {
       keyed.push_back(r);
     }
   }
   for (size_t p = 0; p < keyed.size(); p += kMaxItems) {
-    const int n = (int)std::min<size_t>(kMaxItems, keyed.size() - p);
+    const int R = (int)std::min<size_t>(kMaxItems, keyed.size() - p);
     ItemKeys it{};
     it.shared = 0;
-    for (int i = 0; i < n; ++i) {
+    it.per = R;
+    it.out_ct_stride = ocs;
+    for (int i = 0; i < R; ++i) {
       it.key[i] = keys[keyed[p + i]];
       it.g[i] = (uint32_t)galois[keyed[p + i]];
       it.pos[i] = (int16_t)(keyed[p + i] - keyed[p]);
     }
-    rc = ip_moddown(ctx, ct + (size_t)l * kN, 0, ext, 0, n, l, it, ct, nullptr,
-                    0, out + (size_t)keyed[p] * cs, cs, acc, conv, s);
-    if (rc) return rc;
+    const int group = std::max(1, kMaxItems / R);  // ciphertexts per launch group
+    for (int c0 = 0; c0 < num_cts; c0 += group) {
+      const int nc = std::min(group, num_cts - c0);
+      rc = ip_moddown(ctx, ct + c0 * cs + (size_t)l * kN, cs, ext + c0 * es, es,
+                      nc * R, l, it, ct + c0 * cs, nullptr, cs,
+                      out + c0 * ocs + (size_t)keyed[p] * cs, cs, acc, conv, s);
+      if (rc) return rc;
+    }
   }
   return B2F_OK;
+}
+
+int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
+                       const uint64_t *ext, int count, const uint64_t *galois,
+                       const uint64_t *const *keys, uint64_t *out, void *ws,
+                       size_t ws_bytes, void *stream) {
+  return b2f_rotate_hoisted_batch(ctx, ct, 1, l, ext, count, galois, keys, out,
+                                  ws, ws_bytes, stream);
 }
 
 size_t b2f_rotate_hoisted_ext_workspace(const b2f_context *ctx, int count, int l) {
@@ -815,6 +863,8 @@ int b2f_rotate_hoisted_ext(b2f_context *ctx, const uint64_t *ct, int l,
       }
     }
     if (keyed) {
+      it.shared = 0;
+      it.per = keyed;  // one ciphertext: item i is keyed rotation i
       key_inner_product_kernel<<<dim3(kN / TPB, keyed, lk), TPB, 0, s>>>(
           ct + (size_t)l * kN, 0, ext, 0, it, acc, ctx->d_mod, l, K, ctx->L,
           ctx->alpha, T.beta);

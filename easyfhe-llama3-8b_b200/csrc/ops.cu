@@ -137,17 +137,20 @@ __global__ void __launch_bounds__(TPB) scalar_kernel(
   out[idx] = r;
 }
 
-// out[ct][g] (2 polys, l limbs) = sum_b pt[g0+g][b] * babies[ct][b]
-// grid (N/TPB, l, cts); up to GMAX giants per launch.  The plaintext rows are
-// read once and dominate the traffic, so the babies are taken two at a time
-// with every load of the pair issued before its multiplies.
+// out[ct][g] (2 polys, l limbs; giant-major [g][ct] when giant_major) =
+// sum_b pt[g0+g][b] * babies[ct][b].  grid (cts, N/TPB, l): the ciphertexts
+// of a batch are the fastest grid axis, so they read each plaintext tile
+// while it is in L2 and the plaintext rows stream from HBM once per batch.
+// Up to GMAX giants per launch; babies are taken two at a time with every
+// load of the pair issued before its multiplies.
 __global__ void __launch_bounds__(TPB) mac_kernel(
     const uint64_t *__restrict__ babies, int baby_count,
     const uint64_t *__restrict__ pts, int g0, int G, int l,
-    uint64_t *__restrict__ out, int out_giants, const Mod *__restrict__ mods) {
+    uint64_t *__restrict__ out, int out_giants, int giant_major,
+    const Mod *__restrict__ mods) {
   constexpr int BU = 2;
-  const int n = blockIdx.x * TPB + threadIdx.x;
-  const int i = blockIdx.y, ct = blockIdx.z;
+  const int n = blockIdx.y * TPB + threadIdx.x;
+  const int i = blockIdx.z, ct = blockIdx.x, cts = gridDim.x;
   const Mod M = mods[i];
   const size_t limb = (size_t)i * kN + n;
   const size_t ct_words = 2 * (size_t)l * kN, pt_words = (size_t)l * kN;
@@ -190,12 +193,14 @@ __global__ void __launch_bounds__(TPB) mac_kernel(
         }
     }
   }
-  uint64_t *o = out + ((size_t)ct * out_giants + g0) * ct_words + limb;
 #pragma unroll
   for (int g = 0; g < GMAX; ++g)
     if (g < G) {
-      o[(size_t)g * ct_words] = reduce128(acc[g][0].hi, acc[g][0].lo, M);
-      o[(size_t)g * ct_words + pt_words] = reduce128(acc[g][1].hi, acc[g][1].lo, M);
+      const size_t slot = giant_major ? (size_t)(g0 + g) * cts + ct
+                                      : (size_t)ct * out_giants + g0 + g;
+      uint64_t *o = out + slot * ct_words + limb;
+      o[0] = reduce128(acc[g][0].hi, acc[g][0].lo, M);
+      o[pt_words] = reduce128(acc[g][1].hi, acc[g][1].lo, M);
     }
 }
 
@@ -229,11 +234,12 @@ __global__ void __launch_bounds__(TPB) pairwise_mac_kernel(
 
 int launch_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
                const uint64_t *pts, int giant_count, int l, uint64_t *out,
-               int cts, cudaStream_t s) {
+               int cts, cudaStream_t s, int giant_major = 0) {
   for (int g0 = 0; g0 < giant_count; g0 += GMAX) {
     const int G = std::min(GMAX, giant_count - g0);
-    mac_kernel<<<dim3(kN / TPB, l, cts), TPB, 0, s>>>(
-        babies, baby_count, pts, g0, G, l, out, giant_count, ctx->d_mod);
+    mac_kernel<<<dim3(cts, kN / TPB, l), TPB, 0, s>>>(
+        babies, baby_count, pts, g0, G, l, out, giant_count, giant_major,
+        ctx->d_mod);
     B2F_LAUNCHED("mac_kernel");
   }
   return B2F_OK;
@@ -424,25 +430,34 @@ int b2f_pairwise_mac(b2f_context *ctx, const uint64_t *cts, const uint64_t *pts,
   return B2F_OK;
 }
 
-size_t b2f_bsgs_mac_workspace(const b2f_context *ctx, int l) {
-  if (!ctx || l < 1 || l > ctx->L) return 0;
-  // inner results for up to 64 giants + accumulator + rotated + rotate scratch
-  return 0;  // computed per call from giant_count; see b2f_bsgs_mac
+size_t b2f_bsgs_mac_batch_workspace(const b2f_context *ctx, int num_cts,
+                                    int giant_count, int l) {
+  if (!ctx || l < 1 || l > ctx->L || num_cts < 0 || giant_count < 1) return 0;
+  const size_t ct_words = 2 * (size_t)l * kN * std::max(num_cts, 1);
+  return (giant_count + 1) * ct_words * 8 + rotate_workspace(ctx, num_cts, l) + 512;
 }
 
-int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
-                 const uint64_t *pts, int giant_count, int l,
-                 uint64_t giant_galois, const uint64_t *giant_key,
-                 uint64_t *out, void *ws, size_t ws_bytes, void *stream) {
+size_t b2f_bsgs_mac_workspace(const b2f_context *ctx, int l) {
+  if (!ctx || l < 1 || l > ctx->L) return 0;
+  return 0;  // depends on giant_count: b2f_bsgs_mac_batch_workspace
+}
+
+int b2f_bsgs_mac_batch(b2f_context *ctx, const uint64_t *babies, int num_cts,
+                       int baby_count, const uint64_t *pts, int giant_count,
+                       int l, uint64_t giant_galois, const uint64_t *giant_key,
+                       uint64_t *out, void *ws, size_t ws_bytes, void *stream) {
   B2F_CHECK_ARG(ctx && babies && pts && out, "b2f_bsgs_mac: null argument");
   B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_bsgs_mac: bad limbs %d", l);
-  B2F_CHECK_ARG(baby_count >= 1 && giant_count >= 1, "b2f_bsgs_mac: bad counts");
+  B2F_CHECK_ARG(baby_count >= 1 && giant_count >= 1 && num_cts >= 0,
+                "b2f_bsgs_mac: bad counts");
   B2F_CHECK_ARG(giant_count == 1 || giant_key,
                 "b2f_bsgs_mac: giant_count > 1 needs the giant rotation key");
+  if (!num_cts) return B2F_OK;
   cudaStream_t s = (cudaStream_t)stream;
   const size_t ct_words = 2 * (size_t)l * kN;
-  const size_t rot_ws = rotate_workspace(ctx, 1, l);
-  const size_t need = (giant_count + 1) * ct_words * 8 + rot_ws + 512;
+  const size_t batch_words = ct_words * num_cts;
+  const size_t rot_ws = rotate_workspace(ctx, num_cts, l);
+  const size_t need = b2f_bsgs_mac_batch_workspace(ctx, num_cts, giant_count, l);
   void *owned = nullptr;
   if (!ws) {
     B2F_CUDA(cudaMallocAsync(&owned, need, s));
@@ -451,26 +466,38 @@ int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
     B2F_CHECK_ARG(ws_bytes >= need, "b2f_bsgs_mac: workspace %zu < %zu", ws_bytes,
                   need);
   }
+  // inner[g] (all ciphertexts of giant g contiguous), then a rotation buffer
   uint64_t *inner = static_cast<uint64_t *>(ws);
-  uint64_t *rot = inner + giant_count * ct_words;
-  void *rws = rot + ct_words;
-  int rc = launch_mac(ctx, babies, baby_count, pts, giant_count, l, inner, 1, s);
+  uint64_t *rot = inner + giant_count * batch_words;
+  void *rws = rot + batch_words;
+  int rc = launch_mac(ctx, babies, baby_count, pts, giant_count, l, inner, num_cts,
+                      s, 1);
   if (!rc && giant_count == 1) {
-    cudaError_t e = cudaMemcpyAsync(out, inner, ct_words * 8,
+    cudaError_t e = cudaMemcpyAsync(out, inner, batch_words * 8,
                                     cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) rc = cuda_status(e, "b2f_bsgs_mac copy");
   }
   // Horner over the giants: acc = inner[G-1]; acc = rot(acc) + inner[g]
-  const uint64_t *acc = inner + (size_t)(giant_count - 1) * ct_words;
+  const uint64_t *acc = inner + (size_t)(giant_count - 1) * batch_words;
   for (int g = giant_count - 2; !rc && g >= 0; --g) {
-    rc = b2f_rotate(ctx, acc, rot, 1, l, giant_galois, giant_key, rws, rot_ws, s);
+    rc = b2f_rotate(ctx, acc, rot, num_cts, l, giant_galois, giant_key, rws, rot_ws,
+                    s);
     if (rc) break;
-    uint64_t *dst = g == 0 ? out : inner + (size_t)(g + 1) * ct_words;
-    rc = b2f_elementwise(ctx, 0, rot, inner + (size_t)g * ct_words, dst, 2, l, 2, s);
+    uint64_t *dst = g == 0 ? out : inner + (size_t)(g + 1) * batch_words;
+    rc = b2f_elementwise(ctx, 0, rot, inner + (size_t)g * batch_words, dst,
+                         2 * num_cts, l, 2 * num_cts, s);
     acc = dst;
   }
   if (owned) cudaFreeAsync(owned, s);
   return rc;
+}
+
+int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
+                 const uint64_t *pts, int giant_count, int l,
+                 uint64_t giant_galois, const uint64_t *giant_key,
+                 uint64_t *out, void *ws, size_t ws_bytes, void *stream) {
+  return b2f_bsgs_mac_batch(ctx, babies, 1, baby_count, pts, giant_count, l,
+                            giant_galois, giant_key, out, ws, ws_bytes, stream);
 }
 
 }  // extern "C"

@@ -66,6 +66,14 @@ _SIGS = {
     "b2f_mul_i": (_int, [_vp, _vp, _vp, _int, _int, _int, _vp]),
     "b2f_scalar_op": (_int, [_vp, _vp, _vp, _int, _int, _vp, _vp, _int, _vp]),
     "b2f_tensor": (_int, [_vp, _vp, _vp, _vp, _int, _int, _vp]),
+    "b2f_modup_batch_workspace": (_size, [_vp, _int, _int]),
+    "b2f_modup_batch": (_int, [_vp, _vp, _int, _int, _vp, _vp, _size, _vp]),
+    "b2f_rotate_hoisted_batch_workspace": (_size, [_vp, _int, _int, _int]),
+    "b2f_rotate_hoisted_batch": (_int, [_vp, _vp, _int, _int, _vp, _int, _vp, _vp, _vp,
+                                        _vp, _size, _vp]),
+    "b2f_bsgs_mac_batch_workspace": (_size, [_vp, _int, _int, _int]),
+    "b2f_bsgs_mac_batch": (_int, [_vp, _vp, _int, _int, _vp, _int, _int, _u64, _vp, _vp,
+                                  _vp, _size, _vp]),
     "b2f_bsgs_mac_workspace": (_size, [_vp, _int]),
     "b2f_bsgs_mac": (_int, [_vp, _vp, _int, _vp, _int, _int, _u64, _vp, _vp, _vp, _size,
                             _vp]),

@@ -403,6 +403,7 @@ def bootstrap(ct: fhe.Ciphertext, context, program: Program) -> fhe.Ciphertext:
 
     ctx = fhe._ctx_of(context)
     spec = program.spec
+    C = ct.batch_size  # a ciphertext batch goes through every step together
     if int(ct.slots) != spec.slots:
         raise ValueError(f"bootstrap input slots={ct.slots}, program slots={spec.slots}")
     if int(ct.state.scale_degree) != 1 or ct.is_ext or ct.polys != 2:
@@ -417,7 +418,8 @@ def bootstrap(ct: fhe.Ciphertext, context, program: Program) -> fhe.Ciphertext:
     x = fhe.rescale(fhe.homo_mul_scalar(ct, enc, ctx), ctx)
     x = fhe.align_to(x, x.state.replace(cur_limbs=1), ctx)
     # 1. ModRaise to all limbs
-    raised = ctx.native.modraise(x.data, 2, ctx.L).view(2, ctx.L, -1)
+    raised = ctx.native.modraise(x.data, 2 * C, ctx.L)
+    raised = raised.view((2, ctx.L, -1) if x.data.dim() == 3 else (C, 2, ctx.L, -1))
     # read t + q_0 I at the scale the CoeffToSlot factor alpha assumes
     delta = ctx.scale_at(ctx.L)
     y = fhe.Ciphertext(raised, fhe.CipherState(ctx.L, 1, delta), x.slots, ctx)
@@ -432,9 +434,11 @@ def bootstrap(ct: fhe.Ciphertext, context, program: Program) -> fhe.Ciphertext:
     conj = fhe.homo_rotate(y, ctx.M - 1, ctx)
     x_re = fhe.homo_add(y, conj, ctx)
     x_im = fhe.homo_mul_i(fhe.homo_sub(y, conj, ctx), ctx, negative=True)
-    # 4. EvalMod on both parts as one batch of two ciphertexts
+    # 4. EvalMod on both parts as one batch (real parts, then imaginary parts)
     both = _evalmod(fhe.pack_cipher_batch((x_re, x_im)), program.cheb, delta, ctx)
-    s_re, s_im = fhe.unpack_cipher_batch(both)
+    halves = both.data.view((2, C) + tuple(both.data.shape[-3:]))
+    s_re, s_im = (fhe.Ciphertext(h if C > 1 else h[0], both.state, both.slots, ctx)
+                  for h in halves)
     # 5. recombine and SlotToCoeff
     z = fhe.homo_add(s_re, fhe.homo_mul_i(s_im, ctx), ctx)
     for level in program.stc:

@@ -220,24 +220,33 @@ class NativeContext:
              _ptr(ws), ws.numel(), _stream())
         return out
 
-    def modup(self, ct: torch.Tensor, l: int) -> torch.Tensor:
+    def modup(self, ct: torch.Tensor, l: int, num_cts: int = 1) -> torch.Tensor:
+        """ModUp digits of c1: [beta, l+K, N] (one ciphertext) or
+        [num_cts, beta, l+K, N]."""
+
         beta = -(-l // self.alpha)
-        ext = self.empty(beta, l + self.K)
-        ws = self.workspace(lib.b2f_modup_workspace(self.handle, l))
-        call("b2f_modup", self.handle, _ptr(ct), l, _ptr(ext), _ptr(ws), ws.numel(),
-             _stream())
+        ext = self.empty(beta, l + self.K) if num_cts == 1 else \
+            self.empty(num_cts * beta, l + self.K).view(num_cts, beta, l + self.K, self.n)
+        ws = self.workspace(lib.b2f_modup_batch_workspace(self.handle, num_cts, l))
+        call("b2f_modup_batch", self.handle, _ptr(ct), num_cts, l, _ptr(ext), _ptr(ws),
+             ws.numel(), _stream())
         return ext
 
     def rotate_hoisted(self, ct: torch.Tensor, l: int, ext: torch.Tensor, galois, keys,
-                       out: torch.Tensor | None = None) -> torch.Tensor:
+                       out: torch.Tensor | None = None, num_cts: int = 1) -> torch.Tensor:
+        """Hoisted rotations: [count, 2, l, N] (one ciphertext) or
+        [num_cts, count, 2, l, N]."""
+
         count = len(galois)
         if out is None:
-            out = self.empty(count, 2, l)
+            out = self.empty(count, 2, l) if num_cts == 1 else \
+                self.empty(num_cts * count, 2, l).view(num_cts, count, 2, l, self.n)
         g = (ctypes.c_uint64 * max(count, 1))(*[int(v) for v in galois])
         kp = (ctypes.c_void_p * max(count, 1))(*[_ptr(k) if k is not None else None
                                                   for k in keys])
-        ws = self.workspace(lib.b2f_rotate_hoisted_workspace(self.handle, count, l))
-        call("b2f_rotate_hoisted", self.handle, _ptr(ct), l,
+        ws = self.workspace(lib.b2f_rotate_hoisted_batch_workspace(self.handle, num_cts,
+                                                                   count, l))
+        call("b2f_rotate_hoisted_batch", self.handle, _ptr(ct), num_cts, l,
              _ptr(ext) if ext is not None else None, count, g, kp,
              _ptr(out), _ptr(ws), ws.numel(), _stream())
         return out
@@ -326,11 +335,17 @@ class NativeContext:
 
     def bsgs_mac(self, babies: torch.Tensor, baby_count: int, pts: torch.Tensor,
                  giant_count: int, l: int, giant_galois: int,
-                 giant_key: torch.Tensor | None) -> torch.Tensor:
-        out = self.empty(2, l)
-        call("b2f_bsgs_mac", self.handle, _ptr(babies), baby_count, _ptr(pts), giant_count, l,
-             int(giant_galois), _ptr(giant_key) if giant_key is not None else None, _ptr(out),
-             None, 0, _stream())
+                 giant_key: torch.Tensor | None, num_cts: int = 1) -> torch.Tensor:
+        """[2, l, N] (one ciphertext) or [num_cts, 2, l, N]."""
+
+        out = self.empty(2, l) if num_cts == 1 else \
+            self.empty(num_cts * 2, l).view(num_cts, 2, l, self.n)
+        ws = self.workspace(lib.b2f_bsgs_mac_batch_workspace(self.handle, num_cts,
+                                                             giant_count, l))
+        call("b2f_bsgs_mac_batch", self.handle, _ptr(babies), num_cts, baby_count, _ptr(pts),
+             giant_count, l, int(giant_galois),
+             _ptr(giant_key) if giant_key is not None else None, _ptr(out), _ptr(ws),
+             ws.numel(), _stream())
         return out
 
     def pack_diagonals(self, weight: torch.Tensor, dimension: int, token_lanes: int,

@@ -597,10 +597,12 @@ def homo_mul_relin_rescale_postop(left: Ciphertext, right: Ciphertext, context,
 
 class BabyRotations(tuple):
     """Hoisted baby rotations of one ciphertext: block 0 is a Ciphertext batch
-    [B, 2, l, N] (baby b = rotation by baby_offsets[b]); iterable like the
+    [B, 2, l, N] (baby b = rotation by baby_offsets[b]); for a batch of C
+    ciphertexts it is [C * B, 2, l, N], ciphertext-major.  Iterable like the
     reference's block tuple (llama3fhe/operators/linear/operator.py:119-122)."""
 
     offsets: tuple[int, ...] = ()
+    cts: int = 1
 
 
 def prepare_hoisted_baby_rotations(ct: Ciphertext, baby_offsets, context,
@@ -618,11 +620,15 @@ def prepare_hoisted_baby_rotations(ct: Ciphertext, baby_offsets, context,
         g = galois_element(off, ctx.logN)
         gal.append(g)
         keys.append(None if g == 1 else ctx.rotation_key(off)[1])
-    ext = nat.modup(ct.data, l) if any(g != 1 for g in gal) else None
-    out = nat.rotate_hoisted(ct.data, l, ext, gal, keys)
-    block = Ciphertext(out, ct.state, ct.slots, ctx)
+    C = ct.batch_size
+    ext = nat.modup(ct.data, l, C) if any(g != 1 for g in gal) else None
+    out = nat.rotate_hoisted(ct.data, l, ext, gal, keys, num_cts=C)
+    # a ciphertext batch keeps its babies ciphertext-major: [C * B, 2, l, N]
+    block = Ciphertext(out.reshape(-1, 2, l, out.shape[-1]) if C > 1 else out, ct.state,
+                       ct.slots, ctx)
     babies = BabyRotations((block,))
     babies.offsets = offsets
+    babies.cts = C
     return babies
 
 
@@ -644,6 +650,10 @@ def hoisted_mac_sum(ct: Ciphertext, baby_offsets, plaintexts: Plaintext, giant_o
     block = tuple(baby_rotations)[0]
     if int(block.state.cur_limbs) != l:
         raise ValueError("baby rotations were prepared at a different level")
+    C = ct.batch_size
+    if block.batch_size != C * B:
+        raise ValueError(f"{block.batch_size} baby rotations for {C} ciphertexts x {B} "
+                         "offsets")
     if plaintexts.rows < G * B:
         raise ValueError(f"{plaintexts.rows} plaintext rows < giants*babies = {G * B}")
     pts = plaintexts.q_part(l)
@@ -651,7 +661,7 @@ def hoisted_mac_sum(ct: Ciphertext, baby_offsets, plaintexts: Plaintext, giant_o
         gg, gkey = ctx.rotation_key(int(giant_offset))
     else:
         gg, gkey = 1, None
-    out = ctx.native.bsgs_mac(block.data, B, pts, G, l, gg, gkey)
+    out = ctx.native.bsgs_mac(block.data, B, pts, G, l, gg, gkey, num_cts=C)
     state = ct.state.replace(
         scale_degree=int(ct.state.scale_degree) + int(plaintexts.state.scale_degree),
         scaling_factor=float(ct.state.scaling_factor) * float(plaintexts.state.scaling_factor))
@@ -811,8 +821,9 @@ def pack_cipher_batch(items: Iterable[Ciphertext]) -> Ciphertext:
     for it in items:
         if it.data.shape[-2:] != first.data.shape[-2:] or it.is_ext != first.is_ext:
             raise ValueError("pack_cipher_batch: items differ in limbs or basis")
-    data = torch.stack([it.data if it.data.dim() == 3 else it.data.squeeze(0)
-                        for it in items]).contiguous()
+    shape = tuple(first.data.shape[-3:])
+    # items may themselves be batches: they are concatenated ciphertext-wise
+    data = torch.cat([it.data.reshape((-1,) + shape) for it in items]).contiguous()
     return Ciphertext(data, first.state, first.slots, first.context, first.is_ext)
 
 

@@ -115,6 +115,24 @@ int b2f_rotate_hoisted(b2f_context *ctx, const uint64_t *ct, int l,
                        const uint64_t *const *keys, uint64_t *out, void *ws,
                        size_t ws_bytes, void *stream);
 
+/* The same for a batch of num_cts ciphertexts (ct [num_cts][2][l][N]): the
+ * ModUp digits are ext [num_cts][beta][l+K][N] and the rotations out
+ * [num_cts][count][2][l][N]; all ciphertexts x keyed rotations run in launch
+ * groups of up to 64, so a batch fills the GPU with one ModUp, one inner
+ * product and one ModDown per group.  Serves prepare_hoisted_baby_rotations /
+ * hoisted_mac_sum on a ciphertext batch (fhe.pack_cipher_batch) and the
+ * bootstrapping transforms of several ciphertexts. */
+size_t b2f_modup_batch_workspace(const b2f_context *ctx, int num_cts, int l);
+int b2f_modup_batch(b2f_context *ctx, const uint64_t *ct, int num_cts, int l,
+                    uint64_t *ext, void *ws, size_t ws_bytes, void *stream);
+size_t b2f_rotate_hoisted_batch_workspace(const b2f_context *ctx, int num_cts,
+                                          int count, int l);
+int b2f_rotate_hoisted_batch(b2f_context *ctx, const uint64_t *ct, int num_cts,
+                             int l, const uint64_t *ext, int count,
+                             const uint64_t *galois, const uint64_t *const *keys,
+                             uint64_t *out, void *ws, size_t ws_bytes,
+                             void *stream);
+
 /* Hoisted rotations left in the extended basis (double hoisting): out[r]
  * (2 polys x (l+K) limbs, Q limbs then P limbs) = (pi_g(P c0 + acc0),
  * pi_g(acc1)), P times the rotation before ModDown; galois 1 gives (P c0,
@@ -198,6 +216,16 @@ int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
                  const uint64_t *pts, int giant_count, int l,
                  uint64_t giant_galois, const uint64_t *giant_key,
                  uint64_t *out, void *ws, size_t ws_bytes, void *stream);
+/* b2f_bsgs_mac for num_cts ciphertexts sharing the plaintext rows: babies
+ * [num_cts][baby_count][2][l][N] -> out [num_cts][2][l][N]; every plaintext
+ * row streams from HBM once per batch and each giant rotation of the Horner
+ * chain is one batched HRotate. */
+size_t b2f_bsgs_mac_batch_workspace(const b2f_context *ctx, int num_cts,
+                                    int giant_count, int l);
+int b2f_bsgs_mac_batch(b2f_context *ctx, const uint64_t *babies, int num_cts,
+                       int baby_count, const uint64_t *pts, int giant_count,
+                       int l, uint64_t giant_galois, const uint64_t *giant_key,
+                       uint64_t *out, void *ws, size_t ws_bytes, void *stream);
 /* out[g] = sum_{i in group g} ct[i] * pt[i] over q_limbs Q limbs and p_limbs
  * P limbs (extended ciphertexts and plaintexts), count pairs split into
  * `groups` consecutive groups; plaintext rows are pt_limb_stride limbs apart.

@@ -150,3 +150,24 @@ def test_bootstrap_sparse_slots():
     err = np.max(np.abs(client.decrypt_complex(out) - z))
     print(f"sparse (2^7 slots) bootstrap: max error 2^{np.log2(err):.1f}")
     assert err < 2.0 ** -17
+
+
+def test_bootstrap_batch_matches_single():
+    """Two ciphertexts bootstrapped as one batch equal the two bootstraps
+    one at a time, bit for bit (every step is exact integer arithmetic on
+    the same constants)."""
+
+    from easyfhe import fhe
+    from easyfhe.bs import openfhe as bs
+
+    client, ctx, program = _layer_context()
+    rng = np.random.default_rng(65)
+    zs = [rng.uniform(-1, 1, ctx.max_slots) + 1j * rng.uniform(-1, 1, ctx.max_slots)
+          for _ in range(2)]
+    cts = [_encrypt(client, ctx, z, 2) for z in zs]
+    batch = bs.bootstrap(fhe.pack_cipher_batch(cts), ctx, program)
+    assert batch.batch_size == 2
+    for i, c in enumerate(cts):
+        one = bs.bootstrap(c, ctx, program)
+        assert np.array_equal(to_host(batch.data[i]), to_host(one.data)), f"ct {i}"
+        assert batch.state == one.state
