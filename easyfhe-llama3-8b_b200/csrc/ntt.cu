@@ -12,7 +12,9 @@
 //      memory (radix-16 per thread, 512 threads x 16 words, two CTAs per
 //      SM); the second and third passes of a warp touch only its own
 //      512-word segment, so they exchange data under __syncwarp; the last
-//      stage pairs neighbouring words across lanes tid, tid^1 (shuffle);
+//      stage pairs neighbouring words across lanes tid, tid^1: of each two
+//      butterflies the even lane computes one and the odd lane the other,
+//      with one shuffle in and one out, so no product is computed twice;
 //   4. each warp stages its segment through shared memory and writes it
 //      with 16-byte coalesced stores.
 // The inverse (Gentleman-Sande, bit-reversed in, natural out) runs the same
@@ -20,7 +22,10 @@
 // the final stage.  Butterflies use Harvey's lazy reduction: forward values
 // live in [0, 4q), inverse values in [0, 2q), outputs are fully reduced.
 // Shared memory holds the block with two pad words per 32 so that every
-// pass is free of bank conflicts.
+// pass is free of bank conflicts.  Stages outside the register passes apply
+// one twiddle to both columns before loading the next and the cluster
+// exchange uses 32-bit shared::cluster addresses, which keeps the
+// 64-register budget of two CTAs per SM nearly free of spills.
 #include <cooperative_groups.h>
 
 #include "b2f_internal.h"
@@ -155,29 +160,46 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     x[8 + k] = v.y;
   }
   {
-    const ulonglong2 w1 = ldtw(tw, 1), w2 = ldtw(tw, 2), w3 = ldtw(tw, 3);
+    // stage by stage over both columns, one twiddle live at a time
+    {
+      const ulonglong2 w = ldtw(tw, 1);
 #pragma unroll
-    for (int h = 0; h < 16; h += 8) {
+      for (int h = 0; h < 16; h += 8)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) ct_bfly(x[h + k], x[h + k + 4], w1, q, q2);
-      ct_bfly(x[h + 0], x[h + 2], w2, q, q2);
-      ct_bfly(x[h + 1], x[h + 3], w2, q, q2);
-      ct_bfly(x[h + 4], x[h + 6], w3, q, q2);
-      ct_bfly(x[h + 5], x[h + 7], w3, q, q2);
+        for (int k = 0; k < 4; ++k) ct_bfly(x[h + k], x[h + k + 4], w, q, q2);
+    }
 #pragma unroll
-      for (int k = 0; k < 8; k += 2)
-        ct_bfly(x[h + k], x[h + k + 1], ldtw(tw, 4 + k / 2), q, q2);
+    for (int m = 0; m < 2; ++m) {
+      const ulonglong2 w = ldtw(tw, 2 + m);
+#pragma unroll
+      for (int h = 0; h < 16; h += 8) {
+        ct_bfly(x[h + 4 * m], x[h + 4 * m + 2], w, q, q2);
+        ct_bfly(x[h + 4 * m + 1], x[h + 4 * m + 3], w, q, q2);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      const ulonglong2 w = ldtw(tw, 4 + k / 2);
+#pragma unroll
+      for (int h = 0; h < 16; h += 8) ct_bfly(x[h + k], x[h + k + 1], w, q, q2);
     }
   }
   // every CTA of the cluster is resident before its shared memory is written;
   // nothing needs publishing yet, so the arrive is relaxed
   asm volatile("barrier.cluster.arrive.relaxed.aligned;\n"
                "barrier.cluster.wait.aligned;\n" ::: "memory");
-  // row k of every column belongs to block k
+  // row k of every column belongs to block k (32-bit cluster addresses)
+  {
+    const uint32_t local = (uint32_t)__cvta_generic_to_shared(buf + pad(c0));
 #pragma unroll
-  for (int k = 0; k < 8; ++k)
-    *reinterpret_cast<ulonglong2 *>(cluster.map_shared_rank(buf, k) + pad(c0)) =
-        make_ulonglong2(x[k], x[8 + k]);
+    for (int k = 0; k < 8; ++k) {
+      uint32_t remote;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(k));
+      asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};" ::"r"(remote), "l"(x[k]),
+                   "l"(x[8 + k])
+                   : "memory");
+    }
+  }
   cluster.sync();
 
   const int jb = rank * BLK;
@@ -195,17 +217,27 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   ct_pass(x, tw, 11, jb + lc, 2, q, q2);
   const bool odd = tid & 1;
   const int je = jb + (tid >> 1) * 32;
+  // butterflies k (even lane) and k+1 (odd lane) of each pair: one
+  // exchange brings each lane the operand it lacks, one sends back the half
+  // of the result the other lane owns, and no product is computed twice
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const uint64_t mine = x[k];
-    const uint64_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
-    const uint64_t X = odd ? other : mine, Y = odd ? mine : other;
-    const ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * k));
+  for (int k = 0; k < 16; k += 2) {
+    // even lane holds X_k, X_{k+1}; odd lane holds Y_k, Y_{k+1}
+    const uint64_t give = odd ? x[k] : x[k + 1];
+    const uint64_t got = __shfl_xor_sync(0xffffffffu, give, 1);
+    const uint64_t X = odd ? got : x[k], Y = odd ? x[k + 1] : got;
+    const ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * (k + (odd ? 1 : 0))));
     const uint64_t u = X >= q2 ? X - q2 : X;
     const uint64_t t = Y * w.x - __umul64hi(Y, w.y) * q;
-    uint64_t r = odd ? u - t + q2 : u + t;
-    r = r >= q2 ? r - q2 : r;
-    x[k] = r >= q ? r - q : r;
+    uint64_t a = u + t, b = u - t + q2;  // outputs of this lane's butterfly
+    a = a >= q2 ? a - q2 : a;
+    a = a >= q ? a - q : a;
+    b = b >= q2 ? b - q2 : b;
+    b = b >= q ? b - q : b;
+    // even lane keeps a = X'_k and sends b = Y'_k; odd keeps b = Y'_{k+1}, sends a
+    const uint64_t back = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
+    x[k] = odd ? back : a;       // even: X'_k;  odd: Y'_k (from even)
+    x[k + 1] = odd ? b : back;   // even: X'_{k+1} (from odd);  odd: Y'_{k+1}
   }
   // each lane rewrites the words it read in pass C, then the warp writes its
   // 512-word segment with coalesced 16-byte stores
@@ -286,24 +318,36 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     x[k] = v.x;
     x[8 + k] = v.y;
   }
-  const ulonglong2 w1 = ldtw(tw, 1), w2 = ldtw(tw, 2), w3 = ldtw(tw, 3);
-  const ulonglong2 sc = P.scales[job.scale_idx];
   const int c0 = rank * 1024 + 2 * tid;
+  // stage by stage over both columns, one twiddle live at a time
 #pragma unroll
-  for (int h = 0; h < 16; h += 8) {
+  for (int k = 0; k < 8; k += 2) {
+    const ulonglong2 w = ldtw(tw, 4 + k / 2);
 #pragma unroll
-    for (int k = 0; k < 8; k += 2)
-      gs_bfly(x[h + k], x[h + k + 1], ldtw(tw, 4 + k / 2), q, q2);
-    gs_bfly(x[h + 0], x[h + 2], w2, q, q2);
-    gs_bfly(x[h + 1], x[h + 3], w2, q, q2);
-    gs_bfly(x[h + 4], x[h + 6], w3, q, q2);
-    gs_bfly(x[h + 5], x[h + 7], w3, q, q2);
+    for (int h = 0; h < 16; h += 8) gs_bfly(x[h + k], x[h + k + 1], w, q, q2);
+  }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) gs_bfly(x[h + k], x[h + k + 4], w1, q, q2);
+  for (int m = 0; m < 2; ++m) {
+    const ulonglong2 w = ldtw(tw, 2 + m);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint64_t r = x[h + k] * sc.x - __umul64hi(x[h + k], sc.y) * q;
-      x[h + k] = r >= q ? r - q : r;
+    for (int h = 0; h < 16; h += 8) {
+      gs_bfly(x[h + 4 * m], x[h + 4 * m + 2], w, q, q2);
+      gs_bfly(x[h + 4 * m + 1], x[h + 4 * m + 3], w, q, q2);
+    }
+  }
+  {
+    const ulonglong2 w = ldtw(tw, 1);
+#pragma unroll
+    for (int h = 0; h < 16; h += 8)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) gs_bfly(x[h + k], x[h + k + 4], w, q, q2);
+  }
+  {
+    const ulonglong2 sc = P.scales[job.scale_idx];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint64_t r = x[k] * sc.x - __umul64hi(x[k], sc.y) * q;
+      x[k] = r >= q ? r - q : r;
     }
   }
 #pragma unroll
