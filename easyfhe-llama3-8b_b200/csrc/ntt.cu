@@ -54,6 +54,7 @@ struct NttParams {
   const uint64_t *primes;
   const ulonglong2 *scales;  // inverse only
   int jobs_per_item;
+  int items;
 };
 
 __device__ __forceinline__ ulonglong2 ldtw(const ulonglong2 *tw, int idx) {
@@ -142,9 +143,12 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // job-major order: consecutive clusters transform the same limb job (one
+  // prime) of consecutive items, so clusters running together share one
+  // twiddle table in L2
   const long long job_id = blockIdx.x / CL;
-  const long long item = job_id / P.jobs_per_item;
-  const LimbJob job = P.jobs[job_id % P.jobs_per_item];
+  const long long item = job_id % P.items;
+  const LimbJob job = P.jobs[job_id / P.items];
   const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
   uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
   const uint64_t q = P.primes[job.prime], q2 = 2 * q;
@@ -257,9 +261,12 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // job-major order: consecutive clusters transform the same limb job (one
+  // prime) of consecutive items, so clusters running together share one
+  // twiddle table in L2
   const long long job_id = blockIdx.x / CL;
-  const long long item = job_id / P.jobs_per_item;
-  const LimbJob job = P.jobs[job_id % P.jobs_per_item];
+  const long long item = job_id % P.items;
+  const LimbJob job = P.jobs[job_id / P.items];
   const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
   uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
   const uint64_t q = P.primes[job.prime], q2 = 2 * q;
@@ -383,6 +390,7 @@ int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
   P.primes = ctx->d_primes;
   P.scales = scales ? scales : ctx->d_ninv;
   P.jobs_per_item = jobs_per_item;
+  P.items = items;
   const long long blocks = (long long)items * jobs_per_item * CL;
   if (blocks > 0x7fffffffLL) {
     set_error("launch_ntt: batch too large (%lld limbs)", blocks / CL);
