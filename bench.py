@@ -507,6 +507,10 @@ def main() -> None:
     ntt_ms = e0.elapsed_time(e1) / (2 * reps)  # per launch (fwd and inv averaged)
     ntt_bytes = 16 * N * ntt_limbs
     ntt_gbs = ntt_bytes / (ntt_ms / 1e3) / 1e9
+    # the NTT is bound by 64-bit multiplies on CUDA cores: its butterfly rate
+    # against the register-only rate of the same butterfly on this GPU
+    ntt_bfly = ntt_limbs * (N // 2) * 16 / (ntt_ms / 1e3)
+    bfly_peak = ctx.butterfly_peak()
     if a.workload == "ntt":
         if rank == 0:
             print(json.dumps({"workload": "ntt", "limbs": ntt_limbs, "ms": ntt_ms,
@@ -617,6 +621,13 @@ def main() -> None:
                 "peak_source": peak_src,
                 "algorithmic_bytes_per_launch": ntt_bytes,
                 "launch": f"{ntt_limbs} limbs of 2^16 words (16 N bytes per limb)",
+            },
+            "compute_roofline": {
+                "bound": "imad", "kernel": "ntt_fwd_kernel/ntt_inv_kernel",
+                "achieved": ntt_bfly, "peak": bfly_peak, "unit": "butterflies/s",
+                "frac": ntt_bfly / bfly_peak,
+                "peak_source": "measured live: b2f_butterfly_peak (lazy Shoup butterfly "
+                               "from registers, every SM full)",
             },
             "ntt_hbm_gbs": ntt_gbs,
             "keyswitch_hbm_gbs": algorithmic_mib(a) * MiB / (ms / 1e3) / 1e9,

@@ -306,6 +306,14 @@ class NativeContext:
              num_polys if b_polys is None else b_polys, _stream())
         return out
 
+    def butterfly_peak(self, iters: int = 2000) -> float:
+        """Lazy Shoup butterflies per second from registers alone (the
+        integer-multiply roofline of the NTT kernels)."""
+
+        out = ctypes.c_double(0.0)
+        call("b2f_butterfly_peak", self.handle, int(iters), ctypes.byref(out), _stream())
+        return float(out.value)
+
     def tensor(self, a: torch.Tensor, b: torch.Tensor, num_cts: int, l: int) -> torch.Tensor:
         out = self.empty(num_cts, 3, l)
         call("b2f_tensor", self.handle, _ptr(a), _ptr(b), _ptr(out), num_cts, l, _stream())

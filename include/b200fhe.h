@@ -240,6 +240,14 @@ int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
             const uint64_t *pts, int giant_count, int l, uint64_t *out,
             int num_cts, void *stream);
 
+/* ---- calibration (no reference counterpart) ----
+ * Rate of the NTT's lazy Shoup butterfly from registers alone (every SM
+ * full, `iters` rounds of 8 butterflies per thread), per second: the
+ * integer-multiply roofline the NTT kernels are measured against, since
+ * their 64-bit products on CUDA cores bound them before HBM does. */
+int b2f_butterfly_peak(b2f_context *ctx, int iters, double *per_second,
+                       void *stream);
+
 /* ---- encoding ----
  * Slot vectors (complex128 interleaved re/im, device) -> plaintexts at
  * q_limbs (+ p_limbs) in NTT form: special inverse FFT, times scale, round
