@@ -8,6 +8,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../include/b200fhe.h"
 #include "modarith.cuh"
 
@@ -31,6 +33,17 @@ int cuda_status(cudaError_t e, const char *what);
     cudaError_t _e = (call);                                  \
     if (_e != cudaSuccess) return ::b2f::cuda_status(_e, #call); \
   } while (0)
+// NVTX range over one entry point (header-only NVTX v3: a no-op unless a
+// profiler is attached), so profiles group kernels by the operation that
+// launched them.
+struct NvtxRange {
+  explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange &) = delete;
+  NvtxRange &operator=(const NvtxRange &) = delete;
+};
+#define B2F_RANGE(name) ::b2f::NvtxRange b2f_range_guard_(name)
+
 #define B2F_LAUNCHED(what)                                        \
   do {                                                            \
     cudaError_t _e = cudaGetLastError();                          \

@@ -310,6 +310,7 @@ size_t b2f_encode_workspace(const b2f_context *ctx, int num_rows, int slots) {
 int b2f_encode(b2f_context *ctx, const double *values, int num_rows, int slots,
                double scale, int q_limbs, int p_limbs, uint64_t *out, void *ws,
                size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_encode");
   B2F_CHECK_ARG(ctx && values && out, "b2f_encode: null argument");
   B2F_CHECK_ARG(pow2(slots) && slots <= kN / 2, "b2f_encode: slots %d must be a "
                 "power of two <= N/2", slots);
@@ -355,6 +356,7 @@ size_t b2f_decode_workspace(const b2f_context *ctx, int slots) {
 int b2f_decode(b2f_context *ctx, const uint64_t *pt, int l, int slots,
                double scale, double *values, void *ws, size_t ws_bytes,
                void *stream) {
+  B2F_RANGE("b2f_decode");
   B2F_CHECK_ARG(ctx && pt && values, "b2f_decode: null argument");
   B2F_CHECK_ARG(pow2(slots) && slots <= kN / 2, "b2f_decode: bad slots %d", slots);
   B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_decode: bad limbs %d", l);
@@ -405,6 +407,7 @@ int b2f_pack_diagonals(b2f_context *ctx, const void *weight, int dtype,
                        int dimension, int token_lanes, int baby_steps,
                        int giant_base, int giant_count, int slots, double *out,
                        void *stream) {
+  B2F_RANGE("b2f_pack_diagonals");
   B2F_CHECK_ARG(ctx && weight && out, "b2f_pack_diagonals: null argument");
   B2F_CHECK_ARG(dtype >= 0 && dtype <= 2, "b2f_pack_diagonals: bad dtype %d", dtype);
   B2F_CHECK_ARG(slots > 0 && dimension > 0 && token_lanes > 0 &&
@@ -432,6 +435,7 @@ int b2f_pack_structured(b2f_context *ctx, const void *const *sources,
                         int dimension, int token_lanes, int baby_steps,
                         int giant_base, int giant_count, int slots, double *out,
                         void *stream) {
+  B2F_RANGE("b2f_pack_structured");
   B2F_CHECK_ARG(ctx && sources && strides && out && real_source && real_row &&
                     real_scale && imag_source && imag_row && imag_scale &&
                     column && column_scale,

@@ -227,6 +227,7 @@ int b2f_secret_to_ntt(b2f_context *ctx, const int8_t *s_coeff, uint64_t *s_ntt,
 int b2f_keygen_switch(b2f_context *ctx, const uint64_t *s_from,
                       const uint64_t *s_to, uint64_t seed, uint32_t tag,
                       uint64_t *key, void *stream) {
+  B2F_RANGE("b2f_keygen_switch");
   B2F_CHECK_ARG(ctx && s_from && s_to && key, "b2f_keygen_switch: null argument");
   cudaStream_t st = (cudaStream_t)stream;
   const int np = ctx->L + ctx->K;
@@ -252,6 +253,7 @@ int b2f_keygen_switch(b2f_context *ctx, const uint64_t *s_from,
 
 int b2f_keygen_rotation(b2f_context *ctx, const uint64_t *s_ntt, uint64_t galois,
                         uint64_t seed, uint64_t *key, void *stream) {
+  B2F_RANGE("b2f_keygen_rotation");
   B2F_CHECK_ARG(ctx && s_ntt && key, "b2f_keygen_rotation: null argument");
   const uint64_t m = 2ull * kN;
   B2F_CHECK_ARG((galois & 1) && galois < m, "b2f_keygen_rotation: bad galois");
@@ -276,6 +278,7 @@ int b2f_keygen_rotation(b2f_context *ctx, const uint64_t *s_ntt, uint64_t galois
 
 int b2f_keygen_relin(b2f_context *ctx, const uint64_t *s_ntt, uint64_t seed,
                      uint64_t *key, void *stream) {
+  B2F_RANGE("b2f_keygen_relin");
   B2F_CHECK_ARG(ctx && s_ntt && key, "b2f_keygen_relin: null argument");
   cudaStream_t st = (cudaStream_t)stream;
   const int np = ctx->L + ctx->K;
@@ -293,6 +296,7 @@ int b2f_keygen_relin(b2f_context *ctx, const uint64_t *s_ntt, uint64_t seed,
 int b2f_encrypt(b2f_context *ctx, const uint64_t *m_ntt, int l,
                 const uint64_t *s_ntt, uint64_t seed, uint64_t nonce,
                 uint64_t *ct, void *stream) {
+  B2F_RANGE("b2f_encrypt");
   B2F_CHECK_ARG(ctx && m_ntt && s_ntt && ct, "b2f_encrypt: null argument");
   B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_encrypt: bad limbs %d", l);
   cudaStream_t st = (cudaStream_t)stream;
@@ -308,6 +312,7 @@ int b2f_encrypt(b2f_context *ctx, const uint64_t *m_ntt, int l,
 
 int b2f_decrypt(b2f_context *ctx, const uint64_t *ct, int l, const uint64_t *s_ntt,
                 uint64_t *m_ntt, void *stream) {
+  B2F_RANGE("b2f_decrypt");
   B2F_CHECK_ARG(ctx && ct && s_ntt && m_ntt, "b2f_decrypt: null argument");
   B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_decrypt: bad limbs %d", l);
   decrypt_kernel<<<dim3(kN / TPB, l), TPB, 0, (cudaStream_t)stream>>>(

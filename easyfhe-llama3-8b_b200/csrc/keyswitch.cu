@@ -639,6 +639,7 @@ size_t b2f_rotate_workspace(const b2f_context *ctx, int num_cts, int l) {
 int b2f_rotate(b2f_context *ctx, const uint64_t *ct_in, uint64_t *ct_out,
                int num_cts, int l, uint64_t galois, const uint64_t *key,
                void *ws, size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_rotate");
   int rc = check_level(ctx, l, "b2f_rotate");
   if (rc) return rc;
   B2F_CHECK_ARG(ct_in && ct_out && key && num_cts >= 0,
@@ -675,6 +676,7 @@ size_t b2f_relinearize_workspace(const b2f_context *ctx, int num_cts, int l) {
 int b2f_relinearize(b2f_context *ctx, const uint64_t *ct3_in, uint64_t *ct_out,
                     int num_cts, int l, const uint64_t *relin_key, void *ws,
                     size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_relinearize");
   int rc = check_level(ctx, l, "b2f_relinearize");
   if (rc) return rc;
   B2F_CHECK_ARG(ct3_in && ct_out && relin_key && num_cts >= 0,
@@ -707,6 +709,7 @@ size_t b2f_modup_batch_workspace(const b2f_context *ctx, int num_cts, int l) {
 
 int b2f_modup_batch(b2f_context *ctx, const uint64_t *ct, int num_cts, int l,
                     uint64_t *ext, void *ws, size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_modup_batch");
   int rc = check_level(ctx, l, "b2f_modup");
   if (rc) return rc;
   B2F_CHECK_ARG(ct && ext && num_cts >= 0, "b2f_modup: null argument");
@@ -744,6 +747,7 @@ int b2f_rotate_hoisted_batch(b2f_context *ctx, const uint64_t *ct, int num_cts,
                              const uint64_t *galois, const uint64_t *const *keys,
                              uint64_t *out, void *ws, size_t ws_bytes,
                              void *stream) {
+  B2F_RANGE("b2f_rotate_hoisted_batch");
   int rc = check_level(ctx, l, "b2f_rotate_hoisted");
   if (rc) return rc;
   B2F_CHECK_ARG(ct && out && count >= 0 && num_cts >= 0 &&
@@ -826,6 +830,7 @@ int b2f_rotate_hoisted_ext(b2f_context *ctx, const uint64_t *ct, int l,
                            const uint64_t *ext, int count, const uint64_t *galois,
                            const uint64_t *const *keys, uint64_t *out, void *ws,
                            size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_rotate_hoisted_ext");
   int rc = check_level(ctx, l, "b2f_rotate_hoisted_ext");
   if (rc) return rc;
   B2F_CHECK_ARG(ct && out && count >= 0 && (count == 0 || galois),
@@ -885,6 +890,7 @@ size_t b2f_moddown_ext_workspace(const b2f_context *ctx, int num_cts, int l) {
 
 int b2f_moddown_ext(b2f_context *ctx, const uint64_t *in, int num_cts, int l,
                     uint64_t *out, void *ws, size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_moddown_ext");
   int rc = check_level(ctx, l, "b2f_moddown_ext");
   if (rc) return rc;
   B2F_CHECK_ARG(in && out && num_cts >= 0, "b2f_moddown_ext: null argument");

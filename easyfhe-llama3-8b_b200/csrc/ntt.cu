@@ -426,6 +426,7 @@ using namespace b2f;
 
 extern "C" int b2f_ntt(b2f_context *ctx, uint64_t *data, int num_polys,
                        int q_limbs, int p_limbs, int inverse, void *stream) {
+  B2F_RANGE("b2f_ntt");
   B2F_CHECK_ARG(ctx && data, "b2f_ntt: null argument");
   B2F_CHECK_ARG(num_polys >= 0 && q_limbs >= 0 && q_limbs <= ctx->L &&
                     p_limbs >= 0 && p_limbs <= ctx->K && q_limbs + p_limbs > 0,

@@ -259,6 +259,7 @@ size_t b2f_rescale_workspace(const b2f_context *ctx, int num_polys, int l) {
 
 int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
                 int num_polys, int l, void *ws, size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_rescale");
   B2F_CHECK_ARG(ctx && in && out && num_polys >= 0, "b2f_rescale: null argument");
   B2F_CHECK_ARG(l >= 2 && l <= ctx->L, "b2f_rescale: needs 2..%d limbs, got %d",
                 ctx->L, l);
@@ -305,6 +306,7 @@ int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
 
 int b2f_modraise(b2f_context *ctx, const uint64_t *in, int num_polys, int l_out,
                  uint64_t *out, void *stream) {
+  B2F_RANGE("b2f_modraise");
   B2F_CHECK_ARG(ctx && in && out && num_polys >= 0, "b2f_modraise: null argument");
   B2F_CHECK_ARG(l_out >= 1 && l_out <= ctx->L, "b2f_modraise: bad target limbs %d", l_out);
   B2F_CHECK_ARG(in != out, "b2f_modraise: in-place ModRaise is not supported");
@@ -364,6 +366,7 @@ int b2f_mul_i(b2f_context *ctx, const uint64_t *a, uint64_t *out, int num_polys,
 
 int b2f_tensor(b2f_context *ctx, const uint64_t *a, const uint64_t *b,
                uint64_t *out, int num_cts, int l, void *stream) {
+  B2F_RANGE("b2f_tensor");
   B2F_CHECK_ARG(ctx && a && b && out && num_cts >= 0, "b2f_tensor: null argument");
   B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_tensor: bad limbs %d", l);
   B2F_CHECK_ARG(out != a && out != b, "b2f_tensor: output overlaps an input");
@@ -404,6 +407,7 @@ int b2f_scalar_op(b2f_context *ctx, const uint64_t *a, uint64_t *out,
 int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
             const uint64_t *pts, int giant_count, int l, uint64_t *out,
             int num_cts, void *stream) {
+  B2F_RANGE("b2f_mac");
   B2F_CHECK_ARG(ctx && babies && pts && out, "b2f_mac: null argument");
   B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_mac: bad limbs %d", l);
   B2F_CHECK_ARG(baby_count >= 1 && giant_count >= 1 && num_cts >= 0,
@@ -416,6 +420,7 @@ int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
 int b2f_pairwise_mac(b2f_context *ctx, const uint64_t *cts, const uint64_t *pts,
                      int count, int groups, int q_limbs, int p_limbs,
                      int pt_limb_stride, uint64_t *out, void *stream) {
+  B2F_RANGE("b2f_pairwise_mac");
   B2F_CHECK_ARG(ctx && cts && pts && out, "b2f_pairwise_mac: null argument");
   B2F_CHECK_ARG(count >= 1 && groups >= 1 && count % groups == 0,
                 "b2f_pairwise_mac: %d pairs do not split into %d groups", count, groups);
@@ -446,6 +451,7 @@ int b2f_bsgs_mac_batch(b2f_context *ctx, const uint64_t *babies, int num_cts,
                        int baby_count, const uint64_t *pts, int giant_count,
                        int l, uint64_t giant_galois, const uint64_t *giant_key,
                        uint64_t *out, void *ws, size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_bsgs_mac_batch");
   B2F_CHECK_ARG(ctx && babies && pts && out, "b2f_bsgs_mac: null argument");
   B2F_CHECK_ARG(l >= 1 && l <= ctx->L, "b2f_bsgs_mac: bad limbs %d", l);
   B2F_CHECK_ARG(baby_count >= 1 && giant_count >= 1 && num_cts >= 0,

@@ -827,6 +827,47 @@ def pack_cipher_batch(items: Iterable[Ciphertext]) -> Ciphertext:
     return Ciphertext(data, first.state, first.slots, first.context, first.is_ext)
 
 
+# ---------------------------------------------------------------------------
+# encrypted-state serialisation (resumable runs: limbs + state at a stage
+# boundary; the reference has no counterpart, SURVEY-style optional)
+# ---------------------------------------------------------------------------
+
+
+def save_ciphertext(ct: Ciphertext, path) -> None:
+    """Write a (batch of) ciphertext(s) to `path` (.npz): the uint64 limbs as
+    they sit in HBM plus state, slots and basis."""
+
+    import numpy as np
+
+    st = ct.state
+    np.savez(path, limbs=ct.data.detach().cpu().numpy(),
+             cur_limbs=int(st.cur_limbs), scale_degree=int(st.scale_degree),
+             scaling_factor=np.float64(st.scaling_factor if st.scaling_factor is not None
+                                       else np.nan),
+             slots=int(ct.slots), is_ext=bool(ct.is_ext))
+
+
+def load_ciphertext(path, context) -> Ciphertext:
+    """Read a ciphertext written by save_ciphertext onto the context's device;
+    the limb count must match the stored state."""
+
+    import numpy as np
+
+    ctx = _ctx_of(context)
+    with np.load(path) as f:
+        limbs = f["limbs"]
+        sf = float(f["scaling_factor"])
+        state = CipherState(int(f["cur_limbs"]), int(f["scale_degree"]),
+                            None if np.isnan(sf) else sf)
+        slots, is_ext = int(f["slots"]), bool(f["is_ext"])
+    expect = state.cur_limbs + (ctx.K if is_ext else 0)
+    if limbs.dtype != np.int64 or limbs.shape[-1] != ctx.N or limbs.shape[-2] != expect:
+        raise ValueError(f"{path}: limbs {limbs.shape} {limbs.dtype} do not match "
+                         f"{expect} limbs of {ctx.N} words")
+    data = torch.from_numpy(limbs).to(ctx.device)
+    return Ciphertext(data, state, slots, ctx, is_ext)
+
+
 def grouped_pairwise_mac(batch: Ciphertext, plaintexts: Plaintext, groups: int,
                          context) -> Ciphertext:
     """sum_i batch[i] * plaintexts[i] in `groups` consecutive groups; extended

@@ -72,3 +72,41 @@ def test_two_gloo_ranks_gather_and_max(total):
     for _, _, full, mx in results:
         assert full == expect
         assert mx == 2.0
+
+
+def _dropping_worker(rank: int, port: int, queue) -> None:
+    import datetime
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(root / "easyfhe-llama3-8b_b200"))
+    import torch.distributed as dist
+
+    from easyfhe import shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=10))
+    shard.max_over_ranks(1.0)  # one step together
+    if rank == 1:
+        os._exit(0)  # this rank leaves between steps, with nothing in flight
+    try:
+        shard.max_over_ranks(2.0)
+        queue.put("no error")
+    except Exception as exc:  # the survivor learns of it at its next collective
+        queue.put(type(exc).__name__)
+
+
+def test_dropped_rank_surfaces_as_an_error_on_the_survivor():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dropping_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    result = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert result != "no error"
