@@ -37,6 +37,29 @@ def test_mac_bit_exact():
     assert np.array_equal(got[0], _mac_ref(babies, pts, G, B, ctx.primes[:l]))
 
 
+@pytest.mark.parametrize("C,B,G", [(5, 64, 8), (9, 24, 3), (2, 33, 11)])
+def test_batched_mac_bit_exact(C, B, G):
+    """A batch through one MAC launch sequence: every ciphertext of the
+    batch, every giant (more than 8 split over launches) equals the modular
+    sum of products."""
+
+    ctx, orc = pair(8, 2, 3)
+    l = 2
+    rng = np.random.default_rng(34 + C)
+    babies = rand_residues(rng, ctx.primes[:l], C * B * 2).reshape(C, B, 2, l, N)
+    pts = rand_residues(rng, ctx.primes[:l], G * B)
+    got = to_host(ctx.mac(to_dev(babies.reshape(C * B, 2, l, N)), B, to_dev(pts), G, l,
+                          num_cts=C))
+    q = np.array(ctx.primes[:l], dtype=np.uint64)[None, :, None]
+    for c in (0, C - 1):  # the first and the last ciphertext of the batch
+        for g in range(G):
+            want = np.zeros((2, l, N), dtype=np.uint64)
+            for b in range(B):  # modular products from the oracle, sums mod q
+                want = want + orc.mul_plain(babies[c, b], pts[g * B + b], l)
+                want = np.where(want >= q, want - q, want)
+            assert np.array_equal(got[c, g], want), (c, g)
+
+
 def test_bsgs_mac_horner_bit_exact():
     from easyfhe import core
 
