@@ -137,6 +137,29 @@ __global__ void __launch_bounds__(TPB) scalar_kernel(
   out[idx] = r;
 }
 
+// out[c][p][i] = sum_k w_k[i] * term_k[c][p][i] (mod q_i): ciphertexts
+// (or batches) of different limb counts combined with per-limb scalar weights
+// in one pass.  The weights travel by value (Barrett products: the kernel is
+// bound by reading the terms).  grid (N/TPB, l, cts * polys)
+constexpr int LC_MAX = 8;    // terms
+constexpr int LC_LMAX = 40;  // limbs
+struct LinTerms {
+  const uint64_t *in[LC_MAX];
+  int limbs[LC_MAX];
+  int count;
+  uint64_t w[LC_MAX][LC_LMAX];
+};
+__global__ void __launch_bounds__(TPB) linear_combination_kernel(
+    const LinTerms T, uint64_t *__restrict__ out, const Mod *__restrict__ mods, int l) {
+  const int n = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, cp = blockIdx.z;  // cp = ciphertext * polys + poly
+  const Mod M = mods[i];
+  U128 acc = {0, 0};
+  for (int k = 0; k < T.count; ++k)
+    mac128(acc, T.in[k][((size_t)cp * T.limbs[k] + i) * kN + n], T.w[k][i]);
+  out[((size_t)cp * l + i) * kN + n] = reduce128(acc.hi, acc.lo, M);
+}
+
 // out[ct][g] (2 polys, l limbs; giant-major [g][ct] when giant_major) =
 // sum_b pt[g0+g][b] * babies[ct][b].  grid (cts, N/TPB, l): the ciphertexts
 // of a batch are the fastest grid axis, so they read each plaintext tile
@@ -374,6 +397,38 @@ int b2f_tensor(b2f_context *ctx, const uint64_t *a, const uint64_t *b,
   tensor_kernel<<<dim3(kN / TPB, l, num_cts), TPB, 0, (cudaStream_t)stream>>>(
       a, b, out, ctx->d_mod, l);
   B2F_LAUNCHED("tensor_kernel");
+  return B2F_OK;
+}
+
+int b2f_linear_combination(b2f_context *ctx, int num_terms,
+                           const uint64_t *const *terms, const int *term_limbs,
+                           const uint64_t *weights, int num_cts, int polys, int l,
+                           uint64_t *out, void *stream) {
+  B2F_RANGE("b2f_linear_combination");
+  B2F_CHECK_ARG(ctx && terms && term_limbs && weights && out,
+                "b2f_linear_combination: null argument");
+  B2F_CHECK_ARG(num_terms >= 1 && num_cts >= 0 && polys >= 1 && polys <= 3 && l >= 1 &&
+                    l <= ctx->L,
+                "b2f_linear_combination: bad shape (terms=%d, l=%d, cts=%d, polys=%d)",
+                num_terms, l, num_cts, polys);
+  if (num_terms > LC_MAX || l > LC_LMAX) {
+    set_error("b2f_linear_combination: at most %d terms of %d limbs", LC_MAX, LC_LMAX);
+    return B2F_ERR_UNSUPPORTED;
+  }
+  LinTerms T{};
+  T.count = num_terms;
+  for (int k = 0; k < num_terms; ++k) {
+    B2F_CHECK_ARG(terms[k] && term_limbs[k] >= l && term_limbs[k] <= ctx->L,
+                  "b2f_linear_combination: term %d has %d limbs, fewer than %d", k,
+                  term_limbs[k], l);
+    T.in[k] = terms[k];
+    T.limbs[k] = term_limbs[k];
+    for (int i = 0; i < l; ++i) T.w[k][i] = weights[(size_t)k * l + i] % ctx->primes[i];
+  }
+  if (!num_cts) return B2F_OK;
+  linear_combination_kernel<<<dim3(kN / TPB, l, num_cts * polys), TPB, 0,
+                              (cudaStream_t)stream>>>(T, out, ctx->d_mod, l);
+  B2F_LAUNCHED("linear_combination_kernel");
   return B2F_OK;
 }
 

@@ -66,6 +66,8 @@ _SIGS = {
     "b2f_mul_i": (_int, [_vp, _vp, _vp, _int, _int, _int, _vp]),
     "b2f_scalar_op": (_int, [_vp, _vp, _vp, _int, _int, _vp, _vp, _int, _vp]),
     "b2f_tensor": (_int, [_vp, _vp, _vp, _vp, _int, _int, _vp]),
+    "b2f_linear_combination": (_int, [_vp, _int, _vp, _vp, _vp, _int, _int, _int, _vp,
+                                      _vp]),
     "b2f_butterfly_peak": (_int, [_vp, _int, ctypes.POINTER(ctypes.c_double), _vp]),
     "b2f_modup_batch_workspace": (_size, [_vp, _int, _int]),
     "b2f_modup_batch": (_int, [_vp, _vp, _int, _int, _vp, _vp, _size, _vp]),

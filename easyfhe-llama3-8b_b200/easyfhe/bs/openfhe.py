@@ -343,15 +343,13 @@ def _cheb_eval(T: dict, coeffs: np.ndarray, target: float, ctx: fhe.Context) -> 
         ks = [k for k in range(1, len(c)) if abs(c[k]) >= 1e-30]
         limbs = min(int(T[k].state.cur_limbs) for k in ks)
         pre = target * ctx.rescale_divisor_at(limbs - 1)  # scale before the rescale
-        acc = None
-        for k in ks:
-            tk = fhe.align_to(T[k], T[k].state.replace(cur_limbs=limbs), ctx)
-            enc = fhe.encode_scalar(float(c[k]), cur_limbs=limbs, scale_degree=1,
-                                    scaling_factor=pre / float(tk.state.scaling_factor),
-                                    context=ctx)
-            term = fhe.homo_mul_scalar(tk, enc, ctx)
-            term.state = term.state.replace(scaling_factor=pre)
-            acc = term if acc is None else fhe.homo_add(acc, term, ctx)
+        encs = [fhe.encode_scalar(float(c[k]), cur_limbs=limbs, scale_degree=1,
+                                  scaling_factor=pre / float(T[k].state.scaling_factor),
+                                  context=ctx) for k in ks]
+        # one pass over the terms at their own levels: sum_k c_k T_k, every
+        # product at scale pre (up to the rounding of each encoded c_k)
+        acc = fhe.homo_linear_combination([T[k] for k in ks], encs, ctx)
+        acc.state = acc.state.replace(scaling_factor=pre)
         acc = fhe.rescale(acc, ctx)
         acc.state = acc.state.replace(scaling_factor=target)
         if abs(c[0]) >= 1e-30:

@@ -314,6 +314,20 @@ class NativeContext:
         call("b2f_butterfly_peak", self.handle, int(iters), ctypes.byref(out), _stream())
         return float(out.value)
 
+    def linear_combination(self, terms, term_limbs, weights, num_cts: int, polys: int,
+                           l: int) -> torch.Tensor:
+        """sum_k weights[k] * terms[k] over num_cts x polys polynomials at l
+        limbs; weights[k] is a sequence of l residues."""
+
+        k = len(terms)
+        out = self.empty(num_cts * polys, l)
+        tp = (ctypes.c_void_p * k)(*[_ptr(t) for t in terms])
+        tl = (ctypes.c_int * k)(*[int(v) for v in term_limbs])
+        w = (ctypes.c_uint64 * (k * l))(*[int(v) for ws in weights for v in ws[:l]])
+        call("b2f_linear_combination", self.handle, k, tp, tl, w, num_cts, polys, l,
+             _ptr(out), _stream())
+        return out
+
     def tensor(self, a: torch.Tensor, b: torch.Tensor, num_cts: int, l: int) -> torch.Tensor:
         out = self.empty(num_cts, 3, l)
         call("b2f_tensor", self.handle, _ptr(a), _ptr(b), _ptr(out), num_cts, l, _stream())

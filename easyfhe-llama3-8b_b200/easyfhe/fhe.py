@@ -465,6 +465,50 @@ def homo_mul_scalar_rescale(ct: Ciphertext, enc: EncodedScalar, context) -> Ciph
     return rescale(homo_mul_scalar(ct, enc, context), context)
 
 
+def homo_linear_combination(cts, scalars, context) -> Ciphertext:
+    """sum_k scalars[k] * cts[k] in one pass, at the fewest limbs among the
+    terms (no modulus drop of the others first).  Every product must land on
+    the same state (scale degree and tracked scaling factor), as the caller
+    arranges by encoding each scalar for its term.  No reference counterpart:
+    the fused form of homo_mul_scalar + homo_add chains
+    (llama3fhe/operators/nonlinear/polynomial.py:41-88)."""
+
+    ctx = _ctx_of(context)
+    cts, scalars = list(cts), list(scalars)
+    if not cts or len(cts) != len(scalars):
+        raise ValueError("homo_linear_combination needs one scalar per ciphertext")
+    first = cts[0]
+    for c in cts:
+        if c.is_ext or c.polys != first.polys or c.batch_size != first.batch_size:
+            raise ValueError("homo_linear_combination: terms differ in basis, polys or batch")
+    l = min(_limbs(c) for c in cts)
+    states = set()
+    for c, e in zip(cts, scalars):
+        states.add((int(c.state.scale_degree) + int(e.state.scale_degree),
+                    float(c.state.scaling_factor) * float(e.state.scaling_factor)))
+    degree, scale = states.pop()
+    if any(d != degree or abs(sf - scale) > 1e-9 * abs(scale) for d, sf in states):
+        raise ValueError("homo_linear_combination: the products do not share one state")
+    weights = []
+    for e in scalars:
+        if len(e.residues) < l:
+            raise ValueError(f"scalar encoded for {len(e.residues)} limbs, terms have {l}")
+        weights.append(e.residues[:l])
+    state = first.state.replace(cur_limbs=l, scale_degree=degree, scaling_factor=scale)
+    try:
+        data = ctx.native.linear_combination([c.data for c in cts], [_limbs(c) for c in cts],
+                                             weights, first.batch_size, first.polys, l)
+    except NotImplementedError:  # more terms or limbs than one pass carries
+        acc = None
+        for c, e in zip(cts, scalars):
+            t = homo_mul_scalar(align_to(c, c.state.replace(cur_limbs=l), ctx), e, ctx)
+            acc = t if acc is None else _addsub(0, acc, t, ctx)
+        return Ciphertext(acc.data, state, first.slots, ctx)
+    shape = list(first.data.shape)
+    shape[-2] = l
+    return Ciphertext(data.view(shape), state, first.slots, ctx)
+
+
 def homo_add_scalar(ct: Ciphertext, enc: EncodedScalar, context) -> Ciphertext:
     """ct + scalar, added to c0 (llama3fhe/operators/nonlinear/polynomial.py:84-88)."""
 

@@ -195,6 +195,18 @@ int b2f_mul_i(b2f_context *ctx, const uint64_t *a, uint64_t *out,
  * (llama3fhe/operators/attention/qk.py:399, primitives.py:21-31). */
 int b2f_tensor(b2f_context *ctx, const uint64_t *a, const uint64_t *b,
                uint64_t *out, int num_cts, int l, void *stream);
+/* out = sum_k weights[k][i] * terms[k] (mod q_i) over num_cts ciphertexts of
+ * `polys` polynomials at l limbs; term k (device pointer) has term_limbs[k]
+ * >= l limbs per polynomial (its limbs beyond l are skipped, so no modulus
+ * drop is needed first); weights is a host array [num_terms][l] of
+ * residues.  At most 8 terms of 40 limbs (B2F_ERR_UNSUPPORTED beyond).  No
+ * reference counterpart: one pass for the scalar-weighted sums of the
+ * bootstrapping polynomial (homo_mul_scalar + homo_add per term,
+ * llama3fhe/operators/nonlinear/polynomial.py:41-88). */
+int b2f_linear_combination(b2f_context *ctx, int num_terms,
+                           const uint64_t *const *terms, const int *term_limbs,
+                           const uint64_t *weights, int num_cts, int polys, int l,
+                           uint64_t *out, void *stream);
 /* out = a * c (+ add) with per-limb integer constants c[l], add[l]
  * (residues, NULL = none); add goes to poly add_poly, to every poly (-1) or
  * to c0 of every ciphertext of a batch of 2-poly ciphertexts (-2):

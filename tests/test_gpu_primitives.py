@@ -246,3 +246,30 @@ def test_encrypt_rotate_decrypt_values():
         dec = ctx.decode(ctx.decrypt(rot, 4, s_ntt), 4, 32768, scale)
         ref = np.conj(z) if r == 131071 else np.roll(z, -r)
         assert np.max(np.abs(dec - ref)) < 1e-4, r
+
+
+def test_linear_combination_matches_scalar_ops():
+    """homo_linear_combination equals align_to + homo_mul_scalar + homo_add,
+    bit for bit, for a batch whose terms sit at different levels."""
+
+    from easyfhe import fhe
+
+    client, ctx = fhe.generate_client_context(
+        fhe.CKKSContextSpec(depth=6, log_n=16, dnum=2, dcrt_bits=45, first_mod=55,
+                            rotations=(1,)), "cuda:0")
+    rng = np.random.default_rng(72)
+    n = ctx.max_slots
+    terms, scalars = [], []
+    for k, limbs in enumerate((7, 5, 6, 5)):
+        cts = [client.encrypt(rng.uniform(-1, 1, n), slots=n, cur_limbs=limbs,
+                              scaling_factor=ctx.scale_at(limbs)) for _ in range(3)]
+        terms.append(fhe.pack_cipher_batch(cts))
+        scalars.append(fhe.encode_scalar(0.37 * (k + 1) - 0.8, cur_limbs=5, scale_degree=1,
+                                         scaling_factor=ctx.scale_at(5), context=ctx))
+    got = fhe.homo_linear_combination(terms, scalars, ctx)
+    acc = None
+    for t, e in zip(terms, scalars):
+        p = fhe.homo_mul_scalar(fhe.align_to(t, t.state.replace(cur_limbs=5), ctx), e, ctx)
+        acc = p if acc is None else fhe.homo_add(acc, p, ctx)
+    assert got.state.cur_limbs == 5 and got.batch_size == 3
+    assert np.array_equal(to_host(got.data), to_host(acc.data))
