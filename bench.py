@@ -91,7 +91,8 @@ class Clocks:
         if not enabled:
             return
         try:
-            out_dir = ROOT / "gpurun_out"
+            # the raw clock samples beside the JSON line's summary
+            out_dir = Path(os.environ.get("B2F_BENCH_OUT", ROOT / "bench_out"))
             out_dir.mkdir(exist_ok=True)
             self.path = out_dir / f"clocks_bench_{device_index}.csv"
             self.fh = open(self.path, "w")

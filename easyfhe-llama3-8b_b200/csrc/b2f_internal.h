@@ -81,6 +81,16 @@ struct LevelTables {
   // rescale: for i < l-1, [q_{l-1}^-1] mod q_i and [q_{l-1}] mod q_i
   ulonglong2 *rescale_inv = nullptr;
   uint64_t *rescale_qlast = nullptr;
+  // relinearisation fused with its rescale (l >= 2, K >= 1): the removed
+  // limbs R = {q_{l-1}} u P (r = 0 is q_{l-1}, r = 1 + k is p_k), M = P q_{l-1}
+  //   mdr_scale[r]: N^-1 [(M/r)^-1] mod r (Shoup pair w.r.t. r)
+  //   mdr_rinv[r]:  1 / r in binary64
+  //   mdr_bytes:    conv_bytes of the conversion of K+2 words (the K+1 removed
+  //                 residues, then the rounding word v) to q_0..q_{l-2}, with
+  //                 constants [M/r] mod q_i and -[M] mod q_i for v
+  ulonglong2 *mdr_scale = nullptr;
+  double *mdr_rinv = nullptr;
+  uint8_t *mdr_bytes = nullptr;
 };
 
 // Byte-split operands of a base conversion out_t = sum_{i<w} x_i c_{t,i} mod

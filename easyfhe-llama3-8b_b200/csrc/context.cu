@@ -260,6 +260,41 @@ static int build_tables(b2f_context *ctx) {
     }
     if ((rc = upload(ctx, &T.rescale_inv, rinv))) return rc;
     if ((rc = upload(ctx, &T.rescale_qlast, rq))) return rc;
+    if (l >= 2 && K >= 1) {
+      // removed limbs of the fused relinearise + rescale
+      const int R = K + 1;
+      std::vector<uint64_t> rp(R);
+      rp[0] = P[l - 1];
+      for (int k = 0; k < K; ++k) rp[1 + k] = P[L + k];
+      auto mhat = [&](int r, uint64_t m) {  // (M / r) mod m
+        uint64_t v = 1 % m;
+        for (int r2 = 0; r2 < R; ++r2)
+          if (r2 != r) v = h_mulmod(v, rp[r2] % m, m);
+        return v;
+      };
+      std::vector<ulonglong2> msc(R);
+      std::vector<double> mri(R);
+      for (int r = 0; r < R; ++r) {
+        const uint64_t pr = rp[r];
+        msc[r] = shoup_pair(
+            h_mulmod(h_inv((uint64_t)n % pr, pr), h_inv(mhat(r, pr), pr), pr), pr);
+        mri[r] = 1.0 / (double)pr;
+      }
+      const int kp = conv_kpad(R + 1);
+      std::vector<uint8_t> mb(conv_rows(l - 1) * kp);
+      conv_bytes(
+          mb.data(), l - 1, R + 1, kp,
+          [&](int t, int r) -> uint64_t {
+            const uint64_t qt = P[t];
+            if (r < R) return mhat(r, qt);
+            const uint64_t m = h_mulmod(mhat(0, qt), rp[0] % qt, qt);  // M mod q_t
+            return m ? qt - m : 0;
+          },
+          [&](int t) { return P[t]; });
+      if ((rc = upload(ctx, &T.mdr_scale, msc))) return rc;
+      if ((rc = upload(ctx, &T.mdr_rinv, mri))) return rc;
+      if ((rc = upload(ctx, &T.mdr_bytes, mb))) return rc;
+    }
   }
 
   // FFT tables: ksi_k = exp(2 pi i k / M), rotation group 5^j mod M

@@ -156,12 +156,16 @@ __device__ __forceinline__ uint64_t reduce79(uint64_t hi, uint64_t lo, const Red
 
 // out(t): limb pointer of target t < T; red(t): its reduce79 constants.
 // x: limb 0 of the w input limbs; the block converts coefficients
-// [n0, n0 + CNB).  KW = 32-bit words per operand row (kp / 4).
-template <int KW, class Out, class Rd>
+// [n0, n0 + CNB).  KW = 32-bit words per operand row (kp / 4).  With ROUND,
+// input word w is v = floor(sum_{i<w} x_i * rinv[i] + 1/2), evaluated in
+// binary64 with each product and sum rounded to nearest in i order (A holds
+// the constants of w + 1 words).
+template <int KW, bool ROUND = false, class Out, class Rd>
 __device__ __forceinline__ void conv_mma_block(const uint64_t *__restrict__ x,
                                                int w,
                                                const uint8_t *__restrict__ A,
-                                               int T, Out out, Rd red, int n0) {
+                                               int T, Out out, Rd red, int n0,
+                                               const double *__restrict__ rinv = nullptr) {
   constexpr int ST = KW + 4;
   extern __shared__ __align__(16) uint32_t csm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -179,11 +183,23 @@ __device__ __forceinline__ void conv_mma_block(const uint64_t *__restrict__ x,
     d[2] = v.z;
     d[3] = v.w;
   }
+  uint64_t xv[KW / 2];
+#pragma unroll
+  for (int i = 0; i < KW / 2; ++i) xv[i] = i < w ? x[(size_t)i * kN + n0 + tid] : 0;
+  if (ROUND) {
+    double f = 0.0;
+#pragma unroll
+    for (int i = 0; i < KW / 2; ++i)
+      if (i < w) f = __dadd_rn(f, __dmul_rn(__ull2double_rn(xv[i]), __ldg(rinv + i)));
+    const uint64_t v = __double2ull_rz(__dadd_rn(f, 0.5));
+#pragma unroll
+    for (int i = 0; i < KW / 2; ++i)
+      if (i == w) xv[i] = v;
+  }
 #pragma unroll
   for (int i = 0; i < KW / 2; ++i) {
-    const uint64_t v = i < w ? x[(size_t)i * kN + n0 + tid] : 0;
-    Xs[tid * ST + 2 * i] = (uint32_t)v;
-    Xs[tid * ST + 2 * i + 1] = (uint32_t)(v >> 32);
+    Xs[tid * ST + 2 * i] = (uint32_t)xv[i];
+    Xs[tid * ST + 2 * i + 1] = (uint32_t)(xv[i] >> 32);
   }
   __syncthreads();
   // the warp's four n-tiles: B fragments stay in registers for every group
@@ -284,6 +300,22 @@ __global__ void __launch_bounds__(CNB) moddown_conv_mma_kernel(
       blockIdx.x * CNB);
 }
 
+// Fused relinearise + rescale, step 4: the K+1 removed limbs (coefficient
+// form, times N^-1 (M/r)^-1, limbs l-1 .. l+K-1 of acc) and their rounding
+// word to each q_i, i < l-1.  grid (N/CNB, 2, cts); conv [ct][2][l-1][N]
+template <int KW>
+__global__ void __launch_bounds__(CNB) moddown_rescale_conv_mma_kernel(
+    const uint64_t *__restrict__ acc, uint64_t *__restrict__ conv_out,
+    const uint8_t *__restrict__ bytes, const double *__restrict__ rinv,
+    const Red79 *__restrict__ reds, int l, int K) {
+  const int b = blockIdx.y, ct = blockIdx.z, lk = l + K;
+  uint64_t *o = conv_out + (((size_t)ct * 2 + b) * (l - 1)) * kN;
+  conv_mma_block<KW, true>(
+      acc + (((size_t)ct * 2 + b) * lk + l - 1) * kN, K + 1, bytes, l - 1,
+      [=](int t) { return o + (size_t)t * kN; }, [=](int t) { return reds[t]; },
+      blockIdx.x * CNB, rinv);
+}
+
 template <class Kern>
 int set_smem(Kern k, size_t bytes) {
   if (bytes > 48 * 1024)
@@ -338,6 +370,29 @@ int launch_moddown_conv(b2f_context *ctx, const uint64_t *acc, uint64_t *conv,
   return B2F_OK;
 }
 
+int launch_moddown_rescale_conv(b2f_context *ctx, const uint64_t *acc,
+                                uint64_t *conv, int l, int cts, cudaStream_t s) {
+  const LevelTables &T = ctx->levels[l];
+  const int K = ctx->K, kp = conv_kpad(K + 2);
+  const size_t sm = conv_mma_smem(kp, l - 1);
+  const dim3 grid(kN / CNB, 2, cts);
+  int rc;
+#define B2F_MDR(KWV)                                                              \
+  if ((rc = set_smem(moddown_rescale_conv_mma_kernel<KWV>, sm))) return rc;       \
+  moddown_rescale_conv_mma_kernel<KWV><<<grid, CNB, sm, s>>>(                     \
+      acc, conv, T.mdr_bytes, T.mdr_rinv, ctx->d_red79, l, K);
+  if (kp == 32) {
+    B2F_MDR(8)
+  } else if (kp == 64) {
+    B2F_MDR(16)
+  } else {
+    B2F_MDR(32)
+  }
+#undef B2F_MDR
+  B2F_LAUNCHED("moddown_rescale_conv_mma_kernel");
+  return B2F_OK;
+}
+
 // Step 3: key inner product.  grid (N/TPB, items, l+K): the slowest grid
 // axis is the target limb, so a key limb shared by a batch, or an ext limb
 // shared by the hoisted rotations of one ciphertext (ext_stride = 0, c1_stride
@@ -346,7 +401,9 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
     const uint64_t *__restrict__ c1, long long c1_stride,
     const uint64_t *__restrict__ ext, long long ext_stride, const ItemKeys items,
     uint64_t *__restrict__ acc, const Mod *__restrict__ mods, int l, int K,
-    int L, int alpha, int beta) {
+    int L, int alpha, int beta, const uint64_t *__restrict__ pre0 = nullptr,
+    const uint64_t *__restrict__ pre1 = nullptr, long long pre_stride = 0,
+    const uint64_t *__restrict__ pmod = nullptr) {
   const int n = blockIdx.x * TPB + threadIdx.x;
   const int it = blockIdx.y, t = blockIdx.z, ct = items.ct(it);
   const int lk = l + K, np = L + K;
@@ -380,6 +437,12 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
         mac128(s1, e[u], k1[u]);
       }
     }
+  }
+  if (pre0 != nullptr && t < l) {  // + P (pre0, pre1) on the Q limbs
+    const uint64_t pm = pmod[t];
+    const size_t at = ct * pre_stride + (size_t)t * kN + n;
+    mac128(s0, pre0[at], pm);
+    mac128(s1, pre1[at], pm);
   }
   uint64_t *o = acc + ((size_t)it * 2 * lk + t) * kN + n;
   o[0] = reduce128(s0.hi, s0.lo, M);
@@ -443,6 +506,27 @@ __global__ void __launch_bounds__(TPB) moddown_combine_kernel(
     const uint64_t *add = b ? add1 : add0;
     if (add) v = add_mod(v, add[ct * add_stride + (size_t)i * kN + src], q);
     out[items.out(it, out_stride) + ((size_t)b * l + i) * kN + k] = v;
+  }
+}
+
+// Fused relinearise + rescale, step 6: out_b[i] = (acc_b[i] - conv_b[i]) *
+// P^-1 * q_{l-1}^-1 mod q_i (acc already holds P d_b + IP_b), i < l-1.
+// grid (N/TPB, l-1, cts)
+__global__ void __launch_bounds__(TPB) moddown_rescale_combine_kernel(
+    const uint64_t *__restrict__ acc, const uint64_t *__restrict__ conv,
+    uint64_t *__restrict__ out, long long out_stride,
+    const ulonglong2 *__restrict__ pinv, const ulonglong2 *__restrict__ qinv,
+    const uint64_t *__restrict__ primes, int l, int K) {
+  const int k = blockIdx.x * TPB + threadIdx.x;
+  const int i = blockIdx.y, ct = blockIdx.z, lk = l + K;
+  const uint64_t q = primes[i];
+  const ulonglong2 pi = pinv[i], qi = qinv[i];
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    const uint64_t a = acc[(((size_t)ct * 2 + b) * lk + i) * kN + k];
+    const uint64_t c = conv[(((size_t)ct * 2 + b) * (l - 1) + i) * kN + k];
+    const uint64_t v = shoup(shoup(sub_mod(a, c, q), pi.x, pi.y, q), qi.x, qi.y, q);
+    out[ct * out_stride + ((size_t)b * (l - 1) + i) * kN + k] = v;
   }
 }
 
@@ -700,6 +784,72 @@ int b2f_relinearize(b2f_context *ctx, const uint64_t *ct3_in, uint64_t *ct_out,
   return ip_moddown(ctx, d2, s3, ext, (long long)beta * lk * kN, num_cts, l, it,
                     ct3_in, ct3_in + (size_t)l * kN, s3, ct_out, 2LL * l * kN,
                     acc, conv, s);
+}
+
+size_t b2f_relinearize_rescale_workspace(const b2f_context *ctx, int num_cts,
+                                         int l) {
+  if (!ctx || l < 2 || l > ctx->L || num_cts < 0) return 0;
+  return rotate_workspace(ctx, num_cts, l);
+}
+
+// Relinearisation and the rescale after it as one exact rounding division by
+// M = P q_{l-1}: Y_b = P d_b + IP_b(ModUp(d2), key) over Q_l u P, then
+// out_b = round(Y_b / M) over Q_{l-1}, with the removed limbs R = {q_{l-1}}
+// u P converted by the rounded (centred) fast base conversion.  Saves the
+// forward NTT of the l ModDown outputs and the rescale's own transforms.
+int b2f_relinearize_rescale(b2f_context *ctx, const uint64_t *ct3_in,
+                            uint64_t *ct_out, int num_cts, int l,
+                            const uint64_t *relin_key, void *ws, size_t ws_bytes,
+                            void *stream) {
+  B2F_RANGE("b2f_relinearize_rescale");
+  int rc = check_level(ctx, l, "b2f_relinearize_rescale");
+  if (rc) return rc;
+  B2F_CHECK_ARG(l >= 2, "b2f_relinearize_rescale: needs at least 2 limbs, got %d", l);
+  B2F_CHECK_ARG(ct3_in && ct_out && relin_key && num_cts >= 0,
+                "b2f_relinearize_rescale: null argument");
+  B2F_CHECK_ARG(ct3_in != ct_out,
+                "b2f_relinearize_rescale: in-place operation is not supported");
+  if (num_cts == 0) return B2F_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  Scratch sc{ctx, s};
+  if ((rc = sc.init(ws, ws_bytes, rotate_workspace(ctx, num_cts, l)))) return rc;
+  const LevelTables &T = ctx->levels[l];
+  const int K = ctx->K, L = ctx->L, beta = T.beta, lk = l + K;
+  uint64_t *xt = sc.take((size_t)num_cts * l * kN);
+  uint64_t *ext = sc.take((size_t)num_cts * beta * lk * kN);
+  uint64_t *acc = sc.take((size_t)num_cts * 2 * lk * kN);
+  uint64_t *conv = sc.take((size_t)num_cts * 2 * l * kN);
+  const long long s3 = 3LL * l * kN;
+  const uint64_t *d2 = ct3_in + 2 * (size_t)l * kN;
+  if ((rc = modup(ctx, d2, s3, num_cts, l, xt, ext, s))) return rc;
+  ItemKeys it{};
+  it.key[0] = relin_key;
+  it.g[0] = 1u;
+  it.shared = 1;
+  key_inner_product_kernel<<<dim3(kN / TPB, num_cts, lk), TPB, 0, s>>>(
+      d2, s3, ext, (long long)beta * lk * kN, it, acc, ctx->d_mod, l, K, L,
+      ctx->alpha, beta, ct3_in, ct3_in + (size_t)l * kN, s3, ctx->d_pmod);
+  B2F_LAUNCHED("key_inner_product_kernel");
+  // iNTT of the removed limbs of both polys, scaled by N^-1 (M/r)^-1
+  std::vector<LimbJob> rj;
+  for (int b = 0; b < 2; ++b)
+    for (int r = 0; r <= K; ++r) {
+      const uint32_t off = (uint32_t)(b * lk + l - 1 + r);
+      rj.push_back(LimbJob{off, off, (uint16_t)(r ? L + r - 1 : l - 1), (uint16_t)r, 0});
+    }
+  const LimbJob *d = job_table(ctx, {7, l}, rj);
+  if (!d) return B2F_ERR_NOMEM;
+  const long long as = 2LL * lk * kN;
+  if ((rc = launch_ntt(ctx, acc, as, acc, as, d, 2 * (K + 1), num_cts, 1,
+                       T.mdr_scale, s)))
+    return rc;
+  if ((rc = launch_moddown_rescale_conv(ctx, acc, conv, l, num_cts, s))) return rc;
+  if ((rc = ntt_polys(ctx, conv, 2 * num_cts, l - 1, 0, 0, s))) return rc;
+  moddown_rescale_combine_kernel<<<dim3(kN / TPB, l - 1, num_cts), TPB, 0, s>>>(
+      acc, conv, ct_out, 2LL * (l - 1) * kN, ctx->d_moddown_pinv, T.rescale_inv,
+      ctx->d_primes, l, K);
+  B2F_LAUNCHED("moddown_rescale_combine_kernel");
+  return B2F_OK;
 }
 
 size_t b2f_modup_batch_workspace(const b2f_context *ctx, int num_cts, int l) {

@@ -220,6 +220,16 @@ class NativeContext:
              _ptr(ws), ws.numel(), _stream())
         return out
 
+    def relinearize_rescale(self, ct3: torch.Tensor, l: int, key: torch.Tensor) -> torch.Tensor:
+        """Relinearise and rescale in one pass: [.., 3, l, N] -> [.., 2, l-1, N]."""
+
+        num = ct3.numel() // (3 * l * self.n)
+        out = self.empty(num, 2, l - 1) if ct3.dim() == 4 else self.empty(2, l - 1)
+        ws = self.workspace(lib.b2f_relinearize_rescale_workspace(self.handle, num, l))
+        call("b2f_relinearize_rescale", self.handle, _ptr(ct3), _ptr(out), num, l,
+             _ptr(key), _ptr(ws), ws.numel(), _stream())
+        return out
+
     def modup(self, ct: torch.Tensor, l: int, num_cts: int = 1) -> torch.Tensor:
         """ModUp digits of c1: [beta, l+K, N] (one ciphertext) or
         [num_cts, beta, l+K, N]."""

@@ -1,7 +1,7 @@
 """``easyfhe.fhe`` -- the CKKS evaluation surface llama3fhe calls, on libb200fhe.
 
 Names, argument meanings, ownership and error types follow the reference's
-call sites (SURVEY section 8(b) lists them; each function cites one).  Every
+call sites (each function cites one).  Every
 operation runs in the CUDA kernels of libb200fhe on the current torch stream;
 Python only validates levels and bookkeeps ciphertext state.
 
@@ -536,11 +536,15 @@ def rescale(ct: Ciphertext, context) -> Ciphertext:
     out = ctx.native.rescale(ct.data, _polys_total(ct), l)
     shape = list(ct.data.shape)
     shape[-2] = l - 1
-    state = ct.state.replace(
+    return _new(out.view(shape), ct, _rescaled_state(ct, ctx))
+
+
+def _rescaled_state(ct: Ciphertext, ctx) -> CipherState:
+    l = _limbs(ct)
+    return ct.state.replace(
         cur_limbs=l - 1,
         scale_degree=max(1, int(ct.state.scale_degree) - 1),
         scaling_factor=float(ct.state.scaling_factor) / ctx.rescale_divisor_at(l - 1))
-    return _new(out.view(shape), ct, state)
 
 
 def align_to(ct: Ciphertext, state: CipherState, context) -> Ciphertext:
@@ -612,6 +616,23 @@ def homo_relinearize(ct: Ciphertext, context) -> Ciphertext:
     return _new(out, ct)
 
 
+def _relinearize_rescale(ct: Ciphertext, context) -> Ciphertext:
+    """rescale(homo_relinearize(ct)) as one native pass (b2f_relinearize_rescale):
+    the ModDown by P and the division by the last prime merged into one
+    rounding division."""
+
+    ctx = _ctx_of(context)
+    if ct.polys == 2:
+        return rescale(ct, context)
+    if ctx.relin_key is None:
+        raise ValueError("context has no relinearisation key")
+    l = _limbs(ct)
+    if l < 2:
+        raise ValueError("rescale needs at least two limbs")
+    out = ctx.native.relinearize_rescale(ct.data, l, ctx.relin_key)
+    return _new(out, ct, _rescaled_state(ct, ctx))
+
+
 def homo_mul_relin(a: Ciphertext, b: Ciphertext, context) -> Ciphertext:
     """a * b, relinearised (llama3fhe/operators/primitives.py:21-31)."""
 
@@ -624,7 +645,7 @@ def homo_mul_relin_rescale_postop(left: Ciphertext, right: Ciphertext, context,
     """rescale(relin(l * r)), then optionally times 2, minus `sub`, plus `scalar`
     (llama3fhe/operators/nonlinear/polynomial.py:108-159)."""
 
-    out = rescale(homo_mul_relin(left, right, context), context)
+    out = _relinearize_rescale(homo_mul_no_relin(left, right, context), context)
     if apply_double:
         out = homo_add(out, out, context)
     if sub is not None:
@@ -873,7 +894,7 @@ def pack_cipher_batch(items: Iterable[Ciphertext]) -> Ciphertext:
 
 # ---------------------------------------------------------------------------
 # encrypted-state serialisation (resumable runs: limbs + state at a stage
-# boundary; the reference has no counterpart, SURVEY-style optional)
+# boundary; the reference has no counterpart of its own)
 # ---------------------------------------------------------------------------
 
 

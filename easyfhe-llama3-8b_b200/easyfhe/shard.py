@@ -1,6 +1,6 @@
 """Work partitioning across the GPUs of one box (one process per GPU).
 
-The CKKS path shards by independent units (SURVEY section 8(e)): the
+The CKKS path shards by independent units: the
 feature-major token-shard ciphertexts, their complex pairs and the output
 ciphertexts of a linear are independent through every linear, elementwise
 op and bootstrap.  Each rank owns a contiguous block of units; the only data

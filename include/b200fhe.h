@@ -64,8 +64,7 @@ int b2f_context_destroy(b2f_context *ctx);
 /* log_n, L, K, dnum, alpha (limbs per digit), digits (top level) */
 int b2f_context_info(const b2f_context *ctx, int *info6);
 
-/* ---- number-theoretic transform (no direct Python site; inside every op,
- * SURVEY a10) ---- */
+/* ---- number-theoretic transform (inside every op; no direct Python site) ---- */
 int b2f_ntt(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
             int p_limbs, int inverse, void *stream);
 
@@ -96,6 +95,20 @@ size_t b2f_relinearize_workspace(const b2f_context *ctx, int num_cts, int l);
 int b2f_relinearize(b2f_context *ctx, const uint64_t *ct3_in, uint64_t *ct_out,
                     int num_cts, int l, const uint64_t *relin_key, void *ws,
                     size_t ws_bytes, void *stream);
+
+/* Relinearisation and the rescale after it in one pass: the rescale of
+ * homo_mul_relin_rescale_postop (llama3fhe/operators/nonlinear/polynomial.py:
+ * 108-159) merged into the ModDown as one rounding division by P q_{l-1}.
+ * ct3_in [num_cts][3][l][N] -> ct_out [num_cts][2][l-1][N] (l >= 2): each
+ * coefficient is round(Y / (P q_{l-1})) for Y = P (d0, d1) + KeySwitch
+ * accumulator, the same ciphertext as b2f_relinearize then b2f_rescale except
+ * where a rounding tie moves (probability about K / q per coefficient). */
+size_t b2f_relinearize_rescale_workspace(const b2f_context *ctx, int num_cts,
+                                         int l);
+int b2f_relinearize_rescale(b2f_context *ctx, const uint64_t *ct3_in,
+                            uint64_t *ct_out, int num_cts, int l,
+                            const uint64_t *relin_key, void *ws,
+                            size_t ws_bytes, void *stream);
 
 /* Hoisting: ModUp of c1 once into the extended digits
  * ext[digit][l+K][N] (NTT form) ...

@@ -650,6 +650,94 @@ void orc_rotate_hoisted_ext(const orc_ctx *c, const uint64_t *ct, int l,
   free(ext);
 }
 
+/* Relinearisation fused with the rescale that follows it
+ * (homo_mul_relin_rescale_postop, llama3fhe/operators/nonlinear/polynomial.py:
+ * 108-159): for ct3 = (d0, d1, d2) at l limbs, acc = IP(ModUp(d2), relin key)
+ * over Q_l u P and Y_b = P d_b + acc_b (the P limbs of P d_b are zero); with
+ * R = {q_{l-1}} u P and M = P q_{l-1},
+ *   out_b = (Y_b - C(Y_b[R])) * M^-1   over Q_{l-1},
+ * C(y) = sum_r y_r (M/r) - v M mod q_i,  y_r = [Y_r (M/r)^-1]_r,
+ * v = floor(sum_r y_r / r + 1/2) in binary64 (products y_r * (1/r), then
+ * sums in r order, no fused multiply-add): C(y) is the centred residue of Y
+ * mod M (Halevi-Polyakov-Shoup 2019), so out is Y / M rounded to the
+ * nearest integer.  One exact rounding division by P q_{l-1} in place of
+ * ModDown by P followed by the rescale by q_{l-1}. */
+void orc_relin_rescale(const orc_ctx *c, const uint64_t *ct3, int l,
+                       const uint64_t *key, uint64_t *out) {
+  const uint64_t n = c->n;
+  const int K = c->K, lk = l + K, R = K + 1;
+  int beta;
+  uint64_t *ext = modup(c, ct3 + 2 * (uint64_t)l * n, l, &beta);
+  uint64_t *acc[2];
+  acc[0] = (uint64_t *)malloc(8 * n * lk);
+  acc[1] = (uint64_t *)malloc(8 * n * lk);
+  key_inner_product(c, ext, l, beta, key, acc[0], acc[1]);
+  int rp[65];  /* prime index of removed limb r */
+  rp[0] = l - 1;
+  for (int k = 0; k < K; k++) rp[1 + k] = c->L + k;
+  uint64_t *z = (uint64_t *)malloc(8 * n * R);
+  double rinv[65];
+  for (int r = 0; r < R; r++) rinv[r] = 1.0 / (double)c->primes[rp[r]];
+  for (int b = 0; b < 2; b++) {
+    const uint64_t *d = ct3 + (uint64_t)b * l * n, *Y = acc[b];
+    /* removed limbs in NTT form, then coefficients times (M/r)^-1 mod r */
+    for (int r = 0; r < R; r++) {
+      const uint64_t pr = c->primes[rp[r]];
+      uint64_t pm = 1, mr = 1; /* P mod pr, (M/r) mod pr */
+      for (int k = 0; k < K; k++) pm = mulmod(pm, c->primes[c->L + k] % pr, pr);
+      for (int r2 = 0; r2 < R; r2++)
+        if (r2 != r) mr = mulmod(mr, c->primes[rp[r2]] % pr, pr);
+      uint64_t *zr = z + (uint64_t)r * n;
+      for (uint64_t x = 0; x < n; x++)
+        zr[x] = r == 0 ? addmod(mulmod(pm, d[(uint64_t)(l - 1) * n + x], pr),
+                                Y[(uint64_t)(l - 1) * n + x], pr)
+                       : Y[((uint64_t)l + r - 1) * n + x];
+      orc_ntt_inverse(c, zr, rp[r]);
+      const uint64_t inv = invmod(mr, pr);
+      for (uint64_t x = 0; x < n; x++) zr[x] = mulmod(zr[x], inv, pr);
+    }
+#pragma omp parallel for schedule(dynamic)
+    for (int i = 0; i < l - 1; i++) {
+      const uint64_t qi = c->primes[i];
+      uint64_t mhat[65], pm = 1, minv = 1;
+      for (int k = 0; k < K; k++) pm = mulmod(pm, c->primes[c->L + k] % qi, qi);
+      for (int r = 0; r < R; r++) {
+        uint64_t m = 1;
+        for (int r2 = 0; r2 < R; r2++)
+          if (r2 != r) m = mulmod(m, c->primes[rp[r2]] % qi, qi);
+        mhat[r] = m;
+      }
+      const uint64_t mq = mulmod(pm, c->primes[l - 1] % qi, qi); /* M mod q_i */
+      minv = invmod(mq, qi);
+      uint64_t *conv = (uint64_t *)malloc(8 * n);
+      for (uint64_t x = 0; x < n; x++) {
+        u128 sum = 0;
+        volatile double f = 0.0;
+        for (int r = 0; r < R; r++) {
+          const uint64_t y = z[(uint64_t)r * n + x];
+          sum += (u128)y * mhat[r];
+          volatile double t = (double)y * rinv[r];
+          f = f + t;
+        }
+        volatile double h = f + 0.5;
+        const uint64_t v = (uint64_t)h;
+        conv[x] = submod((uint64_t)(sum % qi), mulmod(v % qi, mq, qi), qi);
+      }
+      orc_ntt_forward(c, conv, i);
+      for (uint64_t x = 0; x < n; x++) {
+        const uint64_t y = addmod(mulmod(pm, d[(uint64_t)i * n + x], qi),
+                                  Y[(uint64_t)i * n + x], qi);
+        out[((uint64_t)b * (l - 1) + i) * n + x] = mulmod(submod(y, conv[x], qi), minv, qi);
+      }
+      free(conv);
+    }
+  }
+  free(z);
+  free(acc[0]);
+  free(acc[1]);
+  free(ext);
+}
+
 /* ModDown of num_polys extended polys (l+K limbs each) to l limbs. */
 void orc_moddown(const orc_ctx *c, const uint64_t *in, int num_polys, int l,
                  uint64_t *out) {

@@ -87,6 +87,10 @@ void orc_rotate_hoisted(const orc_ctx *ctx, const uint64_t *ct, int l,
 void orc_rotate_hoisted_ext(const orc_ctx *ctx, const uint64_t *ct, int l,
                             int count, const uint64_t *galois,
                             const uint64_t *const *keys, uint64_t *out);
+/* relinearisation fused with the following rescale: ct3 (3 x l limbs) ->
+ * out (2 x (l-1) limbs), one division by P q_{l-1} */
+void orc_relin_rescale(const orc_ctx *c, const uint64_t *ct3, int l,
+                       const uint64_t *key, uint64_t *out);
 void orc_moddown(const orc_ctx *ctx, const uint64_t *in, int num_polys, int l,
                  uint64_t *out);
 void orc_rescale(const orc_ctx *ctx, const uint64_t *in, int num_polys, int l,

@@ -72,6 +72,7 @@ def lib():
                                              _u64p]
         L.orc_moddown.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p]
         L.orc_rescale.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p]
+        L.orc_relin_rescale.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, _u64p, _u64p]
         L.orc_modraise.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p]
         L.orc_mul_i.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.orc_sample_secret.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int, _i64p]
@@ -219,6 +220,13 @@ class Oracle:
         keys = [_u64(k) if k is not None else np.zeros(1, dtype=np.uint64) for k in keys]
         arr = (_u64p * count)(*[_p(k) for k in keys])
         lib().orc_rotate_hoisted_ext(self._h, _p(_u64(ct)), l, count, _p(g), arr, _p(out))
+        return out
+
+    def relin_rescale(self, ct3: np.ndarray, l: int, key: np.ndarray) -> np.ndarray:
+        """Relinearise (3 x l limbs) and rescale in one division by P q_{l-1}."""
+
+        out = np.zeros((2, l - 1, self.n), dtype=np.uint64)
+        lib().orc_relin_rescale(self._h, _p(_u64(ct3)), l, _p(_u64(key)), _p(out))
         return out
 
     def moddown(self, data: np.ndarray, num_polys: int, l: int) -> np.ndarray:

@@ -1,4 +1,4 @@
-"""CKKS bootstrapping on the GPU: ModRaise bit-exact against
+"""CKKS bootstrapping on the GPU (bs.bootstrap): ModRaise bit-exact against
 the oracle, then bs.bootstrap at the reference's layer parameters
 (assets/feature_major.json: logN 16, depth 37, dnum 5, dcrtBits 59, firstMod
 60; BootstrapSpec(15, (4, 4), output_levels = depth - 18), llama3fhe/model.py:

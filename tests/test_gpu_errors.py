@@ -1,4 +1,4 @@
-"""Failure paths on the GPU (SURVEY section 5, failure detection): argument
+"""Failure paths on the GPU (failure detection): argument
 and level errors surface as Python exceptions from the C-ABI status codes,
 before any kernel runs, and leave the context usable; ciphertexts survive a
 save / load round trip at a stage boundary."""

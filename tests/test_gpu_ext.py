@@ -1,4 +1,4 @@
-"""GPU parity of the extended-basis batch ops (SURVEY row a7): hoisted
+"""GPU parity of the extended-basis batch ops: hoisted
 rotations left in Q_l u P, the grouped pairwise MAC and ModDown, bit-exact
 against the oracle, and the attention input call sequence
 (llama3fhe/operators/attention/input.py:792-827) decrypted."""

@@ -1,4 +1,4 @@
-"""GPU parity of the feature-major linear path (SURVEY rows a1-a3): the
+"""GPU parity of the feature-major linear path: the
 plaintext x ciphertext MAC and its Horner over giant rotations against the CPU
 oracle (bit-exact), the CUDA diagonal packers against the reference formula
 pinned by the golden fixtures, and the whole LinearOperator.apply call sequence

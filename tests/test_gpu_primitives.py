@@ -1,5 +1,5 @@
 """GPU parity of the CKKS primitives against the CPU oracle, bit-exact in RNS
-residues.  Inputs are seeded uniform
+residues (rotation, rescale, elementwise ops, NTT, keys).  Inputs are seeded uniform
 residues at N = 2^16 with 50-bit NTT primes (q = 1 mod 2^17), the primitive
 microbench parameters, plus one small parameter set whose special primes
 cover a digit so that decrypted values are meaningful."""
@@ -170,6 +170,30 @@ def test_relinearize_bit_exact():
     w1 = (ct3[1].astype(object) + d1.astype(object)) % q
     assert np.array_equal(got[0], w0.astype(np.uint64))
     assert np.array_equal(got[1], w1.astype(np.uint64))
+
+
+@pytest.mark.parametrize("L,K,dnum,l,cts", [(8, 2, 3, 6, 1), (8, 2, 3, 2, 2),
+                                             (10, 4, 5, 10, 1), (12, 8, 3, 7, 2)])
+def test_relinearize_rescale_bit_exact(L, K, dnum, l, cts):
+    """The fused relinearise + rescale against the oracle's rounding division
+    by P q_{l-1}, and against the GPU's own relinearise then rescale (equal but
+    for rounding ties, probability about K / q per coefficient).  K = 2, 4, 8
+    reach the three widths of the tensor-core conversion (K + 2 words)."""
+
+    from easyfhe import core
+
+    ctx, orc = pair(L, K, dnum)
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(9, 192))
+    rk = ctx.keygen_relin(s_ntt, seed=6)
+    rng = np.random.default_rng(100 + l + K)
+    ct3 = np.stack([rand_residues(rng, ctx.primes[:l], 3) for _ in range(cts)])
+    got = to_host(ctx.relinearize_rescale(to_dev(ct3), l, rk))
+    assert got.shape == (cts, 2, l - 1, N)
+    rk_h = to_host(rk)
+    for c in range(cts):
+        assert np.array_equal(got[c], orc.relin_rescale(ct3[c], l, rk_h)), c
+    two = to_host(ctx.rescale(ctx.relinearize(to_dev(ct3), l, rk), 2 * cts, l))
+    assert np.array_equal(got.reshape(two.shape), two)
 
 
 @pytest.mark.parametrize("l", [2, 9, 16])

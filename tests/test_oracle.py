@@ -196,6 +196,12 @@ def test_relinearisation_decrypts(oracle_mod):
     rs = o.rescale(prod.reshape(2 * l, -1), 2, l)
     dec = o.decode(o.decrypt(rs, l - 1, s_ntt), l - 1, slots, scale * scale / o.q[l - 1])
     assert np.max(np.abs(dec.real - x * y)) < 1e-3
+    # relinearise + rescale as one rounding division by P q_{l-1}: the same
+    # ciphertext as the two steps (they differ only at rounding ties, with
+    # probability about K / q per coefficient)
+    ct3 = np.stack([d0, d1, d2]).astype(np.uint64)
+    fused = o.relin_rescale(ct3, l, rk)
+    assert np.array_equal(fused.reshape(rs.shape), rs)
 
 
 def test_secret_sampler(oracle_mod):
