@@ -141,6 +141,10 @@ struct b2f_context {
   b2f::Red79 *d_red79 = nullptr;      // L+K constants of reduce79
   ulonglong2 *d_tw_fwd = nullptr;     // (L+K) x N  (psi^bitrev(k), Shoup)
   ulonglong2 *d_tw_inv = nullptr;     // (L+K) x N
+  // binary64 butterflies, when every prime is below 2^50: the same twiddles
+  // as doubles, and 1/q per prime
+  bool ntt_fp64_ok = false, ntt_fp64 = false;
+  double *d_twd_fwd = nullptr, *d_twd_inv = nullptr, *d_qinv = nullptr;
   ulonglong2 *d_ninv = nullptr;       // L+K: N^-1
   ulonglong2 *d_i_factor = nullptr;   // L+K: psi^(N/2) (multiply by i)
   ulonglong2 *d_moddown_scale = nullptr;  // K: N^-1 * [Phat_k^-1] mod p_k

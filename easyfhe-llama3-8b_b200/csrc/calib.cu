@@ -1,33 +1,33 @@
-// Integer-multiply roofline of this GPU: the rate of the NTT's lazy Shoup
-// butterfly when nothing but registers is involved (16 independent values per
-// thread, one twiddle, every SM full).  The NTT kernels are bound by this
-// 64-bit multiply work on CUDA cores rather than by HBM, so bench.py reports
-// their butterfly rate against the rate measured here.
+// Butterfly roofline of this GPU: the rate of the NTT's lazy forward
+// butterfly, in the arithmetic the context's NTT uses (64-bit integer Shoup,
+// or binary64 when every prime is below 2^50), when nothing but registers is
+// involved (16 independent values per thread, one twiddle, every SM full).
+// The NTT kernels are bound by this multiply work on CUDA cores rather than
+// by HBM, so bench.py reports their butterfly rate against the rate measured
+// here.
 #include "b2f_internal.h"
+#include "ntt_arith.cuh"
 
 namespace b2f {
 namespace {
 
-__global__ void __launch_bounds__(256) butterfly_peak_kernel(uint64_t *out, uint64_t q,
-                                                             uint64_t w, uint64_t ws,
-                                                             int iters) {
-  uint64_t x[16];
-  const uint64_t q2 = 2 * q;
+template <class A>
+__global__ void __launch_bounds__(256) butterfly_peak_kernel(uint64_t *out,
+                                                             const uint64_t *primes,
+                                                             const double *qinv,
+                                                             ulonglong2 w_int, int iters) {
+  const A ar(primes, qinv, 0);
+  const typename A::W w = A::scale(w_int);
+  typename A::V x[16];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) x[i] = (threadIdx.x * 16 + i + blockIdx.x) % q;
+  for (int i = 0; i < 16; ++i) x[i] = A::from_word((threadIdx.x * 16 + i + blockIdx.x) % primes[0]);
   for (int it = 0; it < iters; ++it) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint64_t &a = x[i], &b = x[i + 8];
-      const uint64_t u = a >= q2 ? a - q2 : a;
-      const uint64_t t = b * w - __umul64hi(b, ws) * q;
-      a = u + t;
-      b = u - t + q2;
-    }
+    for (int i = 0; i < 8; ++i) ct_bfly(ar, x[i], x[i + 8], w);
   }
   uint64_t s = 0;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) s ^= x[i];
+  for (int i = 0; i < 16; ++i) s ^= A::bits(x[i]);
   out[(size_t)blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
@@ -53,9 +53,18 @@ extern "C" int b2f_butterfly_peak(b2f_context *ctx, int iters, double *per_secon
   cudaError_t err = cudaEventCreate(&e0);
   if (err == cudaSuccess) err = cudaEventCreate(&e1);
   if (err == cudaSuccess) {
-    butterfly_peak_kernel<<<blocks, threads, 0, s>>>(out, q, w, ws, iters);  // warm-up
+    const ulonglong2 wi = make_ulonglong2(w, ws);
+    auto run = [&]() {
+      if (ctx->ntt_fp64)
+        butterfly_peak_kernel<FpArith><<<blocks, threads, 0, s>>>(out, ctx->d_primes,
+                                                                  ctx->d_qinv, wi, iters);
+      else
+        butterfly_peak_kernel<IntArith><<<blocks, threads, 0, s>>>(out, ctx->d_primes,
+                                                                   ctx->d_qinv, wi, iters);
+    };
+    run();  // warm-up
     cudaEventRecord(e0, s);
-    butterfly_peak_kernel<<<blocks, threads, 0, s>>>(out, q, w, ws, iters);
+    run();
     cudaEventRecord(e1, s);
     err = cudaEventSynchronize(e1);
   }

@@ -167,6 +167,21 @@ static int build_tables(b2f_context *ctx) {
   }
   if ((rc = upload(ctx, &ctx->d_tw_fwd, twf))) return rc;
   if ((rc = upload(ctx, &ctx->d_tw_inv, twi))) return rc;
+  // binary64 NTT (every prime below 2^50): twiddles as doubles and 1/q
+  ctx->ntt_fp64_ok = true;
+  for (int i = 0; i < np; ++i) ctx->ntt_fp64_ok = ctx->ntt_fp64_ok && P[i] < (1ull << 50);
+  if (ctx->ntt_fp64_ok) {
+    std::vector<double> tdf((size_t)np * n), tdi((size_t)np * n), qinv(np);
+    for (size_t k = 0; k < tdf.size(); ++k) {
+      tdf[k] = (double)twf[k].x;
+      tdi[k] = (double)twi[k].x;
+    }
+    for (int i = 0; i < np; ++i) qinv[i] = 1.0 / (double)P[i];
+    if ((rc = upload(ctx, &ctx->d_twd_fwd, tdf))) return rc;
+    if ((rc = upload(ctx, &ctx->d_twd_inv, tdi))) return rc;
+    if ((rc = upload(ctx, &ctx->d_qinv, qinv))) return rc;
+  }
+  ctx->ntt_fp64 = ctx->ntt_fp64_ok;
   if ((rc = upload(ctx, &ctx->d_ninv, ninv))) return rc;
   if ((rc = upload(ctx, &ctx->d_i_factor, ifac))) return rc;
 
@@ -423,6 +438,23 @@ int b2f_context_destroy(b2f_context *ctx) {
   for (void *p : ctx->owned) cudaFree(p);
   delete ctx;
   return B2F_OK;
+}
+
+int b2f_context_set_ntt_arith(b2f_context *ctx, int mode) {
+  B2F_CHECK_ARG(ctx, "b2f_context_set_ntt_arith: null context");
+  B2F_CHECK_ARG(mode >= 0 && mode <= 2, "b2f_context_set_ntt_arith: mode %d not in 0..2",
+                mode);
+  if (mode == 2 && !ctx->ntt_fp64_ok) {
+    set_error("b2f_context_set_ntt_arith: binary64 butterflies need every prime "
+              "below 2^50");
+    return B2F_ERR_UNSUPPORTED;
+  }
+  ctx->ntt_fp64 = mode == 1 ? false : ctx->ntt_fp64_ok;
+  return B2F_OK;
+}
+
+int b2f_context_ntt_arith(const b2f_context *ctx) {
+  return ctx && ctx->ntt_fp64 ? 2 : 1;
 }
 
 int b2f_context_info(const b2f_context *ctx, int *info) {

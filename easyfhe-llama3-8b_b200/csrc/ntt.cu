@@ -29,6 +29,7 @@
 #include <cooperative_groups.h>
 
 #include "b2f_internal.h"
+#include "ntt_arith.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -50,81 +51,61 @@ struct NttParams {
   uint64_t *out;
   const LimbJob *jobs;
   long long in_stride, out_stride;
-  const ulonglong2 *tw;      // [prime][N]
+  const void *tw;            // [prime][N]: ulonglong2 (integer) or double
   const uint64_t *primes;
+  const double *qinv;        // binary64 arithmetic only
   const ulonglong2 *scales;  // inverse only
   int jobs_per_item;
   int items;
 };
-
-__device__ __forceinline__ ulonglong2 ldtw(const ulonglong2 *tw, int idx) {
-  return __ldg(tw + idx);
-}
 
 // twiddle index of stage s for global element j: 2^s + j / 2^(16-s)
 __device__ __forceinline__ int tw_index(int s, int j) {
   return (1 << s) + (j >> (kLogN - s));
 }
 
-// forward butterfly, values in [0, 4q): (x, y) -> (x + w y, x - w y)
-__device__ __forceinline__ void ct_bfly(uint64_t &x, uint64_t &y, ulonglong2 w,
-                                        uint64_t q, uint64_t q2) {
-  uint64_t u = x >= q2 ? x - q2 : x;
-  uint64_t t = y * w.x - __umul64hi(y, w.y) * q;
-  x = u + t;
-  y = u - t + q2;
-}
-
-// inverse butterfly, values in [0, 2q): (x, y) -> (x + y, (x - y) w)
-__device__ __forceinline__ void gs_bfly(uint64_t &x, uint64_t &y, ulonglong2 w,
-                                        uint64_t q, uint64_t q2) {
-  uint64_t u = x + y;
-  u = u >= q2 ? u - q2 : u;
-  uint64_t t = x - y + q2;
-  x = u;
-  y = t * w.x - __umul64hi(t, w.y) * q;
-}
-
 // Four CT stages s0..s0+3 on 16 registers with element index
 // j(k) = base + k * stride; at local stage t the pairs are (k, k + d),
 // d = 8 >> t, and each block of 2d registers shares one twiddle.
-__device__ __forceinline__ void ct_pass(uint64_t (&x)[16], const ulonglong2 *tw,
-                                        int s0, int base, int stride,
-                                        uint64_t q, uint64_t q2) {
+template <class A>
+__device__ __forceinline__ void ct_pass(const A &ar, typename A::V (&x)[16],
+                                        const typename A::W *tw, int s0, int base,
+                                        int stride) {
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const int d = 8 >> t;
 #pragma unroll
     for (int blk = 0; blk < 16; blk += 2 * d) {
-      const ulonglong2 w = ldtw(tw, tw_index(s0 + t, base + blk * stride));
+      const typename A::W w = A::ldtw(tw, tw_index(s0 + t, base + blk * stride));
 #pragma unroll
-      for (int k = blk; k < blk + d; ++k) ct_bfly(x[k], x[k + d], w, q, q2);
+      for (int k = blk; k < blk + d; ++k) ct_bfly(ar, x[k], x[k + d], w);
     }
   }
 }
 
-__device__ __forceinline__ void gs_pass(uint64_t (&x)[16], const ulonglong2 *tw,
-                                        int s0, int base, int stride,
-                                        uint64_t q, uint64_t q2) {
+template <class A>
+__device__ __forceinline__ void gs_pass(const A &ar, typename A::V (&x)[16],
+                                        const typename A::W *tw, int s0, int base,
+                                        int stride) {
 #pragma unroll
   for (int t = 3; t >= 0; --t) {
     const int d = 8 >> t;
 #pragma unroll
     for (int blk = 0; blk < 16; blk += 2 * d) {
-      const ulonglong2 w = ldtw(tw, tw_index(s0 + t, base + blk * stride));
+      const typename A::W w = A::ldtw(tw, tw_index(s0 + t, base + blk * stride));
 #pragma unroll
-      for (int k = blk; k < blk + d; ++k) gs_bfly(x[k], x[k + d], w, q, q2);
+      for (int k = blk; k < blk + d; ++k) gs_bfly(ar, x[k], x[k + d], w);
     }
   }
 }
 
-template <int STRIDE>
-__device__ __forceinline__ void load16(uint64_t (&x)[16], const uint64_t *buf, int l) {
+template <int STRIDE, class V>
+__device__ __forceinline__ void load16(V (&x)[16], const V *buf, int l) {
 #pragma unroll
   for (int k = 0; k < 16; ++k) x[k] = buf[pad(l + STRIDE * k)];
 }
-template <int STRIDE>
-__device__ __forceinline__ void store16(const uint64_t (&x)[16], uint64_t *buf, int l) {
+template <int STRIDE, class V>
+__device__ __forceinline__ void store16(const V (&x)[16], V *buf, int l) {
 #pragma unroll
   for (int k = 0; k < 16; ++k) buf[pad(l + STRIDE * k)] = x[k];
 }
@@ -137,9 +118,13 @@ __device__ __forceinline__ void store16(const uint64_t (&x)[16], uint64_t *buf, 
 // Warp w touches only words [512 w, 512 w + 512) in B and C, so the B <-> C
 // exchange and the output staging need only warp synchronisation.
 
+template <class A>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     ntt_fwd_kernel(NttParams P) {
+  using V = typename A::V;
+  using W = typename A::W;
   extern __shared__ __align__(16) uint64_t buf[];
+  V *vb = reinterpret_cast<V *>(buf);
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -151,41 +136,41 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   const LimbJob job = P.jobs[job_id / P.items];
   const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
   uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
-  const uint64_t q = P.primes[job.prime], q2 = 2 * q;
-  const ulonglong2 *tw = P.tw + (size_t)job.prime * kN;
+  const A ar(P.primes, P.qinv, job.prime);
+  const W *tw = static_cast<const W *>(P.tw) + (size_t)job.prime * kN;
 
-  uint64_t x[16];
+  V x[16];
   // stages 0-2 on columns c0, c0+1 (rows k at stride 8192), straight from HBM
   const int c0 = rank * 1024 + 2 * tid;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + c0 + k * BLK);
-    x[k] = v.x;
-    x[8 + k] = v.y;
+    x[k] = A::from_word(v.x);
+    x[8 + k] = A::from_word(v.y);
   }
   {
     // stage by stage over both columns, one twiddle live at a time
     {
-      const ulonglong2 w = ldtw(tw, 1);
+      const W w = A::ldtw(tw, 1);
 #pragma unroll
       for (int h = 0; h < 16; h += 8)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) ct_bfly(x[h + k], x[h + k + 4], w, q, q2);
+        for (int k = 0; k < 4; ++k) ct_bfly(ar, x[h + k], x[h + k + 4], w);
     }
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
-      const ulonglong2 w = ldtw(tw, 2 + m);
+      const W w = A::ldtw(tw, 2 + m);
 #pragma unroll
       for (int h = 0; h < 16; h += 8) {
-        ct_bfly(x[h + 4 * m], x[h + 4 * m + 2], w, q, q2);
-        ct_bfly(x[h + 4 * m + 1], x[h + 4 * m + 3], w, q, q2);
+        ct_bfly(ar, x[h + 4 * m], x[h + 4 * m + 2], w);
+        ct_bfly(ar, x[h + 4 * m + 1], x[h + 4 * m + 3], w);
       }
     }
 #pragma unroll
     for (int k = 0; k < 8; k += 2) {
-      const ulonglong2 w = ldtw(tw, 4 + k / 2);
+      const W w = A::ldtw(tw, 4 + k / 2);
 #pragma unroll
-      for (int h = 0; h < 16; h += 8) ct_bfly(x[h + k], x[h + k + 1], w, q, q2);
+      for (int h = 0; h < 16; h += 8) ct_bfly(ar, x[h + k], x[h + k + 1], w);
     }
   }
   // every CTA of the cluster is resident before its shared memory is written;
@@ -199,26 +184,26 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     for (int k = 0; k < 8; ++k) {
       uint32_t remote;
       asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(k));
-      asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};" ::"r"(remote), "l"(x[k]),
-                   "l"(x[8 + k])
+      asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};" ::"r"(remote),
+                   "l"(A::bits(x[k])), "l"(A::bits(x[8 + k]))
                    : "memory");
     }
   }
   cluster.sync();
 
   const int jb = rank * BLK;
-  load16<512>(x, buf, tid);
-  ct_pass(x, tw, 3, jb + tid, 512, q, q2);
-  store16<512>(x, buf, tid);
+  load16<512>(x, vb, tid);
+  ct_pass(ar, x, tw, 3, jb + tid, 512);
+  store16<512>(x, vb, tid);
   __syncthreads();
   const int lb = warp * SEG + lane;
-  load16<32>(x, buf, lb);
-  ct_pass(x, tw, 7, jb + lb, 32, q, q2);
-  store16<32>(x, buf, lb);
+  load16<32>(x, vb, lb);
+  ct_pass(ar, x, tw, 7, jb + lb, 32);
+  store16<32>(x, vb, lb);
   __syncwarp();
   const int lc = (tid >> 1) * 32 + (tid & 1);
-  load16<2>(x, buf, lc);
-  ct_pass(x, tw, 11, jb + lc, 2, q, q2);
+  load16<2>(x, vb, lc);
+  ct_pass(ar, x, tw, 11, jb + lc, 2);
   const bool odd = tid & 1;
   const int je = jb + (tid >> 1) * 32;
   // butterflies k (even lane) and k+1 (odd lane) of each pair: one
@@ -227,25 +212,23 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
 #pragma unroll
   for (int k = 0; k < 16; k += 2) {
     // even lane holds X_k, X_{k+1}; odd lane holds Y_k, Y_{k+1}
-    const uint64_t give = odd ? x[k] : x[k + 1];
-    const uint64_t got = __shfl_xor_sync(0xffffffffu, give, 1);
-    const uint64_t X = odd ? got : x[k], Y = odd ? x[k + 1] : got;
-    const ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * (k + (odd ? 1 : 0))));
-    const uint64_t u = X >= q2 ? X - q2 : X;
-    const uint64_t t = Y * w.x - __umul64hi(Y, w.y) * q;
-    uint64_t a = u + t, b = u - t + q2;  // outputs of this lane's butterfly
-    a = a >= q2 ? a - q2 : a;
-    a = a >= q ? a - q : a;
-    b = b >= q2 ? b - q2 : b;
-    b = b >= q ? b - q : b;
-    // even lane keeps a = X'_k and sends b = Y'_k; odd keeps b = Y'_{k+1}, sends a
-    const uint64_t back = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
-    x[k] = odd ? back : a;       // even: X'_k;  odd: Y'_k (from even)
-    x[k + 1] = odd ? b : back;   // even: X'_{k+1} (from odd);  odd: Y'_{k+1}
+    const V give = odd ? x[k] : x[k + 1];
+    const V got = __shfl_xor_sync(0xffffffffu, give, 1);
+    const V X = odd ? got : x[k], Y = odd ? x[k + 1] : got;
+    const W w = A::ldtw(tw, tw_index(15, je + 2 * (k + (odd ? 1 : 0))));
+    const V u = ar.red2(X);
+    const V t = ar.mul(Y, w);
+    // outputs of this lane's butterfly, fully reduced
+    const V ra = ar.red1(ar.red2(ar.add(u, t))), rb = ar.red1(ar.red2(ar.sub2q(u, t)));
+    // even lane keeps ra = X'_k and sends rb = Y'_k; odd keeps rb = Y'_{k+1}, sends ra
+    const V back = __shfl_xor_sync(0xffffffffu, odd ? ra : rb, 1);
+    x[k] = odd ? back : ra;       // even: X'_k;  odd: Y'_k (from even)
+    x[k + 1] = odd ? rb : back;   // even: X'_{k+1} (from odd);  odd: Y'_{k+1}
   }
   // each lane rewrites the words it read in pass C, then the warp writes its
   // 512-word segment with coalesced 16-byte stores
-  store16<2>(x, buf, lc);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) buf[pad(lc + 2 * k)] = A::to_word(x[k]);
   __syncwarp();
 #pragma unroll
   for (int r = 0; r < SEG / 64; ++r) {
@@ -255,9 +238,13 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   }
 }
 
+template <class A>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     ntt_inv_kernel(NttParams P) {
+  using V = typename A::V;
+  using W = typename A::W;
   extern __shared__ __align__(16) uint64_t buf[];
+  V *vb = reinterpret_cast<V *>(buf);
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -269,8 +256,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   const LimbJob job = P.jobs[job_id / P.items];
   const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
   uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
-  const uint64_t q = P.primes[job.prime], q2 = 2 * q;
-  const ulonglong2 *tw = P.tw + (size_t)job.prime * kN;
+  const A ar(P.primes, P.qinv, job.prime);
+  const W *tw = static_cast<const W *>(P.tw) + (size_t)job.prime * kN;
   const int jb = rank * BLK;
 
   // each warp stages its own 512-word segment
@@ -282,84 +269,81 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   }
   __syncwarp();
 
-  uint64_t x[16];
+  V x[16];
   const int lc = (tid >> 1) * 32 + (tid & 1);
-  load16<2>(x, buf, lc);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = A::from_word(buf[pad(lc + 2 * k)]);
   const bool odd = tid & 1;
   const int je = jb + (tid >> 1) * 32;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
-    const uint64_t mine = x[k];
-    const uint64_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
-    const uint64_t X = odd ? other : mine, Y = odd ? mine : other;
+    const V mine = x[k];
+    const V other = __shfl_xor_sync(0xffffffffu, mine, 1);
+    const V X = odd ? other : mine, Y = odd ? mine : other;
     if (odd) {
-      const ulonglong2 w = ldtw(tw, tw_index(15, je + 2 * k));
-      const uint64_t t = X - Y + q2;
-      x[k] = t * w.x - __umul64hi(t, w.y) * q;
+      const W w = A::ldtw(tw, tw_index(15, je + 2 * k));
+      x[k] = ar.mul(ar.sub2q(X, Y), w);
     } else {
-      const uint64_t u = X + Y;
-      x[k] = u >= q2 ? u - q2 : u;
+      x[k] = ar.red2(ar.add(X, Y));
     }
   }
-  gs_pass(x, tw, 11, jb + lc, 2, q, q2);
-  store16<2>(x, buf, lc);
+  gs_pass(ar, x, tw, 11, jb + lc, 2);
+  store16<2>(x, vb, lc);
   __syncwarp();
   const int lb = warp * SEG + lane;
-  load16<32>(x, buf, lb);
-  gs_pass(x, tw, 7, jb + lb, 32, q, q2);
-  store16<32>(x, buf, lb);
+  load16<32>(x, vb, lb);
+  gs_pass(ar, x, tw, 7, jb + lb, 32);
+  store16<32>(x, vb, lb);
   __syncthreads();
-  load16<512>(x, buf, tid);
-  gs_pass(x, tw, 3, jb + tid, 512, q, q2);
+  load16<512>(x, vb, tid);
+  gs_pass(ar, x, tw, 3, jb + tid, 512);
   cluster.sync();  // every CTA has finished reading its own block
   // word l of block `rank` is row `rank` of column l, owned by CTA l/1024
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     const int l = tid + 512 * k;
-    cluster.map_shared_rank(buf, l >> 10)[rank * 1024 + (l & 1023)] = x[k];
+    cluster.map_shared_rank(vb, l >> 10)[rank * 1024 + (l & 1023)] = x[k];
   }
   cluster.sync();
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(buf + k * 1024 + 2 * tid);
-    x[k] = v.x;
-    x[8 + k] = v.y;
+    x[k] = A::from_bits(v.x);
+    x[8 + k] = A::from_bits(v.y);
   }
   const int c0 = rank * 1024 + 2 * tid;
   // stage by stage over both columns, one twiddle live at a time
 #pragma unroll
   for (int k = 0; k < 8; k += 2) {
-    const ulonglong2 w = ldtw(tw, 4 + k / 2);
+    const W w = A::ldtw(tw, 4 + k / 2);
 #pragma unroll
-    for (int h = 0; h < 16; h += 8) gs_bfly(x[h + k], x[h + k + 1], w, q, q2);
+    for (int h = 0; h < 16; h += 8) gs_bfly(ar, x[h + k], x[h + k + 1], w);
   }
 #pragma unroll
   for (int m = 0; m < 2; ++m) {
-    const ulonglong2 w = ldtw(tw, 2 + m);
+    const W w = A::ldtw(tw, 2 + m);
 #pragma unroll
     for (int h = 0; h < 16; h += 8) {
-      gs_bfly(x[h + 4 * m], x[h + 4 * m + 2], w, q, q2);
-      gs_bfly(x[h + 4 * m + 1], x[h + 4 * m + 3], w, q, q2);
+      gs_bfly(ar, x[h + 4 * m], x[h + 4 * m + 2], w);
+      gs_bfly(ar, x[h + 4 * m + 1], x[h + 4 * m + 3], w);
     }
   }
   {
-    const ulonglong2 w = ldtw(tw, 1);
+    const W w = A::ldtw(tw, 1);
 #pragma unroll
     for (int h = 0; h < 16; h += 8)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) gs_bfly(x[h + k], x[h + k + 4], w, q, q2);
+      for (int k = 0; k < 4; ++k) gs_bfly(ar, x[h + k], x[h + k + 4], w);
   }
   {
-    const ulonglong2 sc = P.scales[job.scale_idx];
+    const W sc = A::scale(P.scales[job.scale_idx]);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const uint64_t r = x[k] * sc.x - __umul64hi(x[k], sc.y) * q;
-      x[k] = r >= q ? r - q : r;
-    }
+    for (int k = 0; k < 16; ++k) x[k] = ar.red1(ar.mul(x[k], sc));
   }
 #pragma unroll
   for (int k = 0; k < 8; ++k)
-    *reinterpret_cast<ulonglong2 *>(o + c0 + k * BLK) = make_ulonglong2(x[k], x[8 + k]);
+    *reinterpret_cast<ulonglong2 *>(o + c0 + k * BLK) =
+        make_ulonglong2(A::to_word(x[k]), A::to_word(x[8 + k]));
 }
 
 }  // namespace
@@ -372,22 +356,31 @@ int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
   static unsigned configured = 0;  // one bit per device
   const unsigned bit = 1u << (ctx->device & 31);
   if (!(configured & bit)) {
-    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel,
+    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<IntArith>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SMEM_BYTES));
-    B2F_CUDA(cudaFuncSetAttribute(ntt_inv_kernel,
+    B2F_CUDA(cudaFuncSetAttribute(ntt_inv_kernel<IntArith>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SMEM_BYTES));
+    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<FpArith>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SMEM_BYTES));
+    B2F_CUDA(cudaFuncSetAttribute(ntt_inv_kernel<FpArith>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SMEM_BYTES));
     configured |= bit;
   }
+  const bool fp = ctx->ntt_fp64;
   NttParams P;
   P.in = in;
   P.out = out;
   P.in_stride = in_stride;
   P.out_stride = out_stride;
   P.jobs = jobs;
-  P.tw = inverse ? ctx->d_tw_inv : ctx->d_tw_fwd;
+  P.tw = fp ? (const void *)(inverse ? ctx->d_twd_inv : ctx->d_twd_fwd)
+            : (const void *)(inverse ? ctx->d_tw_inv : ctx->d_tw_fwd);
   P.primes = ctx->d_primes;
+  P.qinv = ctx->d_qinv;
   P.scales = scales ? scales : ctx->d_ninv;
   P.jobs_per_item = jobs_per_item;
   P.items = items;
@@ -396,10 +389,18 @@ int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
     set_error("launch_ntt: batch too large (%lld limbs)", blocks / CL);
     return B2F_ERR_ARG;
   }
-  if (inverse)
-    ntt_inv_kernel<<<(unsigned)blocks, NT, SMEM_BYTES, s>>>(P);
-  else
-    ntt_fwd_kernel<<<(unsigned)blocks, NT, SMEM_BYTES, s>>>(P);
+  const unsigned g = (unsigned)blocks;
+  if (fp) {
+    if (inverse)
+      ntt_inv_kernel<FpArith><<<g, NT, SMEM_BYTES, s>>>(P);
+    else
+      ntt_fwd_kernel<FpArith><<<g, NT, SMEM_BYTES, s>>>(P);
+  } else {
+    if (inverse)
+      ntt_inv_kernel<IntArith><<<g, NT, SMEM_BYTES, s>>>(P);
+    else
+      ntt_fwd_kernel<IntArith><<<g, NT, SMEM_BYTES, s>>>(P);
+  }
   B2F_LAUNCHED("ntt kernel launch");
   return B2F_OK;
 }

@@ -6,6 +6,8 @@ cover a digit so that decrypted values are meaningful."""
 
 from __future__ import annotations
 
+import contextlib
+
 import numpy as np
 import pytest
 
@@ -22,9 +24,62 @@ def test_generated_primes_match_oracle(oracle_mod):
             log_n, bits, count, mode)
 
 
+@contextlib.contextmanager
+def ntt_arith(ctx, mode):
+    ctx.set_ntt_arith(mode)
+    try:
+        yield
+    finally:
+        ctx.set_ntt_arith("auto")
+
+
+def test_ntt_arith_selection():
+    """50-bit primes take the binary64 butterflies by default; a context
+    with a prime of 2^50 or more keeps the integer ones and refuses f64."""
+
+    from easyfhe import core
+
+    ctx, _ = pair(8, 2, 4)
+    assert ctx.ntt_arith == "f64"
+    with ntt_arith(ctx, "int64"):
+        assert ctx.ntt_arith == "int64"
+    assert ctx.ntt_arith == "f64"
+    wide = core.NativeContext(core.Params.uniform(4, 1, 2, bits=59), "cuda:0")
+    assert wide.ntt_arith == "int64"
+    with pytest.raises(NotImplementedError):
+        wide.set_ntt_arith("f64")
+    with pytest.raises(ValueError):
+        ctx.set_ntt_arith("f32")
+
+
+@pytest.mark.parametrize("arith", ["f64", "int64"])
+def test_ntt_extreme_residues(arith):
+    """All-(q-1), all-zero and alternating limbs: the largest products the
+    butterflies see."""
+
+    ctx, orc = pair(8, 2, 4)
+    q = np.array(ctx.primes[:8], dtype=np.uint64)[:, None]
+    ones = np.ones((8, N), dtype=np.uint64)
+    x = np.stack([ones * (q - 1), ones * 0, np.where(np.arange(N) % 2 == 0, q - 1, 0) * ones,
+                  ones * (q - 1) // 2])
+    with ntt_arith(ctx, arith):
+        d = to_dev(x)
+        ctx.ntt(d, 8, 0, inverse=False)
+        assert np.array_equal(to_host(d), orc.ntt(x, 8, 0, inverse=False).reshape(x.shape))
+        d = to_dev(x)
+        ctx.ntt(d, 8, 0, inverse=True)
+        assert np.array_equal(to_host(d), orc.ntt(x, 8, 0, inverse=True).reshape(x.shape))
+
+
+@pytest.mark.parametrize("arith", ["f64", "int64"])
 @pytest.mark.parametrize("L", [8, 16, 24, 32])
-def test_ntt_forward_inverse_bit_exact(L):
+def test_ntt_forward_inverse_bit_exact(L, arith):
     ctx, orc = pair(L, 2, 4)
+    with ntt_arith(ctx, arith):
+        _ntt_round_trip(ctx, orc, L)
+
+
+def _ntt_round_trip(ctx, orc, L):
     rng = np.random.default_rng(1000 + L)
     x = rand_residues(rng, ctx.primes[:L], 3)
     d = to_dev(x)
@@ -69,8 +124,9 @@ def test_secret_and_keys_match_oracle(oracle_mod):
     assert np.array_equal(to_host(rk), orc.keygen_relin(want, 78))
 
 
-@pytest.mark.parametrize("rotation", [1, 3, 1024, 131071])
-def test_rotate_bit_exact(rotation):
+@pytest.mark.parametrize("rotation,arith", [(1, "f64"), (3, "f64"), (1024, "f64"),
+                                             (131071, "f64"), (3, "int64")])
+def test_rotate_bit_exact(rotation, arith):
     from easyfhe import core
 
     L, l = 8, 7
@@ -81,7 +137,8 @@ def test_rotate_bit_exact(rotation):
     key = ctx.keygen_rotation(s_ntt, g, seed=11)
     rng = np.random.default_rng(rotation)
     cts = rand_residues(rng, ctx.primes[:l], 6).reshape(3, 2, l, N)
-    out = to_host(ctx.rotate(to_dev(cts), l, g, key))
+    with ntt_arith(ctx, arith):
+        out = to_host(ctx.rotate(to_dev(cts), l, g, key))
     hkey = to_host(key)
     for c in range(3):
         assert np.array_equal(out[c], orc.rotate(cts[c], l, g, hkey)), f"ct {c}"
