@@ -19,8 +19,10 @@
 //      with 16-byte coalesced stores.
 // The inverse (Gentleman-Sande, bit-reversed in, natural out) runs the same
 // steps backwards and folds N^-1 (times an optional per-limb constant) into
-// the final stage.  Butterflies use Harvey's lazy reduction: forward values
-// live in [0, 4q), inverse values in [0, 2q), outputs are fully reduced.
+// the final stage.  The butterfly arithmetic is a policy (ntt_arith.cuh):
+// 64-bit integer Shoup products with Harvey's lazy reduction, or, when every
+// prime is below 2^50, exact binary64 products on signed residues, which this
+// GPU issues at a higher rate.  Outputs are fully reduced either way.
 // Shared memory holds the block with two pad words per 32 so that every
 // pass is free of bank conflicts.  Stages outside the register passes apply
 // one twiddle to both columns before loading the next and the cluster
@@ -216,10 +218,11 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     const V got = __shfl_xor_sync(0xffffffffu, give, 1);
     const V X = odd ? got : x[k], Y = odd ? x[k + 1] : got;
     const W w = A::ldtw(tw, tw_index(15, je + 2 * (k + (odd ? 1 : 0))));
-    const V u = ar.red2(X);
-    const V t = ar.mul(Y, w);
     // outputs of this lane's butterfly, fully reduced
-    const V ra = ar.red1(ar.red2(ar.add(u, t))), rb = ar.red1(ar.red2(ar.sub2q(u, t)));
+    V ra = X, rb = Y;
+    ar.ct(ra, rb, w);
+    ra = ar.full(ra);
+    rb = ar.full(rb);
     // even lane keeps ra = X'_k and sends rb = Y'_k; odd keeps rb = Y'_{k+1}, sends ra
     const V back = __shfl_xor_sync(0xffffffffu, odd ? ra : rb, 1);
     x[k] = odd ? back : ra;       // even: X'_k;  odd: Y'_k (from even)
@@ -282,9 +285,9 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     const V X = odd ? other : mine, Y = odd ? mine : other;
     if (odd) {
       const W w = A::ldtw(tw, tw_index(15, je + 2 * k));
-      x[k] = ar.mul(ar.sub2q(X, Y), w);
+      x[k] = ar.gs_diff(X, Y, w);
     } else {
-      x[k] = ar.red2(ar.add(X, Y));
+      x[k] = ar.gs_sum(X, Y);
     }
   }
   gs_pass(ar, x, tw, 11, jb + lc, 2);
@@ -338,7 +341,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   {
     const W sc = A::scale(P.scales[job.scale_idx]);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) x[k] = ar.red1(ar.mul(x[k], sc));
+    for (int k = 0; k < 16; ++k) x[k] = ar.scale_out(x[k], sc);
   }
 #pragma unroll
   for (int k = 0; k < 8; ++k)

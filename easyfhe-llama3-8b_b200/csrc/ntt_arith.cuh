@@ -1,5 +1,8 @@
 // The two butterfly arithmetics of the NTT kernels (and of the butterfly
-// rate calibration that serves as their roofline).
+// rate calibration that serves as their roofline).  Each policy provides the
+// forward (Cooley-Tukey) and inverse (Gentleman-Sande) butterflies on its own
+// residue representation, conversion from and to fully reduced 64-bit words,
+// and the final reduction; the kernels are written against these alone.
 #pragma once
 #include <cstdint>
 
@@ -7,8 +10,9 @@
 
 namespace b2f {
 
-// Integer butterflies: 64-bit words, lazy Shoup products with the twiddle's
-// precomputed quotient.
+// Integer butterflies: 64-bit words, Harvey's lazy reduction with Shoup
+// products (the twiddle's precomputed quotient): forward values in [0, 4q),
+// inverse values in [0, 2q).
 struct IntArith {
   using V = uint64_t;
   using W = ulonglong2;
@@ -27,27 +31,47 @@ struct IntArith {
   }
   __device__ __forceinline__ V red2(V a) const { return a >= q2 ? a - q2 : a; }
   __device__ __forceinline__ V red1(V a) const { return a >= q ? a - q : a; }
-  __device__ __forceinline__ V add(V a, V b) const { return a + b; }
-  // a - b + 2q
-  __device__ __forceinline__ V sub2q(V a, V b) const { return a - b + q2; }
+  // (x, y) -> (x + w y, x - w y)
+  __device__ __forceinline__ void ct(V &x, V &y, W w) const {
+    const V u = red2(x), t = mul(y, w);
+    x = u + t;
+    y = u - t + q2;
+  }
+  // (x, y) -> (x + y, (x - y) w), split for lanes that own one output each
+  __device__ __forceinline__ V gs_sum(V x, V y) const { return red2(x + y); }
+  __device__ __forceinline__ V gs_diff(V x, V y, W w) const { return mul(x - y + q2, w); }
+  __device__ __forceinline__ void gs(V &x, V &y, W w) const {
+    const V u = gs_sum(x, y);
+    y = gs_diff(x, y, w);
+    x = u;
+  }
+  // a forward value to [0, q)
+  __device__ __forceinline__ V full(V v) const { return red1(red2(v)); }
+  // an inverse value times the output scale, in [0, q)
+  __device__ __forceinline__ V scale_out(V v, W s) const { return red1(mul(v, s)); }
 };
 
-// Binary64 butterflies for primes below 2^50: residues below 4q < 2^52 are
-// exact doubles.  y * w mod q (y < 4q, w < q): h + l = y w exactly (product
-// and its FMA error term), qt = rint(h / q) from one FMA against 1/q rounded
-// at 2^52, r = (h - qt q) + l exactly; |y w / q - qt| < 1.5, so r lies in
-// (-1.5 q, 1.5 q) and r + 2q (r < 0) lands in [0, 2q).  Every operation is
-// round-to-nearest without contraction; the results equal the integer ones.
+// Binary64 butterflies for primes below 2^50, on signed residues held as
+// exact doubles (forward values within 1.5q + q/2^40 in magnitude, inverse
+// values within q).  Every operation rounds to nearest without contraction.
+//   red(x):    k = rint(x / q) from one FMA against 1/q rounded at 1.5 2^52
+//              (integer ulp for |v| < 2^51), r = x - k q exactly: |r| <= q/2.
+//   mul(y, w): h + l = y w exactly (product and its FMA error term), k =
+//              rint(h / q), r = (h - k q) + l exactly; for |y| <= 2q, w < q,
+//              |y w / q - k| <= 1 so |r| <= q.
+// Forward: (x, y) -> (red(x) + mul(y, w), red(x) - mul(y, w)) keeps |.| <=
+// 1.5q; inverse: (x, y) -> (red(x + y), mul(x - y, w)) keeps |.| <= q.  The
+// residues equal the integer path's after the final reduction.
 struct FpArith {
   using V = double;
   using W = double;
   static constexpr double kTwo52 = 4503599627370496.0;
-  double q, q2, qinv;
+  static constexpr double kMagic = 6755399441055744.0;  // 1.5 * 2^52
+  double q, qinv;
   __device__ __forceinline__ FpArith(const uint64_t *primes, const double *qinvs, int prime)
-      : q(from_word(primes[prime])), q2(2.0 * from_word(primes[prime])),
-        qinv(qinvs[prime]) {}
+      : q(from_word(primes[prime])), qinv(qinvs[prime]) {}
   static __device__ __forceinline__ W ldtw(const W *tw, int idx) { return __ldg(tw + idx); }
-  // exact for v < 2^52: the word as the mantissa of 2^52 + v
+  // exact for 0 <= v < 2^52: the word as the mantissa of 2^52 + v
   static __device__ __forceinline__ V from_word(uint64_t v) {
     return __dadd_rn(__longlong_as_double((long long)(v | 0x4330000000000000ull)), -kTwo52);
   }
@@ -61,37 +85,47 @@ struct FpArith {
     return (uint64_t)__double_as_longlong(v);
   }
   static __device__ __forceinline__ W scale(ulonglong2 s) { return from_word(s.x); }
+  __device__ __forceinline__ V red(V x) const {
+    const double k = __dadd_rn(__fma_rn(x, qinv, kMagic), -kMagic);
+    return __fma_rn(-k, q, x);
+  }
   __device__ __forceinline__ V mul(V y, W w) const {
     const double h = __dmul_rn(y, w);
     const double l = __fma_rn(y, w, -h);
-    const double qt = __dadd_rn(__fma_rn(h, qinv, kTwo52), -kTwo52);
-    const double r = __dadd_rn(__fma_rn(-qt, q, h), l);
-    return r < 0.0 ? __dadd_rn(r, q2) : r;
+    const double k = __dadd_rn(__fma_rn(h, qinv, kMagic), -kMagic);
+    return __dadd_rn(__fma_rn(-k, q, h), l);
   }
-  __device__ __forceinline__ V red2(V a) const { return a >= q2 ? __dadd_rn(a, -q2) : a; }
-  __device__ __forceinline__ V red1(V a) const { return a >= q ? __dadd_rn(a, -q) : a; }
-  __device__ __forceinline__ V add(V a, V b) const { return __dadd_rn(a, b); }
-  __device__ __forceinline__ V sub2q(V a, V b) const { return __dadd_rn(__dadd_rn(a, -b), q2); }
+  __device__ __forceinline__ void ct(V &x, V &y, W w) const {
+    const V u = red(x), t = mul(y, w);
+    x = __dadd_rn(u, t);
+    y = __dadd_rn(u, -t);
+  }
+  __device__ __forceinline__ V gs_sum(V x, V y) const { return red(__dadd_rn(x, y)); }
+  __device__ __forceinline__ V gs_diff(V x, V y, W w) const {
+    return mul(__dadd_rn(x, -y), w);
+  }
+  __device__ __forceinline__ void gs(V &x, V &y, W w) const {
+    const V u = gs_sum(x, y);
+    y = gs_diff(x, y, w);
+    x = u;
+  }
+  __device__ __forceinline__ V full(V v) const {
+    const V r = red(v);
+    return r < 0.0 ? __dadd_rn(r, q) : r;
+  }
+  __device__ __forceinline__ V scale_out(V v, W s) const { return full(mul(v, s)); }
 };
 
-// forward butterfly, values in [0, 4q): (x, y) -> (x + w y, x - w y)
 template <class A>
 __device__ __forceinline__ void ct_bfly(const A &ar, typename A::V &x, typename A::V &y,
                                         typename A::W w) {
-  const typename A::V u = ar.red2(x);
-  const typename A::V t = ar.mul(y, w);
-  x = ar.add(u, t);
-  y = ar.sub2q(u, t);
+  ar.ct(x, y, w);
 }
 
-// inverse butterfly, values in [0, 2q): (x, y) -> (x + y, (x - y) w)
 template <class A>
 __device__ __forceinline__ void gs_bfly(const A &ar, typename A::V &x, typename A::V &y,
                                         typename A::W w) {
-  const typename A::V u = ar.red2(ar.add(x, y));
-  const typename A::V t = ar.sub2q(x, y);
-  x = u;
-  y = ar.mul(t, w);
+  ar.gs(x, y, w);
 }
 
 }  // namespace b2f
