@@ -52,7 +52,7 @@ def parse():
                     help="ntt: only the NTT kernel loop (for profiling); bootstrap: "
                          "BASELINE configs[3]; linear: BASELINE configs[2]")
     ap.add_argument("--no-clocks", action="store_true")
-    ap.add_argument("--ntt-arith", default="auto", choices=["auto", "int64", "f64"],
+    ap.add_argument("--arith", default="auto", choices=["auto", "int64", "f64"],
                     help="butterfly arithmetic of the NTT kernels (auto: binary64 when "
                          "every prime is below 2^50)")
     ap.add_argument("--per-ct", action="store_true",
@@ -478,7 +478,7 @@ def main() -> None:
 
     params = core.Params.uniform(a.limbs, a.special, a.dnum, bits=50)
     ctx = core.NativeContext(params, dev)
-    ctx.set_ntt_arith(a.ntt_arith)
+    ctx.set_arith(a.arith)
     l, C = a.limbs, a.batch
     s_ntt = ctx.secret_to_ntt(core.sample_secret(2024 + rank, 192))
     g = core.galois_element(a.rotation)
@@ -520,7 +520,7 @@ def main() -> None:
         if rank == 0:
             print(json.dumps({"workload": "ntt", "limbs": ntt_limbs, "ms": ntt_ms,
                               "us_per_limb": ntt_ms * 1e3 / ntt_limbs, "gbs": ntt_gbs,
-                              "ntt_arith": ctx.ntt_arith,
+                              "arith": ctx.arith,
                               "butterflies_per_s": ntt_bfly, "butterfly_peak": bfly_peak,
                               "frac": ntt_bfly / bfly_peak}), flush=True)
         if world > 1:
@@ -631,14 +631,14 @@ def main() -> None:
                 "launch": f"{ntt_limbs} limbs of 2^16 words (16 N bytes per limb)",
             },
             "compute_roofline": {
-                "bound": "fp64" if ctx.ntt_arith == "f64" else "imad",
+                "bound": "fp64" if ctx.arith == "f64" else "imad",
                 "kernel": "ntt_fwd_kernel/ntt_inv_kernel",
                 "achieved": ntt_bfly, "peak": bfly_peak, "unit": "butterflies/s",
                 "frac": ntt_bfly / bfly_peak,
                 "peak_source": ("measured live: b2f_butterfly_peak (the NTT's lazy "
-                                f"{ctx.ntt_arith} butterfly from registers, every SM full)"),
+                                f"{ctx.arith} butterfly from registers, every SM full)"),
             },
-            "ntt_arith": ctx.ntt_arith,
+            "arith": ctx.arith,
             "ntt_hbm_gbs": ntt_gbs,
             "keyswitch_hbm_gbs": algorithmic_mib(a) * MiB / (ms / 1e3) / 1e9,
             "cpu_baseline": cpu,

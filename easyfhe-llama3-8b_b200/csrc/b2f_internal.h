@@ -72,9 +72,8 @@ struct LevelTables {
   int l = 0, beta = 0;
   // per Q limb i < l: N^-1 * [Qhat_{j(i),i}^-1] mod q_i (Shoup pair)
   ulonglong2 *modup_scale = nullptr;
-  // [beta][l+K][alpha]: [Qhat_{j,i}] mod p_t (Shoup pair w.r.t. p_t)
-  ulonglong2 *modup_conv = nullptr;
-  // the same conversions as byte-split tensor-core operands: per digit j a
+  // ModUp conversion constants [Qhat_{j,i}] mod p_t as byte-split tensor-core
+  // operands: per digit j a
   // u8 matrix of conv_rows(l+K-width_j) x conv_kpad(alpha) (conv_bytes)
   uint8_t *modup_bytes = nullptr;
   size_t modup_bytes_stride = 0;  // bytes per digit
@@ -141,15 +140,14 @@ struct b2f_context {
   b2f::Red79 *d_red79 = nullptr;      // L+K constants of reduce79
   ulonglong2 *d_tw_fwd = nullptr;     // (L+K) x N  (psi^bitrev(k), Shoup)
   ulonglong2 *d_tw_inv = nullptr;     // (L+K) x N
-  // binary64 butterflies, when every prime is below 2^50: the same twiddles
-  // as doubles, and 1/q per prime
-  bool ntt_fp64_ok = false, ntt_fp64 = false;
+  // binary64 arithmetic (NTT butterflies, key inner product) when every
+  // prime is below 2^50: the same twiddles as doubles, and 1/q per prime
+  bool fp64_ok = false, fp64 = false;
   double *d_twd_fwd = nullptr, *d_twd_inv = nullptr, *d_qinv = nullptr;
   ulonglong2 *d_ninv = nullptr;       // L+K: N^-1
   ulonglong2 *d_i_factor = nullptr;   // L+K: psi^(N/2) (multiply by i)
   ulonglong2 *d_moddown_scale = nullptr;  // K: N^-1 * [Phat_k^-1] mod p_k
-  ulonglong2 *d_moddown_conv = nullptr;   // L x K: [Phat_k] mod q_i
-  uint8_t *d_moddown_bytes = nullptr;     // the same, byte split (conv_bytes)
+  uint8_t *d_moddown_bytes = nullptr;     // [Phat_k] mod q_i, byte split (conv_bytes)
   ulonglong2 *d_moddown_pinv = nullptr;   // L: [P^-1] mod q_i
   uint64_t *d_pmod = nullptr;             // L: [P] mod q_i
   std::vector<b2f::LevelTables> levels;   // index l = 1..L

@@ -55,7 +55,7 @@ extern "C" int b2f_butterfly_peak(b2f_context *ctx, int iters, double *per_secon
   if (err == cudaSuccess) {
     const ulonglong2 wi = make_ulonglong2(w, ws);
     auto run = [&]() {
-      if (ctx->ntt_fp64)
+      if (ctx->fp64)
         butterfly_peak_kernel<FpArith><<<blocks, threads, 0, s>>>(out, ctx->d_primes,
                                                                   ctx->d_qinv, wi, iters);
       else

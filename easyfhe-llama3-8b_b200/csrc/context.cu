@@ -167,10 +167,10 @@ static int build_tables(b2f_context *ctx) {
   }
   if ((rc = upload(ctx, &ctx->d_tw_fwd, twf))) return rc;
   if ((rc = upload(ctx, &ctx->d_tw_inv, twi))) return rc;
-  // binary64 NTT (every prime below 2^50): twiddles as doubles and 1/q
-  ctx->ntt_fp64_ok = true;
-  for (int i = 0; i < np; ++i) ctx->ntt_fp64_ok = ctx->ntt_fp64_ok && P[i] < (1ull << 50);
-  if (ctx->ntt_fp64_ok) {
+  // binary64 arithmetic (every prime below 2^50): twiddles as doubles and 1/q
+  ctx->fp64_ok = true;
+  for (int i = 0; i < np; ++i) ctx->fp64_ok = ctx->fp64_ok && P[i] < (1ull << 50);
+  if (ctx->fp64_ok) {
     std::vector<double> tdf((size_t)np * n), tdi((size_t)np * n), qinv(np);
     for (size_t k = 0; k < tdf.size(); ++k) {
       tdf[k] = (double)twf[k].x;
@@ -181,7 +181,7 @@ static int build_tables(b2f_context *ctx) {
     if ((rc = upload(ctx, &ctx->d_twd_inv, tdi))) return rc;
     if ((rc = upload(ctx, &ctx->d_qinv, qinv))) return rc;
   }
-  ctx->ntt_fp64 = ctx->ntt_fp64_ok;
+  ctx->fp64 = ctx->fp64_ok;
   if ((rc = upload(ctx, &ctx->d_ninv, ninv))) return rc;
   if ((rc = upload(ctx, &ctx->d_i_factor, ifac))) return rc;
 
@@ -205,7 +205,6 @@ static int build_tables(b2f_context *ctx) {
     md_pinv[i] = shoup_pair(h_inv(pm, qi), qi);
   }
   if ((rc = upload(ctx, &ctx->d_moddown_scale, md_scale))) return rc;
-  if ((rc = upload(ctx, &ctx->d_moddown_conv, md_conv))) return rc;
   if (K) {
     std::vector<uint8_t> mdb(conv_rows(L) * conv_kpad(K));
     conv_bytes(
@@ -244,7 +243,6 @@ static int build_tables(b2f_context *ctx) {
       }
     }
     if ((rc = upload(ctx, &T.modup_scale, scale))) return rc;
-    if ((rc = upload(ctx, &T.modup_conv, conv))) return rc;
     {
       // targets of digit j: limbs t < l+K outside [lo, hi), in order
       const int lk = l + K;
@@ -440,21 +438,21 @@ int b2f_context_destroy(b2f_context *ctx) {
   return B2F_OK;
 }
 
-int b2f_context_set_ntt_arith(b2f_context *ctx, int mode) {
-  B2F_CHECK_ARG(ctx, "b2f_context_set_ntt_arith: null context");
-  B2F_CHECK_ARG(mode >= 0 && mode <= 2, "b2f_context_set_ntt_arith: mode %d not in 0..2",
+int b2f_context_set_arith(b2f_context *ctx, int mode) {
+  B2F_CHECK_ARG(ctx, "b2f_context_set_arith: null context");
+  B2F_CHECK_ARG(mode >= 0 && mode <= 2, "b2f_context_set_arith: mode %d not in 0..2",
                 mode);
-  if (mode == 2 && !ctx->ntt_fp64_ok) {
-    set_error("b2f_context_set_ntt_arith: binary64 butterflies need every prime "
+  if (mode == 2 && !ctx->fp64_ok) {
+    set_error("b2f_context_set_arith: binary64 arithmetic needs every prime "
               "below 2^50");
     return B2F_ERR_UNSUPPORTED;
   }
-  ctx->ntt_fp64 = mode == 1 ? false : ctx->ntt_fp64_ok;
+  ctx->fp64 = mode == 1 ? false : ctx->fp64_ok;
   return B2F_OK;
 }
 
-int b2f_context_ntt_arith(const b2f_context *ctx) {
-  return ctx && ctx->ntt_fp64 ? 2 : 1;
+int b2f_context_arith(const b2f_context *ctx) {
+  return ctx && ctx->fp64 ? 2 : 1;
 }
 
 int b2f_context_info(const b2f_context *ctx, int *info) {

@@ -15,6 +15,7 @@
 // Every key limb (digit, poly, prime) is read by one grid row that covers all
 // ciphertexts of the batch, so a batch sharing a key streams it once.
 #include "b2f_internal.h"
+#include "ntt_arith.cuh"
 
 namespace b2f {
 namespace {
@@ -51,58 +52,6 @@ __device__ __forceinline__ uint32_t auto_src(uint32_t k, uint32_t g) {
   return brv16((e2 - 1) >> 1);
 }
 
-// Base conversions: Shoup products with the constant's precomputed
-// quotient, summed lazily in [0, 2p).  A block row covers `tper` targets;
-// small launches (one ciphertext) split the targets over more blocks so the
-// grid still fills the GPU, large batches keep one row per digit so each
-// input word is read once.
-inline int conv_split(int rows, int targets) {
-  const int want = 2048;  // ~14 blocks of 256 threads per SM
-  const int have = rows * (kN / 256);
-  if (have >= want) return targets;
-  const int chunks = std::min(targets, (want + have - 1) / have);
-  return (targets + chunks - 1) / chunks;
-}
-
-// Step 2: fast base conversion of one digit to every target outside it.
-// grid (N/TPB, beta * ceil((l+K)/tper), cts); xt [ct][l][N];
-// ext [ct][beta][l+K][N]
-__global__ void __launch_bounds__(TPB) modup_conv_kernel(
-    const uint64_t *__restrict__ xt, uint64_t *__restrict__ ext,
-    const ulonglong2 *__restrict__ conv, const uint64_t *__restrict__ primes,
-    int l, int K, int L, int alpha, int tper) {
-  const int n = blockIdx.x * TPB + threadIdx.x;
-  const int lk = l + K, tchunks = (lk + tper - 1) / tper;
-  const int j = blockIdx.y / tchunks, tc = blockIdx.y % tchunks;
-  const int ct = blockIdx.z;
-  const int beta = gridDim.y / tchunks;
-  const int lo = j * alpha, hi = min(lo + alpha, l), w = hi - lo;
-  const int t0 = tc * tper, t1 = min(t0 + tper, lk);
-  if (t0 >= lo && t1 <= hi) return;  // the whole chunk lies in the digit
-  const uint64_t *src = xt + ((size_t)ct * l + lo) * kN + n;
-  uint64_t xs[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i)
-    if (i < w) xs[i] = src[(size_t)i * kN];
-  uint64_t *dst = ext + ((size_t)ct * beta + j) * lk * kN + n;
-  const ulonglong2 *cj = conv + (size_t)j * lk * alpha;
-  for (int t = t0; t < t1; ++t) {
-    if (t >= lo && t < hi) continue;
-    const uint64_t p = primes[t < l ? t : L + (t - l)], p2 = 2 * p;
-    const ulonglong2 *c = cj + (size_t)t * alpha;
-    uint64_t acc = 0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      if (i < w) {
-        ulonglong2 cc = __ldg(c + i);
-        acc += shoup_lazy(xs[i], cc.x, cc.y, p);
-        acc = acc >= p2 ? acc - p2 : acc;
-      }
-    }
-    dst[(size_t)t * kN] = acc >= p ? acc - p : acc;
-  }
-}
-
 // ---------------------------------------------------------------------
 // Base conversion on the u8 tensor cores (mma.sync m16n8k32, s32
 // accumulate).  The input words are their own byte matrix: coefficient n's
@@ -112,7 +61,7 @@ __global__ void __launch_bounds__(TPB) modup_conv_kernel(
 // 2m+1 in rows 8-15 of tile m, so after the four tiles the thread holding
 // row g has all eight byte sums of target 8G+g for its two columns:
 // V = sum_b C_b 2^(8b) < 2^79, reduced once (Barrett).  Exact: the residue
-// equals sum_i x_i c_{t,i} mod p_t, as the Shoup kernels compute it.
+// equals sum_i x_i c_{t,i} mod p_t.
 // ---------------------------------------------------------------------
 constexpr int CNB = 256;  // coefficients (= threads) per conversion block
 
@@ -449,39 +398,86 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
   o[(size_t)lk * kN] = reduce128(s1.hi, s1.lo, M);
 }
 
-// Step 4b: convert the P part (coefficient form, pre-scaled) to each q_i.
-// grid (N/TPB, 2 * ceil(l/tper), cts); acc [ct][2][l+K][N] -> conv [ct][2][l][N]
-__global__ void __launch_bounds__(TPB) moddown_conv_kernel(
-    const uint64_t *__restrict__ acc, uint64_t *__restrict__ conv_out,
-    const ulonglong2 *__restrict__ md_conv, const uint64_t *__restrict__ primes,
-    int l, int K, int tper) {
+// Step 3 in binary64 (every prime below 2^50): each product is an exact
+// signed residue of magnitude <= q (FpArith::mul), sums of up to four stay
+// exact integers below 2^53 and are brought back within q/2 by one rounding
+// reduction per group; the result equals the integer kernel's.
+__global__ void __launch_bounds__(TPB) key_inner_product_f64_kernel(
+    const uint64_t *__restrict__ c1, long long c1_stride,
+    const uint64_t *__restrict__ ext, long long ext_stride, const ItemKeys items,
+    uint64_t *__restrict__ acc, const uint64_t *__restrict__ primes,
+    const double *__restrict__ qinvs, int l, int K, int L, int alpha, int beta,
+    const uint64_t *__restrict__ pre0, const uint64_t *__restrict__ pre1,
+    long long pre_stride, const uint64_t *__restrict__ pmod) {
+  using F = FpArith;
   const int n = blockIdx.x * TPB + threadIdx.x;
-  const int ichunks = (l + tper - 1) / tper;
-  const int b = blockIdx.y / ichunks, ic = blockIdx.y % ichunks;
-  const int ct = blockIdx.z;
-  const int lk = l + K;
-  const uint64_t *z = acc + (((size_t)ct * 2 + b) * lk + l) * kN + n;
-  uint64_t zs[16];
+  const int it = blockIdx.y, t = blockIdx.z, ct = items.ct(it);
+  const int lk = l + K, np = L + K;
+  const int gp = t < l ? t : L + (t - l);
+  const F ar(primes, qinvs, gp);
+  const uint64_t *__restrict__ key = items.key[items.at(it)];
+  double s0 = 0.0, s1 = 0.0;
+  auto digit = [&](int j) -> const uint64_t * {
+    const int lo = j * alpha, hi = min(lo + alpha, l);
+    return (t >= lo && t < hi) ? c1 + ct * c1_stride + (size_t)t * kN + n
+                               : ext + ct * ext_stride + ((size_t)j * lk + t) * kN + n;
+  };
+  const size_t kstep = (size_t)2 * np * kN;
+  const uint64_t *kb = key + (size_t)gp * kN + n;
+  for (int j = 0; j < beta; j += 4) {
+    uint64_t e[4], k0[4], k1[4];
 #pragma unroll
-  for (int k = 0; k < 16; ++k)
-    if (k < K) zs[k] = z[(size_t)k * kN];
-  uint64_t *o = conv_out + (((size_t)ct * 2 + b) * l) * kN + n;
-  const int i1 = min((ic + 1) * tper, l);
-  for (int i = ic * tper; i < i1; ++i) {
-    const uint64_t q = primes[i], q2 = 2 * q;
-    const ulonglong2 *c = md_conv + (size_t)i * K;
-    uint64_t a = 0;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      if (k < K) {
-        ulonglong2 cc = __ldg(c + k);
-        a += shoup_lazy(zs[k], cc.x, cc.y, q);
-        a = a >= q2 ? a - q2 : a;
+    for (int u = 0; u < 4; ++u) {
+      if (j + u < beta) {
+        e[u] = *digit(j + u);
+        k0[u] = __ldg(kb + (j + u) * kstep);
+        k1[u] = __ldg(kb + (j + u) * kstep + (size_t)np * kN);
       }
     }
-    o[(size_t)i * kN] = a >= q ? a - q : a;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (j + u < beta) {
+        const double ed = F::from_word(e[u]);
+        s0 = __dadd_rn(s0, ar.mul(ed, F::from_word(k0[u])));
+        s1 = __dadd_rn(s1, ar.mul(ed, F::from_word(k1[u])));
+      }
+    }
+    s0 = ar.red(s0);
+    s1 = ar.red(s1);
   }
+  if (pre0 != nullptr && t < l) {  // + P (pre0, pre1) on the Q limbs
+    const double pm = F::from_word(pmod[t]);
+    const size_t at = ct * pre_stride + (size_t)t * kN + n;
+    s0 = __dadd_rn(s0, ar.mul(F::from_word(pre0[at]), pm));
+    s1 = __dadd_rn(s1, ar.mul(F::from_word(pre1[at]), pm));
+  }
+  uint64_t *o = acc + ((size_t)it * 2 * lk + t) * kN + n;
+  o[0] = F::to_word(ar.full(s0));
+  o[(size_t)lk * kN] = F::to_word(ar.full(s1));
 }
+
+// Step 3 launcher: grid (N/TPB, items, l+K) in the context's arithmetic.
+int launch_key_inner_product(b2f_context *ctx, int items_n, const uint64_t *c1,
+                             long long c1_stride, const uint64_t *ext,
+                             long long ext_stride, const ItemKeys &items,
+                             uint64_t *acc, int l, cudaStream_t s,
+                             const uint64_t *pre0 = nullptr,
+                             const uint64_t *pre1 = nullptr,
+                             long long pre_stride = 0) {
+  const int K = ctx->K, beta = ctx->levels[l].beta;
+  const dim3 grid(kN / TPB, items_n, l + K);
+  if (ctx->fp64)
+    key_inner_product_f64_kernel<<<grid, TPB, 0, s>>>(
+        c1, c1_stride, ext, ext_stride, items, acc, ctx->d_primes, ctx->d_qinv, l, K,
+        ctx->L, ctx->alpha, beta, pre0, pre1, pre_stride, ctx->d_pmod);
+  else
+    key_inner_product_kernel<<<grid, TPB, 0, s>>>(
+        c1, c1_stride, ext, ext_stride, items, acc, ctx->d_mod, l, K, ctx->L,
+        ctx->alpha, beta, pre0, pre1, pre_stride, ctx->d_pmod);
+  B2F_LAUNCHED("key_inner_product_kernel");
+  return B2F_OK;
+}
+
 
 // Step 4c + 5: out_b[i][k] = ((acc_b[i] - conv_b[i]) * P^-1 + add_b[i])[pi_g(k)]
 // grid (N/TPB, l, items), g per item.  add_b may be null (add_stride ignored).
@@ -652,10 +648,9 @@ int ip_moddown(b2f_context *ctx, const uint64_t *c1, long long c1_stride,
                uint64_t *acc, uint64_t *conv, cudaStream_t s) {
   const LevelTables &T = ctx->levels[l];
   const int K = ctx->K, lk = l + K;
-  key_inner_product_kernel<<<dim3(kN / TPB, cts, lk), TPB, 0, s>>>(
-      c1, c1_stride, ext, ext_stride, items, acc, ctx->d_mod, l, K, ctx->L,
-      ctx->alpha, T.beta);
-  B2F_LAUNCHED("key_inner_product_kernel");
+  int rc = launch_key_inner_product(ctx, cts, c1, c1_stride, ext, ext_stride, items,
+                                    acc, l, s);
+  if (rc) return rc;
   // iNTT of the P limbs of both polys, scaled by N^-1 Phat_k^-1
   std::vector<LimbJob> pj;
   for (int b = 0; b < 2; ++b)
@@ -666,7 +661,7 @@ int ip_moddown(b2f_context *ctx, const uint64_t *c1, long long c1_stride,
   const LimbJob *d = job_table(ctx, {3, l}, pj);
   if (!d) return B2F_ERR_NOMEM;
   const long long as = 2LL * lk * kN;
-  int rc = launch_ntt(ctx, acc, as, acc, as, d, 2 * K, cts, 1,
+  rc = launch_ntt(ctx, acc, as, acc, as, d, 2 * K, cts, 1,
                       ctx->d_moddown_scale, s);
   if (rc) return rc;
   if ((rc = launch_moddown_conv(ctx, acc, conv, l, cts, s))) return rc;
@@ -826,10 +821,9 @@ int b2f_relinearize_rescale(b2f_context *ctx, const uint64_t *ct3_in,
   it.key[0] = relin_key;
   it.g[0] = 1u;
   it.shared = 1;
-  key_inner_product_kernel<<<dim3(kN / TPB, num_cts, lk), TPB, 0, s>>>(
-      d2, s3, ext, (long long)beta * lk * kN, it, acc, ctx->d_mod, l, K, L,
-      ctx->alpha, beta, ct3_in, ct3_in + (size_t)l * kN, s3, ctx->d_pmod);
-  B2F_LAUNCHED("key_inner_product_kernel");
+  if ((rc = launch_key_inner_product(ctx, num_cts, d2, s3, ext, (long long)beta * lk * kN,
+                                     it, acc, l, s, ct3_in, ct3_in + (size_t)l * kN, s3)))
+    return rc;
   // iNTT of the removed limbs of both polys, scaled by N^-1 (M/r)^-1
   std::vector<LimbJob> rj;
   for (int b = 0; b < 2; ++b)
@@ -1020,10 +1014,9 @@ int b2f_rotate_hoisted_ext(b2f_context *ctx, const uint64_t *ct, int l,
     if (keyed) {
       it.shared = 0;
       it.per = keyed;  // one ciphertext: item i is keyed rotation i
-      key_inner_product_kernel<<<dim3(kN / TPB, keyed, lk), TPB, 0, s>>>(
-          ct + (size_t)l * kN, 0, ext, 0, it, acc, ctx->d_mod, l, K, ctx->L,
-          ctx->alpha, T.beta);
-      B2F_LAUNCHED("key_inner_product_kernel");
+      if ((rc = launch_key_inner_product(ctx, keyed, ct + (size_t)l * kN, 0, ext, 0, it,
+                                         acc, l, s)))
+        return rc;
     }
     ext_combine_kernel<<<dim3(kN / TPB, lk, 2 * n), TPB, 0, s>>>(
         acc, ct, out + (size_t)p * 2 * lk * kN, ctx->d_mod, ctx->d_pmod, l, K,

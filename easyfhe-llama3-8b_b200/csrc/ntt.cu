@@ -373,7 +373,7 @@ int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
                                   SMEM_BYTES));
     configured |= bit;
   }
-  const bool fp = ctx->ntt_fp64;
+  const bool fp = ctx->fp64;
   NttParams P;
   P.in = in;
   P.out = out;

@@ -44,8 +44,8 @@ _SIGS = {
     "b2f_galois_element": (_u64, [_int, _i64]),
     "b2f_rotate_workspace": (_size, [_vp, _int, _int]),
     "b2f_rotate": (_int, [_vp, _vp, _vp, _int, _int, _u64, _vp, _vp, _size, _vp]),
-    "b2f_context_set_ntt_arith": (_int, [_vp, _int]),
-    "b2f_context_ntt_arith": (_int, [_vp]),
+    "b2f_context_set_arith": (_int, [_vp, _int]),
+    "b2f_context_arith": (_int, [_vp]),
     "b2f_relinearize_workspace": (_size, [_vp, _int, _int]),
     "b2f_relinearize": (_int, [_vp, _vp, _vp, _int, _int, _vp, _vp, _size, _vp]),
     "b2f_relinearize_rescale_workspace": (_size, [_vp, _int, _int]),

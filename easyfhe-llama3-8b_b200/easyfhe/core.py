@@ -317,18 +317,19 @@ class NativeContext:
         return out
 
     @property
-    def ntt_arith(self) -> str:
-        """Butterfly arithmetic of the NTT kernels: "int64" or "f64"."""
+    def arith(self) -> str:
+        """Arithmetic of the NTT butterflies and the key inner product:
+        "int64" or "f64"."""
 
-        return "f64" if lib.b2f_context_ntt_arith(self.handle) == 2 else "int64"
+        return "f64" if lib.b2f_context_arith(self.handle) == 2 else "int64"
 
-    def set_ntt_arith(self, mode: str) -> None:
+    def set_arith(self, mode: str) -> None:
         """"auto" (binary64 when every prime is below 2^50), "int64" or "f64"."""
 
         codes = {"auto": 0, "int64": 1, "f64": 2}
         if mode not in codes:
             raise ValueError(f"ntt arithmetic {mode!r} not in {sorted(codes)}")
-        call("b2f_context_set_ntt_arith", self.handle, codes[mode])
+        call("b2f_context_set_arith", self.handle, codes[mode])
 
     def butterfly_peak(self, iters: int = 2000) -> float:
         """Lazy forward butterflies per second from registers alone, in the

@@ -64,14 +64,15 @@ int b2f_context_destroy(b2f_context *ctx);
 /* log_n, L, K, dnum, alpha (limbs per digit), digits (top level) */
 int b2f_context_info(const b2f_context *ctx, int *info6);
 
-/* Butterfly arithmetic of the NTT kernels: mode 0 = automatic (binary64 when
- * every prime of the context is below 2^50, else 64-bit integer; the default),
- * 1 = 64-bit integer (lazy Shoup products), 2 = binary64 (exact residues below
- * 2^52; B2F_ERR_UNSUPPORTED when a prime is 2^50 or more).  Both give the
- * same fully reduced residues.  b2f_context_ntt_arith returns 1 or 2, the
- * arithmetic in use. */
-int b2f_context_set_ntt_arith(b2f_context *ctx, int mode);
-int b2f_context_ntt_arith(const b2f_context *ctx);
+/* Arithmetic of the NTT butterflies and the key-switch inner product: mode 0 =
+ * automatic (binary64 when every prime of the context is below 2^50, else
+ * 64-bit integer; the default), 1 = 64-bit integer (Shoup products, 128-bit
+ * accumulation), 2 = binary64 (exact products of residues below 2^52;
+ * B2F_ERR_UNSUPPORTED when a prime is 2^50 or more).  Both give the same
+ * fully reduced residues.  b2f_context_arith returns 1 or 2, the arithmetic
+ * in use. */
+int b2f_context_set_arith(b2f_context *ctx, int mode);
+int b2f_context_arith(const b2f_context *ctx);
 
 /* ---- number-theoretic transform (inside every op; no direct Python site) ---- */
 int b2f_ntt(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,

@@ -25,31 +25,31 @@ def test_generated_primes_match_oracle(oracle_mod):
 
 
 @contextlib.contextmanager
-def ntt_arith(ctx, mode):
-    ctx.set_ntt_arith(mode)
+def use_arith(ctx, mode):
+    ctx.set_arith(mode)
     try:
         yield
     finally:
-        ctx.set_ntt_arith("auto")
+        ctx.set_arith("auto")
 
 
-def test_ntt_arith_selection():
+def test_arith_selection():
     """50-bit primes take the binary64 butterflies by default; a context
     with a prime of 2^50 or more keeps the integer ones and refuses f64."""
 
     from easyfhe import core
 
     ctx, _ = pair(8, 2, 4)
-    assert ctx.ntt_arith == "f64"
-    with ntt_arith(ctx, "int64"):
-        assert ctx.ntt_arith == "int64"
-    assert ctx.ntt_arith == "f64"
+    assert ctx.arith == "f64"
+    with use_arith(ctx, "int64"):
+        assert ctx.arith == "int64"
+    assert ctx.arith == "f64"
     wide = core.NativeContext(core.Params.uniform(4, 1, 2, bits=59), "cuda:0")
-    assert wide.ntt_arith == "int64"
+    assert wide.arith == "int64"
     with pytest.raises(NotImplementedError):
-        wide.set_ntt_arith("f64")
+        wide.set_arith("f64")
     with pytest.raises(ValueError):
-        ctx.set_ntt_arith("f32")
+        ctx.set_arith("f32")
 
 
 @pytest.mark.parametrize("arith", ["f64", "int64"])
@@ -62,7 +62,7 @@ def test_ntt_extreme_residues(arith):
     ones = np.ones((8, N), dtype=np.uint64)
     x = np.stack([ones * (q - 1), ones * 0, np.where(np.arange(N) % 2 == 0, q - 1, 0) * ones,
                   ones * (q - 1) // 2])
-    with ntt_arith(ctx, arith):
+    with use_arith(ctx, arith):
         d = to_dev(x)
         ctx.ntt(d, 8, 0, inverse=False)
         assert np.array_equal(to_host(d), orc.ntt(x, 8, 0, inverse=False).reshape(x.shape))
@@ -75,7 +75,7 @@ def test_ntt_extreme_residues(arith):
 @pytest.mark.parametrize("L", [8, 16, 24, 32])
 def test_ntt_forward_inverse_bit_exact(L, arith):
     ctx, orc = pair(L, 2, 4)
-    with ntt_arith(ctx, arith):
+    with use_arith(ctx, arith):
         _ntt_round_trip(ctx, orc, L)
 
 
@@ -137,7 +137,7 @@ def test_rotate_bit_exact(rotation, arith):
     key = ctx.keygen_rotation(s_ntt, g, seed=11)
     rng = np.random.default_rng(rotation)
     cts = rand_residues(rng, ctx.primes[:l], 6).reshape(3, 2, l, N)
-    with ntt_arith(ctx, arith):
+    with use_arith(ctx, arith):
         out = to_host(ctx.rotate(to_dev(cts), l, g, key))
     hkey = to_host(key)
     for c in range(3):
