@@ -492,7 +492,7 @@ def main() -> None:
     ws = ctx.workspace(core.lib.b2f_rotate_workspace(ctx.handle, C, l))
     stream = torch.cuda.current_stream()
 
-    launches_per_rotate = 8  # iNTT, ModUp conv, NTT, inner product, iNTT(P), conv, NTT, combine
+    launches_per_rotate = 7  # iNTT, ModUp conv, NTT, inner product, iNTT(P), conv, NTT+combine
 
     # ---- NTT kernel loop (dominant kernel; roofline) ----
     ntt_buf = ct.view(-1, N)  # C*2*l limbs, 768 MiB

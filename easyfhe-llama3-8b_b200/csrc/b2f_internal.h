@@ -169,6 +169,17 @@ int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
                uint64_t *out, long long out_stride, const LimbJob *jobs,
                int jobs_per_item, int items, int inverse,
                const ulonglong2 *scales, cudaStream_t s);
+struct ItemKeys;
+// The last step of a ModDown: NTT of conv [item][2][q_limbs][N] (the P part
+// converted to Q) whose epilogue writes, for item it and poly b,
+//   out + keys.out(it, out_stride) + (b q_limbs + i) N, at slot dst(j):
+//   ((acc_b[i][j] - NTT(conv)_b[i][j]) [P^-1]_{q_i} (* qinv_i)) + add_b[i][j]
+// acc [item][2][lk][N]; add_b (optional) of ciphertext keys.ct(it) at
+// add_stride; dst the slot permutation of X -> X^(g^-1), g = keys.g[at(it)].
+int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk,
+                const uint64_t *acc, const uint64_t *add0, const uint64_t *add1,
+                long long add_stride, uint64_t *out, long long out_stride,
+                const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s);
 // jobs for num_polys polys of (q_limbs Q + p_limbs P) limbs, contiguous
 int ntt_polys(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
               int p_limbs, int inverse, cudaStream_t s);

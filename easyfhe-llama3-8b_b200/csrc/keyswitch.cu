@@ -9,48 +9,21 @@
 //   4. ModDown: z_k = iNTT(acc_b[P_k]) * [Phat_k^-1]_{p_k};
 //      conv_i = NTT(sum_k z_k [Phat_k]_{q_i});
 //      d_b[i] = (acc_b[i] - conv_i) * [P^-1]_{q_i}
-//   5. HRotate: out = (pi_g(c0 + d0), pi_g(d1)); the automorphism is a
-//      gather folded into the ModDown combine.  Relinearisation adds
+//   5. HRotate: out = (pi_g(c0 + d0), pi_g(d1)).  Step 4's last NTT finishes
+//      the ModDown in its epilogue (ntt_moddown): the combine, the addition
+//      of c0 and the automorphism (a scatter by g^-1) happen as the
+//      transform stores, so conv never returns to HBM.  Relinearisation adds
 //      (d0, d1) of the degree-2 ciphertext instead and uses g = 1.
 // Every key limb (digit, poly, prime) is read by one grid row that covers all
 // ciphertexts of the batch, so a batch sharing a key streams it once.
 #include "b2f_internal.h"
+#include "ksitems.cuh"
 #include "ntt_arith.cuh"
 
 namespace b2f {
 namespace {
 
 constexpr int TPB = 256;
-
-// Per-item key pointers and galois elements of one launch, passed by value.
-// With shared != 0 every item uses entry 0 (a batch sharing one key); hoisted
-// rotations of one ciphertext use one entry per rotation.
-constexpr int kMaxItems = 64;
-// In per-item mode item i is rotation i % per of ciphertext i / per (the
-// ciphertext indexes c1, ext and c0; out_ct_stride and pos[] place the result).
-struct ItemKeys {
-  const uint64_t *key[kMaxItems];
-  uint32_t g[kMaxItems];
-  int16_t pos[kMaxItems];  // output slot of rotation r within its ciphertext
-  int shared;
-  int per = 1;             // rotations per ciphertext (per-item mode)
-  long long out_ct_stride; // words between ciphertexts' outputs (per-item mode)
-  __host__ __device__ int at(int i) const { return shared ? 0 : i % per; }
-  __host__ __device__ int ct(int i) const { return shared ? i : i / per; }
-  __host__ __device__ long long out(int i, long long stride) const {
-    return shared ? (long long)i * stride
-                  : ct(i) * out_ct_stride + (long long)pos[i % per] * stride;
-  }
-};
-
-__device__ __forceinline__ uint32_t brv16(uint32_t x) { return __brev(x) >> 16; }
-
-// source evaluation index of output k under X -> X^g (g odd, < 2N)
-__device__ __forceinline__ uint32_t auto_src(uint32_t k, uint32_t g) {
-  uint32_t e = 2 * brv16(k) + 1;
-  uint32_t e2 = (uint32_t)(((uint64_t)e * g) & (2 * kN - 1));
-  return brv16((e2 - 1) >> 1);
-}
 
 // ---------------------------------------------------------------------
 // Base conversion on the u8 tensor cores (mma.sync m16n8k32, s32
@@ -479,52 +452,7 @@ int launch_key_inner_product(b2f_context *ctx, int items_n, const uint64_t *c1,
 }
 
 
-// Step 4c + 5: out_b[i][k] = ((acc_b[i] - conv_b[i]) * P^-1 + add_b[i])[pi_g(k)]
-// grid (N/TPB, l, items), g per item.  add_b may be null (add_stride ignored).
-__global__ void __launch_bounds__(TPB) moddown_combine_kernel(
-    const uint64_t *__restrict__ acc, const uint64_t *__restrict__ conv,
-    const uint64_t *__restrict__ add0, const uint64_t *__restrict__ add1,
-    long long add_stride, uint64_t *__restrict__ out, long long out_stride,
-    const ulonglong2 *__restrict__ pinv, const uint64_t *__restrict__ primes,
-    int l, int K, const ItemKeys items) {
-  const int k = blockIdx.x * TPB + threadIdx.x;
-  const int i = blockIdx.y, it = blockIdx.z, ct = items.ct(it);
-  const int lk = l + K;
-  const uint32_t g = items.g[items.at(it)];
-  const uint32_t src = g == 1 ? (uint32_t)k : auto_src(k, g);
-  const uint64_t q = primes[i];
-  const ulonglong2 pi = pinv[i];
-#pragma unroll
-  for (int b = 0; b < 2; ++b) {
-    const uint64_t a = acc[(((size_t)it * 2 + b) * lk + i) * kN + src];
-    const uint64_t c = conv[(((size_t)it * 2 + b) * l + i) * kN + src];
-    uint64_t v = shoup(sub_mod(a, c, q), pi.x, pi.y, q);
-    const uint64_t *add = b ? add1 : add0;
-    if (add) v = add_mod(v, add[ct * add_stride + (size_t)i * kN + src], q);
-    out[items.out(it, out_stride) + ((size_t)b * l + i) * kN + k] = v;
-  }
-}
 
-// Fused relinearise + rescale, step 6: out_b[i] = (acc_b[i] - conv_b[i]) *
-// P^-1 * q_{l-1}^-1 mod q_i (acc already holds P d_b + IP_b), i < l-1.
-// grid (N/TPB, l-1, cts)
-__global__ void __launch_bounds__(TPB) moddown_rescale_combine_kernel(
-    const uint64_t *__restrict__ acc, const uint64_t *__restrict__ conv,
-    uint64_t *__restrict__ out, long long out_stride,
-    const ulonglong2 *__restrict__ pinv, const ulonglong2 *__restrict__ qinv,
-    const uint64_t *__restrict__ primes, int l, int K) {
-  const int k = blockIdx.x * TPB + threadIdx.x;
-  const int i = blockIdx.y, ct = blockIdx.z, lk = l + K;
-  const uint64_t q = primes[i];
-  const ulonglong2 pi = pinv[i], qi = qinv[i];
-#pragma unroll
-  for (int b = 0; b < 2; ++b) {
-    const uint64_t a = acc[(((size_t)ct * 2 + b) * lk + i) * kN + k];
-    const uint64_t c = conv[(((size_t)ct * 2 + b) * (l - 1) + i) * kN + k];
-    const uint64_t v = shoup(shoup(sub_mod(a, c, q), pi.x, pi.y, q), qi.x, qi.y, q);
-    out[ct * out_stride + ((size_t)b * (l - 1) + i) * kN + k] = v;
-  }
-}
 
 __global__ void __launch_bounds__(TPB) automorphism_kernel(
     const uint64_t *__restrict__ in, uint64_t *__restrict__ out, uint32_t g) {
@@ -665,13 +593,8 @@ int ip_moddown(b2f_context *ctx, const uint64_t *c1, long long c1_stride,
                       ctx->d_moddown_scale, s);
   if (rc) return rc;
   if ((rc = launch_moddown_conv(ctx, acc, conv, l, cts, s))) return rc;
-  rc = ntt_polys(ctx, conv, 2 * cts, l, 0, 0, s);
-  if (rc) return rc;
-  moddown_combine_kernel<<<dim3(kN / TPB, l, cts), TPB, 0, s>>>(
-      acc, conv, add0, add1, add_stride, out, out_stride, ctx->d_moddown_pinv,
-      ctx->d_primes, l, K, items);
-  B2F_LAUNCHED("moddown_combine_kernel");
-  return B2F_OK;
+  return ntt_moddown(ctx, conv, cts, l, lk, acc, add0, add1, add_stride, out, out_stride,
+                     nullptr, items, s);
 }
 
 int check_level(const b2f_context *ctx, int l, const char *fn) {
@@ -838,12 +761,8 @@ int b2f_relinearize_rescale(b2f_context *ctx, const uint64_t *ct3_in,
                        T.mdr_scale, s)))
     return rc;
   if ((rc = launch_moddown_rescale_conv(ctx, acc, conv, l, num_cts, s))) return rc;
-  if ((rc = ntt_polys(ctx, conv, 2 * num_cts, l - 1, 0, 0, s))) return rc;
-  moddown_rescale_combine_kernel<<<dim3(kN / TPB, l - 1, num_cts), TPB, 0, s>>>(
-      acc, conv, ct_out, 2LL * (l - 1) * kN, ctx->d_moddown_pinv, T.rescale_inv,
-      ctx->d_primes, l, K);
-  B2F_LAUNCHED("moddown_rescale_combine_kernel");
-  return B2F_OK;
+  return ntt_moddown(ctx, conv, num_cts, l - 1, lk, acc, nullptr, nullptr, 0, ct_out,
+                     2LL * (l - 1) * kN, T.rescale_inv, it, s);
 }
 
 size_t b2f_modup_batch_workspace(const b2f_context *ctx, int num_cts, int l) {
@@ -1057,12 +976,8 @@ int b2f_moddown_ext(b2f_context *ctx, const uint64_t *in, int num_cts, int l,
                        ctx->d_moddown_scale, s)))
     return rc;
   if ((rc = launch_moddown_conv(ctx, pcoef, conv, l, num_cts, s))) return rc;
-  if ((rc = ntt_polys(ctx, conv, 2 * num_cts, l, 0, 0, s))) return rc;
-  moddown_combine_kernel<<<dim3(kN / TPB, l, num_cts), TPB, 0, s>>>(
-      in, conv, nullptr, nullptr, 0, out, 2LL * l * kN, ctx->d_moddown_pinv,
-      ctx->d_primes, l, K, ItemKeys{{}, {1u}, {}, 1});
-  B2F_LAUNCHED("moddown_combine_kernel");
-  return B2F_OK;
+  return ntt_moddown(ctx, conv, num_cts, l, lk, in, nullptr, nullptr, 0, out, 2LL * l * kN,
+                     nullptr, ItemKeys{{}, {1u}, {}, 1}, s);
 }
 
 int b2f_automorphism(b2f_context *ctx, const uint64_t *in, uint64_t *out,

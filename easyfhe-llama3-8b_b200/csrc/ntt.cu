@@ -31,6 +31,7 @@
 #include <cooperative_groups.h>
 
 #include "b2f_internal.h"
+#include "ksitems.cuh"
 #include "ntt_arith.cuh"
 
 namespace cg = cooperative_groups;
@@ -112,6 +113,33 @@ __device__ __forceinline__ void store16(const V (&x)[16], V *buf, int l) {
   for (int k = 0; k < 16; ++k) buf[pad(l + STRIDE * k)] = x[k];
 }
 
+// Where the forward transform's outputs go.  PlainOut: the output limb, as
+// transformed.  ModDownOut: the transform is the last step of a ModDown (the
+// NTT of the P part converted to Q) and its epilogue finishes it: for item it
+// (poly p = 2 it + b, limb i) and every evaluation j of the limb,
+//   out_b[i][dst(j)] = (acc_b[i][j] - v[j]) * [P^-1]_{q_i} (* qinv_i) + add_b[i][j]
+// with dst = the slot permutation of X -> X^(g^-1) (the inverse of the
+// gather out[k] = w[src_g(k)]).  Each warp walks its own 512 evaluations in
+// order (coalesced reads of acc and add) and its 32 stores land in one
+// aligned 32-word block, since an automorphism maps aligned blocks of 32
+// evaluations onto aligned blocks.  The converted limbs never reach HBM.
+struct PlainOut {
+  static constexpr bool kModDown = false;
+};
+struct ModDownOut {
+  static constexpr bool kModDown = true;
+  const uint64_t *acc;          // [item][2][lk][N]
+  const uint64_t *add0, *add1;  // [ct][..][N] at add_stride, or null
+  long long add_stride;
+  uint64_t *out;                // items.out(it, out_stride) + (b l_out + i) N
+  long long out_stride;
+  const ulonglong2 *pinv;       // [P^-1] mod q_i
+  const ulonglong2 *qinv;       // a second factor mod q_i, or null
+  const uint64_t *primes;
+  ItemKeys items;
+  int lk, l_out;
+};
+
 // Passes over a CTA's block (element l = base + stride k):
 //   A: stages 3-6,   base tid,                        stride 512 (CTA-wide)
 //   B: stages 7-10,  base (tid/32)*512 + tid%32,      stride 32
@@ -120,9 +148,9 @@ __device__ __forceinline__ void store16(const V (&x)[16], V *buf, int l) {
 // Warp w touches only words [512 w, 512 w + 512) in B and C, so the B <-> C
 // exchange and the output staging need only warp synchronisation.
 
-template <class A>
+template <class A, class E>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
-    ntt_fwd_kernel(NttParams P) {
+    ntt_fwd_kernel(NttParams P, E epi) {
   using V = typename A::V;
   using W = typename A::W;
   extern __shared__ __align__(16) uint64_t buf[];
@@ -141,6 +169,23 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   const A ar(P.primes, P.qinv, job.prime);
   const W *tw = static_cast<const W *>(P.tw) + (size_t)job.prime * kN;
 
+  if constexpr (E::kModDown) {
+    // the epilogue's inputs for this CTA's block: into L2 while the
+    // transform runs (bulk prefetch, 64 KiB per array)
+    if (tid == 0) {
+      const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
+      const uint64_t *accl =
+          epi.acc + (((size_t)it * 2 + b) * epi.lk + i) * kN + (size_t)rank * BLK;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(accl), "r"(BLK * 8)
+                   : "memory");
+      const uint64_t *addl = b ? epi.add1 : epi.add0;
+      if (addl) {
+        addl += epi.items.ct(it) * epi.add_stride + (size_t)i * kN + (size_t)rank * BLK;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(addl), "r"(BLK * 8)
+                     : "memory");
+      }
+    }
+  }
   V x[16];
   // stages 0-2 on columns c0, c0+1 (rows k at stride 8192), straight from HBM
   const int c0 = rank * 1024 + 2 * tid;
@@ -233,11 +278,56 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
 #pragma unroll
   for (int k = 0; k < 16; ++k) buf[pad(lc + 2 * k)] = A::to_word(x[k]);
   __syncwarp();
+  if constexpr (E::kModDown) {
+    const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
+    const uint32_t ginv = galois_inverse(epi.items.g[epi.items.at(it)]);
+    const uint64_t q = epi.primes[i];
+    const ulonglong2 pi = epi.pinv[i];
+    const ulonglong2 qi = epi.qinv ? epi.qinv[i] : make_ulonglong2(0, 0);
+    const uint64_t *accl = epi.acc + (((size_t)it * 2 + b) * epi.lk + i) * kN;
+    const uint64_t *addl = b ? epi.add1 : epi.add0;
+    if (addl) addl += epi.items.ct(it) * epi.add_stride + (size_t)i * kN;
+    uint64_t *outl =
+        epi.out + epi.items.out(it, epi.out_stride) + ((size_t)b * epi.l_out + i) * kN;
+    // pairs of evaluations per lane, four pairs' loads issued together
 #pragma unroll
-  for (int r = 0; r < SEG / 64; ++r) {
-    const int idx = warp * SEG + 2 * (lane + 32 * r);
-    *reinterpret_cast<ulonglong2 *>(o + jb + idx) =
-        *reinterpret_cast<const ulonglong2 *>(buf + pad(idx));
+    for (int r0 = 0; r0 < SEG / 64; r0 += 4) {
+      ulonglong2 av[4], dv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = jb + warp * SEG + 2 * (lane + 32 * (r0 + u));
+        av[u] = *reinterpret_cast<const ulonglong2 *>(accl + j);
+        dv[u] = addl ? *reinterpret_cast<const ulonglong2 *>(addl + j) : make_ulonglong2(0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int kk = warp * SEG + 2 * (lane + 32 * (r0 + u));
+        const uint32_t j = (uint32_t)(jb + kk);
+        uint64_t w0 = shoup(sub_mod(av[u].x, buf[pad(kk)], q), pi.x, pi.y, q);
+        uint64_t w1 = shoup(sub_mod(av[u].y, buf[pad(kk + 1)], q), pi.x, pi.y, q);
+        if (epi.qinv) {
+          w0 = shoup(w0, qi.x, qi.y, q);
+          w1 = shoup(w1, qi.x, qi.y, q);
+        }
+        if (addl) {
+          w0 = add_mod(w0, dv[u].x, q);
+          w1 = add_mod(w1, dv[u].y, q);
+        }
+        if (ginv == 1) {
+          *reinterpret_cast<ulonglong2 *>(outl + j) = make_ulonglong2(w0, w1);
+        } else {
+          outl[auto_src(j, ginv)] = w0;
+          outl[auto_src(j + 1, ginv)] = w1;
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < SEG / 64; ++r) {
+      const int idx = warp * SEG + 2 * (lane + 32 * r);
+      *reinterpret_cast<ulonglong2 *>(o + jb + idx) =
+          *reinterpret_cast<const ulonglong2 *>(buf + pad(idx));
+    }
   }
 }
 
@@ -349,23 +439,29 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
         make_ulonglong2(A::to_word(x[k]), A::to_word(x[8 + k]));
 }
 
-}  // namespace
 
-int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
-               uint64_t *out, long long out_stride, const LimbJob *jobs,
-               int jobs_per_item, int items, int inverse,
-               const ulonglong2 *scales, cudaStream_t s) {
+template <class E>
+int launch_ntt_impl(b2f_context *ctx, const uint64_t *in, long long in_stride,
+                    uint64_t *out, long long out_stride, const LimbJob *jobs,
+                    int jobs_per_item, int items, int inverse,
+                    const ulonglong2 *scales, const E &epi, cudaStream_t s) {
   if (items <= 0 || jobs_per_item <= 0) return B2F_OK;
   static unsigned configured = 0;  // one bit per device
   const unsigned bit = 1u << (ctx->device & 31);
   if (!(configured & bit)) {
-    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<IntArith>,
+    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<IntArith, PlainOut>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SMEM_BYTES));
+    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<IntArith, ModDownOut>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SMEM_BYTES));
     B2F_CUDA(cudaFuncSetAttribute(ntt_inv_kernel<IntArith>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SMEM_BYTES));
-    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<FpArith>,
+    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<FpArith, PlainOut>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SMEM_BYTES));
+    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<FpArith, ModDownOut>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SMEM_BYTES));
     B2F_CUDA(cudaFuncSetAttribute(ntt_inv_kernel<FpArith>,
@@ -393,19 +489,56 @@ int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
     return B2F_ERR_ARG;
   }
   const unsigned g = (unsigned)blocks;
-  if (fp) {
-    if (inverse)
+  if (inverse) {
+    if (fp)
       ntt_inv_kernel<FpArith><<<g, NT, SMEM_BYTES, s>>>(P);
     else
-      ntt_fwd_kernel<FpArith><<<g, NT, SMEM_BYTES, s>>>(P);
-  } else {
-    if (inverse)
       ntt_inv_kernel<IntArith><<<g, NT, SMEM_BYTES, s>>>(P);
+  } else {
+    if (fp)
+      ntt_fwd_kernel<FpArith, E><<<g, NT, SMEM_BYTES, s>>>(P, epi);
     else
-      ntt_fwd_kernel<IntArith><<<g, NT, SMEM_BYTES, s>>>(P);
+      ntt_fwd_kernel<IntArith, E><<<g, NT, SMEM_BYTES, s>>>(P, epi);
   }
   B2F_LAUNCHED("ntt kernel launch");
   return B2F_OK;
+}
+
+}  // namespace
+
+int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
+               uint64_t *out, long long out_stride, const LimbJob *jobs,
+               int jobs_per_item, int items, int inverse,
+               const ulonglong2 *scales, cudaStream_t s) {
+  return launch_ntt_impl(ctx, in, in_stride, out, out_stride, jobs, jobs_per_item,
+                         items, inverse, scales, PlainOut{}, s);
+}
+
+int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk,
+                const uint64_t *acc, const uint64_t *add0, const uint64_t *add1,
+                long long add_stride, uint64_t *out, long long out_stride,
+                const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s) {
+  std::vector<int> key = {0, q_limbs, 0};
+  std::vector<LimbJob> jobs(q_limbs);
+  for (int i = 0; i < q_limbs; ++i)
+    jobs[i] = LimbJob{(uint32_t)i, (uint32_t)i, (uint16_t)i, (uint16_t)i};
+  const LimbJob *d = job_table(ctx, key, jobs);
+  if (!d) return B2F_ERR_NOMEM;
+  ModDownOut E;
+  E.acc = acc;
+  E.add0 = add0;
+  E.add1 = add1;
+  E.add_stride = add_stride;
+  E.out = out;
+  E.out_stride = out_stride;
+  E.pinv = ctx->d_moddown_pinv;
+  E.qinv = qinv;
+  E.primes = ctx->d_primes;
+  E.items = keys;
+  E.lk = lk;
+  E.l_out = q_limbs;
+  const long long st = (long long)q_limbs * kN;
+  return launch_ntt_impl(ctx, conv, st, conv, st, d, q_limbs, 2 * items, 0, nullptr, E, s);
 }
 
 int ntt_polys(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
