@@ -124,17 +124,7 @@ __device__ __forceinline__ void conv_mma_block(const uint64_t *__restrict__ x,
     Xs[tid * ST + 2 * i + 1] = (uint32_t)(xv[i] >> 32);
   }
   __syncthreads();
-  // the warp's four n-tiles: B fragments stay in registers for every group
-  uint32_t bf[4][KW / 4];
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const uint32_t *xr = Xs + ((warp * 4 + u) * 8 + g) * ST + tq;
-#pragma unroll
-    for (int kk = 0; kk < KW / 8; ++kk) {
-      bf[u][2 * kk] = xr[8 * kk];
-      bf[u][2 * kk + 1] = xr[8 * kk + 4];
-    }
-  }
+  // the warp's four n-tiles (B fragments read from shared memory per group)
   const uint32_t *ag = As + g * ST + tq;
   for (int G = 0; G < groups; ++G, ag += 64 * ST) {
     // A fragments of the group's four tiles, reused by the four n-tiles
@@ -159,6 +149,15 @@ __device__ __forceinline__ void conv_mma_block(const uint64_t *__restrict__ x,
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
+      uint32_t bf[KW / 4];
+      {
+        const uint32_t *xr = Xs + ((warp * 4 + u) * 8 + g) * ST + tq;
+#pragma unroll
+        for (int kk = 0; kk < KW / 8; ++kk) {
+          bf[2 * kk] = xr[8 * kk];
+          bf[2 * kk + 1] = xr[8 * kk + 4];
+        }
+      }
       int acc[4][4];
 #pragma unroll
       for (int m = 0; m < 4; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0;
@@ -167,7 +166,7 @@ __device__ __forceinline__ void conv_mma_block(const uint64_t *__restrict__ x,
 #pragma unroll
         for (int m = 0; m < 4; ++m)
           mma_u8(acc[m], af[m][kk][0], af[m][kk][1], af[m][kk][2], af[m][kk][3],
-                 bf[u][2 * kk], bf[u][2 * kk + 1]);
+                 bf[2 * kk], bf[2 * kk + 1]);
       if (live) {
         uint64_t *o = obase + (warp * 4 + u) * 8;
 #pragma unroll
@@ -372,9 +371,10 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
 }
 
 // Step 3 in binary64 (every prime below 2^50): each product is an exact
-// signed residue of magnitude <= q (FpArith::mul), sums of up to four stay
+// signed residue of magnitude <= q (FpArith::mul), sums of up to three stay
 // exact integers below 2^53 and are brought back within q/2 by one rounding
-// reduction per group; the result equals the integer kernel's.
+// reduction per group; the result equals the integer kernel's.  grid
+// (N/(2 TPB), items, l+K): a thread owns coefficients n and n + N/2.
 __global__ void __launch_bounds__(TPB) key_inner_product_f64_kernel(
     const uint64_t *__restrict__ c1, long long c1_stride,
     const uint64_t *__restrict__ ext, long long ext_stride, const ItemKeys items,
@@ -383,13 +383,14 @@ __global__ void __launch_bounds__(TPB) key_inner_product_f64_kernel(
     const uint64_t *__restrict__ pre0, const uint64_t *__restrict__ pre1,
     long long pre_stride, const uint64_t *__restrict__ pmod) {
   using F = FpArith;
+  constexpr int H = kN / 2;  // each thread: coefficients n and n + N/2
   const int n = blockIdx.x * TPB + threadIdx.x;
   const int it = blockIdx.y, t = blockIdx.z, ct = items.ct(it);
   const int lk = l + K, np = L + K;
   const int gp = t < l ? t : L + (t - l);
   const F ar(primes, qinvs, gp);
   const uint64_t *__restrict__ key = items.key[items.at(it)];
-  double s0 = 0.0, s1 = 0.0;
+  double s0[2] = {0.0, 0.0}, s1[2] = {0.0, 0.0};
   auto digit = [&](int j) -> const uint64_t * {
     const int lo = j * alpha, hi = min(lo + alpha, l);
     return (t >= lo && t < hi) ? c1 + ct * c1_stride + (size_t)t * kN + n
@@ -397,36 +398,52 @@ __global__ void __launch_bounds__(TPB) key_inner_product_f64_kernel(
   };
   const size_t kstep = (size_t)2 * np * kN;
   const uint64_t *kb = key + (size_t)gp * kN + n;
-  for (int j = 0; j < beta; j += 4) {
-    uint64_t e[4], k0[4], k1[4];
+  // digits in groups of three: all 18 loads of a group are in flight before
+  // its multiplies
+  for (int j = 0; j < beta; j += 3) {
+    uint64_t e[3][2], k0[3][2], k1[3][2];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 3; ++u) {
       if (j + u < beta) {
-        e[u] = *digit(j + u);
-        k0[u] = __ldg(kb + (j + u) * kstep);
-        k1[u] = __ldg(kb + (j + u) * kstep + (size_t)np * kN);
+        const uint64_t *d = digit(j + u);
+        const uint64_t *k = kb + (j + u) * kstep;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          e[u][h] = d[h * H];
+          k0[u][h] = __ldg(k + h * H);
+          k1[u][h] = __ldg(k + (size_t)np * kN + h * H);
+        }
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 3; ++u) {
       if (j + u < beta) {
-        const double ed = F::from_word(e[u]);
-        s0 = __dadd_rn(s0, ar.mul(ed, F::from_word(k0[u])));
-        s1 = __dadd_rn(s1, ar.mul(ed, F::from_word(k1[u])));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const double ed = F::from_word(e[u][h]);
+          s0[h] = __dadd_rn(s0[h], ar.mul(ed, F::from_word(k0[u][h])));
+          s1[h] = __dadd_rn(s1[h], ar.mul(ed, F::from_word(k1[u][h])));
+        }
       }
     }
-    s0 = ar.red(s0);
-    s1 = ar.red(s1);
-  }
-  if (pre0 != nullptr && t < l) {  // + P (pre0, pre1) on the Q limbs
-    const double pm = F::from_word(pmod[t]);
-    const size_t at = ct * pre_stride + (size_t)t * kN + n;
-    s0 = __dadd_rn(s0, ar.mul(F::from_word(pre0[at]), pm));
-    s1 = __dadd_rn(s1, ar.mul(F::from_word(pre1[at]), pm));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      s0[h] = ar.red(s0[h]);
+      s1[h] = ar.red(s1[h]);
+    }
   }
   uint64_t *o = acc + ((size_t)it * 2 * lk + t) * kN + n;
-  o[0] = F::to_word(ar.full(s0));
-  o[(size_t)lk * kN] = F::to_word(ar.full(s1));
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (pre0 != nullptr && t < l) {  // + P (pre0, pre1) on the Q limbs
+      const double pm = F::from_word(pmod[t]);
+      const size_t at = ct * pre_stride + (size_t)t * kN + n + h * H;
+      s0[h] = __dadd_rn(s0[h], ar.mul(F::from_word(pre0[at]), pm));
+      s1[h] = __dadd_rn(s1[h], ar.mul(F::from_word(pre1[at]), pm));
+    }
+    o[h * H] = F::to_word(ar.full(s0[h]));
+    o[(size_t)lk * kN + h * H] = F::to_word(ar.full(s1[h]));
+  }
 }
 
 // Step 3 launcher: grid (N/TPB, items, l+K) in the context's arithmetic.
@@ -440,7 +457,7 @@ int launch_key_inner_product(b2f_context *ctx, int items_n, const uint64_t *c1,
   const int K = ctx->K, beta = ctx->levels[l].beta;
   const dim3 grid(kN / TPB, items_n, l + K);
   if (ctx->fp64)
-    key_inner_product_f64_kernel<<<grid, TPB, 0, s>>>(
+    key_inner_product_f64_kernel<<<dim3(kN / TPB / 2, items_n, l + K), TPB, 0, s>>>(
         c1, c1_stride, ext, ext_stride, items, acc, ctx->d_primes, ctx->d_qinv, l, K,
         ctx->L, ctx->alpha, beta, pre0, pre1, pre_stride, ctx->d_pmod);
   else
