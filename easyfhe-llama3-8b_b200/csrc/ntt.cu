@@ -186,6 +186,11 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
       }
     }
   }
+  // split-phase cluster barrier: arriving now and waiting just before the
+  // first remote shared-memory write certifies that every CTA of the cluster
+  // is resident, with the barrier's latency hidden behind the loads and
+  // stages 0-2 (nothing needs publishing yet, so the arrive is relaxed)
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
   V x[16];
   // stages 0-2 on columns c0, c0+1 (rows k at stride 8192), straight from HBM
   const int c0 = rank * 1024 + 2 * tid;
@@ -220,10 +225,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
       for (int h = 0; h < 16; h += 8) ct_bfly(ar, x[h + k], x[h + k + 1], w);
     }
   }
-  // every CTA of the cluster is resident before its shared memory is written;
-  // nothing needs publishing yet, so the arrive is relaxed
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n"
-               "barrier.cluster.wait.aligned;\n" ::: "memory");
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
   // row k of every column belongs to block k (32-bit cluster addresses)
   {
     const uint32_t local = (uint32_t)__cvta_generic_to_shared(buf + pad(c0));
@@ -389,8 +391,11 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   store16<32>(x, vb, lb);
   __syncthreads();
   load16<512>(x, vb, tid);
+  // split-phase: this thread's reads of its block are done (release); the
+  // wait after stages 6-3 means every CTA has finished reading its block
+  asm volatile("barrier.cluster.arrive.aligned;\n" ::: "memory");
   gs_pass(ar, x, tw, 3, jb + tid, 512);
-  cluster.sync();  // every CTA has finished reading its own block
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
   // word l of block `rank` is row `rank` of column l, owned by CTA l/1024
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
