@@ -99,17 +99,72 @@ class Context:
 
         return float(self.params.q[int(cur_limbs)])
 
-    def clear_cuda_rotation_cache(self) -> None:
-        """Keys stay resident in HBM (llama3fhe/operators/nonlinear/bootstrap.py:191-215
-        evicts EasyFHE's cache to make room; 180 GB needs no eviction)."""
+    def clear_cuda_rotation_cache(self, keep_rotations=None) -> int:
+        """Evict rotation keys from HBM (llama3fhe/operators/nonlinear/bootstrap.py:
+        191-215, graph.py:1158): every key whose rotation is not in keep_rotations
+        (None: every key) moves to pinned host memory; with spec.auto_load_keys the
+        next use copies it back.  Returns the HBM bytes released to the caching
+        allocator."""
 
-    def rotation_key(self, rotation: int) -> tuple[int, torch.Tensor]:
+        keep = set() if keep_rotations is None else {
+            galois_element(int(r), self.logN) for r in keep_rotations}
+        freed = 0
+        for g, key in list(self.rotation_keys.items()):
+            if g in keep or not key.is_cuda:
+                continue
+            host = torch.empty(key.shape, dtype=key.dtype, pin_memory=True)
+            host.copy_(key)
+            self.rotation_keys[g] = host
+            freed += key.numel() * key.element_size()
+        return freed
+
+    def truncate_rotation_keys(self, max_limbs: int, rotations=None) -> int:
+        """Keep only the digits a key needs up to max_limbs limbs (the first
+        ceil(max_limbs / alpha) of dnum; the key inner product at l limbs reads
+        digits j < ceil(l / alpha)).  For keys only used at low levels (the
+        linears at 13 limbs read 2 of 5 digits at the layer parameters).  A
+        truncated key used above max_limbs raises ValueError.  Returns the
+        bytes released."""
+
+        digits = -(-int(max_limbs) // self.native.alpha)
+        if not 1 <= int(max_limbs) <= self.L:
+            raise ValueError(f"max_limbs {max_limbs} outside [1, {self.L}]")
+        sel = None if rotations is None else {
+            galois_element(int(r), self.logN) for r in rotations}
+        freed = 0
+        for g, key in list(self.rotation_keys.items()):
+            if (sel is not None and g not in sel) or key.shape[0] <= digits:
+                continue
+            freed += (key.shape[0] - digits) * key[0].numel() * key.element_size()
+            self.rotation_keys[g] = key[:digits].clone()
+        return freed
+
+    def key_bytes(self) -> dict:
+        """Bytes of evaluation keys in HBM and in host memory."""
+
+        out = {"device": 0, "host": 0}
+        keys = list(self.rotation_keys.values()) + (
+            [self.relin_key] if self.relin_key is not None else [])
+        for key in keys:
+            out["device" if key.is_cuda else "host"] += key.numel() * key.element_size()
+        return out
+
+    def rotation_key(self, rotation: int, limbs: int | None = None) -> tuple[int, torch.Tensor]:
         g = galois_element(int(rotation), self.logN)
         key = self.rotation_keys.get(g)
         if key is None:
             raise ValueError(
                 f"no rotation key for index {rotation} (galois {g}); the context "
                 "rotation set must include every rotation used")
+        if not key.is_cuda:
+            if not bool(self.spec.auto_load_keys):
+                raise ValueError(f"rotation key {rotation} was evicted from the device and "
+                                 "the context has auto_load_keys=False")
+            key = key.to(self.native.device)
+            self.rotation_keys[g] = key
+        if limbs is not None and key.shape[0] < -(-int(limbs) // self.native.alpha):
+            raise ValueError(f"rotation key {rotation} keeps {key.shape[0]} digits, too few "
+                             f"for {limbs} limbs")
         return g, key
 
     def workspace(self, name: str, nbytes: int) -> torch.Tensor:
@@ -577,8 +632,8 @@ def homo_rotate(ct: Ciphertext, rotation: int, context) -> Ciphertext:
     g = galois_element(int(rotation), ctx.logN)
     if g == 1:
         return ct.deep_copy()
-    _, key = ctx.rotation_key(int(rotation))
     l = _limbs(ct)
+    _, key = ctx.rotation_key(int(rotation), l)
     out = ctx.native.rotate(ct.data, l, g, key)
     return _new(out, ct)
 
@@ -684,7 +739,7 @@ def prepare_hoisted_baby_rotations(ct: Ciphertext, baby_offsets, context,
     for off in offsets:
         g = galois_element(off, ctx.logN)
         gal.append(g)
-        keys.append(None if g == 1 else ctx.rotation_key(off)[1])
+        keys.append(None if g == 1 else ctx.rotation_key(off, l)[1])
     C = ct.batch_size
     ext = nat.modup(ct.data, l, C) if any(g != 1 for g in gal) else None
     out = nat.rotate_hoisted(ct.data, l, ext, gal, keys, num_cts=C)
@@ -723,7 +778,7 @@ def hoisted_mac_sum(ct: Ciphertext, baby_offsets, plaintexts: Plaintext, giant_o
         raise ValueError(f"{plaintexts.rows} plaintext rows < giants*babies = {G * B}")
     pts = plaintexts.q_part(l)
     if G > 1:
-        gg, gkey = ctx.rotation_key(int(giant_offset))
+        gg, gkey = ctx.rotation_key(int(giant_offset), l)
     else:
         gg, gkey = 1, None
     out = ctx.native.bsgs_mac(block.data, B, pts, G, l, gg, gkey, num_cts=C)
@@ -860,7 +915,7 @@ def fast_rotate(ct: Ciphertext, offsets, context, output_ext: bool = False) -> C
     for off in offsets:
         g = galois_element(off, ctx.logN)
         gal.append(g)
-        keys.append(None if g == 1 else ctx.rotation_key(off)[1])
+        keys.append(None if g == 1 else ctx.rotation_key(off, l)[1])
     ext = ctx.native.modup(ct.data, l) if any(g != 1 for g in gal) else None
     out = ctx.native.rotate_hoisted_ext(ct.data, l, ext, gal, keys)
     return Ciphertext(out, ct.state, ct.slots, ctx, is_ext=True)

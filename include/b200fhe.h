@@ -88,8 +88,10 @@ uint64_t b2f_galois_element(int log_n, int64_t rotation);
 
 /* ---- hybrid key switching ----
  * Key layout: [digits][2][L+K][N], NTT form, generated for the top level and
- * used truncated at any level l (limbs 0..l-1 and L..L+K-1).
- * fhe.homo_rotate(ct, r, ctx) (34 call sites, e.g.
+ * used truncated at any level l (limbs 0..l-1 and L..L+K-1).  At l limbs only
+ * digits j < ceil(l / alpha) are read, so a key kept for levels <= l may be
+ * stored as its first ceil(l / alpha) digits (fhe.Context.truncate_rotation_keys). */
+/* fhe.homo_rotate(ct, r, ctx) (34 call sites, e.g.
  * llama3fhe/operators/linear/operator.py:333-337, qkv_kernel.py:829-834):
  * out = (pi_g(c0 + d0), pi_g(d1)), (d0, d1) = KeySwitch(c1).  num_cts
  * ciphertexts at l limbs share one key. */
