@@ -102,15 +102,25 @@ __device__ __forceinline__ void gs_pass(const A &ar, typename A::V (&x)[16],
   }
 }
 
+// pad(l + STRIDE k) = pad(l) + pad_step<STRIDE>() k for k < 16: exact when
+// STRIDE is a multiple of 32 (each step adds STRIDE / 32 blocks), or when
+// l's offset in its 32-word block plus 15 STRIDE stays inside the block (pass
+// C: STRIDE 2, l mod 32 <= 1).  The accesses then use immediate offsets.
+template <int STRIDE>
+__device__ constexpr int pad_step() {
+  return STRIDE % 32 == 0 ? STRIDE + STRIDE / 16 : STRIDE;
+}
 template <int STRIDE, class V>
 __device__ __forceinline__ void load16(V (&x)[16], const V *buf, int l) {
+  const V *p = buf + pad(l);
 #pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = buf[pad(l + STRIDE * k)];
+  for (int k = 0; k < 16; ++k) x[k] = p[pad_step<STRIDE>() * k];
 }
 template <int STRIDE, class V>
 __device__ __forceinline__ void store16(const V (&x)[16], V *buf, int l) {
+  V *p = buf + pad(l);
 #pragma unroll
-  for (int k = 0; k < 16; ++k) buf[pad(l + STRIDE * k)] = x[k];
+  for (int k = 0; k < 16; ++k) p[pad_step<STRIDE>() * k] = x[k];
 }
 
 // Where the forward transform's outputs go.  PlainOut: the output limb, as
@@ -277,8 +287,11 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   }
   // each lane rewrites the words it read in pass C, then the warp writes its
   // 512-word segment with coalesced 16-byte stores
+  {
+    uint64_t *p = buf + pad(lc);
 #pragma unroll
-  for (int k = 0; k < 16; ++k) buf[pad(lc + 2 * k)] = A::to_word(x[k]);
+    for (int k = 0; k < 16; ++k) p[pad_step<2>() * k] = A::to_word(x[k]);
+  }
   __syncwarp();
   if constexpr (E::kModDown) {
     const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
@@ -305,8 +318,9 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
       for (int u = 0; u < 4; ++u) {
         const int kk = warp * SEG + 2 * (lane + 32 * (r0 + u));
         const uint32_t j = (uint32_t)(jb + kk);
-        uint64_t w0 = shoup(sub_mod(av[u].x, buf[pad(kk)], q), pi.x, pi.y, q);
-        uint64_t w1 = shoup(sub_mod(av[u].y, buf[pad(kk + 1)], q), pi.x, pi.y, q);
+        const uint64_t *bk = buf + pad(kk);  // kk even: kk + 1 is in the same block
+        uint64_t w0 = shoup(sub_mod(av[u].x, bk[0], q), pi.x, pi.y, q);
+        uint64_t w1 = shoup(sub_mod(av[u].y, bk[1], q), pi.x, pi.y, q);
         if (epi.qinv) {
           w0 = shoup(w0, qi.x, qi.y, q);
           w1 = shoup(w1, qi.x, qi.y, q);
@@ -324,12 +338,12 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
       }
     }
   } else {
+    const int idx0 = warp * SEG + 2 * lane;
+    const uint64_t *p = buf + pad(idx0);  // idx0 + 64 r: pad adds 68 r
 #pragma unroll
-    for (int r = 0; r < SEG / 64; ++r) {
-      const int idx = warp * SEG + 2 * (lane + 32 * r);
-      *reinterpret_cast<ulonglong2 *>(o + jb + idx) =
-          *reinterpret_cast<const ulonglong2 *>(buf + pad(idx));
-    }
+    for (int r = 0; r < SEG / 64; ++r)
+      *reinterpret_cast<ulonglong2 *>(o + jb + idx0 + 64 * r) =
+          *reinterpret_cast<const ulonglong2 *>(p + 68 * r);
   }
 }
 
@@ -356,18 +370,23 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   const int jb = rank * BLK;
 
   // each warp stages its own 512-word segment
+  {
+    const int idx0 = warp * SEG + 2 * lane;
+    uint64_t *p = buf + pad(idx0);  // idx0 + 64 r: pad adds 68 r
 #pragma unroll
-  for (int r = 0; r < SEG / 64; ++r) {
-    const int idx = warp * SEG + 2 * (lane + 32 * r);
-    *reinterpret_cast<ulonglong2 *>(buf + pad(idx)) =
-        *reinterpret_cast<const ulonglong2 *>(a + jb + idx);
+    for (int r = 0; r < SEG / 64; ++r)
+      *reinterpret_cast<ulonglong2 *>(p + 68 * r) =
+          *reinterpret_cast<const ulonglong2 *>(a + jb + idx0 + 64 * r);
   }
   __syncwarp();
 
   V x[16];
   const int lc = (tid >> 1) * 32 + (tid & 1);
+  {
+    const uint64_t *p = buf + pad(lc);
 #pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = A::from_word(buf[pad(lc + 2 * k)]);
+    for (int k = 0; k < 16; ++k) x[k] = A::from_word(p[pad_step<2>() * k]);
+  }
   const bool odd = tid & 1;
   const int je = jb + (tid >> 1) * 32;
 #pragma unroll
