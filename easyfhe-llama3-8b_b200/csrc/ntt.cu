@@ -62,24 +62,26 @@ struct NttParams {
   int items;
 };
 
-// twiddle index of stage s for global element j: 2^s + j / 2^(16-s)
-__device__ __forceinline__ int tw_index(int s, int j) {
-  return (1 << s) + (j >> (kLogN - s));
-}
+// Twiddles: stage s of element j uses entry 2^s + j / 2^(16-s) of the
+// prime's table (psi powers in bit-reversed order).
 
 // Four CT stages s0..s0+3 on 16 registers with element index
 // j(k) = base + k * stride; at local stage t the pairs are (k, k + d),
-// d = 8 >> t, and each block of 2d registers shares one twiddle.
+// d = 8 >> t, and each block of 2d registers shares one twiddle.  For the
+// three passes' (base, stride) the stage-s index splits without carry:
+// (base + blk stride) >> (16 - s) = (base >> (16 - s)) + (blk stride >> (16 - s)),
+// so each twiddle is a per-stage base plus a constant offset.
 template <class A>
 __device__ __forceinline__ void ct_pass(const A &ar, typename A::V (&x)[16],
                                         const typename A::W *tw, int s0, int base,
                                         int stride) {
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
-    const int d = 8 >> t;
+    const int d = 8 >> t, sh = kLogN - (s0 + t);
+    const typename A::W *tws = tw + (1 << (s0 + t)) + (base >> sh);
 #pragma unroll
     for (int blk = 0; blk < 16; blk += 2 * d) {
-      const typename A::W w = A::ldtw(tw, tw_index(s0 + t, base + blk * stride));
+      const typename A::W w = A::ldtw(tws, (blk * stride) >> sh);
 #pragma unroll
       for (int k = blk; k < blk + d; ++k) ct_bfly(ar, x[k], x[k + d], w);
     }
@@ -92,10 +94,11 @@ __device__ __forceinline__ void gs_pass(const A &ar, typename A::V (&x)[16],
                                         int stride) {
 #pragma unroll
   for (int t = 3; t >= 0; --t) {
-    const int d = 8 >> t;
+    const int d = 8 >> t, sh = kLogN - (s0 + t);
+    const typename A::W *tws = tw + (1 << (s0 + t)) + (base >> sh);
 #pragma unroll
     for (int blk = 0; blk < 16; blk += 2 * d) {
-      const typename A::W w = A::ldtw(tw, tw_index(s0 + t, base + blk * stride));
+      const typename A::W w = A::ldtw(tws, (blk * stride) >> sh);
 #pragma unroll
       for (int k = blk; k < blk + d; ++k) gs_bfly(ar, x[k], x[k + d], w);
     }
@@ -265,6 +268,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   ct_pass(ar, x, tw, 11, jb + lc, 2);
   const bool odd = tid & 1;
   const int je = jb + (tid >> 1) * 32;
+  // stage 15 twiddle of element je + 2 (k + odd): 2^15 + je / 2 + odd + k
+  const W *tw15 = tw + (1 << 15) + (je >> 1) + (odd ? 1 : 0);
   // butterflies k (even lane) and k+1 (odd lane) of each pair: one
   // exchange brings each lane the operand it lacks, one sends back the half
   // of the result the other lane owns, and no product is computed twice
@@ -274,7 +279,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     const V give = odd ? x[k] : x[k + 1];
     const V got = __shfl_xor_sync(0xffffffffu, give, 1);
     const V X = odd ? got : x[k], Y = odd ? x[k + 1] : got;
-    const W w = A::ldtw(tw, tw_index(15, je + 2 * (k + (odd ? 1 : 0))));
+    const W w = A::ldtw(tw15, k);
     // outputs of this lane's butterfly, fully reduced
     V ra = X, rb = Y;
     ar.ct(ra, rb, w);
@@ -389,13 +394,14 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   }
   const bool odd = tid & 1;
   const int je = jb + (tid >> 1) * 32;
+  const W *tw15 = tw + (1 << 15) + (je >> 1);  // stage 15: element je + 2k
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     const V mine = x[k];
     const V other = __shfl_xor_sync(0xffffffffu, mine, 1);
     const V X = odd ? other : mine, Y = odd ? mine : other;
     if (odd) {
-      const W w = A::ldtw(tw, tw_index(15, je + 2 * k));
+      const W w = A::ldtw(tw15, k);
       x[k] = ar.gs_diff(X, Y, w);
     } else {
       x[k] = ar.gs_sum(X, Y);
