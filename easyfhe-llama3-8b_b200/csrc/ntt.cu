@@ -453,15 +453,22 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   }
   {
     const W w = A::ldtw(tw, 1);
-#pragma unroll
-    for (int h = 0; h < 16; h += 8)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) gs_bfly(ar, x[h + k], x[h + k + 4], w);
-  }
-  {
     const W sc = A::scale(P.scales[job.scale_idx]);
+    if constexpr (A::kFoldScale) {
+      // stage 0 with the output scale folded in: ((x + y) s, (x - y) w s)
+      const W wsc = ar.fold(w, sc);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) x[k] = ar.scale_out(x[k], sc);
+      for (int h = 0; h < 16; h += 8)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ar.gs_scaled(x[h + k], x[h + k + 4], sc, wsc);
+    } else {
+#pragma unroll
+      for (int h = 0; h < 16; h += 8)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) gs_bfly(ar, x[h + k], x[h + k + 4], w);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) x[k] = ar.scale_out(x[k], sc);
+    }
   }
 #pragma unroll
   for (int k = 0; k < 8; ++k)

@@ -16,6 +16,7 @@ namespace b2f {
 struct IntArith {
   using V = uint64_t;
   using W = ulonglong2;
+  static constexpr bool kFoldScale = false;  // w s would need its Shoup quotient
   uint64_t q, q2;
   __device__ __forceinline__ IntArith(const uint64_t *primes, const double *, int prime)
       : q(primes[prime]), q2(2 * primes[prime]) {}
@@ -67,6 +68,7 @@ struct FpArith {
   using W = double;
   static constexpr double kTwo52 = 4503599627370496.0;
   static constexpr double kMagic = 6755399441055744.0;  // 1.5 * 2^52
+  static constexpr bool kFoldScale = true;
   double q, qinv;
   __device__ __forceinline__ FpArith(const uint64_t *primes, const double *qinvs, int prime)
       : q(from_word(primes[prime])), qinv(qinvs[prime]) {}
@@ -114,6 +116,14 @@ struct FpArith {
     return r < 0.0 ? __dadd_rn(r, q) : r;
   }
   __device__ __forceinline__ V scale_out(V v, W s) const { return full(mul(v, s)); }
+  // w s mod q in [0, q), and the last inverse butterfly with the output scale
+  // folded in: ((x + y) s, (x - y) ws), fully reduced (|x +- y| <= 2q)
+  __device__ __forceinline__ W fold(W w, W s) const { return full(mul(w, s)); }
+  __device__ __forceinline__ void gs_scaled(V &x, V &y, W s, W ws) const {
+    const V u = full(mul(__dadd_rn(x, y), s));
+    y = full(mul(__dadd_rn(x, -y), ws));
+    x = u;
+  }
 };
 
 template <class A>
