@@ -13,10 +13,19 @@ from _ckks import N, pair, rand_residues, to_dev, to_host
 pytestmark = pytest.mark.gpu
 
 
-def test_ext_rotations_and_moddown_bit_exact():
+@pytest.mark.parametrize("arith", ["f64", "int64"])
+def test_ext_rotations_and_moddown_bit_exact(arith):
     from easyfhe import core
 
     ctx, orc = pair(8, 2, 3)
+    ctx.set_arith(arith)
+    try:
+        _ext_rotations_and_moddown(ctx, orc, core)
+    finally:
+        ctx.set_arith("auto")
+
+
+def _ext_rotations_and_moddown(ctx, orc, core):
     l = 7
     s_ntt = ctx.secret_to_ntt(core.sample_secret(41, 192))
     gs = [1, core.galois_element(5), core.galois_element(131071)]

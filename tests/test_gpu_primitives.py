@@ -144,7 +144,8 @@ def test_rotate_bit_exact(rotation, arith):
         assert np.array_equal(out[c], orc.rotate(cts[c], l, g, hkey)), f"ct {c}"
 
 
-def test_hoisted_rotations_bit_exact():
+@pytest.mark.parametrize("arith", ["f64", "int64"])
+def test_hoisted_rotations_bit_exact(arith):
     from easyfhe import core
 
     L, l = 8, 8
@@ -155,12 +156,13 @@ def test_hoisted_rotations_bit_exact():
     rng = np.random.default_rng(3)
     ct = rand_residues(rng, ctx.primes[:l], 2)
     dct = to_dev(ct)
-    ext = ctx.modup(dct, l)
-    got = to_host(ctx.rotate_hoisted(dct, l, ext, gs, keys))
+    with use_arith(ctx, arith):
+        ext = ctx.modup(dct, l)
+        got = to_host(ctx.rotate_hoisted(dct, l, ext, gs, keys))
+        plain = to_host(ctx.rotate(dct, l, gs[1], keys[1]))
     want = orc.rotate_hoisted(ct, l, gs, [to_host(k) for k in keys])
     assert np.array_equal(got, want)
     # one hoisted rotation equals the plain HRotate
-    plain = to_host(ctx.rotate(dct, l, gs[1], keys[1]))
     assert np.array_equal(got[1], plain)
 
 
@@ -229,9 +231,11 @@ def test_relinearize_bit_exact():
     assert np.array_equal(got[1], w1.astype(np.uint64))
 
 
-@pytest.mark.parametrize("L,K,dnum,l,cts", [(8, 2, 3, 6, 1), (8, 2, 3, 2, 2),
-                                             (10, 4, 5, 10, 1), (12, 8, 3, 7, 2)])
-def test_relinearize_rescale_bit_exact(L, K, dnum, l, cts):
+@pytest.mark.parametrize("L,K,dnum,l,cts,arith", [(8, 2, 3, 6, 1, "f64"), (8, 2, 3, 2, 2, "f64"),
+                                                   (10, 4, 5, 10, 1, "f64"),
+                                                   (12, 8, 3, 7, 2, "f64"),
+                                                   (8, 2, 3, 6, 2, "int64")])
+def test_relinearize_rescale_bit_exact(L, K, dnum, l, cts, arith):
     """The fused relinearise + rescale against the oracle's rounding division
     by P q_{l-1}, and against the GPU's own relinearise then rescale (equal but
     for rounding ties, probability about K / q per coefficient).  K = 2, 4, 8
@@ -244,12 +248,13 @@ def test_relinearize_rescale_bit_exact(L, K, dnum, l, cts):
     rk = ctx.keygen_relin(s_ntt, seed=6)
     rng = np.random.default_rng(100 + l + K)
     ct3 = np.stack([rand_residues(rng, ctx.primes[:l], 3) for _ in range(cts)])
-    got = to_host(ctx.relinearize_rescale(to_dev(ct3), l, rk))
+    with use_arith(ctx, arith):
+        got = to_host(ctx.relinearize_rescale(to_dev(ct3), l, rk))
+        two = to_host(ctx.rescale(ctx.relinearize(to_dev(ct3), l, rk), 2 * cts, l))
     assert got.shape == (cts, 2, l - 1, N)
     rk_h = to_host(rk)
     for c in range(cts):
         assert np.array_equal(got[c], orc.relin_rescale(ct3[c], l, rk_h)), c
-    two = to_host(ctx.rescale(ctx.relinearize(to_dev(ct3), l, rk), 2 * cts, l))
     assert np.array_equal(got.reshape(two.shape), two)
 
 
