@@ -30,6 +30,8 @@
 // 64-register budget of two CTAs per SM nearly free of spills.
 #include <cooperative_groups.h>
 
+#include <atomic>
+
 #include "b2f_internal.h"
 #include "ksitems.cuh"
 #include "ntt_arith.cuh"
@@ -483,9 +485,11 @@ int launch_ntt_impl(b2f_context *ctx, const uint64_t *in, long long in_stride,
                     int jobs_per_item, int items, int inverse,
                     const ulonglong2 *scales, const E &epi, cudaStream_t s) {
   if (items <= 0 || jobs_per_item <= 0) return B2F_OK;
-  static unsigned configured = 0;  // one bit per device
-  const unsigned bit = 1u << (ctx->device & 31);
-  if (!(configured & bit)) {
+  // one bit per device: the attribute calls are idempotent, so threads that
+  // race on a device's first launch only repeat them
+  static std::atomic<uint64_t> configured{0};
+  const uint64_t bit = 1ull << (ctx->device & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
     B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<IntArith, PlainOut>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SMEM_BYTES));
@@ -504,7 +508,7 @@ int launch_ntt_impl(b2f_context *ctx, const uint64_t *in, long long in_stride,
     B2F_CUDA(cudaFuncSetAttribute(ntt_inv_kernel<FpArith>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SMEM_BYTES));
-    configured |= bit;
+    configured.fetch_or(bit, std::memory_order_release);
   }
   const bool fp = ctx->fp64;
   NttParams P;
