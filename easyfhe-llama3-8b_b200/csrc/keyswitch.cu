@@ -171,14 +171,15 @@ __device__ __forceinline__ void conv_mma_block(const uint64_t *__restrict__ x,
         uint64_t *o = obase + (warp * 4 + u) * 8;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          uint64_t lo4 = 0, hi4 = 0;  // byte sums 0-3 and 4-7
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            lo4 += (uint64_t)(uint32_t)acc[m][c] << (16 * m);
-            lo4 += (uint64_t)(uint32_t)acc[m][2 + c] << (16 * m + 8);
-            hi4 += (uint64_t)(uint32_t)acc[m + 2][c] << (16 * m);
-            hi4 += (uint64_t)(uint32_t)acc[m + 2][2 + c] << (16 * m + 8);
-          }
+          // byte sums 0-3 and 4-7 (each < 2^22): u32 x constant + u64 terms,
+          // one wide multiply-add each
+          uint64_t lo4 = (uint32_t)acc[0][c], hi4 = (uint32_t)acc[2][c];
+          lo4 += (uint64_t)(uint32_t)acc[0][2 + c] * 256u;
+          hi4 += (uint64_t)(uint32_t)acc[2][2 + c] * 256u;
+          lo4 += (uint64_t)(uint32_t)acc[1][c] * 65536u;
+          hi4 += (uint64_t)(uint32_t)acc[3][c] * 65536u;
+          lo4 += (uint64_t)(uint32_t)acc[1][2 + c] * 16777216u;
+          hi4 += (uint64_t)(uint32_t)acc[3][2 + c] * 16777216u;
           const uint64_t lo = lo4 + (hi4 << 32);
           const uint64_t hi = (hi4 >> 32) + (lo < lo4);
           o[c] = reduce79(hi, lo, R);
