@@ -447,6 +447,91 @@ __global__ void __launch_bounds__(TPB) key_inner_product_f64_kernel(
   }
 }
 
+// Step 3 in binary64, software-pipelined: a block walks IPR tiles of 2 TPB
+// consecutive coefficients of one (item, target limb); each thread copies its
+// next tile's digit and key words (16-byte pieces: coefficients n, n+1) into
+// its own slots of a double-buffered shared array with cp.async while it
+// computes the current tile, so loads stay in flight through the arithmetic.
+// Slots are private to their thread: cp.async.wait_group alone orders them.
+// grid (N / (2 TPB IPR), items, l+K); dynamic shared memory 2 x 3 beta x TPB
+// x 16 bytes (beta <= 4).  Same arithmetic as key_inner_product_f64_kernel.
+constexpr int IPR = 8;  // tiles per block
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait1() {
+  asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+}
+
+__global__ void __launch_bounds__(TPB, 2) key_inner_product_f64_pipe_kernel(
+    const uint64_t *__restrict__ c1, long long c1_stride,
+    const uint64_t *__restrict__ ext, long long ext_stride, const ItemKeys items,
+    uint64_t *__restrict__ acc, const uint64_t *__restrict__ primes,
+    const double *__restrict__ qinvs, int l, int K, int L, int alpha, int beta) {
+  using F = FpArith;
+  extern __shared__ __align__(16) ulonglong2 ipsm[];  // [stage][3 beta][TPB]
+  const int tid = threadIdx.x;
+  const int it = blockIdx.y, t = blockIdx.z, ct = items.ct(it);
+  const int lk = l + K, np = L + K, A = 3 * beta;
+  const int gp = t < l ? t : L + (t - l);
+  const F ar(primes, qinvs, gp);
+  const uint64_t *__restrict__ key = items.key[items.at(it)];
+  const size_t kstep = (size_t)2 * np * kN;
+  const uint64_t *kb = key + (size_t)gp * kN;
+  const int nb = blockIdx.x * (2 * TPB * IPR);
+  auto issue = [&](int r) {
+    const int n = nb + 2 * (tid + TPB * r);
+    ulonglong2 *slot = ipsm + (size_t)(r & 1) * A * TPB + tid;
+    for (int j = 0; j < beta; ++j) {
+      const int lo = j * alpha, hi = min(lo + alpha, l);
+      const uint64_t *d = (t >= lo && t < hi)
+                              ? c1 + ct * c1_stride + (size_t)t * kN
+                              : ext + ct * ext_stride + ((size_t)j * lk + t) * kN;
+      const uint64_t *k = kb + j * kstep;
+      cp_async16(slot + (3 * j) * TPB, d + n);
+      cp_async16(slot + (3 * j + 1) * TPB, k + n);
+      cp_async16(slot + (3 * j + 2) * TPB, k + (size_t)np * kN + n);
+    }
+    cp_async_commit();
+  };
+  issue(0);
+  for (int r = 0; r < IPR; ++r) {
+    if (r + 1 < IPR)
+      issue(r + 1);
+    else
+      cp_async_commit();  // an empty group keeps "all but the newest" meaning tile r
+    cp_async_wait1();
+    const ulonglong2 *slot = ipsm + (size_t)(r & 1) * A * TPB + tid;
+    double s0[2] = {0.0, 0.0}, s1[2] = {0.0, 0.0};
+    for (int j = 0; j < beta; ++j) {
+      const ulonglong2 e = slot[(3 * j) * TPB], k0 = slot[(3 * j + 1) * TPB],
+                       k1 = slot[(3 * j + 2) * TPB];
+      const double e0 = F::from_word(e.x), e1 = F::from_word(e.y);
+      s0[0] = __dadd_rn(s0[0], ar.mul(e0, F::from_word(k0.x)));
+      s0[1] = __dadd_rn(s0[1], ar.mul(e1, F::from_word(k0.y)));
+      s1[0] = __dadd_rn(s1[0], ar.mul(e0, F::from_word(k1.x)));
+      s1[1] = __dadd_rn(s1[1], ar.mul(e1, F::from_word(k1.y)));
+      if (j % 3 == 2) {  // sums of up to three products stay below 2^53
+        s0[0] = ar.red(s0[0]);
+        s0[1] = ar.red(s0[1]);
+        s1[0] = ar.red(s1[0]);
+        s1[1] = ar.red(s1[1]);
+      }
+    }
+    const int n = nb + 2 * (tid + TPB * r);
+    uint64_t *o = acc + ((size_t)it * 2 * lk + t) * kN + n;
+    *reinterpret_cast<ulonglong2 *>(o) =
+        make_ulonglong2(F::to_word(ar.full(s0[0])), F::to_word(ar.full(s0[1])));
+    *reinterpret_cast<ulonglong2 *>(o + (size_t)lk * kN) =
+        make_ulonglong2(F::to_word(ar.full(s1[0])), F::to_word(ar.full(s1[1])));
+  }
+}
+
 // Step 3 launcher: grid (N/TPB, items, l+K) in the context's arithmetic.
 int launch_key_inner_product(b2f_context *ctx, int items_n, const uint64_t *c1,
                              long long c1_stride, const uint64_t *ext,
@@ -457,7 +542,15 @@ int launch_key_inner_product(b2f_context *ctx, int items_n, const uint64_t *c1,
                              long long pre_stride = 0) {
   const int K = ctx->K, beta = ctx->levels[l].beta;
   const dim3 grid(kN / TPB, items_n, l + K);
-  if (ctx->fp64)
+  if (ctx->fp64 && pre0 == nullptr && beta <= 4) {
+    const size_t sm = (size_t)2 * 3 * beta * TPB * sizeof(ulonglong2);
+    int rc;
+    if ((rc = set_smem(key_inner_product_f64_pipe_kernel, sm))) return rc;
+    key_inner_product_f64_pipe_kernel<<<dim3(kN / (2 * TPB * IPR), items_n, l + K), TPB, sm,
+                                        s>>>(c1, c1_stride, ext, ext_stride, items, acc,
+                                             ctx->d_primes, ctx->d_qinv, l, K, ctx->L,
+                                             ctx->alpha, beta);
+  } else if (ctx->fp64)
     key_inner_product_f64_kernel<<<dim3(kN / TPB / 2, items_n, l + K), TPB, 0, s>>>(
         c1, c1_stride, ext, ext_stride, items, acc, ctx->d_primes, ctx->d_qinv, l, K,
         ctx->L, ctx->alpha, beta, pre0, pre1, pre_stride, ctx->d_pmod);
