@@ -492,7 +492,10 @@ def main() -> None:
     ws = ctx.workspace(core.lib.b2f_rotate_workspace(ctx.handle, C, l))
     stream = torch.cuda.current_stream()
 
-    launches_per_rotate = 7  # iNTT, ModUp conv, NTT, inner product, iNTT(P), conv, NTT+combine
+    # iNTT, ModUp conversion, NTT, inner product, iNTT of the P part, ModDown
+    # conversion, NTT + combine; binary64 with K <= 4 computes the ModDown
+    # conversion inside its NTT (no separate conversion launch)
+    launches_per_rotate = 6 if (ctx.arith == "f64" and a.special <= 4) else 7
 
     # ---- NTT kernel loop (dominant kernel; roofline) ----
     ntt_buf = ct.view(-1, N)  # C*2*l limbs, 768 MiB

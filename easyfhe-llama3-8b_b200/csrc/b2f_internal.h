@@ -144,6 +144,7 @@ struct b2f_context {
   // prime is below 2^50: the same twiddles as doubles, and 1/q per prime
   bool fp64_ok = false, fp64 = false;
   double *d_twd_fwd = nullptr, *d_twd_inv = nullptr, *d_qinv = nullptr;
+  double *d_md_conv_f64 = nullptr;  // L x K: [Phat_k] mod q_i as doubles
   ulonglong2 *d_ninv = nullptr;       // L+K: N^-1
   ulonglong2 *d_i_factor = nullptr;   // L+K: psi^(N/2) (multiply by i)
   ulonglong2 *d_moddown_scale = nullptr;  // K: N^-1 * [Phat_k^-1] mod p_k
@@ -176,10 +177,14 @@ struct ItemKeys;
 //   ((acc_b[i][j] - NTT(conv)_b[i][j]) [P^-1]_{q_i} (* qinv_i)) + add_b[i][j]
 // acc [item][2][lk][N]; add_b (optional) of ciphertext keys.ct(it) at
 // add_stride; dst the slot permutation of X -> X^(g^-1), g = keys.g[at(it)].
+// With z (binary64 contexts, K <= 4) the transform computes its own input,
+// the conversion sum_k z_k [Phat_k]_{q_i} of the scaled P limbs l .. l+K-1 of
+// z [item][2][lk][N] (conv is then not read).
 int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk,
                 const uint64_t *acc, const uint64_t *add0, const uint64_t *add1,
                 long long add_stride, uint64_t *out, long long out_stride,
-                const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s);
+                const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s,
+                const uint64_t *z = nullptr);
 // jobs for num_polys polys of (q_limbs Q + p_limbs P) limbs, contiguous
 int ntt_polys(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
               int p_limbs, int inverse, cudaStream_t s);

@@ -214,6 +214,11 @@ static int build_tables(b2f_context *ctx) {
     if ((rc = upload(ctx, &ctx->d_moddown_bytes, mdb))) return rc;
   }
   if ((rc = upload(ctx, &ctx->d_moddown_pinv, md_pinv))) return rc;
+  if (ctx->fp64_ok && K >= 1 && K <= 4) {
+    std::vector<double> mdd((size_t)L * K);
+    for (size_t i = 0; i < mdd.size(); ++i) mdd[i] = (double)md_conv[i].x;
+    if ((rc = upload(ctx, &ctx->d_md_conv_f64, mdd))) return rc;
+  }
   if ((rc = upload(ctx, &ctx->d_pmod, pmod))) return rc;
 
   // per-level ModUp and rescale constants

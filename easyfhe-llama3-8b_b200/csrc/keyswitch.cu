@@ -703,6 +703,9 @@ int ip_moddown(b2f_context *ctx, const uint64_t *c1, long long c1_stride,
   rc = launch_ntt(ctx, acc, as, acc, as, d, 2 * K, cts, 1,
                       ctx->d_moddown_scale, s);
   if (rc) return rc;
+  if (ctx->fp64 && ctx->d_md_conv_f64)  // the conversion inside the transform
+    return ntt_moddown(ctx, conv, cts, l, lk, acc, add0, add1, add_stride, out,
+                       out_stride, nullptr, items, s, acc);
   if ((rc = launch_moddown_conv(ctx, acc, conv, l, cts, s))) return rc;
   return ntt_moddown(ctx, conv, cts, l, lk, acc, add0, add1, add_stride, out, out_stride,
                      nullptr, items, s);
@@ -1086,6 +1089,9 @@ int b2f_moddown_ext(b2f_context *ctx, const uint64_t *in, int num_cts, int l,
   if ((rc = launch_ntt(ctx, in, as, pcoef, as, d, 2 * K, num_cts, 1,
                        ctx->d_moddown_scale, s)))
     return rc;
+  if (ctx->fp64 && ctx->d_md_conv_f64)
+    return ntt_moddown(ctx, conv, num_cts, l, lk, in, nullptr, nullptr, 0, out,
+                       2LL * l * kN, nullptr, ItemKeys{{}, {1u}, {}, 1}, s, pcoef);
   if ((rc = launch_moddown_conv(ctx, pcoef, conv, l, num_cts, s))) return rc;
   return ntt_moddown(ctx, conv, num_cts, l, lk, in, nullptr, nullptr, 0, out, 2LL * l * kN,
                      nullptr, ItemKeys{{}, {1u}, {}, 1}, s);

@@ -153,6 +153,14 @@ struct ModDownOut {
   const uint64_t *primes;
   ItemKeys items;
   int lk, l_out;
+  // binary64 only, zK > 0: the transform's input is the ModDown conversion
+  // itself, sum_k z_k [Phat_k]_{q_i} with z the K scaled P limbs of item it,
+  // poly b (limbs l_out .. l_out + zK - 1 of z [item][2][lk][N]); zconv
+  // [i][zK] the constants as doubles.  Replaces the conversion kernel and its
+  // round trip through HBM when K is small.
+  const uint64_t *z;
+  const double *zconv;
+  int zK;
 };
 
 // Passes over a CTA's block (element l = base + stride k):
@@ -209,11 +217,37 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   V x[16];
   // stages 0-2 on columns c0, c0+1 (rows k at stride 8192), straight from HBM
   const int c0 = rank * 1024 + 2 * tid;
+  bool converted = false;
+  if constexpr (E::kModDown && A::kFoldScale) {
+    if (epi.zK > 0) {
+      // x = sum_k z_k c_{i,k}: K exact products (|.| <= q each, sum below
+      // 2^52 for K <= 4), reduced to |x| <= q/2 before the first stage
+      const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
+      const uint64_t *zb = epi.z + (((size_t)it * 2 + b) * epi.lk + epi.l_out) * kN + c0;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + c0 + k * BLK);
-    x[k] = A::from_word(v.x);
-    x[8 + k] = A::from_word(v.y);
+      for (int k = 0; k < 16; ++k) x[k] = 0.0;
+      for (int kk = 0; kk < epi.zK; ++kk) {
+        const double c = __ldg(epi.zconv + (size_t)i * epi.zK + kk);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const ulonglong2 v =
+              *reinterpret_cast<const ulonglong2 *>(zb + (size_t)kk * kN + k * BLK);
+          x[k] = __dadd_rn(x[k], ar.mul(A::from_word(v.x), c));
+          x[8 + k] = __dadd_rn(x[8 + k], ar.mul(A::from_word(v.y), c));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) x[k] = ar.red(x[k]);
+      converted = true;
+    }
+  }
+  if (!converted) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + c0 + k * BLK);
+      x[k] = A::from_word(v.x);
+      x[8 + k] = A::from_word(v.y);
+    }
   }
   {
     // stage by stage over both columns, one twiddle live at a time
@@ -558,7 +592,8 @@ int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
 int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk,
                 const uint64_t *acc, const uint64_t *add0, const uint64_t *add1,
                 long long add_stride, uint64_t *out, long long out_stride,
-                const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s) {
+                const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s,
+                const uint64_t *z) {
   std::vector<int> key = {0, q_limbs, 0};
   std::vector<LimbJob> jobs(q_limbs);
   for (int i = 0; i < q_limbs; ++i)
@@ -578,6 +613,13 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
   E.items = keys;
   E.lk = lk;
   E.l_out = q_limbs;
+  E.z = z;
+  E.zconv = ctx->d_md_conv_f64;
+  E.zK = (z != nullptr) ? ctx->K : 0;
+  if (E.zK > 0 && !(ctx->fp64 && ctx->K <= 4 && ctx->d_md_conv_f64)) {
+    set_error("ntt_moddown: the in-transform conversion needs binary64 and K <= 4");
+    return B2F_ERR_UNSUPPORTED;
+  }
   const long long st = (long long)q_limbs * kN;
   return launch_ntt_impl(ctx, conv, st, conv, st, d, q_limbs, 2 * items, 0, nullptr, E, s);
 }

@@ -166,6 +166,28 @@ def test_hoisted_rotations_bit_exact(arith):
     assert np.array_equal(got[1], plain)
 
 
+@pytest.mark.parametrize("L,K,dnum", [(9, 3, 3), (12, 4, 3), (12, 6, 4)])
+def test_rotate_special_prime_counts(L, K, dnum):
+    """HRotate with K = 3, 4 (the ModDown conversion computed inside its NTT,
+    binary64) and K = 6 (the tensor-core conversion) against the oracle."""
+
+    from easyfhe import core
+
+    ctx, orc = pair(L, K, dnum)
+    l = L - 1
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(K, 192))
+    g = core.galois_element(7)
+    key = ctx.keygen_rotation(s_ntt, g, seed=30 + K)
+    rng = np.random.default_rng(K)
+    cts = rand_residues(rng, ctx.primes[:l], 4).reshape(2, 2, l, N)
+    hkey = to_host(key)
+    for arith in ("f64", "int64"):
+        with use_arith(ctx, arith):
+            out = to_host(ctx.rotate(to_dev(cts), l, g, key))
+        for c in range(2):
+            assert np.array_equal(out[c], orc.rotate(cts[c], l, g, hkey)), (arith, c)
+
+
 def test_hoisted_rotations_identity_items_and_groups():
     """Identity items (galois 1, no key) anywhere in the list are copies, and
     more than 64 rotations run as several launch groups."""
