@@ -185,6 +185,12 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
                 long long add_stride, uint64_t *out, long long out_stride,
                 const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s,
                 const uint64_t *z = nullptr);
+// Rescale of num_polys polys [poly][l][N] (NTT form) to out [poly][l-1][N]:
+// last [poly][N] holds each poly's last limb in coefficient form; one forward
+// NTT launch lifts it to every q_i in its input stage and finishes
+// (c_i - NTT(lift)) q_{l-1}^-1 in its epilogue.
+int ntt_rescale(b2f_context *ctx, const uint64_t *last, const uint64_t *in, uint64_t *out,
+                int num_polys, int l, cudaStream_t s);
 // jobs for num_polys polys of (q_limbs Q + p_limbs P) limbs, contiguous
 int ntt_polys(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
               int p_limbs, int inverse, cudaStream_t s);

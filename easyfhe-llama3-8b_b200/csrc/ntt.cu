@@ -161,6 +161,15 @@ struct ModDownOut {
   const uint64_t *z;
   const double *zconv;
   int zK;
+  // rescale (lift != 0): the input is the centred lift of the last limb's
+  // coefficients zlast [item][N] (below q_last) modulo q_i, and the epilogue
+  // with pinv = [q_last^-1]_{q_i} and acc = the input ciphertext gives the
+  // rescaled limb: (c_i - NTT(lift)) q_last^-1
+  int lift;
+  const uint64_t *zlast;
+  const uint64_t *qlast_mod;  // [q_last]_{q_i}
+  uint64_t q_last;
+  const Mod *mods;
 };
 
 // Passes over a CTA's block (element l = base + stride k):
@@ -218,8 +227,38 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   // stages 0-2 on columns c0, c0+1 (rows k at stride 8192), straight from HBM
   const int c0 = rank * 1024 + 2 * tid;
   bool converted = false;
+  if constexpr (E::kModDown) {
+    if (epi.lift) {
+      const int i = (int)job.out_off;
+      const uint64_t *zb = epi.zlast + item * kN + c0;
+      const uint64_t half = (epi.q_last - 1) / 2;
+      if constexpr (A::kFoldScale) {  // binary64: signed lift, then |x| <= q_i/2
+        const double ql = A::from_word(epi.q_last);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(zb + k * BLK);
+          x[k] = ar.red(v.x > half ? __dadd_rn(A::from_word(v.x), -ql) : A::from_word(v.x));
+          x[8 + k] =
+              ar.red(v.y > half ? __dadd_rn(A::from_word(v.y), -ql) : A::from_word(v.y));
+        }
+      } else {  // integer: z mod q_i, minus q_last for the upper half
+        const Mod M = epi.mods[i];
+        const uint64_t qm = epi.qlast_mod[i];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(zb + k * BLK);
+          uint64_t r0 = reduce128(0, v.x, M), r1 = reduce128(0, v.y, M);
+          if (v.x > half) r0 = sub_mod(r0, qm, M.q);
+          if (v.y > half) r1 = sub_mod(r1, qm, M.q);
+          x[k] = A::from_word(r0);
+          x[8 + k] = A::from_word(r1);
+        }
+      }
+      converted = true;
+    }
+  }
   if constexpr (E::kModDown && A::kFoldScale) {
-    if (epi.zK > 0) {
+    if (!converted && epi.zK > 0) {
       // x = sum_k z_k c_{i,k}: K exact products (|.| <= q each, sum below
       // 2^52 for K <= 4), reduced to |x| <= q/2 before the first stage
       const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
@@ -616,12 +655,48 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
   E.z = z;
   E.zconv = ctx->d_md_conv_f64;
   E.zK = (z != nullptr) ? ctx->K : 0;
+  E.lift = 0;
+  E.zlast = nullptr;
+  E.qlast_mod = nullptr;
+  E.q_last = 0;
+  E.mods = ctx->d_mod;
   if (E.zK > 0 && !(ctx->fp64 && ctx->K <= 4 && ctx->d_md_conv_f64)) {
     set_error("ntt_moddown: the in-transform conversion needs binary64 and K <= 4");
     return B2F_ERR_UNSUPPORTED;
   }
   const long long st = (long long)q_limbs * kN;
   return launch_ntt_impl(ctx, conv, st, conv, st, d, q_limbs, 2 * items, 0, nullptr, E, s);
+}
+
+int ntt_rescale(b2f_context *ctx, const uint64_t *last, const uint64_t *in, uint64_t *out,
+                int num_polys, int l, cudaStream_t s) {
+  const int lo = l - 1;
+  std::vector<LimbJob> jobs(lo);
+  for (int i = 0; i < lo; ++i) jobs[i] = LimbJob{0u, (uint32_t)i, (uint16_t)i, (uint16_t)i};
+  const LimbJob *d = job_table(ctx, {9, l}, jobs);
+  if (!d) return B2F_ERR_NOMEM;
+  const LevelTables &T = ctx->levels[l];
+  ModDownOut E;
+  E.acc = in;
+  E.add0 = E.add1 = nullptr;
+  E.add_stride = 0;
+  E.out = out;
+  E.out_stride = 2LL * lo * kN;
+  E.pinv = T.rescale_inv;
+  E.qinv = nullptr;
+  E.primes = ctx->d_primes;
+  E.items = ItemKeys{{}, {1u}, {}, 1};
+  E.lk = l;
+  E.l_out = lo;
+  E.z = nullptr;
+  E.zconv = nullptr;
+  E.zK = 0;
+  E.lift = 1;
+  E.zlast = last;
+  E.qlast_mod = T.rescale_qlast;
+  E.q_last = ctx->primes[l - 1];
+  E.mods = ctx->d_mod;
+  return launch_ntt_impl(ctx, last, 0, out, 0, d, lo, num_polys, 0, nullptr, E, s);
 }
 
 int ntt_polys(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,

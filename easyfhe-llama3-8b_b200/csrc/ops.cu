@@ -299,8 +299,6 @@ int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
                   need);
   }
   uint64_t *last = static_cast<uint64_t *>(ws);
-  uint64_t *lifted = last + (size_t)num_polys * kN;
-  const LevelTables &T = ctx->levels[l];
   int rc;
   {
     std::vector<LimbJob> j = {
@@ -310,19 +308,8 @@ int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
                         nullptr, s)
            : B2F_ERR_NOMEM;
   }
-  if (!rc) {
-    rescale_lift_kernel<<<dim3(kN / TPB, l - 1, num_polys), TPB, 0, s>>>(
-        last, lifted, ctx->d_primes, T.rescale_qlast, l, ctx->primes[l - 1]);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) rc = cuda_status(e, "rescale_lift_kernel");
-  }
-  if (!rc) rc = ntt_polys(ctx, lifted, num_polys, l - 1, 0, 0, s);
-  if (!rc) {
-    rescale_combine_kernel<<<dim3(kN / TPB, l - 1, num_polys), TPB, 0, s>>>(
-        in, lifted, out, ctx->d_primes, T.rescale_inv, l);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) rc = cuda_status(e, "rescale_combine_kernel");
-  }
+  // lift, NTT and combine in one launch (ntt_rescale)
+  if (!rc) rc = ntt_rescale(ctx, last, in, out, num_polys, l, s);
   if (owned) cudaFreeAsync(owned, s);
   return rc;
 }

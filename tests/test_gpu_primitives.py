@@ -280,13 +280,15 @@ def test_relinearize_rescale_bit_exact(L, K, dnum, l, cts, arith):
     assert np.array_equal(got.reshape(two.shape), two)
 
 
-@pytest.mark.parametrize("l", [2, 9, 16])
-def test_rescale_bit_exact(l):
+@pytest.mark.parametrize("l,polys,arith", [(2, 2, "f64"), (9, 2, "f64"), (16, 3, "f64"),
+                                           (2, 2, "int64"), (16, 3, "int64")])
+def test_rescale_bit_exact(l, polys, arith):
     ctx, orc = pair(16, 2, 4)
     rng = np.random.default_rng(l)
-    x = rand_residues(rng, ctx.primes[:l], 2)
-    got = to_host(ctx.rescale(to_dev(x), 2, l))
-    assert np.array_equal(got, orc.rescale(x, 2, l))
+    x = rand_residues(rng, ctx.primes[:l], polys)
+    with use_arith(ctx, arith):
+        got = to_host(ctx.rescale(to_dev(x), polys, l))
+    assert np.array_equal(got, orc.rescale(x, polys, l))
 
 
 @pytest.mark.parametrize("negative", [False, True])
