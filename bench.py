@@ -560,7 +560,7 @@ def main() -> None:
     dev_in = [torch.empty_like(ct) for _ in range(2)]
     dev_out = [torch.empty_like(ct) for _ in range(2)]
     s_up, s_rot, s_down = (torch.cuda.Stream(device=dev) for _ in range(3))
-    e2e_steps = max(4, min(a.steps, 12))
+    e2e_steps = max(4, min(a.steps, 30))
 
     def e2e_run(steps: int) -> float:
         up_done = [torch.cuda.Event() for _ in range(steps)]
