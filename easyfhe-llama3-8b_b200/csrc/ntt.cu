@@ -1,33 +1,33 @@
 // Batched negacyclic NTT / inverse NTT for N = 2^16 on sm_100a.
 //
-// One thread-block cluster of 8 CTAs owns one limb (2^16 words = 512 KiB):
+// One thread-block cluster of 16 CTAs owns one limb (2^16 words = 512 KiB):
 // the limb is read from HBM once and written once, and everything in between
-// stays on chip.  Forward (Cooley-Tukey, natural order in, bit-reversed out):
-//   1. each CTA loads 1024 columns x 8 rows (row stride 8192) straight from
-//      HBM and runs stages 0-2 as radix-8 butterflies in registers;
-//   2. each column's 8 outputs are scattered to the 8 CTAs of the cluster
-//      through distributed shared memory, so CTA r then holds the contiguous
-//      block [8192 r, 8192 (r+1));
-//   3. stages 3-15 run in three register passes of 4 stages over shared
-//      memory (radix-16 per thread, 512 threads x 16 words, two CTAs per
-//      SM); the second and third passes of a warp touch only its own
-//      512-word segment, so they exchange data under __syncwarp; the last
-//      stage pairs neighbouring words across lanes tid, tid^1: of each two
-//      butterflies the even lane computes one and the odd lane the other,
-//      with one shuffle in and one out, so no product is computed twice;
-//   4. each warp stages its segment through shared memory and writes it
-//      with 16-byte coalesced stores.
+// stays on chip.  Seen as a 16 x 4096 matrix (element g = 4096 r + c), the
+// forward transform (Cooley-Tukey, natural order in, bit-reversed out):
+//   1. each thread takes one column c (the 16 rows at stride 4096, straight
+//      from HBM) and runs stages 0-3 on it as a radix-16 step in registers;
+//   2. row r of every column goes to CTA r through distributed shared memory,
+//      so CTA r then holds the contiguous block [4096 r, 4096 (r+1));
+//   3. stages 4-15 run in three radix-16 register passes over the block:
+//      stride 256 (CTA-wide), stride 16 (each half-warp owns a 256-word
+//      segment, so only warp synchronisation is needed) and stride 1 (a
+//      thread's 16 consecutive words, entirely in registers);
+//   4. each thread writes its 16 consecutive outputs with 16-byte stores.
+// 256 threads x 16 words per CTA and 64 registers give four CTAs per SM.
 // The inverse (Gentleman-Sande, bit-reversed in, natural out) runs the same
 // steps backwards and folds N^-1 (times an optional per-limb constant) into
 // the final stage.  The butterfly arithmetic is a policy (ntt_arith.cuh):
 // 64-bit integer Shoup products with Harvey's lazy reduction, or, when every
 // prime is below 2^50, exact binary64 products on signed residues, which this
 // GPU issues at a higher rate.  Outputs are fully reduced either way.
-// Shared memory holds the block with two pad words per 32 so that every
-// pass is free of bank conflicts.  Stages outside the register passes apply
-// one twiddle to both columns before loading the next and the cluster
-// exchange uses 32-bit shared::cluster addresses, which keeps the
-// 64-register budget of two CTAs per SM nearly free of spills.
+// Shared memory holds the block padded by one word per 16 (pad(e) = e + e/16),
+// which keeps all three pass patterns and both cluster exchanges free of bank
+// conflicts; the passes address it and the twiddle tables as per-pass bases
+// plus immediate offsets.  Cluster barriers are split-phase, their latency
+// hidden behind loads and butterflies.
+// The forward transform that finishes a ModDown (or a rescale) in its
+// epilogue keeps 8-CTA clusters of 512 threads: with its extra input and
+// epilogue traffic that shape measured faster (namespace md below).
 #include <cooperative_groups.h>
 
 #include <atomic>
@@ -41,15 +41,13 @@ namespace cg = cooperative_groups;
 namespace b2f {
 namespace {
 
-constexpr int CL = 8;                       // CTAs per cluster = per limb
-constexpr int BLK = kN / CL;                // 8192 words per CTA
-constexpr int NT = 512;                     // threads per CTA, 16 words each
-constexpr int SEG = 512;                    // words owned by one warp in B/C
-constexpr int SMEM_WORDS = BLK + 2 * (BLK / 32);
-constexpr int SMEM_BYTES = SMEM_WORDS * 8;  // 69632
+constexpr int CL = 16;                      // CTAs per cluster = per limb
+constexpr int BLK = kN / CL;                // 4096 words per CTA
+constexpr int NT = 256;                     // threads per CTA, 16 words each
+constexpr int SMEM_BYTES = (BLK + BLK / 16) * 8;  // 34816
 
-// two pad words per 32 keep every pass free of shared-memory bank conflicts
-__device__ __forceinline__ int pad(int l) { return l + ((l >> 5) << 1); }
+// one pad word per 16 keeps every access pattern free of bank conflicts
+__device__ __forceinline__ int pad(int e) { return e + (e >> 4); }
 
 struct NttParams {
   const uint64_t *in;
@@ -70,7 +68,7 @@ struct NttParams {
 // Four CT stages s0..s0+3 on 16 registers with element index
 // j(k) = base + k * stride; at local stage t the pairs are (k, k + d),
 // d = 8 >> t, and each block of 2d registers shares one twiddle.  For the
-// three passes' (base, stride) the stage-s index splits without carry:
+// four steps' (base, stride) the stage-s index splits without carry:
 // (base + blk stride) >> (16 - s) = (base >> (16 - s)) + (blk stride >> (16 - s)),
 // so each twiddle is a per-stage base plus a constant offset.
 template <class A>
@@ -90,12 +88,13 @@ __device__ __forceinline__ void ct_pass(const A &ar, typename A::V (&x)[16],
   }
 }
 
-template <class A>
+// GS stages s0+3 down to s0+TMIN (the inverse order)
+template <class A, int TMIN>
 __device__ __forceinline__ void gs_pass(const A &ar, typename A::V (&x)[16],
                                         const typename A::W *tw, int s0, int base,
                                         int stride) {
 #pragma unroll
-  for (int t = 3; t >= 0; --t) {
+  for (int t = 3; t >= TMIN; --t) {
     const int d = 8 >> t, sh = kLogN - (s0 + t);
     const typename A::W *tws = tw + (1 << (s0 + t)) + (base >> sh);
 #pragma unroll
@@ -107,42 +106,173 @@ __device__ __forceinline__ void gs_pass(const A &ar, typename A::V (&x)[16],
   }
 }
 
-// pad(l + STRIDE k) = pad(l) + pad_step<STRIDE>() k for k < 16: exact when
-// STRIDE is a multiple of 32 (each step adds STRIDE / 32 blocks), or when
-// l's offset in its 32-word block plus 15 STRIDE stays inside the block (pass
-// C: STRIDE 2, l mod 32 <= 1).  The accesses then use immediate offsets.
-template <int STRIDE>
-__device__ constexpr int pad_step() {
-  return STRIDE % 32 == 0 ? STRIDE + STRIDE / 16 : STRIDE;
-}
-template <int STRIDE, class V>
-__device__ __forceinline__ void load16(V (&x)[16], const V *buf, int l) {
-  const V *p = buf + pad(l);
+// Register passes over a CTA's block (element e of the block, 16 per thread):
+//   A: e = tid + 256 k                    (pad: +272 k)
+//   B: e = 256 (tid/16) + tid%16 + 16 k   (pad: +17 k; a half-warp's segment)
+//   C: e = 16 tid + k                     (pad: +k; the same segment)
+
+template <class A>
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 4)
+    ntt_fwd_kernel(NttParams P) {
+  using V = typename A::V;
+  using W = typename A::W;
+  extern __shared__ __align__(16) uint64_t buf[];
+  V *vb = reinterpret_cast<V *>(buf);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int tid = threadIdx.x;
+  // job-major order: consecutive clusters transform the same limb job (one
+  // prime) of consecutive items, so clusters running together share one
+  // twiddle table in L2
+  const long long job_id = blockIdx.x / CL;
+  const long long item = job_id % P.items;
+  const LimbJob job = P.jobs[job_id / P.items];
+  const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
+  uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
+  const A ar(P.primes, P.qinv, job.prime);
+  const W *tw = static_cast<const W *>(P.tw) + (size_t)job.prime * kN;
+  const int jb = rank * BLK;
+  // split-phase cluster barrier: arriving now and waiting just before the
+  // first remote shared-memory write certifies that every CTA of the cluster
+  // is resident, with the barrier's latency hidden behind the loads and
+  // stages 0-3 (nothing needs publishing yet, so the arrive is relaxed)
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+  // stages 0-3 on column col (rows r at stride 4096), straight from HBM
+  const int col = rank * 256 + tid;
+  V x[16];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) x[k] = p[pad_step<STRIDE>() * k];
-}
-template <int STRIDE, class V>
-__device__ __forceinline__ void store16(const V (&x)[16], V *buf, int l) {
-  V *p = buf + pad(l);
+  for (int r = 0; r < 16; ++r) x[r] = A::from_word(a[r * BLK + col]);
+  ct_pass(ar, x, tw, 0, col, BLK);
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+  // row r of this column goes to CTA r, position col of its block
 #pragma unroll
-  for (int k = 0; k < 16; ++k) p[pad_step<STRIDE>() * k] = x[k];
+  for (int r = 0; r < 16; ++r) cluster.map_shared_rank(vb, r)[pad(col)] = x[r];
+  cluster.sync();
+  {
+    V *p = vb + pad(tid);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = p[272 * k];
+    ct_pass(ar, x, tw, 4, jb + tid, 256);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) p[272 * k] = x[k];
+  }
+  __syncthreads();
+  {
+    const int e0 = 256 * (tid >> 4) + (tid & 15);
+    V *p = vb + pad(e0);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = p[17 * k];
+    ct_pass(ar, x, tw, 8, jb + e0, 16);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) p[17 * k] = x[k];
+  }
+  __syncwarp();
+  {
+    const V *p = vb + pad(16 * tid);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = p[k];
+  }
+  ct_pass(ar, x, tw, 12, jb + 16 * tid, 1);
+  // x[k] is element 16 tid + k of the block: 16-byte stores
+  o += jb + 16 * tid;
+#pragma unroll
+  for (int m = 0; m < 8; ++m)
+    *reinterpret_cast<ulonglong2 *>(o + 2 * m) =
+        make_ulonglong2(A::to_word(ar.full(x[2 * m])), A::to_word(ar.full(x[2 * m + 1])));
 }
 
-// Where the forward transform's outputs go.  PlainOut: the output limb, as
-// transformed.  ModDownOut: the transform is the last step of a ModDown (the
-// NTT of the P part converted to Q) and its epilogue finishes it: for item it
-// (poly p = 2 it + b, limb i) and every evaluation j of the limb,
+template <class A>
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 4)
+    ntt_inv_kernel(NttParams P) {
+  using V = typename A::V;
+  using W = typename A::W;
+  extern __shared__ __align__(16) uint64_t buf[];
+  V *vb = reinterpret_cast<V *>(buf);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int tid = threadIdx.x;
+  // job-major order, as the forward
+  const long long job_id = blockIdx.x / CL;
+  const long long item = job_id % P.items;
+  const LimbJob job = P.jobs[job_id / P.items];
+  const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
+  uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
+  const A ar(P.primes, P.qinv, job.prime);
+  const W *tw = static_cast<const W *>(P.tw) + (size_t)job.prime * kN;
+  const int jb = rank * BLK;
+  V x[16];
+  // stages 15-12 on the thread's 16 consecutive words, straight from HBM
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + jb + 16 * tid + 2 * m);
+    x[2 * m] = A::from_word(v.x);
+    x[2 * m + 1] = A::from_word(v.y);
+  }
+  gs_pass<A, 0>(ar, x, tw, 12, jb + 16 * tid, 1);
+  {
+    V *p = vb + pad(16 * tid);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) p[k] = x[k];
+  }
+  __syncwarp();
+  {
+    const int e0 = 256 * (tid >> 4) + (tid & 15);
+    V *p = vb + pad(e0);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = p[17 * k];
+    gs_pass<A, 0>(ar, x, tw, 8, jb + e0, 16);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) p[17 * k] = x[k];
+  }
+  __syncthreads();
+  {
+    const V *p = vb + pad(tid);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = p[272 * k];
+  }
+  // split-phase: this thread's reads of its block are done (release); the
+  // wait after stages 7-4 means every CTA has finished reading its block
+  asm volatile("barrier.cluster.arrive.aligned;\n" ::: "memory");
+  gs_pass<A, 0>(ar, x, tw, 4, jb + tid, 256);
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+  // element tid + 256 k of row `rank` is column tid + 256 k: CTA k keeps it
+  // at [row rank][column tid]
+#pragma unroll
+  for (int k = 0; k < 16; ++k) cluster.map_shared_rank(vb, k)[pad(rank * 256 + tid)] = x[k];
+  cluster.sync();
+  const int col = rank * 256 + tid;
+#pragma unroll
+  for (int r = 0; r < 16; ++r) x[r] = vb[pad(r * 256 + tid)];
+  gs_pass<A, 1>(ar, x, tw, 0, col, BLK);  // stages 3-1
+  {
+    const W w = A::ldtw(tw, 1);
+    const W sc = A::scale(P.scales[job.scale_idx]);
+    if constexpr (A::kFoldScale) {
+      // stage 0 with the output scale folded in: ((x + y) s, (x - y) w s)
+      const W wsc = ar.fold(w, sc);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ar.gs_scaled(x[k], x[k + 8], sc, wsc);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gs_bfly(ar, x[k], x[k + 8], w);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) x[k] = ar.scale_out(x[k], sc);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 16; ++r) o[r * BLK + col] = A::to_word(x[r]);
+}
+
+// The forward transform as the last step of a ModDown (the NTT of the P part
+// converted to Q), its epilogue finishing the ModDown: for item it (poly
+// p = 2 it + b, limb i) and every evaluation j of the limb,
 //   out_b[i][dst(j)] = (acc_b[i][j] - v[j]) * [P^-1]_{q_i} (* qinv_i) + add_b[i][j]
 // with dst = the slot permutation of X -> X^(g^-1) (the inverse of the
 // gather out[k] = w[src_g(k)]).  Each warp walks its own 512 evaluations in
 // order (coalesced reads of acc and add) and its 32 stores land in one
 // aligned 32-word block, since an automorphism maps aligned blocks of 32
 // evaluations onto aligned blocks.  The converted limbs never reach HBM.
-struct PlainOut {
-  static constexpr bool kModDown = false;
-};
 struct ModDownOut {
-  static constexpr bool kModDown = true;
   const uint64_t *acc;          // [item][2][lk][N]
   const uint64_t *add0, *add1;  // [ct][..][N] at add_stride, or null
   long long add_stride;
@@ -172,6 +302,44 @@ struct ModDownOut {
   const Mod *mods;
 };
 
+// The forward transform that finishes a ModDown runs on clusters of 8 CTAs
+// of 512 threads (8192 words per CTA, two CTAs per SM), which measured
+// faster than 16-CTA clusters for this kernel's larger input and epilogue
+// traffic.  Stages 0-2 run on two columns of 8 rows per thread before the
+// cluster exchange, stages 3-15 in three register passes, the last stage
+// across lane pairs tid, tid^1.
+namespace md {
+
+constexpr int CL = 8;                       // CTAs per cluster = per limb
+constexpr int BLK = kN / CL;                // 8192 words per CTA
+constexpr int NT = 512;                     // threads per CTA, 16 words each
+constexpr int SEG = 512;                    // words owned by one warp in B/C
+constexpr int SMEM_BYTES = (BLK + 2 * (BLK / 32)) * 8;  // 69632
+
+// two pad words per 32 keep every pass free of shared-memory bank conflicts
+__device__ __forceinline__ int pad(int l) { return l + ((l >> 5) << 1); }
+
+// pad(l + STRIDE k) = pad(l) + pad_step<STRIDE>() k for k < 16: exact when
+// STRIDE is a multiple of 32 (each step adds STRIDE / 32 blocks), or when
+// l's offset in its 32-word block plus 15 STRIDE stays inside the block (pass
+// C: STRIDE 2, l mod 32 <= 1).  The accesses then use immediate offsets.
+template <int STRIDE>
+__device__ constexpr int pad_step() {
+  return STRIDE % 32 == 0 ? STRIDE + STRIDE / 16 : STRIDE;
+}
+template <int STRIDE, class V>
+__device__ __forceinline__ void load16(V (&x)[16], const V *buf, int l) {
+  const V *p = buf + pad(l);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = p[pad_step<STRIDE>() * k];
+}
+template <int STRIDE, class V>
+__device__ __forceinline__ void store16(const V (&x)[16], V *buf, int l) {
+  V *p = buf + pad(l);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) p[pad_step<STRIDE>() * k] = x[k];
+}
+
 // Passes over a CTA's block (element l = base + stride k):
 //   A: stages 3-6,   base tid,                        stride 512 (CTA-wide)
 //   B: stages 7-10,  base (tid/32)*512 + tid%32,      stride 32
@@ -180,9 +348,9 @@ struct ModDownOut {
 // Warp w touches only words [512 w, 512 w + 512) in B and C, so the B <-> C
 // exchange and the output staging need only warp synchronisation.
 
-template <class A, class E>
+template <class A>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
-    ntt_fwd_kernel(NttParams P, E epi) {
+    ntt_moddown_kernel(NttParams P, ModDownOut epi) {
   using V = typename A::V;
   using W = typename A::W;
   extern __shared__ __align__(16) uint64_t buf[];
@@ -197,11 +365,10 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   const long long item = job_id % P.items;
   const LimbJob job = P.jobs[job_id / P.items];
   const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
-  uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
   const A ar(P.primes, P.qinv, job.prime);
   const W *tw = static_cast<const W *>(P.tw) + (size_t)job.prime * kN;
 
-  if constexpr (E::kModDown) {
+  {
     // the epilogue's inputs for this CTA's block: into L2 while the
     // transform runs (bulk prefetch, 64 KiB per array)
     if (tid == 0) {
@@ -227,7 +394,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   // stages 0-2 on columns c0, c0+1 (rows k at stride 8192), straight from HBM
   const int c0 = rank * 1024 + 2 * tid;
   bool converted = false;
-  if constexpr (E::kModDown) {
+  {
     if (epi.lift) {
       const int i = (int)job.out_off;
       const uint64_t *zb = epi.zlast + item * kN + c0;
@@ -257,7 +424,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
       converted = true;
     }
   }
-  if constexpr (E::kModDown && A::kFoldScale) {
+  if constexpr (A::kFoldScale) {
     if (!converted && epi.zK > 0) {
       // x = sum_k z_k c_{i,k}: K exact products (|.| <= q each, sum below
       // 2^52 for K <= 4), reduced to |x| <= q/2 before the first stage
@@ -365,222 +532,87 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     x[k] = odd ? back : ra;       // even: X'_k;  odd: Y'_k (from even)
     x[k + 1] = odd ? rb : back;   // even: X'_{k+1} (from odd);  odd: Y'_{k+1}
   }
-  // each lane rewrites the words it read in pass C, then the warp writes its
-  // 512-word segment with coalesced 16-byte stores
+  // each lane rewrites the words it read in pass C, then the warp finishes
+  // its 512-word segment in lane-interleaved pairs
   {
     uint64_t *p = buf + pad(lc);
 #pragma unroll
     for (int k = 0; k < 16; ++k) p[pad_step<2>() * k] = A::to_word(x[k]);
   }
   __syncwarp();
-  if constexpr (E::kModDown) {
-    const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
-    const uint32_t ginv = galois_inverse(epi.items.g[epi.items.at(it)]);
-    const uint64_t q = epi.primes[i];
-    const ulonglong2 pi = epi.pinv[i];
-    const ulonglong2 qi = epi.qinv ? epi.qinv[i] : make_ulonglong2(0, 0);
-    const uint64_t *accl = epi.acc + (((size_t)it * 2 + b) * epi.lk + i) * kN;
-    const uint64_t *addl = b ? epi.add1 : epi.add0;
-    if (addl) addl += epi.items.ct(it) * epi.add_stride + (size_t)i * kN;
-    uint64_t *outl =
-        epi.out + epi.items.out(it, epi.out_stride) + ((size_t)b * epi.l_out + i) * kN;
-    // pairs of evaluations per lane, four pairs' loads issued together
+  const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
+  const uint32_t ginv = galois_inverse(epi.items.g[epi.items.at(it)]);
+  const uint64_t q = epi.primes[i];
+  const ulonglong2 pi = epi.pinv[i];
+  const ulonglong2 qi = epi.qinv ? epi.qinv[i] : make_ulonglong2(0, 0);
+  const uint64_t *accl = epi.acc + (((size_t)it * 2 + b) * epi.lk + i) * kN;
+  const uint64_t *addl = b ? epi.add1 : epi.add0;
+  if (addl) addl += epi.items.ct(it) * epi.add_stride + (size_t)i * kN;
+  uint64_t *outl =
+      epi.out + epi.items.out(it, epi.out_stride) + ((size_t)b * epi.l_out + i) * kN;
+  // pairs of evaluations per lane, four pairs' loads issued together
 #pragma unroll
-    for (int r0 = 0; r0 < SEG / 64; r0 += 4) {
-      ulonglong2 av[4], dv[4];
+  for (int r0 = 0; r0 < SEG / 64; r0 += 4) {
+    ulonglong2 av[4], dv[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = jb + warp * SEG + 2 * (lane + 32 * (r0 + u));
-        av[u] = *reinterpret_cast<const ulonglong2 *>(accl + j);
-        dv[u] = addl ? *reinterpret_cast<const ulonglong2 *>(addl + j) : make_ulonglong2(0, 0);
+    for (int u = 0; u < 4; ++u) {
+      const int j = jb + warp * SEG + 2 * (lane + 32 * (r0 + u));
+      av[u] = *reinterpret_cast<const ulonglong2 *>(accl + j);
+      dv[u] = addl ? *reinterpret_cast<const ulonglong2 *>(addl + j) : make_ulonglong2(0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int kk = warp * SEG + 2 * (lane + 32 * (r0 + u));
+      const uint32_t j = (uint32_t)(jb + kk);
+      const uint64_t *bk = buf + pad(kk);  // kk even: kk + 1 is in the same block
+      uint64_t w0 = shoup(sub_mod(av[u].x, bk[0], q), pi.x, pi.y, q);
+      uint64_t w1 = shoup(sub_mod(av[u].y, bk[1], q), pi.x, pi.y, q);
+      if (epi.qinv) {
+        w0 = shoup(w0, qi.x, qi.y, q);
+        w1 = shoup(w1, qi.x, qi.y, q);
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int kk = warp * SEG + 2 * (lane + 32 * (r0 + u));
-        const uint32_t j = (uint32_t)(jb + kk);
-        const uint64_t *bk = buf + pad(kk);  // kk even: kk + 1 is in the same block
-        uint64_t w0 = shoup(sub_mod(av[u].x, bk[0], q), pi.x, pi.y, q);
-        uint64_t w1 = shoup(sub_mod(av[u].y, bk[1], q), pi.x, pi.y, q);
-        if (epi.qinv) {
-          w0 = shoup(w0, qi.x, qi.y, q);
-          w1 = shoup(w1, qi.x, qi.y, q);
-        }
-        if (addl) {
-          w0 = add_mod(w0, dv[u].x, q);
-          w1 = add_mod(w1, dv[u].y, q);
-        }
-        if (ginv == 1) {
-          *reinterpret_cast<ulonglong2 *>(outl + j) = make_ulonglong2(w0, w1);
-        } else {
-          outl[auto_src(j, ginv)] = w0;
-          outl[auto_src(j + 1, ginv)] = w1;
-        }
+      if (addl) {
+        w0 = add_mod(w0, dv[u].x, q);
+        w1 = add_mod(w1, dv[u].y, q);
+      }
+      if (ginv == 1) {
+        *reinterpret_cast<ulonglong2 *>(outl + j) = make_ulonglong2(w0, w1);
+      } else {
+        outl[auto_src(j, ginv)] = w0;
+        outl[auto_src(j + 1, ginv)] = w1;
       }
     }
-  } else {
-    const int idx0 = warp * SEG + 2 * lane;
-    const uint64_t *p = buf + pad(idx0);  // idx0 + 64 r: pad adds 68 r
-#pragma unroll
-    for (int r = 0; r < SEG / 64; ++r)
-      *reinterpret_cast<ulonglong2 *>(o + jb + idx0 + 64 * r) =
-          *reinterpret_cast<const ulonglong2 *>(p + 68 * r);
   }
 }
 
-template <class A>
-__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
-    ntt_inv_kernel(NttParams P) {
-  using V = typename A::V;
-  using W = typename A::W;
-  extern __shared__ __align__(16) uint64_t buf[];
-  V *vb = reinterpret_cast<V *>(buf);
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = (int)cluster.block_rank();
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // job-major order: consecutive clusters transform the same limb job (one
-  // prime) of consecutive items, so clusters running together share one
-  // twiddle table in L2
-  const long long job_id = blockIdx.x / CL;
-  const long long item = job_id % P.items;
-  const LimbJob job = P.jobs[job_id / P.items];
-  const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
-  uint64_t *o = P.out + item * P.out_stride + (long long)job.out_off * kN;
-  const A ar(P.primes, P.qinv, job.prime);
-  const W *tw = static_cast<const W *>(P.tw) + (size_t)job.prime * kN;
-  const int jb = rank * BLK;
+}  // namespace md
 
-  // each warp stages its own 512-word segment
-  {
-    const int idx0 = warp * SEG + 2 * lane;
-    uint64_t *p = buf + pad(idx0);  // idx0 + 64 r: pad adds 68 r
-#pragma unroll
-    for (int r = 0; r < SEG / 64; ++r)
-      *reinterpret_cast<ulonglong2 *>(p + 68 * r) =
-          *reinterpret_cast<const ulonglong2 *>(a + jb + idx0 + 64 * r);
-  }
-  __syncwarp();
-
-  V x[16];
-  const int lc = (tid >> 1) * 32 + (tid & 1);
-  {
-    const uint64_t *p = buf + pad(lc);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) x[k] = A::from_word(p[pad_step<2>() * k]);
-  }
-  const bool odd = tid & 1;
-  const int je = jb + (tid >> 1) * 32;
-  const W *tw15 = tw + (1 << 15) + (je >> 1);  // stage 15: element je + 2k
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const V mine = x[k];
-    const V other = __shfl_xor_sync(0xffffffffu, mine, 1);
-    const V X = odd ? other : mine, Y = odd ? mine : other;
-    if (odd) {
-      const W w = A::ldtw(tw15, k);
-      x[k] = ar.gs_diff(X, Y, w);
-    } else {
-      x[k] = ar.gs_sum(X, Y);
-    }
-  }
-  gs_pass(ar, x, tw, 11, jb + lc, 2);
-  store16<2>(x, vb, lc);
-  __syncwarp();
-  const int lb = warp * SEG + lane;
-  load16<32>(x, vb, lb);
-  gs_pass(ar, x, tw, 7, jb + lb, 32);
-  store16<32>(x, vb, lb);
-  __syncthreads();
-  load16<512>(x, vb, tid);
-  // split-phase: this thread's reads of its block are done (release); the
-  // wait after stages 6-3 means every CTA has finished reading its block
-  asm volatile("barrier.cluster.arrive.aligned;\n" ::: "memory");
-  gs_pass(ar, x, tw, 3, jb + tid, 512);
-  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
-  // word l of block `rank` is row `rank` of column l, owned by CTA l/1024
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int l = tid + 512 * k;
-    cluster.map_shared_rank(vb, l >> 10)[rank * 1024 + (l & 1023)] = x[k];
-  }
-  cluster.sync();
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(buf + k * 1024 + 2 * tid);
-    x[k] = A::from_bits(v.x);
-    x[8 + k] = A::from_bits(v.y);
-  }
-  const int c0 = rank * 1024 + 2 * tid;
-  // stage by stage over both columns, one twiddle live at a time
-#pragma unroll
-  for (int k = 0; k < 8; k += 2) {
-    const W w = A::ldtw(tw, 4 + k / 2);
-#pragma unroll
-    for (int h = 0; h < 16; h += 8) gs_bfly(ar, x[h + k], x[h + k + 1], w);
-  }
-#pragma unroll
-  for (int m = 0; m < 2; ++m) {
-    const W w = A::ldtw(tw, 2 + m);
-#pragma unroll
-    for (int h = 0; h < 16; h += 8) {
-      gs_bfly(ar, x[h + 4 * m], x[h + 4 * m + 2], w);
-      gs_bfly(ar, x[h + 4 * m + 1], x[h + 4 * m + 3], w);
-    }
-  }
-  {
-    const W w = A::ldtw(tw, 1);
-    const W sc = A::scale(P.scales[job.scale_idx]);
-    if constexpr (A::kFoldScale) {
-      // stage 0 with the output scale folded in: ((x + y) s, (x - y) w s)
-      const W wsc = ar.fold(w, sc);
-#pragma unroll
-      for (int h = 0; h < 16; h += 8)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) ar.gs_scaled(x[h + k], x[h + k + 4], sc, wsc);
-    } else {
-#pragma unroll
-      for (int h = 0; h < 16; h += 8)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) gs_bfly(ar, x[h + k], x[h + k + 4], w);
-#pragma unroll
-      for (int k = 0; k < 16; ++k) x[k] = ar.scale_out(x[k], sc);
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < 8; ++k)
-    *reinterpret_cast<ulonglong2 *>(o + c0 + k * BLK) =
-        make_ulonglong2(A::to_word(x[k]), A::to_word(x[8 + k]));
-}
-
-
-template <class E>
+// epi: null for a plain transform, else the ModDown the forward transform
+// finishes
 int launch_ntt_impl(b2f_context *ctx, const uint64_t *in, long long in_stride,
                     uint64_t *out, long long out_stride, const LimbJob *jobs,
                     int jobs_per_item, int items, int inverse,
-                    const ulonglong2 *scales, const E &epi, cudaStream_t s) {
+                    const ulonglong2 *scales, const ModDownOut *epi, cudaStream_t s) {
   if (items <= 0 || jobs_per_item <= 0) return B2F_OK;
   // one bit per device: the attribute calls are idempotent, so threads that
   // race on a device's first launch only repeat them
   static std::atomic<uint64_t> configured{0};
   const uint64_t bit = 1ull << (ctx->device & 63);
   if (!(configured.load(std::memory_order_acquire) & bit)) {
-    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<IntArith, PlainOut>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  SMEM_BYTES));
-    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<IntArith, ModDownOut>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  SMEM_BYTES));
+    // 16-CTA clusters are beyond the portable size of 8: opt in per kernel
+    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<IntArith>,
+                                  cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     B2F_CUDA(cudaFuncSetAttribute(ntt_inv_kernel<IntArith>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  SMEM_BYTES));
-    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<FpArith, PlainOut>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  SMEM_BYTES));
-    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<FpArith, ModDownOut>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  SMEM_BYTES));
+                                  cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    B2F_CUDA(cudaFuncSetAttribute(ntt_fwd_kernel<FpArith>,
+                                  cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     B2F_CUDA(cudaFuncSetAttribute(ntt_inv_kernel<FpArith>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  SMEM_BYTES));
+                                  cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    // the 8-CTA kernel's 68 KiB of shared memory are above the default 48
+    B2F_CUDA(cudaFuncSetAttribute(md::ntt_moddown_kernel<IntArith>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, md::SMEM_BYTES));
+    B2F_CUDA(cudaFuncSetAttribute(md::ntt_moddown_kernel<FpArith>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, md::SMEM_BYTES));
     configured.fetch_or(bit, std::memory_order_release);
   }
   const bool fp = ctx->fp64;
@@ -597,9 +629,10 @@ int launch_ntt_impl(b2f_context *ctx, const uint64_t *in, long long in_stride,
   P.scales = scales ? scales : ctx->d_ninv;
   P.jobs_per_item = jobs_per_item;
   P.items = items;
-  const long long blocks = (long long)items * jobs_per_item * CL;
+  const int cl = epi ? md::CL : CL;
+  const long long blocks = (long long)items * jobs_per_item * cl;
   if (blocks > 0x7fffffffLL) {
-    set_error("launch_ntt: batch too large (%lld limbs)", blocks / CL);
+    set_error("launch_ntt: batch too large (%lld limbs)", blocks / cl);
     return B2F_ERR_ARG;
   }
   const unsigned g = (unsigned)blocks;
@@ -608,11 +641,16 @@ int launch_ntt_impl(b2f_context *ctx, const uint64_t *in, long long in_stride,
       ntt_inv_kernel<FpArith><<<g, NT, SMEM_BYTES, s>>>(P);
     else
       ntt_inv_kernel<IntArith><<<g, NT, SMEM_BYTES, s>>>(P);
+  } else if (epi) {
+    if (fp)
+      md::ntt_moddown_kernel<FpArith><<<g, md::NT, md::SMEM_BYTES, s>>>(P, *epi);
+    else
+      md::ntt_moddown_kernel<IntArith><<<g, md::NT, md::SMEM_BYTES, s>>>(P, *epi);
   } else {
     if (fp)
-      ntt_fwd_kernel<FpArith, E><<<g, NT, SMEM_BYTES, s>>>(P, epi);
+      ntt_fwd_kernel<FpArith><<<g, NT, SMEM_BYTES, s>>>(P);
     else
-      ntt_fwd_kernel<IntArith, E><<<g, NT, SMEM_BYTES, s>>>(P, epi);
+      ntt_fwd_kernel<IntArith><<<g, NT, SMEM_BYTES, s>>>(P);
   }
   B2F_LAUNCHED("ntt kernel launch");
   return B2F_OK;
@@ -625,7 +663,7 @@ int launch_ntt(b2f_context *ctx, const uint64_t *in, long long in_stride,
                int jobs_per_item, int items, int inverse,
                const ulonglong2 *scales, cudaStream_t s) {
   return launch_ntt_impl(ctx, in, in_stride, out, out_stride, jobs, jobs_per_item,
-                         items, inverse, scales, PlainOut{}, s);
+                         items, inverse, scales, nullptr, s);
 }
 
 int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk,
@@ -665,7 +703,7 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
     return B2F_ERR_UNSUPPORTED;
   }
   const long long st = (long long)q_limbs * kN;
-  return launch_ntt_impl(ctx, conv, st, conv, st, d, q_limbs, 2 * items, 0, nullptr, E, s);
+  return launch_ntt_impl(ctx, conv, st, conv, st, d, q_limbs, 2 * items, 0, nullptr, &E, s);
 }
 
 int ntt_rescale(b2f_context *ctx, const uint64_t *last, const uint64_t *in, uint64_t *out,
@@ -696,7 +734,7 @@ int ntt_rescale(b2f_context *ctx, const uint64_t *last, const uint64_t *in, uint
   E.qlast_mod = T.rescale_qlast;
   E.q_last = ctx->primes[l - 1];
   E.mods = ctx->d_mod;
-  return launch_ntt_impl(ctx, last, 0, out, 0, d, lo, num_polys, 0, nullptr, E, s);
+  return launch_ntt_impl(ctx, last, 0, out, 0, d, lo, num_polys, 0, nullptr, &E, s);
 }
 
 int ntt_polys(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
