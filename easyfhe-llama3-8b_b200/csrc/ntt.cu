@@ -358,12 +358,15 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // job-major order: consecutive clusters transform the same limb job (one
-  // prime) of consecutive items, so clusters running together share one
-  // twiddle table in L2
+  // when every limb of an item reads the same input (the K scaled P words of
+  // the in-transform conversion, or the last limb of a rescale), item-major
+  // order: the clusters of one item run together and that input stays in L2
+  // (job-major, it is evicted between an item's limbs); otherwise job-major,
+  // so clusters running together share one twiddle table
   const long long job_id = blockIdx.x / CL;
-  const long long item = job_id % P.items;
-  const LimbJob job = P.jobs[job_id / P.items];
+  const bool item_major = epi.zK > 0 || epi.lift;
+  const long long item = item_major ? job_id / P.jobs_per_item : job_id % P.items;
+  const LimbJob job = P.jobs[item_major ? job_id % P.jobs_per_item : job_id / P.items];
   const uint64_t *a = P.in + item * P.in_stride + (long long)job.in_off * kN;
   const A ar(P.primes, P.qinv, job.prime);
   const W *tw = static_cast<const W *>(P.tw) + (size_t)job.prime * kN;
