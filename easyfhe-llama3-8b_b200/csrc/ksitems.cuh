@@ -34,7 +34,7 @@ __device__ __forceinline__ uint32_t brv16(uint32_t x) { return __brev(x) >> 16; 
 // source evaluation index of output k under X -> X^g (g odd, < 2N)
 __device__ __forceinline__ uint32_t auto_src(uint32_t k, uint32_t g) {
   uint32_t e = 2 * brv16(k) + 1;
-  uint32_t e2 = (uint32_t)(((uint64_t)e * g) & (2 * kN - 1));
+  uint32_t e2 = (e * g) & (2 * kN - 1);  // modulo 2^17: the low word suffices
   return brv16((e2 - 1) >> 1);
 }
 

@@ -269,9 +269,12 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 4)
 //   out_b[i][dst(j)] = (acc_b[i][j] - v[j]) * [P^-1]_{q_i} (* qinv_i) + add_b[i][j]
 // with dst = the slot permutation of X -> X^(g^-1) (the inverse of the
 // gather out[k] = w[src_g(k)]).  Each warp walks its own 512 evaluations in
-// order (coalesced reads of acc and add) and its 32 stores land in one
-// aligned 32-word block, since an automorphism maps aligned blocks of 32
-// evaluations onto aligned blocks.  The converted limbs never reach HBM.
+// lane-interleaved pairs (coalesced reads of acc and add); a pair j, j + 1
+// (j even) lands on one aligned pair of words, since bit-reversing j + 1 adds
+// 2^16 to the exponent 2 brv(j) + 1, which an odd g keeps at 2^16 modulo 2^17,
+// so the source indices differ in bit 0 only: one 16-byte store per pair,
+// and the 32 stores of a warp land in one aligned 64-word block.  The
+// converted limbs never reach HBM.
 struct ModDownOut {
   const uint64_t *acc;          // [item][2][lk][N]
   const uint64_t *add0, *add1;  // [ct][..][N] at add_stride, or null
@@ -581,8 +584,11 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
       if (ginv == 1) {
         *reinterpret_cast<ulonglong2 *>(outl + j) = make_ulonglong2(w0, w1);
       } else {
-        outl[auto_src(j, ginv)] = w0;
-        outl[auto_src(j + 1, ginv)] = w1;
+        // j even: auto_src(j + 1) = auto_src(j) ^ 1, so the pair lands on one
+        // aligned pair of words, in order or swapped
+        const uint32_t d = auto_src(j, ginv);
+        *reinterpret_cast<ulonglong2 *>(outl + (d & ~1u)) =
+            (d & 1u) ? make_ulonglong2(w1, w0) : make_ulonglong2(w0, w1);
       }
     }
   }
