@@ -49,6 +49,21 @@ constexpr int SMEM_BYTES = (BLK + BLK / 16) * 8;  // 34816
 // one pad word per 16 keeps every access pattern free of bank conflicts
 __device__ __forceinline__ int pad(int e) { return e + (e >> 4); }
 
+// 32-byte accesses (one full sector per lane; the launch checks the 32-byte
+// alignment of the limbs): a thread's 16 consecutive words in four requests,
+// neither sector half requested twice
+__device__ __forceinline__ void ld32(const uint64_t *p, uint64_t (&w)[4]) {
+  asm volatile("ld.global.v4.u64 {%0, %1, %2, %3}, [%4];"
+               : "=l"(w[0]), "=l"(w[1]), "=l"(w[2]), "=l"(w[3])
+               : "l"(p));
+}
+__device__ __forceinline__ void st32(uint64_t *p, uint64_t a, uint64_t b, uint64_t c,
+                                     uint64_t d) {
+  asm volatile("st.global.v4.u64 [%0], {%1, %2, %3, %4};" ::"l"(p), "l"(a), "l"(b), "l"(c),
+               "l"(d)
+               : "memory");
+}
+
 struct NttParams {
   const uint64_t *in;
   uint64_t *out;
@@ -173,12 +188,12 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 4)
     for (int k = 0; k < 16; ++k) x[k] = p[k];
   }
   ct_pass(ar, x, tw, 12, jb + 16 * tid, 1);
-  // x[k] is element 16 tid + k of the block: 16-byte stores
+  // x[k] is element 16 tid + k of the block: 32-byte stores
   o += jb + 16 * tid;
 #pragma unroll
-  for (int m = 0; m < 8; ++m)
-    *reinterpret_cast<ulonglong2 *>(o + 2 * m) =
-        make_ulonglong2(A::to_word(ar.full(x[2 * m])), A::to_word(ar.full(x[2 * m + 1])));
+  for (int m = 0; m < 4; ++m)
+    st32(o + 4 * m, A::to_word(ar.full(x[4 * m])), A::to_word(ar.full(x[4 * m + 1])),
+         A::to_word(ar.full(x[4 * m + 2])), A::to_word(ar.full(x[4 * m + 3])));
 }
 
 template <class A>
@@ -203,10 +218,11 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 4)
   V x[16];
   // stages 15-12 on the thread's 16 consecutive words, straight from HBM
 #pragma unroll
-  for (int m = 0; m < 8; ++m) {
-    const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(a + jb + 16 * tid + 2 * m);
-    x[2 * m] = A::from_word(v.x);
-    x[2 * m + 1] = A::from_word(v.y);
+  for (int m = 0; m < 4; ++m) {
+    uint64_t w[4];
+    ld32(a + jb + 16 * tid + 4 * m, w);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) x[4 * m + u] = A::from_word(w[u]);
   }
   gs_pass<A, 0>(ar, x, tw, 12, jb + 16 * tid, 1);
   {
@@ -603,6 +619,11 @@ int launch_ntt_impl(b2f_context *ctx, const uint64_t *in, long long in_stride,
                     int jobs_per_item, int items, int inverse,
                     const ulonglong2 *scales, const ModDownOut *epi, cudaStream_t s) {
   if (items <= 0 || jobs_per_item <= 0) return B2F_OK;
+  if ((((uintptr_t)in | (uintptr_t)out) & 31) || ((in_stride | out_stride) & 3)) {
+    set_error("launch_ntt: limbs must be 32-byte aligned (in %p, out %p, strides %lld, %lld)",
+              (const void *)in, (const void *)out, in_stride, out_stride);
+    return B2F_ERR_ARG;
+  }
   // one bit per device: the attribute calls are idempotent, so threads that
   // race on a device's first launch only repeat them
   static std::atomic<uint64_t> configured{0};
@@ -774,7 +795,7 @@ extern "C" int b2f_ntt(b2f_context *ctx, uint64_t *data, int num_polys,
                     p_limbs >= 0 && p_limbs <= ctx->K && q_limbs + p_limbs > 0,
                 "b2f_ntt: bad limb counts q=%d p=%d (L=%d K=%d)", q_limbs,
                 p_limbs, ctx->L, ctx->K);
-  B2F_CHECK_ARG(((uintptr_t)data & 15) == 0, "b2f_ntt: data must be 16-byte aligned");
+  B2F_CHECK_ARG(((uintptr_t)data & 31) == 0, "b2f_ntt: data must be 32-byte aligned");
   return ntt_polys(ctx, data, num_polys, q_limbs, p_limbs, inverse,
                    (cudaStream_t)stream);
 }

@@ -74,7 +74,9 @@ int b2f_context_info(const b2f_context *ctx, int *info6);
 int b2f_context_set_arith(b2f_context *ctx, int mode);
 int b2f_context_arith(const b2f_context *ctx);
 
-/* ---- number-theoretic transform (inside every op; no direct Python site) ---- */
+/* ---- number-theoretic transform (inside every op; no direct Python site) ----
+ * data: num_polys polynomials of q_limbs + p_limbs limbs, 32-byte aligned
+ * (B2F_ERR_ARG otherwise). */
 int b2f_ntt(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
             int p_limbs, int inverse, void *stream);
 

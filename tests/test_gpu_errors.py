@@ -47,6 +47,24 @@ def test_bad_level_galois_and_workspace_raise_then_context_still_works():
     assert core.lib.b2f_last_error()
 
 
+def test_misaligned_limbs_raise_before_any_launch():
+    """The transforms move 32-byte sectors: a buffer that is only 16-byte
+    aligned is refused on the host and the context keeps working."""
+    import torch
+
+    from easyfhe import _native
+
+    ctx, orc = pair(8, 2, 3)
+    rng = np.random.default_rng(72)
+    x = rand_residues(rng, ctx.primes[:2], 1)
+    buf = torch.zeros(2 * N + 4, dtype=torch.int64, device="cuda:0")
+    with pytest.raises(ValueError, match="32-byte aligned"):
+        _native.call("b2f_ntt", ctx.handle, buf.data_ptr() + 16, 1, 2, 0, 0, None)
+    d = to_dev(x)
+    ctx.ntt(d, 2, 0, inverse=False)
+    assert np.array_equal(to_host(d), orc.ntt(x, 2, 0, inverse=False).reshape(x.shape))
+
+
 def test_fhe_level_errors_are_value_errors():
     from easyfhe import fhe
 
