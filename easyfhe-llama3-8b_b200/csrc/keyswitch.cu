@@ -611,6 +611,12 @@ struct Scratch {
   size_t used = 0, cap = 0;
   int init(void *ws, size_t ws_bytes, size_t need) {
     if (ws) {
+      // buffers are carved at 256-byte granularity and read and written with
+      // vector accesses of up to 32 bytes
+      if ((uintptr_t)ws & 255) {
+        set_error("workspace must be 256-byte aligned (%p)", ws);
+        return B2F_ERR_ARG;
+      }
       if (ws_bytes < need) {
         set_error("workspace too small: %zu bytes given, %zu needed", ws_bytes,
                   need);

@@ -14,10 +14,15 @@
  *    otherwise; evaluation k is a(psi^(2*bitrev(k)+1)), psi the smallest
  *    primitive 2N-th root of unity modulo the limb's prime.
  *  - Residues are fully reduced ([0, q)) on input and output.
+ *  - Device buffers start on a 32-byte boundary (every cudaMalloc'd or
+ *    torch-allocated buffer, and any limb offset into one, does); the kernels
+ *    move whole 32-byte sectors.
  *  - `stream` is a cudaStream_t (NULL = legacy default stream); every call is
  *    asynchronous on it.  Scratch memory is passed in as `ws`/`ws_bytes`
- *    (size from the matching *_workspace query); ws == NULL makes the call
- *    allocate and free its scratch stream-ordered (cudaMallocAsync).
+ *    (size from the matching *_workspace query, 256-byte aligned); ws == NULL
+ *    makes the call allocate and free its scratch stream-ordered
+ *    (cudaMallocAsync).  A misaligned buffer is refused with B2F_ERR_ARG
+ *    where a transform or a workspace receives it.
  *  - Every function returns 0 (B2F_OK) or a b2f_status; the message of the
  *    last failure on the calling thread is b2f_last_error().
  *

@@ -60,6 +60,18 @@ def test_misaligned_limbs_raise_before_any_launch():
     buf = torch.zeros(2 * N + 4, dtype=torch.int64, device="cuda:0")
     with pytest.raises(ValueError, match="32-byte aligned"):
         _native.call("b2f_ntt", ctx.handle, buf.data_ptr() + 16, 1, 2, 0, 0, None)
+    from easyfhe import core
+
+    g = core.galois_element(1)
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(22, 192))
+    key = ctx.keygen_rotation(s_ntt, g, seed=6)
+    ct = to_dev(rand_residues(rng, ctx.primes[:6], 2))
+    out = ct.clone()
+    need = core.lib.b2f_rotate_workspace(ctx.handle, 1, 6)
+    ws = torch.empty(need + 512, dtype=torch.uint8, device="cuda:0")
+    with pytest.raises(ValueError, match="256-byte aligned"):
+        _native.call("b2f_rotate", ctx.handle, ct.data_ptr(), out.data_ptr(), 1, 6, g,
+                     key.data_ptr(), ws.data_ptr() + 128, need, None)
     d = to_dev(x)
     ctx.ntt(d, 2, 0, inverse=False)
     assert np.array_equal(to_host(d), orc.ntt(x, 2, 0, inverse=False).reshape(x.shape))
