@@ -121,6 +121,58 @@ __device__ __forceinline__ void gs_pass(const A &ar, typename A::V (&x)[16],
   }
 }
 
+// The stride-1 pass (stages s0..s0+3 on a thread's 16 consecutive elements
+// from base, a multiple of 16): stage s0 + t uses 2^t consecutive table
+// entries starting at 2^(s0+t) + base / 2^(16-s0-t), which are loaded four
+// (or two) at a time with vector loads, each lane taking whole sectors
+// instead of one word of each of several sectors per instruction.
+template <class A, bool INV>
+__device__ __forceinline__ void pass1(const A &ar, typename A::V (&x)[16],
+                                      const typename A::W *tw, int s0, int base) {
+  using W = typename A::W;
+  auto bfly = [&](int k, int d, W w) {
+    if constexpr (INV)
+      gs_bfly(ar, x[k], x[k + d], w);
+    else
+      ct_bfly(ar, x[k], x[k + d], w);
+  };
+  auto stage = [&](int t) {
+    const int d = 8 >> t, sh = kLogN - (s0 + t);
+    const W *tws = tw + (1 << (s0 + t)) + (base >> sh);
+    if (t == 0) {
+      const W w = A::ldtw(tws, 0);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) bfly(k, 8, w);
+    } else if (t == 1) {
+      W w[2];
+      A::ldtw2(tws, w);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        bfly(k, 4, w[0]);
+        bfly(8 + k, 4, w[1]);
+      }
+    } else {
+      // 4 or 8 twiddles, four at a time: block b of 2d registers uses w[b]
+#pragma unroll
+      for (int q = 0; q < (1 << t); q += 4) {
+        W w[4];
+        A::ldtw4(tws + q, w);
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+#pragma unroll
+          for (int k = 0; k < d; ++k) bfly((q + b) * 2 * d + k, d, w[b]);
+      }
+    }
+  };
+  if constexpr (INV) {
+#pragma unroll
+    for (int t = 3; t >= 0; --t) stage(t);
+  } else {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) stage(t);
+  }
+}
+
 // Register passes over a CTA's block (element e of the block, 16 per thread):
 //   A: e = tid + 256 k                    (pad: +272 k)
 //   B: e = 256 (tid/16) + tid%16 + 16 k   (pad: +17 k; a half-warp's segment)
@@ -187,7 +239,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 4)
 #pragma unroll
     for (int k = 0; k < 16; ++k) x[k] = p[k];
   }
-  ct_pass(ar, x, tw, 12, jb + 16 * tid, 1);
+  pass1<A, false>(ar, x, tw, 12, jb + 16 * tid);
   // x[k] is element 16 tid + k of the block: 32-byte stores
   o += jb + 16 * tid;
 #pragma unroll
@@ -224,7 +276,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 4)
 #pragma unroll
     for (int u = 0; u < 4; ++u) x[4 * m + u] = A::from_word(w[u]);
   }
-  gs_pass<A, 0>(ar, x, tw, 12, jb + 16 * tid, 1);
+  pass1<A, true>(ar, x, tw, 12, jb + 16 * tid);
   {
     V *p = vb + pad(16 * tid);
 #pragma unroll

@@ -21,6 +21,19 @@ struct IntArith {
   __device__ __forceinline__ IntArith(const uint64_t *primes, const double *, int prime)
       : q(primes[prime]), q2(2 * primes[prime]) {}
   static __device__ __forceinline__ W ldtw(const W *tw, int idx) { return __ldg(tw + idx); }
+  // four consecutive twiddles from a 64-byte aligned entry: two 32-byte loads
+  static __device__ __forceinline__ void ldtw4(const W *tw, W (&w)[4]) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      asm("ld.global.nc.v4.u64 {%0, %1, %2, %3}, [%4];"
+          : "=l"(w[2 * h].x), "=l"(w[2 * h].y), "=l"(w[2 * h + 1].x), "=l"(w[2 * h + 1].y)
+          : "l"(tw + 2 * h));
+  }
+  static __device__ __forceinline__ void ldtw2(const W *tw, W (&w)[2]) {
+    asm("ld.global.nc.v4.u64 {%0, %1, %2, %3}, [%4];"
+        : "=l"(w[0].x), "=l"(w[0].y), "=l"(w[1].x), "=l"(w[1].y)
+        : "l"(tw));
+  }
   static __device__ __forceinline__ V from_word(uint64_t v) { return v; }
   static __device__ __forceinline__ uint64_t to_word(V v) { return v; }
   static __device__ __forceinline__ V from_bits(uint64_t v) { return v; }
@@ -73,6 +86,17 @@ struct FpArith {
   __device__ __forceinline__ FpArith(const uint64_t *primes, const double *qinvs, int prime)
       : q(from_word(primes[prime])), qinv(qinvs[prime]) {}
   static __device__ __forceinline__ W ldtw(const W *tw, int idx) { return __ldg(tw + idx); }
+  // four (two) consecutive twiddles from a 32-byte (16-byte) aligned entry
+  static __device__ __forceinline__ void ldtw4(const W *tw, W (&w)[4]) {
+    asm("ld.global.nc.v4.f64 {%0, %1, %2, %3}, [%4];"
+        : "=d"(w[0]), "=d"(w[1]), "=d"(w[2]), "=d"(w[3])
+        : "l"(tw));
+  }
+  static __device__ __forceinline__ void ldtw2(const W *tw, W (&w)[2]) {
+    const double2 v = __ldg(reinterpret_cast<const double2 *>(tw));
+    w[0] = v.x;
+    w[1] = v.y;
+  }
   // exact for 0 <= v < 2^52: the word as the mantissa of 2^52 + v
   static __device__ __forceinline__ V from_word(uint64_t v) {
     return __dadd_rn(__longlong_as_double((long long)(v | 0x4330000000000000ull)), -kTwo52);
