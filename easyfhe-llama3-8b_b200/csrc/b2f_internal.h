@@ -191,6 +191,11 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
 // (c_i - NTT(lift)) q_{l-1}^-1 in its epilogue.
 int ntt_rescale(b2f_context *ctx, const uint64_t *last, const uint64_t *in, uint64_t *out,
                 int num_polys, int l, cudaStream_t s);
+// The same with its job table given: l-1 rows LimbJob{0, i, i, i} in device
+// memory (ntt_rescale takes them from the context's cache).
+int ntt_rescale_jobs(b2f_context *ctx, const uint64_t *last, const uint64_t *in,
+                     uint64_t *out, int num_polys, int l, const LimbJob *jobs,
+                     cudaStream_t s);
 // jobs for num_polys polys of (q_limbs Q + p_limbs P) limbs, contiguous
 int ntt_polys(b2f_context *ctx, uint64_t *data, int num_polys, int q_limbs,
               int p_limbs, int inverse, cudaStream_t s);

@@ -795,6 +795,12 @@ int ntt_rescale(b2f_context *ctx, const uint64_t *last, const uint64_t *in, uint
   for (int i = 0; i < lo; ++i) jobs[i] = LimbJob{0u, (uint32_t)i, (uint16_t)i, (uint16_t)i};
   const LimbJob *d = job_table(ctx, {9, l}, jobs);
   if (!d) return B2F_ERR_NOMEM;
+  return ntt_rescale_jobs(ctx, last, in, out, num_polys, l, d, s);
+}
+
+int ntt_rescale_jobs(b2f_context *ctx, const uint64_t *last, const uint64_t *in,
+                     uint64_t *out, int num_polys, int l, const LimbJob *d, cudaStream_t s) {
+  const int lo = l - 1;
   const LevelTables &T = ctx->levels[l];
   ModDownOut E;
   E.acc = in;

@@ -563,8 +563,9 @@ int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
 namespace b2f {
 namespace {
 
-// scratch: the last limb of every poly (num_polys N words) followed by its
-// lift to the other primes (num_polys (l-1) N words)
+// scratch: the last limb of every poly in coefficient form (num_polys N
+// words); the rescale's forward transform lifts it to the other primes in its
+// input stage and writes the result straight to `out`
 constexpr size_t kNoAllocBytes = 16u << 20;
 constexpr size_t kNoAllocWords = kNoAllocBytes / sizeof(uint64_t);
 __device__ __align__(256) uint64_t g_noalloc_scratch[kNoAllocWords];
@@ -584,7 +585,7 @@ __global__ void noalloc_jobs_kernel(LimbJob *jobs, int l) {
   const int i = threadIdx.x;
   if (i == 0)
     jobs[0] = LimbJob{(uint32_t)(l - 1), 0u, (uint16_t)(l - 1), (uint16_t)(l - 1), 0};
-  if (i < l - 1) jobs[64 + i] = LimbJob{(uint32_t)i, (uint32_t)i, (uint16_t)i, (uint16_t)i, 0};
+  if (i < l - 1) jobs[64 + i] = LimbJob{0u, (uint32_t)i, (uint16_t)i, (uint16_t)i, 0};
 }
 
 // The host-side names of the arrays above are stand-ins, not device
@@ -619,33 +620,28 @@ extern "C" int b2f_rescale_noalloc(b2f_context *ctx, const uint64_t *in,
   B2F_CHECK_ARG(l >= 2 && l <= ctx->L && l <= 64,
                 "b2f_rescale_noalloc: needs 2..%d limbs, got %d", ctx->L, l);
   B2F_CHECK_ARG(in != out, "b2f_rescale_noalloc: in-place rescale is not supported");
-  const size_t need = (size_t)num_polys * l * kN;
+  const size_t need = (size_t)num_polys * kN;
   B2F_CHECK_ARG(need <= kNoAllocWords,
-                "b2f_rescale_noalloc: %d polys x %d limbs need %zu bytes of scratch, "
-                "more than its fixed %zu (num_polys * l must be <= %zu)",
-                num_polys, l, need * 8, kNoAllocBytes, kNoAllocWords / kN);
+                "b2f_rescale_noalloc: %d polys need %zu bytes of scratch, more than "
+                "its fixed %zu (num_polys must be <= %zu)",
+                num_polys, need * 8, kNoAllocBytes, kNoAllocWords / kN);
+  int cur = -1;
+  B2F_CUDA(cudaGetDevice(&cur));
+  B2F_CHECK_ARG(cur == ctx->device,
+                "b2f_rescale_noalloc: the context's device %d must be current (is %d)",
+                ctx->device, cur);
   if (!num_polys) return B2F_OK;
   NoAllocDevice *d = nullptr;
   int rc = noalloc_setup(ctx, &d);
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   uint64_t *last = d->scratch;
-  uint64_t *lifted = last + (size_t)num_polys * kN;
-  const LevelTables &T = ctx->levels[l];
   noalloc_jobs_kernel<<<1, 64, 0, s>>>(d->jobs, l);
   B2F_LAUNCHED("noalloc_jobs_kernel");
+  // the last limb back to coefficients, then lift, forward NTT and combine in
+  // one launch, as b2f_rescale does
   rc = launch_ntt(ctx, in, (long long)l * kN, last, kN, d->jobs, 1, num_polys, 1,
                   nullptr, s);
   if (rc) return rc;
-  rescale_lift_kernel<<<dim3(kN / TPB, l - 1, num_polys), TPB, 0, s>>>(
-      last, lifted, ctx->d_primes, T.rescale_qlast, l, ctx->primes[l - 1]);
-  B2F_LAUNCHED("rescale_lift_kernel");
-  const long long ls = (long long)(l - 1) * kN;
-  rc = launch_ntt(ctx, lifted, ls, lifted, ls, d->jobs + 64, l - 1, num_polys, 0,
-                  nullptr, s);
-  if (rc) return rc;
-  rescale_combine_kernel<<<dim3(kN / TPB, l - 1, num_polys), TPB, 0, s>>>(
-      in, lifted, out, ctx->d_primes, T.rescale_inv, l);
-  B2F_LAUNCHED("rescale_combine_kernel");
-  return B2F_OK;
+  return ntt_rescale_jobs(ctx, last, in, out, num_polys, l, d->jobs + 64, s);
 }

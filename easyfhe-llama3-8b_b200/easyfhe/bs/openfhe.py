@@ -173,8 +173,14 @@ class Program:
     constants: _Constants = field(repr=False, default=None)
 
     def release(self) -> None:
+        """Drop the encoded diagonals (BootstrapOperator.release at teardown,
+        llama3fhe/operators/nonlinear/bootstrap.py); the program is unusable
+        afterwards."""
+
         for lv in self.cts + self.stc:
-            lv.pts.release()
+            lv.pts = None
+        if self.constants is not None:
+            self.constants._pts = []
 
 
 def level_rows(diags: dict, plan: _Plan, slots: int) -> np.ndarray:
@@ -410,16 +416,18 @@ def bootstrap(ct: fhe.Ciphertext, context, program: Program) -> fhe.Ciphertext:
     if l_in < 2:
         raise ValueError("bootstrap needs an input with at least two limbs")
     in_scale = float(ct.state.scaling_factor)
-    # 0. pre-scale by 2^-k at the scale of the dropped prime
-    enc = fhe.encode_scalar(2.0 ** -PRESCALE_BITS, cur_limbs=l_in, scale_degree=1,
-                            scaling_factor=ctx.rescale_divisor_at(l_in - 1), context=ctx)
+    # read t + q_0 I at the scale the CoeffToSlot factor alpha assumes
+    delta = ctx.scale_at(ctx.L)
+    # 0. pre-scale by 2^-k delta / in_scale at the scale of the dropped prime:
+    # t = u delta 2^-k for the message u, whatever scale the input tracked
+    enc = fhe.encode_scalar(2.0 ** -PRESCALE_BITS * delta / in_scale, cur_limbs=l_in,
+                            scale_degree=1, scaling_factor=ctx.rescale_divisor_at(l_in - 1),
+                            context=ctx)
     x = fhe.rescale(fhe.homo_mul_scalar(ct, enc, ctx), ctx)
     x = fhe.align_to(x, x.state.replace(cur_limbs=1), ctx)
     # 1. ModRaise to all limbs
     raised = ctx.native.modraise(x.data, 2 * C, ctx.L)
     raised = raised.view((2, ctx.L, -1) if x.data.dim() == 3 else (C, 2, ctx.L, -1))
-    # read t + q_0 I at the scale the CoeffToSlot factor alpha assumes
-    delta = ctx.scale_at(ctx.L)
     y = fhe.Ciphertext(raised, fhe.CipherState(ctx.L, 1, delta), x.slots, ctx)
     # 1b. sparse messages: SubSum (trace onto Z[X^gap]) keeps the subring
     # coefficients of t = Delta u 2^-k + q_0 I, times the gap (folded into alpha)
@@ -441,8 +449,12 @@ def bootstrap(ct: fhe.Ciphertext, context, program: Program) -> fhe.Ciphertext:
     z = fhe.homo_add(s_re, fhe.homo_mul_i(s_im, ctx), ctx)
     for level in program.stc:
         z = _linear(z, level, ctx)
-    # the slots hold u in_scale / delta at tracked scale delta: u at in_scale
-    out = fhe.Ciphertext(z.data, z.state.replace(scale_degree=1, scaling_factor=in_scale),
+    # the slots hold u at tracked scale delta = scale_at(L), the nominal scale:
+    # a refresh starts its output's scale afresh, so the ratio of a tracked
+    # scale to 2^dcrt_bits, which every product squares (e.g. the
+    # Paterson-Stockmeyer doubling basis, operators/nonlinear/polynomial.py:
+    # 138-151), does not compound from one polynomial-and-refresh to the next
+    out = fhe.Ciphertext(z.data, z.state.replace(scale_degree=1, scaling_factor=delta),
                          ct.slots, ctx)
     if int(spec.output_levels):
         out = fhe.align_to(out, out.state.replace(cur_limbs=int(spec.output_levels) + 1), ctx)

@@ -412,6 +412,46 @@ class NativeContext:
              baby_steps, giant_base, giant_count, slots, _ptr(out), _stream())
         return out
 
+    _STRUCT_MAPS = ("real_source", "real_row", "real_scale", "imag_source", "imag_row",
+                    "imag_scale", "column", "column_scale")
+
+    def pack_structured(self, sources, maps: dict, dimension: int, token_lanes: int,
+                        baby_steps: int, giant_base: int, giant_count: int,
+                        slots: int) -> torch.Tensor:
+        """BSGS diagonals read through a StructuredLinearWeight's maps
+        (llama3fhe/operators/linear/structured_weight.py:1-20): 1-3 real
+        source matrices (float32 or float64, one dtype), int64 index maps and
+        float64 scales of length `dimension`.  Host arrays are uploaded."""
+
+        import ctypes
+
+        srcs = [torch.as_tensor(s) for s in sources]
+        if not 1 <= len(srcs) <= 3:
+            raise ValueError("structured packing takes one to three sources")
+        want = torch.float32 if all(s.dtype == torch.float32 for s in srcs) else torch.float64
+        srcs = [s.to(device=self.device, dtype=want) for s in srcs]
+        if any(s.dim() != 2 for s in srcs):
+            raise ValueError("structured sources must be matrices")
+        dev = {}
+        for name in self._STRUCT_MAPS:
+            t = torch.as_tensor(maps[name])
+            dt = torch.float64 if name.endswith("scale") else torch.int64
+            t = t.to(device=self.device, dtype=dt).contiguous()
+            if t.numel() != int(dimension):
+                raise ValueError(f"structured map {name} has {t.numel()} entries, "
+                                 f"expected {dimension}")
+            dev[name] = t
+        ptrs = (ctypes.c_void_p * 3)(*([s.data_ptr() for s in srcs] + [0] * (3 - len(srcs))))
+        strides = (ctypes.c_int64 * 6)(*([v for s in srcs for v in s.stride()]
+                                         + [0] * (6 - 2 * len(srcs))))
+        rows = giant_count * baby_steps
+        out = torch.empty(rows, slots, dtype=torch.complex128, device=self.device)
+        call("b2f_pack_structured", self.handle, ptrs, strides, len(srcs),
+             1 if want == torch.float32 else 0,
+             *[dev[n].data_ptr() for n in self._STRUCT_MAPS], dimension, token_lanes,
+             baby_steps, giant_base, giant_count, slots, _ptr(out), _stream())
+        return out
+
 
 def galois_element(rotation: int, log_n: int = LOG_N) -> int:
     return int(lib.b2f_galois_element(log_n, int(rotation)))

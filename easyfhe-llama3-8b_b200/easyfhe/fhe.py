@@ -90,6 +90,11 @@ class Context:
         self.rotation_keys: dict[int, torch.Tensor] = {}
         self.relin_key: torch.Tensor | None = None
         self._ws: dict[str, torch.Tensor] = {}
+        # Declared rotations whose keys materialise on first use (auto_load_keys):
+        # galois element -> True.  _keygen holds (secret in NTT form, seed).
+        self._deferred: set[int] = set()
+        self._keygen: tuple[torch.Tensor, int] | None = None
+        self.keys_generated = 0
 
     def scale_at(self, cur_limbs: int) -> float:
         return float(2.0 ** int(self.spec.dcrt_bits))
@@ -137,6 +142,7 @@ class Context:
                 continue
             freed += (key.shape[0] - digits) * key[0].numel() * key.element_size()
             self.rotation_keys[g] = key[:digits].clone()
+            self._deferred.discard(g)  # an explicit truncation is final
         return freed
 
     def key_bytes(self) -> dict:
@@ -149,9 +155,27 @@ class Context:
             out["device" if key.is_cuda else "host"] += key.numel() * key.element_size()
         return out
 
+    def _materialize_key(self, g: int, digits: int) -> torch.Tensor:
+        """Generate the key for galois element g and keep its first `digits`
+        digits.  Keygen is deterministic in (seed, g), so this equals the key
+        generate_client_context makes eagerly, truncated."""
+
+        secret, seed = self._keygen
+        full = self.native.keygen_rotation(secret, g, seed ^ g)
+        self.keys_generated += 1
+        key = full if digits >= full.shape[0] else full[:digits].clone()
+        self.rotation_keys[g] = key
+        return key
+
     def rotation_key(self, rotation: int, limbs: int | None = None) -> tuple[int, torch.Tensor]:
         g = galois_element(int(rotation), self.logN)
         key = self.rotation_keys.get(g)
+        need = self.native.digits if limbs is None else -(-int(limbs) // self.native.alpha)
+        if g in self._deferred and (key is None or key.shape[0] < need):
+            # auto_load_keys: a declared key appears (or grows to the digits
+            # this level reads) on first use, sized for that level: a key used
+            # by the 13-limb linears keeps 2 of 5 digits at the layer parameters
+            key = self._materialize_key(g, need)
         if key is None:
             raise ValueError(
                 f"no rotation key for index {rotation} (galois {g}); the context "
@@ -213,8 +237,12 @@ class Ciphertext:
         return Ciphertext(data, self.state, self.slots if slots is None else slots,
                           self.context, self.is_ext)
 
-    def release(self) -> None:
-        self.data = None
+    # No release(): handles use Python ownership, as the EasyFHE the reference
+    # targets does (llama3fhe/backend.py:336-346).  The reference's helpers
+    # "release" values that other names still alias (the PS evaluator's
+    # `su = t_basis[k - 1]`, operators/nonlinear/polynomial.py:300-324), which
+    # is safe only because release_if_supported finds no release method; the
+    # device memory goes back to the caching allocator with the last reference.
 
 
 class Plaintext:
@@ -253,8 +281,6 @@ class Plaintext:
             return d
         return d[:, :limbs].contiguous()
 
-    def release(self) -> None:
-        self.data = None
 
 
 class Client:
@@ -322,10 +348,20 @@ def generate_client_context(spec: CKKSContextSpec, device: str = "cuda"):
     s = client._s_ntt
     if spec.relin_key:
         ctx.relin_key = ctx.native.keygen_relin(s, int(spec.seed) ^ 0xE1)
+    # auto_load_keys (the reference's setting, session.py:42): each declared
+    # rotation key is generated on its first use with the digits that level
+    # reads, instead of all of them at the top level up front (the layer
+    # preset declares 674 rotations: 163 GB at 230 MiB each would not fit
+    # beside the working set in one GPU's HBM).  Otherwise: every key now.
+    ctx._keygen = (s, int(spec.seed))
     for r in sorted({int(v) for v in spec.rotations}):
         g = galois_element(r, spec.log_n)
-        if g != 1 and g not in ctx.rotation_keys:
-            ctx.rotation_keys[g] = ctx.native.keygen_rotation(s, g, int(spec.seed) ^ g)
+        if g == 1 or g in ctx.rotation_keys:
+            continue
+        if bool(spec.auto_load_keys):
+            ctx._deferred.add(g)
+        else:
+            ctx._materialize_key(g, ctx.native.digits)
     return client, ctx
 
 
@@ -809,6 +845,54 @@ class UnpackedRaw:
         self.packer = packer
 
 
+# Counters of how linear-weight chunks were packed (tests read them).
+PACK_STATS = {"dense": 0, "structured": 0, "foreign": 0}
+
+
+def _native_chunk_pack(raw: UnpackedRaw, slots: int, context) -> torch.Tensor | None:
+    """Pack a linear-weight chunk with the CUDA packers when `raw.packer` is the
+    reference's chunk packer (the `pack` closure of
+    llama3fhe/operators/linear/weight.py:50-104).  That closure would call the
+    Triton kernels of gpu_packer.py:144-184 / 317-424 (or the NumPy
+    `_cpu_packer`, weight.py:18-47); its bound plan, chunk and weight give every
+    argument those kernels take, so the same rows come from
+    b2f_pack_diagonals / b2f_pack_structured instead and Triton is never
+    imported.  Returns None for any other packer callable."""
+
+    import inspect
+
+    fn = raw.packer
+    if (getattr(fn, "__qualname__", "") != "_chunk_packer.<locals>.pack"
+            or not str(getattr(fn, "__module__", "")).endswith("operators.linear.weight")):
+        PACK_STATS["foreign"] += 1
+        return None
+    nl = inspect.getclosurevars(fn).nonlocals
+    plan, chunk, weight = nl["plan"], nl["chunk"], nl["weight"]
+    bound_slots = int(nl["slots"])
+    if int(slots) != bound_slots:
+        raise ValueError(f"linear weight expects slots={bound_slots}, got {slots}.")
+    ctx = _ctx_of(context)
+    geometry = dict(dimension=int(plan.dimension), token_lanes=int(plan.token_lanes),
+                    baby_steps=int(plan.baby_steps), giant_base=int(chunk.giant_base),
+                    giant_count=int(chunk.giant_count), slots=bound_slots)
+    if hasattr(weight, "real_source") and hasattr(weight, "sources"):
+        # StructuredLinearWeight (structured_weight.py:47-192): reuse the device
+        # copies LinearWeight.prepare made when it made them, else its arrays.
+        dev_src = tuple(nl.get("structured_device_sources") or ())
+        dev_meta = nl.get("structured_device_metadata") or {}
+        sources = dev_src if dev_src else tuple(weight.sources)
+        maps = {n: dev_meta.get(n, getattr(weight, n)) for n in NativeContext._STRUCT_MAPS}
+        PACK_STATS["structured"] += 1
+        return ctx.native.pack_structured(sources, maps, **geometry)
+    # dense square page: the raw source handed to UnpackedRaw (a device or host
+    # tensor of the weight), or the NumPy weight the closure holds
+    src = raw.source if torch.is_tensor(raw.source) else torch.as_tensor(np.asarray(weight))
+    if src.dim() != 2 or tuple(src.shape) != (geometry["dimension"],) * 2:
+        src = torch.as_tensor(np.asarray(weight))
+    PACK_STATS["dense"] += 1
+    return ctx.native.pack_diagonals(src.to(ctx.device), **geometry)
+
+
 class ConstantBundle:
     """Named constant vectors encoded on demand at a requested state
     (llama3fhe/backend.py:231-297, llama3fhe/operators/linear/weight.py:344-357).
@@ -840,7 +924,9 @@ class ConstantBundle:
         self._stats["middle_misses"] += 1
         raw = self.vectors[name]
         if isinstance(raw, UnpackedRaw):
-            values = raw.packer(raw.source, slots, context)
+            values = _native_chunk_pack(raw, slots, context)
+            if values is None:  # a caller's own packer: run it as given
+                values = raw.packer(raw.source, slots, context)
         elif isinstance(raw, PackedRaw):
             values = raw.tensor
         else:

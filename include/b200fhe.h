@@ -192,11 +192,13 @@ int b2f_rescale(b2f_context *ctx, const uint64_t *in, uint64_t *out,
  * callers that cannot allocate device memory (their HBM is owned by another
  * allocator, or the step runs under a fixed memory budget).  No counterpart
  * in the reference.  Scratch is a fixed 16 MiB array in device memory that
- * every GPU loading this library holds until exit; num_polys * l must be
- * <= 32 (e.g. one ciphertext at up to 16 limbs), larger requests fail with
- * B2F_ERR_ARG.  The first call on a device looks up that device's array
- * address; make it before any stream capture.  All calls share the array:
- * calls that overlap on the GPU (other streams, other threads) race. */
+ * every GPU loading this library holds until exit: it keeps the last limb of
+ * each poly, so num_polys must be <= 32 (16 ciphertexts, at any level);
+ * larger requests fail with B2F_ERR_ARG.  The context's device must be the
+ * current device (else B2F_ERR_ARG).  The first call on a device looks up
+ * that device's array address; make it before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU (other streams, other
+ * threads) race. */
 int b2f_rescale_noalloc(b2f_context *ctx, const uint64_t *in, uint64_t *out,
                         int num_polys, int l, void *stream);
 /* ModRaise of bootstrapping: num_polys polys at one limb (q_0, NTT form)

@@ -69,6 +69,25 @@ def test_bootstrap_layer_parameters():
     assert err < 2.0 ** -17  # 2^-19.3 measured on B200
 
 
+def test_bootstrap_output_is_at_the_nominal_scale():
+    """An input whose tracked scale is off 2^dcrt_bits (the Paterson-Stockmeyer
+    evaluator's outputs are: every product squares the ratio) comes out with
+    the same message at the nominal scale scale_at(L), so the ratio does not
+    compound over a layer's polynomial-and-refresh cycles."""
+
+    from easyfhe.bs import openfhe as bs
+
+    client, ctx, program = _layer_context()
+    rng = np.random.default_rng(62)
+    z = rng.uniform(-1, 1, ctx.max_slots) + 1j * rng.uniform(-1, 1, ctx.max_slots)
+    ct = client.encrypt(np.asarray(z), slots=ctx.max_slots, cur_limbs=3,
+                        scaling_factor=ctx.scale_at(3) * 1.37)
+    out = bs.bootstrap(ct, ctx, program)
+    assert out.state.scaling_factor == ctx.scale_at(ctx.L)
+    err = np.max(np.abs(client.decrypt_complex(out) - z))
+    assert err < 2.0 ** -17, np.log2(err)
+
+
 def test_meta_bts_two_pass_correction():
     """The reference's two-pass correction (bootstrap.py:398-431) with
     precision_bits = 16 on top of bs.bootstrap."""

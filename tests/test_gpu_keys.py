@@ -64,3 +64,34 @@ def test_evicted_key_without_auto_load_is_an_error():
     ctx.clear_cuda_rotation_cache()
     with pytest.raises(ValueError):
         fhe.homo_rotate(ct, 1, ctx)
+
+
+def test_keys_materialised_on_first_use_equal_eager_keys():
+    """With auto_load_keys each declared key is generated on its first use, with
+    the digits that level reads (and regrown when a higher level needs more).
+    Rotations through those keys equal rotations through the keys generated
+    eagerly at the top level, at a low and at the top level."""
+
+    from easyfhe import fhe
+
+    client_l, lazy = _context(True)
+    client_e, eager = _context(False)
+    assert not lazy.rotation_keys and len(eager.rotation_keys) == 3
+    z = np.random.default_rng(9).uniform(-1, 1, lazy.max_slots)
+    for ctx, client in ((lazy, client_l), (eager, client_e)):
+        ctx._probe = client.encrypt(z, slots=ctx.max_slots, cur_limbs=ctx.L,
+                                    scaling_factor=ctx.scale_at(ctx.L))
+    g5 = fhe.galois_element(5, 16)
+    outs = {}
+    for ctx in (lazy, eager):
+        low = fhe.align_to(ctx._probe, ctx._probe.state.replace(cur_limbs=2), ctx)
+        outs[id(ctx)] = [to_host(fhe.homo_rotate(low, 5, ctx).data)]
+        if ctx is lazy:  # sized for two limbs: the first ceil(2 / alpha) digits
+            assert lazy.rotation_keys[g5].shape[0] == -(-2 // lazy.native.alpha)
+        outs[id(ctx)].append(to_host(fhe.homo_rotate(ctx._probe, 5, ctx).data))
+    assert lazy.rotation_keys[g5].shape[0] == eager.rotation_keys[g5].shape[0]
+    assert np.array_equal(outs[id(lazy)][0], outs[id(eager)][0])
+    assert np.array_equal(outs[id(lazy)][1], outs[id(eager)][1])
+    assert lazy.keys_generated == 2  # once at two limbs, once regrown at the top
+    with pytest.raises(ValueError):
+        fhe.homo_rotate(lazy._probe, 3, lazy)  # 3 was never declared

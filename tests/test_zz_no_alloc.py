@@ -25,20 +25,24 @@ def _noalloc(ctx, data, num_polys, l):
     return out
 
 
-def test_rescale_noalloc_matches_rescale_twice_in_a_row():
-    ctx, orc = pair(16, 2, 4)
-    rng = np.random.default_rng(99)
-    for l in (16, 9):  # two calls in a row, different shapes and data
-        x = rand_residues(rng, ctx.primes[:l], 2)
+@pytest.mark.parametrize("bits", [50, 60])
+def test_rescale_noalloc_matches_rescale_twice_in_a_row(bits):
+    """50-bit primes run the binary64 transforms, 60-bit ones the integer
+    transforms; both must agree with b2f_rescale and the oracle."""
+
+    ctx, orc = pair(16, 2, 4, bits=bits)
+    rng = np.random.default_rng(99 + bits)
+    for l, polys in ((16, 2), (9, 4)):  # two calls in a row, different shapes and data
+        x = rand_residues(rng, ctx.primes[:l], polys)
         d = to_dev(x)
-        got = to_host(_noalloc(ctx, d, 2, l))
-        want = to_host(ctx.rescale(d, 2, l))
+        got = to_host(_noalloc(ctx, d, polys, l))
+        want = to_host(ctx.rescale(d, polys, l))
         assert np.array_equal(got, want)
-        assert np.array_equal(got, orc.rescale(x, 2, l))
+        assert np.array_equal(got, orc.rescale(x, polys, l))
 
 
 def test_rescale_noalloc_rejects_oversized_requests():
     ctx, _ = pair(16, 2, 4)
-    d = ctx.empty(3, 16)
+    d = ctx.empty(33, 2)
     with pytest.raises(ValueError, match="scratch"):
-        _noalloc(ctx, d, 3, 16)
+        _noalloc(ctx, d, 33, 2)  # the fixed scratch holds 32 polys' last limbs
