@@ -1,16 +1,20 @@
-"""Benchmark of the CKKS hot path on B200: HRotate key switching (headline),
-with the NTT kernel's HBM roofline, an end-to-end number through the C ABI
-with host buffers, and the CPU oracle timed on the host cores.
+"""Benchmark of the CKKS evaluation hot path of encrypted Llama-3-8B prefill on
+B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload linear|hrotate|ntt|bootstrap|layer0]
 
-Workload (the CKKS primitive microbench): N = 2^16,
-l = 24 limbs of 50-bit NTT primes (q = 1 mod 2^17), dnum = 3 (alpha = 8,
-beta = 3), K = 2 special primes, batches of 32 ciphertexts sharing one
-rotation key, uniform residues from a seed.  One step = one HRotate of the
-whole batch.  Inputs (768 MiB per batch) exceed the 126 MB L2, so no flush
-is needed between steps.  Under torchrun every rank rotates its own batch
-(independent ciphertexts, no collective on the data path: weak scaling).
+Default workload: the encrypted linear block of a layer, the 4096 -> 4096
+feature-major BSGS plaintext x ciphertext matmul at l = 13 with the
+reference's production plan, over a fixed set of 16 token-shard ciphertexts
+(N = 2^16, depth 37, dnum 5, 59/60-bit primes).  One step = the linear on
+every ciphertext; under torchrun the ciphertexts are sharded by output
+ciphertext over the ranks and the outputs are all-gathered over NCCL inside
+the step (strong scaling).  At N = 1 the line also carries the HRotate
+microbench (50-bit primes, l = 24, dnum 3, K = 2, 32 ciphertexts sharing one
+key) with the NTT kernel's roofline, and one encrypted decoder layer through
+the reference's own graph (s/layer).  Inputs exceed the 126 MB L2, so no
+flush is needed between steps.
 """
 
 from __future__ import annotations
@@ -47,10 +51,15 @@ def parse():
     ap.add_argument("--batch", type=int, default=None,
                     help="ciphertexts per rank (hrotate 32, bootstrap 16, linear 16)")
     ap.add_argument("--rotation", type=int, default=1)
-    ap.add_argument("--workload", default="hrotate",
-                    choices=["hrotate", "ntt", "bootstrap", "linear"],
-                    help="ntt: only the NTT kernel loop (for profiling); bootstrap: "
-                         "BASELINE configs[3]; linear: BASELINE configs[2]")
+    ap.add_argument("--workload", default="linear",
+                    choices=["linear", "hrotate", "ntt", "bootstrap", "layer0"],
+                    help="linear (default): the encrypted 4096x4096 linear block sharded "
+                         "over the ranks with an all-gather; hrotate: the key-switching "
+                         "microbench; ntt: only the NTT kernel loop (for profiling); "
+                         "bootstrap: full-slot bootstrapping; layer0: one encrypted "
+                         "decoder layer through the reference's graph")
+    ap.add_argument("--no-layer", action="store_true",
+                    help="skip the Layer-0 run the default line carries at N = 1")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--arith", default="auto", choices=["auto", "int64", "f64"],
                     help="butterfly arithmetic of the NTT kernels (auto: binary64 when "
@@ -62,7 +71,8 @@ def parse():
                     help="rotations timed on the CPU oracle")
     a = ap.parse_args()
     if a.batch is None:
-        a.batch = {"hrotate": 32, "ntt": 32, "bootstrap": 16, "linear": 16}[a.workload]
+        a.batch = {"hrotate": 32, "ntt": 32, "bootstrap": 16, "linear": 16,
+                   "layer0": 16}[a.workload]
     return a
 
 
@@ -162,27 +172,51 @@ def cpu_oracle_rate(a, samples: int) -> dict:
 
 
 def run_reference(a) -> None:
+    """The reference arm: the reference's implementation of the path, EasyFHE,
+    is not in the reference tree (nor installable), so this times the CPU
+    restatement of the same algorithm (oracle/, C with OpenMP) on the host
+    cores for the same workload and metric.  Under torchrun rank 0 alone runs
+    it; torchrun sets OMP_NUM_THREADS=1, so the thread count is set here to
+    every host core before the oracle loads."""
+
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    base = cpu_oracle_rate(a, max(1, a.steps))
+    os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
+    samples = max(1, min(a.steps, 3))
+    if a.workload in ("hrotate", "ntt"):
+        base = cpu_oracle_rate(a, samples)
+        metric, unit, cfg, scaling = METRIC, UNIT, config(a), "weak"
+    elif a.workload == "linear":
+        base = linear_cpu_rate(samples=samples)
+        metric = ("encrypted linear-block ciphertexts/s (4096x4096 feature-major BSGS "
+                  "plaintext x ciphertext matmul, l=13)")
+        unit, scaling = "ciphertexts/s", "strong"
+        cfg = {"workload": (f"linear 4096->4096 D=4096 l={LINEAR_LEVEL} B=64 babies, 64 giants "
+                            "in 8 chunks of 512 rows, one ciphertext per sample"),
+               "ciphertexts_total": a.batch}
+    else:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"no CPU restatement of the {a.workload} workload in the oracle"}))
+        return
     line = {
-        "impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT,
+        "impl": "reference", "metric": metric, "value": base["value"], "unit": unit,
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": 1000.0 / base["value"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
-        "config": config(a),
+        "scaling": scaling, "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+        "config": cfg,
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
-        "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+        "e2e": {"value": base["value"], "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "note": "reference EasyFHE is not in the reference tree; the arm times the CPU "
-                "restatement of the same algorithm (oracle/), one ciphertext per step",
+        "note": ("reference EasyFHE is not in the reference tree; the arm times the CPU "
+                 f"restatement of the same algorithm (oracle/), {samples} bounded samples "
+                 f"on {base['cores']} host threads"),
     }
     print(json.dumps(line), flush=True)
 
 
 def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) -> None:
-    """full-slot bootstrapping at the layer parameters
+    """Full-slot CKKS bootstrapping at the layer parameters
     (logN 16, depth 37, dnum 5, 59/60-bit primes, BootstrapSpec(15, (4, 4),
     19)) of `batch` ciphertexts per rank with uniform complex slots in
     [-1, 1]^2.  One step bootstraps every ciphertext of the batch once."""
@@ -253,7 +287,7 @@ def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) ->
     if rank == 0:
         unit = "bootstraps/s"
         line = {
-            "metric": "bootstraps/s (full-slot CKKS bootstrapping, BASELINE configs[3])",
+            "metric": "bootstraps/s (full-slot CKKS bootstrapping, 2^15 slots, 16-112 ciphertexts)",
             "value": world * a.batch / (ms / 1e3), "unit": unit, "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -280,32 +314,104 @@ def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) ->
         print(json.dumps(line), flush=True)
 
 
-def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
-    """the QKV-shaped 4096 -> 4096 feature-major BSGS
-    linear at l = 13 with the reference's production plan (B = 64 babies at
-    offsets 8 b, giant offset 512, 8 chunks of 512 plaintext rows,
-    llama3fhe/operators/linear/config.py:163-317), QuaRot-like synthetic
-    weight W = G H (G ~ N(0, 1/sqrt(4096)), H a random-sign Hadamard /
-    sqrt(4096)).  The 4096 diagonals are packed and encoded once (timed
-    separately); one step runs LinearOperator.apply's call sequence
-    (operator.py:320-394) on `batch` token-shard ciphertexts per rank."""
+LINEAR_D, LINEAR_LANES, LINEAR_B, LINEAR_ROWS, LINEAR_LEVEL = 4096, 8, 64, 512, 13
+
+
+def linear_plan():
+    """The production plan of the 4096 -> 4096 feature-major linear
+    (llama3fhe/operators/linear/config.py:163-317): B = 64 babies at offsets
+    8 b, giant offset 512, chunks of 512 plaintext rows (8 giants)."""
+
+    D, lanes, B, rows = LINEAR_D, LINEAR_LANES, LINEAR_B, LINEAR_ROWS
+    G = D // B
+    per = rows // B
+    chunks = [(base, min(per, G - base)) for base in range(0, G, per)]
+    offsets = tuple(b * lanes for b in range(B))
+    return chunks, offsets, B * lanes
+
+
+def linear_cpu_rate(samples: int = 1, samples_rows: int = 64) -> dict:
+    """The linear block on the CPU oracle, one token-shard ciphertext, from a
+    bounded sample: the 63 hoisted baby rotations, then `samples_rows`
+    plaintext rows of the multiply-accumulate and one giant rotation, scaled
+    to the full 4096 rows, 56 Horner giant rotations and 7 chunk alignments
+    (every rotation costs one key switch at l = 13)."""
+
+    import numpy as np
+
+    from oracle import oracle as O
+
+    O.build()
+    l, K, dnum = LINEAR_LEVEL, 8, 5
+    allp = O.gen_primes(16, 59, l + K)
+    q, p = allp[:l], allp[l:]
+    orc = O.Oracle(16, q, p, dnum)
+    s_ntt = orc.secret_to_ntt(O.sample_secret(16, 2024, 192))
+    chunks, offsets, giant_offset = linear_plan()
+    rng = np.random.default_rng(5)
+    ct = np.empty((2, l, N), dtype=np.uint64)
+    for i, qi in enumerate(q):
+        ct[:, i] = rng.integers(0, qi, (2, N), dtype=np.uint64)
+    gal = [O.galois_element(16, r) for r in offsets[1:]]
+    keys = [orc.keygen_rotation(s_ntt, g, 40 + j) for j, g in enumerate(gal[:2])]
+    pts = np.empty((samples_rows, l, N), dtype=np.uint64)
+    for i, qi in enumerate(q):
+        pts[:, i] = rng.integers(0, qi, (samples_rows, N), dtype=np.uint64)
+    t_two = t_rot = t_mac = 0.0
+    for _ in range(samples):
+        # 63 babies share one ModUp: time two and scale the key switches
+        t0 = time.perf_counter()
+        babies2 = orc.rotate_hoisted(ct, l, gal[:2], keys)
+        t_two += (time.perf_counter() - t0) / samples
+        t0 = time.perf_counter()
+        orc.rotate(ct, l, gal[0], keys[0])
+        t_rot += (time.perf_counter() - t0) / samples
+        babies = np.concatenate([ct[None], np.repeat(babies2[:1], samples_rows - 1, 0)])
+        t0 = time.perf_counter()
+        orc.bsgs_mac(babies, 1, samples_rows, pts, 1, l)
+        t_mac += (time.perf_counter() - t0) / samples
+    rotations = len(offsets) - 1
+    giants = sum(c for _, c in chunks) - len(chunks)  # Horner steps
+    align = len(chunks) - 1
+    per_ct = (t_two * rotations / 2 + t_mac * LINEAR_D / samples_rows
+              + t_rot * (giants + align))
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": 1.0 / per_ct, "unit": "ciphertexts/s", "cores": cores, "kind": "port",
+            "sample": (f"C oracle (OpenMP over limbs) on one ciphertext at l={l}: 2 hoisted "
+                       f"rotations ({t_two:.2f} s), one rotation ({t_rot:.2f} s), "
+                       f"{samples_rows} of 4096 plaintext rows of the MAC ({t_mac:.2f} s), "
+                       f"scaled to 63 babies + 4096 rows + {giants + align} rotations"),
+            "seconds": t_two + t_rot + t_mac}
+
+
+def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict | None:
+    """The encrypted linear block (the 4096 -> 4096 q/o shape) on a fixed
+    set of token-shard ciphertexts, sharded by output ciphertext over the
+    ranks: rank r runs LinearOperator.apply's call sequence
+    (llama3fhe/operators/linear/operator.py:320-394) with the production plan
+    on its 16/N ciphertexts as one batch, then the outputs are all-gathered
+    over NCCL into every rank's HBM (the stage-boundary exchange).  The
+    weight is QuaRot-like synthetic, W = G H (G ~ N(0, 1/sqrt(4096)), H a
+    random-sign Hadamard / sqrt(4096)); its 4096 diagonals are packed and
+    encoded once per rank, outside the timed step."""
 
     import numpy as np
     import torch
+    import torch.distributed as dist
 
-    from easyfhe import fhe
+    from easyfhe import _native, fhe
 
-    D, lanes, B, rows_per_chunk, level = 4096, 8, 64, 512, 13
+    D, lanes, B, level = LINEAR_D, LINEAR_LANES, LINEAR_B, LINEAR_LEVEL
     slots = 32768
-    chunk_giants = rows_per_chunk // B
-    G = D // B
-    chunks = [(base, min(chunk_giants, G - base)) for base in range(0, G, chunk_giants)]
-    giant_offset = B * lanes
-    offsets = tuple(b * lanes for b in range(B))
+    total = a.batch
+    if total % world:
+        raise SystemExit(f"{total} ciphertexts do not split over {world} ranks")
+    per = total // world
+    chunks, offsets, giant_offset = linear_plan()
     rotations = set(offsets[1:]) | {giant_offset} | {b * giant_offset for b, _ in chunks if b}
     client, ctx = fhe.generate_client_context(
         fhe.CKKSContextSpec(depth=37, log_n=16, dnum=5, dcrt_bits=59, first_mod=60,
-                            rotations=tuple(sorted(rotations)), seed=21 + rank), dev)
+                            rotations=tuple(sorted(rotations)), seed=21), dev)
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
     Gm = torch.randn(D, D, dtype=torch.float64, device=dev, generator=gen) / math.sqrt(D)
@@ -316,7 +422,6 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
     W = (Gm @ (H * signs[None, :])) / math.sqrt(D)
     del Gm, H
     scale = ctx.scale_at(level)
-    # pack + encode every diagonal once at the working level (timed)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     pts = []
@@ -327,18 +432,21 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
         del vals
     torch.cuda.synchronize()
     encode_s = time.perf_counter() - t0
-    rng = np.random.default_rng(5 + rank)
-    tokens = [rng.normal(0, 1, (lanes, D)) for _ in range(a.batch)]
+    rng = np.random.default_rng(5)
+    tokens = [rng.normal(0, 1, (lanes, D)) for _ in range(total)]  # every rank: same set
 
     def layout(t):
         return np.ascontiguousarray(t.T).reshape(-1)  # feature f at slots [8 f, 8 f + 8)
 
-    cts = [client.encrypt(layout(t), slots=slots, cur_limbs=level, scaling_factor=scale)
-           for t in tokens]
+    mine = range(rank * per, (rank + 1) * per)
+    cts = [client.encrypt(layout(tokens[i]), slots=slots, cur_limbs=level, scaling_factor=scale)
+           for i in mine]
     stream = torch.cuda.current_stream()
+    gathered = torch.empty(total, 2, level - 1, N, dtype=torch.int64, device=dev)
+    gather_ev = []
 
     def apply(ct):
-        # LinearOperator.apply's call sequence; ct may be a ciphertext batch
+        # LinearOperator.apply's call sequence; ct is this rank's batch
         babies = fhe.prepare_hoisted_baby_rotations(ct, offsets, ctx)
         acc = None
         for (base, count), pt in zip(chunks, pts):
@@ -349,10 +457,22 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
             acc = r if acc is None else fhe.homo_add(acc, r, ctx)
         return fhe.rescale(acc, ctx)
 
-    def step(inputs):
-        if a.per_ct:
-            return [apply(c) for c in inputs]
-        return list(fhe.unpack_cipher_batch(apply(fhe.pack_cipher_batch(inputs))))
+    out_state = {}
+
+    def step(inputs, record=False):
+        res = apply(fhe.pack_cipher_batch(inputs))
+        out_state["state"] = res.state
+        out = res.data.reshape(per, 2, level - 1, N)
+        if world > 1:  # the stage-boundary exchange: every rank gets every output
+            if record:
+                e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                e[0].record(stream)
+            dist.all_gather_into_tensor(gathered, out.contiguous())
+            if record:
+                e[1].record(stream)
+                gather_ev.append(e)
+            return gathered
+        return out
 
     for _ in range(a.warmup):
         outs = step(cts)
@@ -361,20 +481,44 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    n0 = _native.lib.b2f_launch_count()
     e0.record(stream)
     for _ in range(a.steps):
-        outs = step(cts)
+        outs = step(cts, record=True)
     e1.record(stream)
     torch.cuda.synchronize()
+    launches = (_native.lib.b2f_launch_count() - n0) // a.steps
     barrier()
     clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
-    Wn = W.cpu().numpy()
-    err = max(float(np.max(np.abs(client.decrypt(o) - layout(t @ Wn.T))))
-              for o, t in zip(outs[:2], tokens[:2]))
+    gather_ms = max_over_ranks(sum(x.elapsed_time(y) for x, y in gather_ev) / a.steps
+                               if gather_ev else 0.0)
+    err = None
+    if rank == 0:  # the first and the last ciphertext of the whole (gathered) set
+        Wn = W.cpu().numpy()
+        err = max(float(np.max(np.abs(
+            client.decrypt(fhe.Ciphertext(outs[j], out_state["state"], slots, ctx))
+            - layout(tokens[j] @ Wn.T)))) for j in (0, total - 1))
 
+    # ---- the MAC kernel alone: one chunk's launch on this rank's batch ----
+    batch = fhe.pack_cipher_batch(cts)
+    babies = tuple(fhe.prepare_hoisted_baby_rotations(batch, offsets, ctx))[0]
+    G0 = chunks[0][1]
+    mac_reps = max(3, min(a.steps, 10))
+    ctx.native.mac(babies.data, B, pts[0].data, G0, level, num_cts=per)
+    torch.cuda.synchronize()
+    m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    m0.record(stream)
+    for _ in range(mac_reps):
+        ctx.native.mac(babies.data, B, pts[0].data, G0, level, num_cts=per)
+    m1.record(stream)
+    torch.cuda.synchronize()
+    mac_ms = m0.elapsed_time(m1) / mac_reps
+    del babies, batch
+
+    # ---- end to end: pinned host ciphertexts in, outputs out ----
     host_in = [c.data.cpu().pin_memory() for c in cts]
-    host_out = [torch.empty(o.data.shape, dtype=torch.int64, pin_memory=True) for o in outs]
+    host_out = torch.empty(tuple(outs.shape), dtype=torch.int64, pin_memory=True)
     dev_in = [torch.empty_like(c.data) for c in cts]
     e2e_steps = max(1, min(a.steps, 3))
     barrier()
@@ -386,95 +530,81 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> None:
             d.copy_(h, non_blocking=True)
             ins.append(fhe.Ciphertext(d, c.state, c.slots, ctx))
         res = step(ins)
-        for h, o in zip(host_out, res):
-            h.copy_(o.data, non_blocking=True)
+        if rank == 0:  # the job's result: every output ciphertext, on rank 0's host
+            host_out.copy_(res, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    if rank == 0:
-        peaks = {}
+    if rank != 0:
+        return None
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    lim = N * 8
+    # algorithmic bytes of one mac_kernel launch (one chunk of G0 giants on
+    # `per` ciphertexts): the plaintext rows once, the babies once, outputs
+    mac_bytes = (G0 * B * level + per * B * 2 * level + per * G0 * 2 * level) * lim
+    traffic = None
+    tpath = ROOT / "profiles" / "mac_traffic.json"
+    if tpath.exists():
         try:
-            peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+            t = json.loads(tpath.read_text())
+            # DRAM bytes per launch scale with the ciphertexts of the launch
+            traffic = float(t["bytes_fixed"]) + float(t["bytes_per_ct"]) * per
         except Exception:
-            pass
-        hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-        # algorithmic bytes: the plaintext rows once per call (once per
-        # ciphertext when called per ciphertext, as the reference does; once
-        # per batch otherwise), babies and outputs once
-        lim = N * 8
-        pt_reads = a.batch if a.per_ct else 1
-        alg = (pt_reads * D * level * lim
-               + a.batch * (B * 2 * level * lim + 2 * level * lim))
-        unit = "ciphertexts/s"
-        line = {
-            "metric": "linear-block ciphertexts/s (QKV-shaped 4096x4096 BSGS, BASELINE configs[2])",
-            "value": world * a.batch / (ms / 1e3), "unit": unit, "n_gpus": world,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "u64", "data": "synthetic",
-            "config": {"workload": (f"QKV-shaped linear D=4096 l={level} B=64 G=64 in 8 chunks, "
-                                    f"{a.batch} token-shard ciphertexts/rank, depth 37 dnum 5"),
-                       "batch_per_rank": a.batch,
-                       "calls": "one per ciphertext" if a.per_ct else "one batched call",
-                       "l2": "plaintexts 26 GiB > L2; no flush"},
-            "pt_x_ct_per_s": world * a.batch * D / (ms / 1e3),
-            "encode_rows_per_s": D / encode_s,
-            "max_abs_error": err,
-            "roofline": {"bound": "hbm", "kernel": "whole step", "achieved":
-                         alg / (ms / 1e3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": alg / (ms / 1e3) / 1e9 / hbm_peak, "traffic": None},
-            "cpu_baseline": None,
-            "note": "cpu_baseline is reported on the hrotate line",
-            "e2e": {"value": world * a.batch / (e2e_ms / 1e3), "unit": unit,
-                    "h2d_bytes_per_step": sum(h.numel() * 8 for h in host_in),
-                    "d2h_bytes_per_step": sum(h.numel() * 8 for h in host_out)},
-            "clocks": clk,
-        }
-        print(json.dumps(line), flush=True)
+            traffic = None
+    unit = "ciphertexts/s"
+    return {
+        "metric": ("encrypted linear-block ciphertexts/s (4096x4096 feature-major BSGS "
+                   "plaintext x ciphertext matmul, l=13)"),
+        "value": total / (ms / 1e3), "unit": unit, "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "u64", "data": "synthetic",
+        "config": {"workload": (f"linear 4096->4096 D=4096 l={level} B=64 babies, 64 giants in "
+                                f"8 chunks of 512 rows (the reference's production plan), "
+                                f"{total} token-shard ciphertexts sharded {per}/rank, outputs "
+                                "all-gathered over NCCL in every step; logN 16 depth 37 dnum 5 "
+                                "59/60-bit primes"),
+                   "ciphertexts_total": total, "ciphertexts_per_rank": per,
+                   "parallelism": f"output-ciphertext sharding x{world} + all-gather",
+                   "l2": "plaintexts 3.3 GB per chunk, babies 13.6 GB per 16 ciphertexts: "
+                         "inputs far larger than L2; no flush"},
+        "pt_x_ct_per_s": total * D / (ms / 1e3),
+        "encode_rows_per_s": D / encode_s,
+        "max_abs_error": err,
+        "gather_ms_per_step": gather_ms,
+        "gather_share": gather_ms / ms if ms else None,
+        "roofline": {"bound": "hbm", "kernel": "mac_kernel",
+                     "achieved": mac_bytes / (mac_ms / 1e3) / 1e9, "peak": hbm_peak,
+                     "unit": "GB/s", "frac": mac_bytes / (mac_ms / 1e3) / 1e9 / hbm_peak,
+                     "traffic": traffic, "peak_source": "measured" if peaks else "fallback",
+                     "algorithmic_bytes_per_launch": mac_bytes,
+                     "launch": (f"one chunk: {G0} giants x {B} babies x {per} ciphertexts "
+                                f"at l={level}; {mac_ms:.3f} ms per launch"),
+                     "mac128_per_s": G0 * B * per * 2 * level * N / (mac_ms / 1e3)},
+        "gpu_launches": launches,
+        "e2e": {"value": total / (e2e_ms / 1e3), "unit": unit,
+                "h2d_bytes_per_step": sum(h.numel() * 8 for h in host_in) * world,
+                "d2h_bytes_per_step": host_out.numel() * 8},
+        "clocks": clk,
+    }
 
 
-def main() -> None:
-    a = parse()
-    if a.impl == "reference":
-        run_reference(a)
-        return
+def run_hrotate(a, dev, rank: int, world: int, barrier, max_over_ranks,
+                with_cpu: bool = True) -> dict | None:
+    """HRotate of `a.batch` ciphertexts per rank sharing one key (the CKKS
+    primitive microbench): device-resident key-switches/s, the NTT kernel's
+    roofline, and the same rotations end to end through the C ABI with
+    pinned host buffers.  Returns rank 0's JSON line."""
 
     import torch
-    import torch.distributed as dist
 
-    from easyfhe import core
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-
-    from easyfhe import shard
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local])
-
-    def max_over_ranks(x: float) -> float:
-        return shard.max_over_ranks(x, dev)
-
-    if a.workload == "bootstrap":
-        run_bootstrap(a, dev, rank, world, barrier, max_over_ranks)
-        if world > 1:
-            dist.destroy_process_group()
-        return
-    if a.workload == "linear":
-        run_linear(a, dev, rank, world, barrier, max_over_ranks)
-        if world > 1:
-            dist.destroy_process_group()
-        return
+    from easyfhe import _native, core
 
     params = core.Params.uniform(a.limbs, a.special, a.dnum, bits=50)
     ctx = core.NativeContext(params, dev)
@@ -491,11 +621,6 @@ def main() -> None:
     out = torch.empty_like(ct)
     ws = ctx.workspace(core.lib.b2f_rotate_workspace(ctx.handle, C, l))
     stream = torch.cuda.current_stream()
-
-    # iNTT, ModUp conversion, NTT, inner product, iNTT of the P part, ModDown
-    # conversion, NTT + combine; binary64 with K <= 4 computes the ModDown
-    # conversion inside its NTT (no separate conversion launch)
-    launches_per_rotate = 6 if (ctx.arith == "f64" and a.special <= 4) else 7
 
     # ---- NTT kernel loop (dominant kernel; roofline) ----
     ntt_buf = ct.view(-1, N)  # C*2*l limbs, 768 MiB
@@ -520,28 +645,25 @@ def main() -> None:
     ntt_bfly = ntt_limbs * (N // 2) * 16 / (ntt_ms / 1e3)
     bfly_peak = ctx.butterfly_peak()
     if a.workload == "ntt":
-        if rank == 0:
-            print(json.dumps({"workload": "ntt", "limbs": ntt_limbs, "ms": ntt_ms,
-                              "us_per_limb": ntt_ms * 1e3 / ntt_limbs, "gbs": ntt_gbs,
-                              "arith": ctx.arith,
-                              "butterflies_per_s": ntt_bfly, "butterfly_peak": bfly_peak,
-                              "frac": ntt_bfly / bfly_peak}), flush=True)
-        if world > 1:
-            dist.destroy_process_group()
-        return
+        return {"workload": "ntt", "limbs": ntt_limbs, "ms": ntt_ms,
+                "us_per_limb": ntt_ms * 1e3 / ntt_limbs, "gbs": ntt_gbs, "arith": ctx.arith,
+                "butterflies_per_s": ntt_bfly, "butterfly_peak": bfly_peak,
+                "frac": ntt_bfly / bfly_peak} if rank == 0 else None
 
     # ---- headline: HRotate batch, device-resident ----
     for _ in range(a.warmup):
         ctx.rotate(ct, l, g, key, out, ws)
     torch.cuda.synchronize()
-    clocks = Clocks(local, not a.no_clocks)
+    clocks = Clocks(dev.index or 0, not a.no_clocks)
     barrier()
     torch.cuda.synchronize()
+    n0 = _native.lib.b2f_launch_count()
     e0.record(stream)
     for _ in range(a.steps):
         ctx.rotate(ct, l, g, key, out, ws)
     e1.record(stream)
     torch.cuda.synchronize()
+    launches = (_native.lib.b2f_launch_count() - n0) // a.steps
     barrier()
     clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
@@ -595,7 +717,7 @@ def main() -> None:
     ct_bytes = ct.numel() * 8
 
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and with_cpu:
         try:
             cpu = cpu_oracle_rate(a, a.cpu_sample)
             cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -647,12 +769,154 @@ def main() -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": world * C / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": ct_bytes, "d2h_bytes_per_step": ct_bytes},
-            "gpu_launches": launches_per_rotate * a.steps,
+            "gpu_launches": launches,
             "clocks": clk,
         }
-        print(json.dumps(line), flush=True)
+        return line
+    return None
+
+
+
+
+def layer0_result(warmup: int = 1, repetitions: int = 1) -> dict:
+    """Layer-0 of encrypted Llama-3-8B through the reference's own llama3fhe
+    (its runner's Layer-0 preset, unchanged) on this backend: s/layer from the
+    runner's timed repetition, and the decrypted output against the fp64
+    layer."""
+
+    import llama3_layer
+
+    from easyfhe import _native
+
+    if llama3_layer.reference_root() is None:
+        return {"unavailable": "the reference llama3fhe tree is not installed (baseline/_ref)"}
+    n0 = _native.lib.b2f_launch_count()
+    r = llama3_layer.run_layer0(warmup=warmup, repetitions=repetitions)
+    launches = _native.lib.b2f_launch_count() - n0
+    perf = r["payload"]["performance"]
+    return {
+        "s_per_layer": r["s_per_layer"],
+        "stage_seconds": perf["median_stage_seconds"],
+        "context_keygen_seconds": perf["context_keygen_seconds"],
+        "input_pack_encrypt_seconds": perf["input_pack_encrypt_seconds"],
+        "bootstrap_prepare_seconds": perf["application_bootstrap_prepare_seconds"],
+        "final_decrypt_seconds": perf["final_decrypt_seconds"],
+        "warmup": warmup, "repetitions": repetitions,
+        "cuda_allocator_peak_bytes": perf["cuda_allocator_peak_bytes"],
+        "vs_fp64_exact": r["checks"]["vs_fp64_exact"],
+        "vs_fp64_poly": r["checks"]["vs_fp64_poly"],
+        "native_bootstrap_calls": r["payload"]["runtime"]["native_bootstrap_calls"],
+        "linear_chunks_packed_by_cuda": r["pack_stats"],
+        "gpu_launches_total": launches,
+        "source": ("llama3fhe.application.runner.run, Layer-0 synthetic preset "
+                   "(seed 26081461), unchanged, on this backend"),
+    }
+
+
+def single_gpu_extras(a, dev, barrier, max_over_ranks) -> dict:
+    """At N = 1 the default line also carries the HRotate microbench (with the
+    NTT roofline), the Layer-0 s/layer of the reference's own graph, and the
+    CPU oracle's linear-block rate."""
+
+    import copy
+    import gc
+
+    import torch
+
+    out = {}
+    h = copy.copy(a)
+    h.workload, h.batch = "hrotate", 32
+    try:
+        line = run_hrotate(h, dev, 0, 1, barrier, max_over_ranks, with_cpu=False)
+        out["hrotate"] = {k: line[k] for k in ("metric", "value", "unit", "ms_per_step",
+                                               "config", "roofline", "compute_roofline",
+                                               "keyswitch_hbm_gbs", "e2e", "gpu_launches")}
+    except Exception as exc:  # reported, never fatal to the headline
+        out["hrotate"] = {"error": repr(exc)}
+    gc.collect()
+    torch.cuda.empty_cache()
+    if not a.no_layer:
+        try:
+            out["layer0"] = layer0_result()
+        except Exception as exc:
+            out["layer0"] = {"error": repr(exc)}
+        gc.collect()
+        torch.cuda.empty_cache()
+    try:
+        cpu = linear_cpu_rate()
+        out["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    except Exception as exc:  # the oracle is a reported baseline only
+        out["cpu_baseline"] = {"value": None, "unit": "ciphertexts/s", "cores": 0,
+                               "kind": "port", "sample": f"unavailable: {exc}"}
+    return out
+
+
+def run_layer0(a, world: int) -> dict:
+    """The Layer-0 workload as its own line: seconds per encrypted layer."""
+
+    r = layer0_result(warmup=max(1, min(a.warmup, 2)), repetitions=max(1, min(a.steps, 3)))
+    if "s_per_layer" not in r:
+        return {"metric": "encrypted Llama-3-8B prefill s/layer at seq128", **r}
+    return {"metric": "encrypted Llama-3-8B prefill s/layer at seq128 (Layer-0 preset)",
+            "value": r["s_per_layer"], "unit": "s/layer", "n_gpus": 1,
+            "steps": max(1, min(a.steps, 3)), "warmup": max(1, min(a.warmup, 2)),
+            "ms_per_step": r["s_per_layer"] * 1e3, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+            "config": {"workload": ("one Llama-3-8B decoder layer, seq 128, hidden 4096, "
+                                    "32/8 heads, SwiGLU 14336; logN 16 depth 37 dnum 5 "
+                                    "59/60-bit primes; the reference's graph")},
+            "layer0": r}
+
+
+def main() -> None:
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     if world > 1:
-        dist.destroy_process_group()
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    from easyfhe import shard
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        return shard.max_over_ranks(x, dev)
+
+    try:
+        if a.workload == "bootstrap":
+            run_bootstrap(a, dev, rank, world, barrier, max_over_ranks)
+        elif a.workload == "layer0":
+            line = run_layer0(a, world) if rank == 0 else None
+            if line:
+                print(json.dumps(line), flush=True)
+        elif a.workload in ("hrotate", "ntt"):
+            line = run_hrotate(a, dev, rank, world, barrier, max_over_ranks)
+            if line:
+                print(json.dumps(line), flush=True)
+        else:
+            line = run_linear(a, dev, rank, world, barrier, max_over_ranks)
+            if rank == 0 and world == 1:
+                line.update(single_gpu_extras(a, dev, barrier, max_over_ranks))
+            if line:
+                print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -15,6 +15,9 @@
 
 namespace b2f {
 
+// Counts one kernel launch (relaxed atomic; read by b2f_launch_count).
+void note_launch();
+
 constexpr int kLogN = 16;
 constexpr int kN = 1 << kLogN;
 
@@ -44,8 +47,13 @@ struct NvtxRange {
 };
 #define B2F_RANGE(name) ::b2f::NvtxRange b2f_range_guard_(name)
 
+// Every kernel launch of the library is followed by B2F_LAUNCHED (or, where
+// the launch site cleans up before returning, by note_launch and its own
+// error check): the launch is counted (b2f_launch_count) and a launch error
+// becomes the entry point's status.
 #define B2F_LAUNCHED(what)                                        \
   do {                                                            \
+    ::b2f::note_launch();                                         \
     cudaError_t _e = cudaGetLastError();                          \
     if (_e != cudaSuccess) return ::b2f::cuda_status(_e, what);   \
   } while (0)

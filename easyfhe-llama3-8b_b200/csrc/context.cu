@@ -1,3 +1,4 @@
+#include <atomic>
 // Context creation: RNS primes, NTT twiddle tables, key-switch constants.
 #include <cmath>
 #include <cstdarg>
@@ -333,6 +334,9 @@ static int build_tables(b2f_context *ctx) {
   return B2F_OK;
 }
 
+std::atomic<unsigned long long> g_launch_count{0};
+void note_launch() { g_launch_count.fetch_add(1, std::memory_order_relaxed); }
+
 const LimbJob *job_table(b2f_context *ctx, const std::vector<int> &key,
                          const std::vector<LimbJob> &jobs) {
   std::lock_guard<std::mutex> g(ctx->mu);
@@ -360,6 +364,9 @@ using namespace b2f;
 extern "C" {
 
 const char *b2f_last_error(void) { return g_err; }
+unsigned long long b2f_launch_count(void) {
+  return g_launch_count.load(std::memory_order_relaxed);
+}
 int b2f_abi_version(void) { return 1; }
 
 int b2f_generate_primes(int log_n, int bits, int count, int mode,

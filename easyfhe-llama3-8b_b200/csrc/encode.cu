@@ -339,6 +339,7 @@ int b2f_encode(b2f_context *ctx, const double *values, int num_rows, int slots,
     encode_round_kernel<<<dim3(kN / TPB, limbs, num_rows), TPB, 0, s>>>(
         v, slots, log2i(slots), 1.0 / (double)slots, scale, out, limbs, q_limbs,
         ctx->L, ctx->d_mod);
+    note_launch();
     e = cudaGetLastError();
     if (e != cudaSuccess) rc = cuda_status(e, "encode_round_kernel");
   }
@@ -395,6 +396,7 @@ int b2f_decode(b2f_context *ctx, const uint64_t *pt, int l, int slots,
     decode_gather_kernel<<<(slots + TPB - 1) / TPB, TPB, 0, s>>>(
         coef, use, slots, log2i(slots), scale, reinterpret_cast<double2 *>(values),
         q0, q1, invp);
+    note_launch();
     e = cudaGetLastError();
     if (e != cudaSuccess) rc = cuda_status(e, "decode_gather_kernel");
   }

@@ -212,6 +212,7 @@ int b2f_secret_to_ntt(b2f_context *ctx, const int8_t *s_coeff, uint64_t *s_ntt,
   if (!rc) {
     secret_residue_kernel<<<dim3(kN / TPB, ctx->L + ctx->K), TPB, 0, st>>>(
         d, s_ntt, ctx->d_primes);
+    note_launch();
     e = cudaGetLastError();
     if (e != cudaSuccess) rc = cuda_status(e, "secret_residue_kernel");
   }
@@ -269,6 +270,7 @@ int b2f_keygen_rotation(b2f_context *ctx, const uint64_t *s_ntt, uint64_t galois
   B2F_CUDA(cudaMallocAsync(&s_to, (size_t)np * kN * 8, st));
   permute_kernel<<<dim3(kN / TPB, np), TPB, 0, st>>>(s_ntt, s_to, (uint32_t)ginv);
   int rc = B2F_OK;
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) rc = cuda_status(e, "permute_kernel");
   if (!rc) rc = b2f_keygen_switch(ctx, s_ntt, s_to, seed, (uint32_t)galois, key, st);
@@ -286,6 +288,7 @@ int b2f_keygen_relin(b2f_context *ctx, const uint64_t *s_ntt, uint64_t seed,
   B2F_CUDA(cudaMallocAsync(&s2, (size_t)np * kN * 8, st));
   square_kernel<<<dim3(kN / TPB, np), TPB, 0, st>>>(s_ntt, s2, ctx->d_mod);
   int rc = B2F_OK;
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) rc = cuda_status(e, "square_kernel");
   if (!rc) rc = b2f_keygen_switch(ctx, s2, s_ntt, seed, 0u, key, st);

@@ -89,6 +89,7 @@ _SIGS = {
     "b2f_encode_workspace": (_size, [_vp, _int, _int]),
     "b2f_decode": (_int, [_vp, _vp, _int, _int, _dbl, _vp, _vp, _size, _vp]),
     "b2f_decode_workspace": (_size, [_vp, _int]),
+    "b2f_launch_count": (ctypes.c_ulonglong, []),
     "b2f_pack_diagonals": (_int, [_vp, _vp, _int, _int, _int, _int, _int, _int, _int, _vp,
                                   _vp]),
     "b2f_pack_structured": (_int, [_vp, _vp, _vp, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp,

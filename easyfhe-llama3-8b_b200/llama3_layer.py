@@ -172,6 +172,47 @@ def synthetic_layer(seed: int = 26081461):
     return hidden, weights, approx
 
 
+class ReferenceSession:
+    """The reference's Layer-0 preset resolved as its runner resolves it
+    (``runner.py:128-176``): CKKS config, frozen schedule, layouts, and the
+    context with every rotation key the layer declares
+    (``session._create_context``, ``session.py:24-53``), for driving single
+    reference operators on this backend."""
+
+    def __init__(self, extra_args=()):
+        import_reference()
+        from llama3fhe import Llama3CKKSConfig
+        from llama3fhe.application import args as ref_args
+        from llama3fhe.application import session, settings
+        from llama3fhe.layouts import AttentionPairLayout, FeatureMajorPrefillLayout
+        from llama3fhe.model import Llama3Model
+
+        args = ref_args.resolve_poly_paths(
+            ref_args.build_parser(layer0_preset=True).parse_args(list(extra_args)))
+        self.config = Llama3CKKSConfig.from_json(args.config)
+        resolved = settings.resolve_settings(args, self.config)
+        self.schedule = settings.layer_schedule(args, resolved)
+        self.feature_layout = FeatureMajorPrefillLayout()
+        self.attention_layout = AttentionPairLayout()
+        model = Llama3Model(config=self.config, num_layers=1,
+                            feature_layout=self.feature_layout,
+                            attention_layout=self.attention_layout)
+        self.rotations = model.required_rotations(
+            self.schedule, bootstrap_deep_level_budget=(
+                (3, 3) if self.schedule.softmax_main_deep_bootstrap else None))
+        self.context = session._create_context(self.config, self.rotations)
+
+    def encrypt(self, values: np.ndarray, cur_limbs: int) -> tuple:
+        """Pack [128, 4096] values feature-major and encrypt them at cur_limbs
+        (``session._encrypt_hidden``, ``session.py:56-85``)."""
+
+        from llama3fhe.application import session
+
+        return session._encrypt_hidden(np.asarray(values), context=self.context,
+                                       layout=self.feature_layout,
+                                       input_level=int(self.context.context.L) - int(cur_limbs))
+
+
 # ---------------------------------------------------------------------------
 # the encrypted run
 # ---------------------------------------------------------------------------

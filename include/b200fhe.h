@@ -51,6 +51,10 @@ typedef enum {
 
 /* Message of the last failure on the calling thread ("" if none). */
 const char *b2f_last_error(void);
+/* Kernel launches the library has issued in this process (all contexts,
+ * all threads; a relaxed counter).  No counterpart in the reference:
+ * instrumentation, so a caller can count the launches inside a timed region. */
+unsigned long long b2f_launch_count(void);
 int b2f_abi_version(void);
 
 /* NTT-friendly primes q = 1 mod 2N: mode 0 descending below 2^bits, mode 1

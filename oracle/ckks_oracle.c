@@ -1165,3 +1165,38 @@ void orc_decode(const orc_ctx *c, const uint64_t *in, int l, int slots,
   free(coef);
   free(a);
 }
+
+/* ------------------------------------------------------------------ */
+/* BSGS inner multiply-accumulate (the pt x baby half of                */
+/* hoisted_mac_sum, llama3fhe/operators/linear/operator.py:320-330):    */
+/*   out[c][g] = sum_b pts[g B + b] * babies[c][b]   (mod q_i, limb-wise) */
+/* babies [C][B][2][l][N], pts [G B][l][N], out [C][G][2][l][N].        */
+/* ------------------------------------------------------------------ */
+void orc_bsgs_mac(const orc_ctx *c, const uint64_t *babies, int num_cts,
+                  int baby_count, const uint64_t *pts, int giant_count, int l,
+                  uint64_t *out) {
+  const uint64_t n = c->n;
+  const uint64_t limb = n, ct_words = 2 * (uint64_t)l * n;
+#pragma omp parallel for schedule(dynamic) collapse(2)
+  for (int g = 0; g < giant_count; g++)
+    for (int i = 0; i < l; i++) {
+      const uint64_t q = c->primes[i];
+      for (int ct = 0; ct < num_cts; ct++)
+        for (int p = 0; p < 2; p++) {
+          uint64_t *o = out + ((uint64_t)ct * giant_count + g) * ct_words +
+                        ((uint64_t)p * l + i) * limb;
+          for (uint64_t k = 0; k < n; k++) {
+            u128 acc = 0;
+            for (int b = 0; b < baby_count; b++) {
+              const uint64_t *bb = babies + ((uint64_t)ct * baby_count + b) * ct_words +
+                                   ((uint64_t)p * l + i) * limb;
+              const uint64_t *pt = pts + ((uint64_t)g * baby_count + b) * l * n +
+                                   (uint64_t)i * limb;
+              acc += (u128)bb[k] * pt[k];
+              if ((b & 7) == 7) acc %= q; /* keep the sum below 2^128 */
+            }
+            o[k] = (uint64_t)(acc % q);
+          }
+        }
+    }
+}

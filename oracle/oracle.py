@@ -90,6 +90,8 @@ def lib():
         L.orc_decode.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int,
                                  ctypes.c_double, _dp, _dp]
         L.orc_special_fft.argtypes = [ctypes.c_int, _dp, _dp, ctypes.c_int, ctypes.c_int]
+        L.orc_bsgs_mac.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p,
+                                   ctypes.c_int, ctypes.c_int, _u64p]
         L.orc_mul_plain.argtypes = [ctypes.c_void_p, _u64p, _u64p, ctypes.c_int, ctypes.c_int,
                                     _u64p]
         _lib = L
@@ -302,4 +304,13 @@ class Oracle:
     def mul_plain(self, ct, pt, l: int) -> np.ndarray:
         out = np.zeros((2, l, self.n), dtype=np.uint64)
         lib().orc_mul_plain(self._h, _p(_u64(ct)), _p(_u64(pt)), l, 0, _p(out))
+        return out
+
+    def bsgs_mac(self, babies, num_cts: int, baby_count: int, pts, giant_count: int,
+                 l: int) -> np.ndarray:
+        """[C, G, 2, l, N]: out[c][g] = sum_b pts[g B + b] * babies[c][b]."""
+
+        out = np.zeros((num_cts, giant_count, 2, l, self.n), dtype=np.uint64)
+        lib().orc_bsgs_mac(self._h, _p(_u64(babies)), num_cts, baby_count, _p(_u64(pts)),
+                           giant_count, l, _p(out))
         return out

@@ -209,3 +209,25 @@ def test_secret_sampler(oracle_mod):
     assert int(np.count_nonzero(s)) == 192 and set(np.unique(s)) <= {-1, 0, 1}
     u = oracle_mod.sample_secret(16, 3, 0)
     assert set(np.unique(u)) == {-1, 0, 1}
+
+
+def test_oracle_bsgs_mac_equals_exact_sum(oracle_mod):
+    """orc_bsgs_mac (the CPU baseline of the linear block) against exact
+    integer sums: out[c][g] = sum_b pts[g B + b] * babies[c][b] mod q."""
+
+    O = oracle_mod
+    primes = O.gen_primes(10, 60, 3)
+    o = O.Oracle(10, primes[:2], primes[2:], 1)
+    n, l, C, B, G = 1 << 10, 2, 2, 9, 3
+    rng = np.random.default_rng(17)
+    qs = np.array(primes[:l], dtype=object)
+    babies = np.stack([rng.integers(0, q, (C, B, 2, n), dtype=np.uint64) for q in primes[:l]],
+                      axis=3)
+    pts = np.stack([rng.integers(0, q, (G * B, n), dtype=np.uint64) for q in primes[:l]],
+                   axis=1)
+    got = o.bsgs_mac(babies, C, B, pts, G, l)
+    for c in range(C):
+        for g in range(G):
+            want = sum(babies[c, b].astype(object) * pts[g * B + b].astype(object)[None]
+                       for b in range(B)) % qs[None, :, None]
+            assert np.array_equal(got[c, g], want.astype(np.uint64))
