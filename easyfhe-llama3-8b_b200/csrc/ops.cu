@@ -79,16 +79,17 @@ __global__ void __launch_bounds__(TPB) tensor_kernel(
   out[o + 2 * lim] = mul_mod(a1, b1, M);
 }
 
-// grid (N/TPB, l, polys)
+// grid (N/TPB, l, polys); limb i is prime i below ql, prime L + i - ql after
+// it (the extended basis Q_ql u P; ql = l outside it)
 __global__ void __launch_bounds__(TPB) elementwise_kernel(
     int op, const uint64_t *__restrict__ a, const uint64_t *__restrict__ b,
     uint64_t *__restrict__ out, const Mod *__restrict__ mods, int l,
-    int b_polys) {
+    int b_polys, int ql, int L) {
   const int n = blockIdx.x * TPB + threadIdx.x;
   const int i = blockIdx.y, p = blockIdx.z;
   const size_t ia = ((size_t)p * l + i) * kN + n;
   const size_t ib = ((size_t)(b_polys == 1 ? 0 : p) * l + i) * kN + n;
-  const Mod M = mods[i];
+  const Mod M = mods[i < ql ? i : L + i - ql];
   const uint64_t x = a[ia], y = b[ib];
   uint64_t r;
   if (op == 0)
@@ -165,16 +166,18 @@ __global__ void __launch_bounds__(TPB) linear_combination_kernel(
 // of a batch are the fastest grid axis, so they read each plaintext tile
 // while it is in L2 and the plaintext rows stream from HBM once per batch.
 // Up to GMAX giants per launch; babies are taken two at a time with every
-// load of the pair issued before its multiplies.
+// load of the pair issued before its multiplies.  l is the limbs of the
+// layout; limb i is prime i for i < ql and prime L + i - ql after it (the
+// extended basis Q_ql u P: ql = l outside it).
 __global__ void __launch_bounds__(TPB) mac_kernel(
     const uint64_t *__restrict__ babies, int baby_count,
     const uint64_t *__restrict__ pts, int g0, int G, int l,
     uint64_t *__restrict__ out, int out_giants, int giant_major,
-    const Mod *__restrict__ mods) {
+    const Mod *__restrict__ mods, int ql, int L) {
   constexpr int BU = 2;
   const int n = blockIdx.y * TPB + threadIdx.x;
   const int i = blockIdx.z, ct = blockIdx.x, cts = gridDim.x;
-  const Mod M = mods[i];
+  const Mod M = mods[i < ql ? i : L + i - ql];
   const size_t limb = (size_t)i * kN + n;
   const size_t ct_words = 2 * (size_t)l * kN, pt_words = (size_t)l * kN;
   const uint64_t *bb = babies + (size_t)ct * baby_count * ct_words + limb;
@@ -257,12 +260,13 @@ __global__ void __launch_bounds__(TPB) pairwise_mac_kernel(
 
 int launch_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
                const uint64_t *pts, int giant_count, int l, uint64_t *out,
-               int cts, cudaStream_t s, int giant_major = 0) {
+               int cts, cudaStream_t s, int giant_major = 0, int ql = -1) {
+  if (ql < 0) ql = l;
   for (int g0 = 0; g0 < giant_count; g0 += GMAX) {
     const int G = std::min(GMAX, giant_count - g0);
     mac_kernel<<<dim3(cts, kN / TPB, l), TPB, 0, s>>>(
         babies, baby_count, pts, g0, G, l, out, giant_count, giant_major,
-        ctx->d_mod);
+        ctx->d_mod, ql, ctx->L);
     B2F_LAUNCHED("mac_kernel");
   }
   return B2F_OK;
@@ -358,7 +362,22 @@ int b2f_elementwise(b2f_context *ctx, int op, const uint64_t *a,
                 "b2f_elementwise: b_polys must be 1 or num_polys");
   if (num_polys <= 0) return B2F_OK;
   elementwise_kernel<<<dim3(kN / TPB, l, num_polys), TPB, 0, (cudaStream_t)stream>>>(
-      op, a, b, out, ctx->d_mod, l, b_polys);
+      op, a, b, out, ctx->d_mod, l, b_polys, l, ctx->L);
+  B2F_LAUNCHED("elementwise_kernel");
+  return B2F_OK;
+}
+
+int b2f_elementwise_ext(b2f_context *ctx, int op, const uint64_t *a,
+                        const uint64_t *b, uint64_t *out, int num_polys, int q_limbs,
+                        int p_limbs, void *stream) {
+  B2F_CHECK_ARG(ctx && a && b && out, "b2f_elementwise_ext: null argument");
+  B2F_CHECK_ARG(op >= 0 && op <= 2, "b2f_elementwise_ext: unknown op %d", op);
+  B2F_CHECK_ARG(q_limbs >= 1 && q_limbs <= ctx->L && p_limbs >= 0 && p_limbs <= ctx->K,
+                "b2f_elementwise_ext: bad limbs q=%d p=%d", q_limbs, p_limbs);
+  if (num_polys <= 0) return B2F_OK;
+  const int l = q_limbs + p_limbs;
+  elementwise_kernel<<<dim3(kN / TPB, l, num_polys), TPB, 0, (cudaStream_t)stream>>>(
+      op, a, b, out, ctx->d_mod, l, num_polys, q_limbs, ctx->L);
   B2F_LAUNCHED("elementwise_kernel");
   return B2F_OK;
 }
@@ -457,6 +476,20 @@ int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
   if (!num_cts) return B2F_OK;
   return launch_mac(ctx, babies, baby_count, pts, giant_count, l, out, num_cts,
                     (cudaStream_t)stream);
+}
+
+int b2f_mac_ext(b2f_context *ctx, const uint64_t *babies, int baby_count,
+                const uint64_t *pts, int giant_count, int q_limbs, int p_limbs,
+                uint64_t *out, int num_cts, void *stream) {
+  B2F_RANGE("b2f_mac_ext");
+  B2F_CHECK_ARG(ctx && babies && pts && out, "b2f_mac_ext: null argument");
+  B2F_CHECK_ARG(q_limbs >= 1 && q_limbs <= ctx->L && p_limbs >= 0 && p_limbs <= ctx->K,
+                "b2f_mac_ext: bad limbs q=%d p=%d", q_limbs, p_limbs);
+  B2F_CHECK_ARG(baby_count >= 1 && giant_count >= 1 && num_cts >= 0,
+                "b2f_mac_ext: bad counts");
+  if (!num_cts) return B2F_OK;
+  return launch_mac(ctx, babies, baby_count, pts, giant_count, q_limbs + p_limbs, out,
+                    num_cts, (cudaStream_t)stream, 0, q_limbs);
 }
 
 int b2f_pairwise_mac(b2f_context *ctx, const uint64_t *cts, const uint64_t *pts,

@@ -66,6 +66,7 @@ _SIGS = {
     "b2f_rescale_noalloc": (_int, [_vp, _vp, _vp, _int, _int, _vp]),
     "b2f_modraise": (_int, [_vp, _vp, _int, _int, _vp, _vp]),
     "b2f_drop_limbs": (_int, [_vp, _vp, _vp, _int, _int, _int, _vp]),
+    "b2f_elementwise_ext": (_int, [_vp, _int, _vp, _vp, _vp, _int, _int, _int, _vp]),
     "b2f_elementwise": (_int, [_vp, _int, _vp, _vp, _vp, _int, _int, _int, _vp]),
     "b2f_mul_i": (_int, [_vp, _vp, _vp, _int, _int, _int, _vp]),
     "b2f_scalar_op": (_int, [_vp, _vp, _vp, _int, _int, _vp, _vp, _int, _vp]),
@@ -85,6 +86,7 @@ _SIGS = {
     "b2f_bsgs_mac": (_int, [_vp, _vp, _int, _vp, _int, _int, _u64, _vp, _vp, _vp, _size,
                             _vp]),
     "b2f_mac": (_int, [_vp, _vp, _int, _vp, _int, _int, _vp, _int, _vp]),
+    "b2f_mac_ext": (_int, [_vp, _vp, _int, _vp, _int, _int, _int, _vp, _int, _vp]),
     "b2f_encode": (_int, [_vp, _vp, _int, _int, _dbl, _int, _int, _vp, _vp, _size, _vp]),
     "b2f_encode_workspace": (_size, [_vp, _int, _int]),
     "b2f_decode": (_int, [_vp, _vp, _int, _int, _dbl, _vp, _vp, _size, _vp]),

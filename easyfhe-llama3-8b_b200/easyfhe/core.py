@@ -380,6 +380,25 @@ class NativeContext:
              _ptr(out), num_cts, _stream())
         return out
 
+    def mac_ext(self, babies: torch.Tensor, baby_count: int, pts: torch.Tensor,
+                giant_count: int, q_limbs: int, num_cts: int = 1) -> torch.Tensor:
+        """[num_cts, G, 2, q_limbs + K, N] over the extended basis."""
+
+        out = self.empty(num_cts, giant_count, 2, q_limbs + self.K)
+        call("b2f_mac_ext", self.handle, _ptr(babies), baby_count, _ptr(pts), giant_count,
+             q_limbs, self.K, _ptr(out), num_cts, _stream())
+        return out
+
+    def elementwise_ext(self, op: int, a: torch.Tensor, b: torch.Tensor, num_polys: int,
+                        q_limbs: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Limb-wise op on polys over Q_{q_limbs} u P."""
+
+        if out is None:
+            out = torch.empty_like(a)
+        call("b2f_elementwise_ext", self.handle, op, _ptr(a), _ptr(b), _ptr(out), num_polys,
+             q_limbs, self.K, _stream())
+        return out
+
     def bsgs_mac(self, babies: torch.Tensor, baby_count: int, pts: torch.Tensor,
                  giant_count: int, l: int, giant_galois: int,
                  giant_key: torch.Tensor | None, num_cts: int = 1) -> torch.Tensor:

@@ -754,74 +754,174 @@ def homo_mul_relin_rescale_postop(left: Ciphertext, right: Ciphertext, context,
 class BabyRotations(tuple):
     """Hoisted baby rotations of one ciphertext: block 0 is a Ciphertext batch
     [B, 2, l, N] (baby b = rotation by baby_offsets[b]); for a batch of C
-    ciphertexts it is [C * B, 2, l, N], ciphertext-major.  Iterable like the
-    reference's block tuple (llama3fhe/operators/linear/operator.py:119-122)."""
+    ciphertexts it is [C * B, 2, l, N], ciphertext-major.  With an extended
+    strategy the block is in Q_l u P ([.., 2, l + K, N], P times the
+    rotation, before ModDown).  Iterable like the reference's block tuple
+    (llama3fhe/operators/linear/operator.py:119-122)."""
 
     offsets: tuple[int, ...] = ()
     cts: int = 1
+    strategy: str = "normal"
+
+
+HOIST_STRATEGIES = ("normal", "ext_normal", "ext_double_hoist")
+
+
+def _strategy(strategy) -> str:
+    """The reference's hoist strategies (llama3fhe/operators/linear/config.py:9)."""
+
+    s = str(strategy).lower()
+    if s not in HOIST_STRATEGIES:
+        raise ValueError(f"unknown hoist strategy {strategy!r}; expected one of "
+                         f"{', '.join(HOIST_STRATEGIES)}")
+    return s
+
+
+def _baby_blocks(offsets: tuple[int, ...], anchor: int) -> list[tuple[int, int]]:
+    """(start, width) blocks of the babies: one block, or blocks of `anchor`
+    babies when 2 <= anchor < B (llama3fhe/operators/linear/config.py:207-240).
+    Anchored blocks need arithmetic offsets b * step."""
+
+    B = len(offsets)
+    if not (int(anchor) >= 2 and B > int(anchor)):
+        return [(0, B)]
+    step = offsets[1] - offsets[0] if B > 1 else 0
+    if any(offsets[b] != offsets[0] + b * step for b in range(B)):
+        raise ValueError("baby_anchor_step needs baby offsets b * step")
+    return [(start, min(int(anchor), B - start)) for start in range(0, B, int(anchor))]
+
+
+def _hoisted_block(ct: Ciphertext, rel: tuple[int, ...], ext: bool, ctx) -> torch.Tensor:
+    """Hoisted rotations of ct by `rel` (one ModUp): [C, n, 2, l(+K), N]."""
+
+    l = _limbs(ct)
+    nat = ctx.native
+    gal, keys = [], []
+    for off in rel:
+        g = galois_element(off, ctx.logN)
+        gal.append(g)
+        keys.append(None if g == 1 else ctx.rotation_key(off, l)[1])
+    C = ct.batch_size
+    if not ext:
+        mod = nat.modup(ct.data, l, C) if any(g != 1 for g in gal) else None
+        out = nat.rotate_hoisted(ct.data, l, mod, gal, keys, num_cts=C)
+        return out.reshape(C, len(rel), 2, l, -1)
+    items = [ct.data] if C == 1 else [ct.data[c] for c in range(C)]
+    outs = []
+    for d in items:
+        mod = nat.modup(d, l) if any(g != 1 for g in gal) else None
+        outs.append(nat.rotate_hoisted_ext(d, l, mod, gal, keys))
+    return torch.stack(outs)
 
 
 def prepare_hoisted_baby_rotations(ct: Ciphertext, baby_offsets, context,
                                    strategy: str = "normal",
                                    baby_anchor_step: int = -1) -> BabyRotations:
-    """One ModUp of c1, then one key inner product + ModDown per baby offset
-    (llama3fhe/operators/linear/operator.py:105-111)."""
+    """Baby rotations of ct by every baby offset (llama3fhe/operators/linear/
+    operator.py:105-111).  One block: one ModUp of c1 and one key inner
+    product (+ ModDown) per offset.  With 2 <= baby_anchor_step < B, blocks of
+    baby_anchor_step babies, each hoisted from an anchor that the one anchor
+    key (baby_anchor_step * step) reaches from the previous anchor
+    (llama3fhe/operators/linear/config.py:50-57, 207-233).  The extended
+    strategies leave the babies in Q_l u P for hoisted_mac_sum."""
 
     ctx = _ctx_of(context)
+    s = _strategy(strategy)
+    ext = s != "normal"
     offsets = tuple(int(v) for v in baby_offsets)
-    l = _limbs(ct)
-    nat = ctx.native
-    gal, keys = [], []
-    for off in offsets:
-        g = galois_element(off, ctx.logN)
-        gal.append(g)
-        keys.append(None if g == 1 else ctx.rotation_key(off, l)[1])
     C = ct.batch_size
-    ext = nat.modup(ct.data, l, C) if any(g != 1 for g in gal) else None
-    out = nat.rotate_hoisted(ct.data, l, ext, gal, keys, num_cts=C)
-    # a ciphertext batch keeps its babies ciphertext-major: [C * B, 2, l, N]
-    block = Ciphertext(out.reshape(-1, 2, l, out.shape[-1]) if C > 1 else out, ct.state,
-                       ct.slots, ctx)
+    blocks = _baby_blocks(offsets, int(baby_anchor_step))
+    parts, anchor = [], ct
+    for k, (start, width) in enumerate(blocks):
+        if k:
+            anchor = homo_rotate(anchor, offsets[start] - offsets[blocks[k - 1][0]], ctx)
+        rel = tuple(offsets[start + b] - offsets[start] + offsets[0] for b in range(width))
+        parts.append(_hoisted_block(anchor, rel, ext, ctx))
+    data = parts[0] if len(parts) == 1 else torch.cat(parts, dim=1)
+    l = _limbs(ct)
+    # a ciphertext batch keeps its babies ciphertext-major: [C * B, 2, l(+K), N]
+    data = data.reshape(C * len(offsets), 2, data.shape[-2], data.shape[-1])
+    block = Ciphertext(data, ct.state, ct.slots, ctx, is_ext=ext)
     babies = BabyRotations((block,))
     babies.offsets = offsets
     babies.cts = C
+    babies.strategy = s
     return babies
 
 
 def hoisted_mac_sum(ct: Ciphertext, baby_offsets, plaintexts: Plaintext, giant_offset: int,
                     giant_count: int, context, strategy: str = "normal",
                     baby_anchor_step: int = -1, baby_rotations=None) -> Ciphertext:
-    """sum_{g<G} rot_{g*giant_offset}(sum_b pt[g*B+b] * rot_{baby_offsets[b]}(ct)),
-    Horner over the giants with the one giant key
+    """sum_{g<G} rot_{g*giant_offset}(sum_b pt[g*B+b] * rot_{baby_offsets[b]}(ct))
     (llama3fhe/operators/linear/operator.py:320-330, transform.py:108-116).
-    The result is at the input level with scale degree 2; the caller rescales."""
+    The result is at the input level with scale degree 2; the caller rescales.
+
+    strategy (llama3fhe/operators/linear/config.py:9, 286-305):
+      normal           babies and MAC in Q_l; Horner over the giants with the
+                       one giant key;
+      ext_normal       babies left in Q_l u P, plaintexts encoded there
+                       (is_ext), MAC over Q_l u P, one ModDown per giant, then
+                       the same Horner chain;
+      ext_double_hoist as ext_normal, but every giant sum but the first is
+                       ModDown'ed, rotated by g * giant_offset with its own
+                       key into Q_l u P, and the sum is ModDown'ed once."""
 
     ctx = _ctx_of(context)
+    s = _strategy(strategy)
+    ext = s != "normal"
     offsets = tuple(int(v) for v in baby_offsets)
     B, G = len(offsets), int(giant_count)
     l = _limbs(ct)
     if baby_rotations is None:
-        baby_rotations = prepare_hoisted_baby_rotations(ct, offsets, ctx, strategy,
-                                                        baby_anchor_step)
+        baby_rotations = prepare_hoisted_baby_rotations(ct, offsets, ctx, s, baby_anchor_step)
     block = tuple(baby_rotations)[0]
     if int(block.state.cur_limbs) != l:
         raise ValueError("baby rotations were prepared at a different level")
+    if bool(block.is_ext) != ext:
+        raise ValueError(f"baby rotations were prepared for a {'n extended' if block.is_ext else ' normal'} "
+                         f"strategy, hoisted_mac_sum called with {s!r}")
     C = ct.batch_size
     if block.batch_size != C * B:
         raise ValueError(f"{block.batch_size} baby rotations for {C} ciphertexts x {B} "
                          "offsets")
     if plaintexts.rows < G * B:
         raise ValueError(f"{plaintexts.rows} plaintext rows < giants*babies = {G * B}")
-    pts = plaintexts.q_part(l)
-    if G > 1:
-        gg, gkey = ctx.rotation_key(int(giant_offset), l)
-    else:
-        gg, gkey = 1, None
-    out = ctx.native.bsgs_mac(block.data, B, pts, G, l, gg, gkey, num_cts=C)
     state = ct.state.replace(
         scale_degree=int(ct.state.scale_degree) + int(plaintexts.state.scale_degree),
         scaling_factor=float(ct.state.scaling_factor) * float(plaintexts.state.scaling_factor))
-    return Ciphertext(out, state, ct.slots, ctx)
+    if not ext:
+        pts = plaintexts.q_part(l)
+        if G > 1:
+            gg, gkey = ctx.rotation_key(int(giant_offset), l)
+        else:
+            gg, gkey = 1, None
+        out = ctx.native.bsgs_mac(block.data, B, pts, G, l, gg, gkey, num_cts=C)
+        return Ciphertext(out, state, ct.slots, ctx)
+    if not plaintexts.is_ext or int(plaintexts.state.cur_limbs) != l:
+        raise ValueError(f"strategy {s!r} needs plaintexts encoded at the ciphertext's level "
+                         "in the extended basis (ConstantBundle.plaintext(is_ext=True))")
+    K = ctx.K
+    pts = plaintexts.cv[0]
+    inner = ctx.native.mac_ext(block.data, B, pts, G, l, num_cts=C)  # [C, G, 2, l+K, N]
+    n = inner.shape[-1]
+    shape = (2, l, n) if C == 1 else (C, 2, l, n)
+
+    def giant(g: int) -> Ciphertext:  # ModDown of giant g's sum, all ciphertexts
+        d = ctx.native.moddown_ext(inner[:, g].contiguous(), C, l)
+        return Ciphertext(d.view(shape), state, ct.slots, ctx)
+
+    if s == "ext_normal":
+        acc = giant(G - 1)
+        for g in range(G - 2, -1, -1):
+            acc = homo_add(homo_rotate(acc, int(giant_offset), ctx), giant(g), ctx)
+        return acc
+    # ext_double_hoist: sum_g P rot_{g off}(giant g) in Q_l u P, one ModDown
+    acc = inner[:, 0].contiguous()  # P * giant 0, as the MAC left it
+    for g in range(1, G):
+        r = _hoisted_block(giant(g), (g * int(giant_offset),), True, ctx)[:, 0]
+        ctx.native.elementwise_ext(0, acc, r.contiguous(), 2 * C, l, out=acc)
+    out = ctx.native.moddown_ext(acc, C, l)
+    return Ciphertext(out.view(shape), state, ct.slots, ctx)
 
 
 # ---------------------------------------------------------------------------

@@ -224,6 +224,14 @@ int b2f_drop_limbs(b2f_context *ctx, const uint64_t *in, uint64_t *out,
 int b2f_elementwise(b2f_context *ctx, int op, const uint64_t *a,
                     const uint64_t *b, uint64_t *out, int num_polys, int l,
                     int b_polys, void *stream);
+/* The same limb-wise op (b with num_polys polys) over the extended basis
+ * Q_{q_limbs} u P: polys of q_limbs + p_limbs limbs, limb t prime t below
+ * q_limbs and prime L + t - q_limbs after it.  Sums of extended ciphertexts
+ * before one ModDown (hoisted_mac_sum, strategy="ext_double_hoist",
+ * llama3fhe/operators/linear/config.py:295-300). */
+int b2f_elementwise_ext(b2f_context *ctx, int op, const uint64_t *a,
+                        const uint64_t *b, uint64_t *out, int num_polys, int q_limbs,
+                        int p_limbs, void *stream);
 /* out = a * X^(N/2) (multiply every slot by i, or -i when negative):
  * fhe.homo_mul_i (llama3fhe/operators/linear/complex.py:22). */
 int b2f_mul_i(b2f_context *ctx, const uint64_t *a, uint64_t *out,
@@ -289,6 +297,16 @@ int b2f_pairwise_mac(b2f_context *ctx, const uint64_t *cts, const uint64_t *pts,
 int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
             const uint64_t *pts, int giant_count, int l, uint64_t *out,
             int num_cts, void *stream);
+/* The same over the extended basis Q_{q_limbs} u P: babies [num_cts][B][2]
+ * [q_limbs + p_limbs][N] and plaintext rows [G*B][q_limbs + p_limbs][N]
+ * (limb t is prime t below q_limbs, prime L + t - q_limbs after), out
+ * [num_cts][G][2][q_limbs + p_limbs][N].  The multiply-accumulate of
+ * fhe.hoisted_mac_sum(..., strategy="ext_normal" | "ext_double_hoist")
+ * (llama3fhe/operators/transform.py:108-116, operators/linear/config.py:9,
+ * 286-305): babies left in Q u P by the key switch, one ModDown per giant. */
+int b2f_mac_ext(b2f_context *ctx, const uint64_t *babies, int baby_count,
+                const uint64_t *pts, int giant_count, int q_limbs, int p_limbs,
+                uint64_t *out, int num_cts, void *stream);
 
 /* ---- calibration (no reference counterpart) ----
  * Rate of the NTT's lazy Shoup butterfly from registers alone (every SM

@@ -1173,14 +1173,15 @@ void orc_decode(const orc_ctx *c, const uint64_t *in, int l, int slots,
 /* babies [C][B][2][l][N], pts [G B][l][N], out [C][G][2][l][N].        */
 /* ------------------------------------------------------------------ */
 void orc_bsgs_mac(const orc_ctx *c, const uint64_t *babies, int num_cts,
-                  int baby_count, const uint64_t *pts, int giant_count, int l,
-                  uint64_t *out) {
+                  int baby_count, const uint64_t *pts, int giant_count, int q_limbs,
+                  int p_limbs, uint64_t *out) {
   const uint64_t n = c->n;
+  const int l = q_limbs + p_limbs; /* limb t: prime t, or P prime t - q_limbs */
   const uint64_t limb = n, ct_words = 2 * (uint64_t)l * n;
 #pragma omp parallel for schedule(dynamic) collapse(2)
   for (int g = 0; g < giant_count; g++)
     for (int i = 0; i < l; i++) {
-      const uint64_t q = c->primes[i];
+      const uint64_t q = c->primes[i < q_limbs ? i : c->L + i - q_limbs];
       for (int ct = 0; ct < num_cts; ct++)
         for (int p = 0; p < 2; p++) {
           uint64_t *o = out + ((uint64_t)ct * giant_count + g) * ct_words +

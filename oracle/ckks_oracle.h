@@ -129,8 +129,8 @@ void orc_special_fft(int log_n, double *re, double *im, int slots, int inverse);
 /* out[c][g] = sum_b pts[g B + b] * babies[c][b] (the inner multiply-accumulate
  * of a BSGS linear, llama3fhe/operators/linear/operator.py:320-330). */
 void orc_bsgs_mac(const orc_ctx *ctx, const uint64_t *babies, int num_cts,
-                  int baby_count, const uint64_t *pts, int giant_count, int l,
-                  uint64_t *out);
+                  int baby_count, const uint64_t *pts, int giant_count, int q_limbs,
+                  int p_limbs, uint64_t *out);
 void orc_mul_plain(const orc_ctx *ctx, const uint64_t *ct, const uint64_t *pt,
                    int l, int q_limbs_pt_stride, uint64_t *out);
 

@@ -91,7 +91,7 @@ def lib():
                                  ctypes.c_double, _dp, _dp]
         L.orc_special_fft.argtypes = [ctypes.c_int, _dp, _dp, ctypes.c_int, ctypes.c_int]
         L.orc_bsgs_mac.argtypes = [ctypes.c_void_p, _u64p, ctypes.c_int, ctypes.c_int, _u64p,
-                                   ctypes.c_int, ctypes.c_int, _u64p]
+                                   ctypes.c_int, ctypes.c_int, ctypes.c_int, _u64p]
         L.orc_mul_plain.argtypes = [ctypes.c_void_p, _u64p, _u64p, ctypes.c_int, ctypes.c_int,
                                     _u64p]
         _lib = L
@@ -307,10 +307,11 @@ class Oracle:
         return out
 
     def bsgs_mac(self, babies, num_cts: int, baby_count: int, pts, giant_count: int,
-                 l: int) -> np.ndarray:
-        """[C, G, 2, l, N]: out[c][g] = sum_b pts[g B + b] * babies[c][b]."""
+                 l: int, p_limbs: int = 0) -> np.ndarray:
+        """[C, G, 2, l + p_limbs, N]: out[c][g] = sum_b pts[g B + b] * babies[c][b]
+        over Q_l (u P when p_limbs > 0)."""
 
-        out = np.zeros((num_cts, giant_count, 2, l, self.n), dtype=np.uint64)
+        out = np.zeros((num_cts, giant_count, 2, l + p_limbs, self.n), dtype=np.uint64)
         lib().orc_bsgs_mac(self._h, _p(_u64(babies)), num_cts, baby_count, _p(_u64(pts)),
-                           giant_count, l, _p(out))
+                           giant_count, l, p_limbs, _p(out))
         return out
