@@ -58,6 +58,9 @@ def parse():
                          "microbench; ntt: only the NTT kernel loop (for profiling); "
                          "bootstrap: full-slot bootstrapping; layer0: one encrypted "
                          "decoder layer through the reference's graph")
+    ap.add_argument("--layer-params", action="store_true",
+                    help="hrotate/ntt: the layer's chain (depth 37, dnum 5, 59/60-bit "
+                         "primes, K = 8) instead of 50-bit primes; --limbs picks the level")
     ap.add_argument("--no-layer", action="store_true",
                     help="skip the Layer-0 run the default line carries at N = 1")
     ap.add_argument("--no-clocks", action="store_true")
@@ -77,6 +80,15 @@ def parse():
 
 
 def config(a) -> dict:
+    if getattr(a, "layer_params", False):
+        return {
+            "workload": (f"HRotate N=2^16 at l={a.limbs} of the layer chain (depth 37, dnum 5, "
+                         f"59/60-bit primes, K=8 special), batch={a.batch} ciphertexts/rank, "
+                         "shared key"),
+            "log_n": 16, "limbs": a.limbs, "dnum": 5, "special_primes": 8,
+            "batch_per_rank": a.batch, "rotation": a.rotation,
+            "l2": "inputs larger than L2; no flush",
+        }
     return {
         "workload": (f"HRotate N=2^16 l={a.limbs} 50-bit primes dnum={a.dnum} "
                      f"K={a.special} batch={a.batch} ciphertexts/rank, shared key"),
@@ -86,11 +98,11 @@ def config(a) -> dict:
     }
 
 
-def algorithmic_mib(a) -> float:
-    """C * 2l MiB (ciphertexts in + out) + beta (l + K) MiB (key read once)."""
+def algorithmic_mib(l: int, batch: int, alpha: int, K: int) -> float:
+    """C * 2l MiB (ciphertexts in + out) + beta (l + K) MiB (key read once),
+    beta = ceil(l / alpha) digits."""
 
-    beta = -(-a.limbs // -(-a.limbs // a.dnum))
-    return a.batch * 2 * a.limbs + beta * (a.limbs + a.special)
+    return batch * 2 * l + (-(-l // alpha)) * (l + K)
 
 
 class Clocks:
@@ -606,17 +618,22 @@ def run_hrotate(a, dev, rank: int, world: int, barrier, max_over_ranks,
 
     from easyfhe import _native, core
 
-    params = core.Params.uniform(a.limbs, a.special, a.dnum, bits=50)
+    if getattr(a, "layer_params", False):  # the layer chain (assets/feature_major.json)
+        params = core.Params.from_depth(37, 16, 5, 59, 60)
+    else:
+        params = core.Params.uniform(a.limbs, a.special, a.dnum, bits=50)
     ctx = core.NativeContext(params, dev)
     ctx.set_arith(a.arith)
     l, C = a.limbs, a.batch
+    if not 1 <= l <= params.L:
+        raise SystemExit(f"--limbs {l} outside the chain's 1..{params.L}")
     s_ntt = ctx.secret_to_ntt(core.sample_secret(2024 + rank, 192))
     g = core.galois_element(a.rotation)
     key = ctx.keygen_rotation(s_ntt, g, seed=7 + rank)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
     ct = torch.empty(C, 2, l, N, dtype=torch.int64, device=dev)
-    for i, q in enumerate(params.q):
+    for i, q in enumerate(params.q[:l]):
         ct[:, :, i].random_(0, q, generator=gen)
     out = torch.empty_like(ct)
     ws = ctx.workspace(core.lib.b2f_rotate_workspace(ctx.handle, C, l))
@@ -737,7 +754,11 @@ def run_hrotate(a, dev, rank: int, world: int, barrier, max_over_ranks,
     if tpath.exists():
         try:
             t = json.loads(tpath.read_text())
-            traffic = float(t["bytes_per_limb"]) * ntt_limbs
+            # the capture is of one arithmetic's kernel: use it for that one only
+            want = "FpArith" if ctx.arith == "f64" else "IntArith"
+            for cap in t.get("captures", [t]):
+                if want in cap["kernel"]:
+                    traffic = float(cap["bytes_per_limb"]) * ntt_limbs
         except Exception:
             traffic = None
 
@@ -765,7 +786,8 @@ def run_hrotate(a, dev, rank: int, world: int, barrier, max_over_ranks,
             },
             "arith": ctx.arith,
             "ntt_hbm_gbs": ntt_gbs,
-            "keyswitch_hbm_gbs": algorithmic_mib(a) * MiB / (ms / 1e3) / 1e9,
+            "keyswitch_hbm_gbs": (algorithmic_mib(l, C, ctx.alpha, ctx.K) * MiB
+                                  / (ms / 1e3) / 1e9),
             "cpu_baseline": cpu,
             "e2e": {"value": world * C / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": ct_bytes, "d2h_bytes_per_step": ct_bytes},
@@ -835,6 +857,22 @@ def single_gpu_extras(a, dev, barrier, max_over_ranks) -> dict:
         out["hrotate"] = {"error": repr(exc)}
     gc.collect()
     torch.cuda.empty_cache()
+    # the same at the layer's parameters (integer arithmetic: 59/60-bit primes)
+    out["hrotate_layer_params"] = []
+    for limbs in (13, 38):
+        h = copy.copy(a)
+        h.workload, h.batch, h.limbs, h.layer_params = "hrotate", 16, limbs, True
+        h.steps, h.warmup = min(a.steps, 20), min(a.warmup, 3)
+        try:
+            line = run_hrotate(h, dev, 0, 1, barrier, max_over_ranks, with_cpu=False)
+            out["hrotate_layer_params"].append(
+                {k: line[k] for k in ("value", "unit", "ms_per_step", "config", "roofline",
+                                      "compute_roofline", "keyswitch_hbm_gbs", "arith",
+                                      "gpu_launches")})
+        except Exception as exc:
+            out["hrotate_layer_params"].append({"limbs": limbs, "error": repr(exc)})
+        gc.collect()
+        torch.cuda.empty_cache()
     if not a.no_layer:
         try:
             out["layer0"] = layer0_result()

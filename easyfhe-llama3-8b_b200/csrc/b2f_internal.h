@@ -188,11 +188,19 @@ struct ItemKeys;
 // With z (binary64 contexts, K <= 4) the transform computes its own input,
 // the conversion sum_k z_k [Phat_k]_{q_i} of the scaled P limbs l .. l+K-1 of
 // z [item][2][lk][N] (conv is then not read).
+// A post-operation folded into that epilogue (the Paterson-Stockmeyer step
+// of homo_mul_relin_rescale_postop): the result times 2 (dbl), add_b
+// subtracted instead of added (add_neg), and cadd[i] added to poly 0.
+struct EpiPostOp {
+  int dbl = 0;
+  int add_neg = 0;
+  const uint64_t *cadd = nullptr;  // [q_limbs] residues, device memory, or null
+};
 int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk,
                 const uint64_t *acc, const uint64_t *add0, const uint64_t *add1,
                 long long add_stride, uint64_t *out, long long out_stride,
                 const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s,
-                const uint64_t *z = nullptr);
+                const uint64_t *z = nullptr, const EpiPostOp *post = nullptr);
 // Rescale of num_polys polys [poly][l][N] (NTT form) to out [poly][l-1][N]:
 // last [poly][N] holds each poly's last limb in coefficient form; one forward
 // NTT launch lifts it to every q_i in its input stage and finishes

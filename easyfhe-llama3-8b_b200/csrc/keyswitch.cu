@@ -835,11 +835,46 @@ size_t b2f_relinearize_rescale_workspace(const b2f_context *ctx, int num_cts,
 // out_b = round(Y_b / M) over Q_{l-1}, with the removed limbs R = {q_{l-1}}
 // u P converted by the rounded (centred) fast base conversion.  Saves the
 // forward NTT of the l ModDown outputs and the rescale's own transforms.
+static int relinearize_rescale_impl(b2f_context *ctx, const uint64_t *ct3_in,
+                                    uint64_t *ct_out, int num_cts, int l,
+                                    const uint64_t *relin_key, void *ws, size_t ws_bytes,
+                                    void *stream, const uint64_t *sub, int sub_limbs,
+                                    const EpiPostOp *post);
+
 int b2f_relinearize_rescale(b2f_context *ctx, const uint64_t *ct3_in,
                             uint64_t *ct_out, int num_cts, int l,
                             const uint64_t *relin_key, void *ws, size_t ws_bytes,
                             void *stream) {
   B2F_RANGE("b2f_relinearize_rescale");
+  return relinearize_rescale_impl(ctx, ct3_in, ct_out, num_cts, l, relin_key, ws, ws_bytes,
+                                  stream, nullptr, 0, nullptr);
+}
+
+int b2f_relinearize_rescale_postop(b2f_context *ctx, const uint64_t *ct3_in,
+                                   uint64_t *ct_out, int num_cts, int l,
+                                   const uint64_t *relin_key, int apply_double,
+                                   const uint64_t *sub, int sub_limbs,
+                                   const uint64_t *scalar_residues, void *ws,
+                                   size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_relinearize_rescale_postop");
+  B2F_CHECK_ARG(!sub || (sub_limbs >= l - 1 && sub_limbs <= ctx->L),
+                "b2f_relinearize_rescale_postop: the subtrahend has %d limbs, the result "
+                "%d", sub_limbs, l - 1);
+  B2F_CHECK_ARG(!sub || (sub != ct_out && sub != ct3_in),
+                "b2f_relinearize_rescale_postop: the subtrahend overlaps an argument");
+  EpiPostOp post;
+  post.dbl = apply_double ? 1 : 0;
+  post.add_neg = sub ? 1 : 0;
+  post.cadd = scalar_residues;
+  return relinearize_rescale_impl(ctx, ct3_in, ct_out, num_cts, l, relin_key, ws, ws_bytes,
+                                  stream, sub, sub_limbs, &post);
+}
+
+static int relinearize_rescale_impl(b2f_context *ctx, const uint64_t *ct3_in,
+                                    uint64_t *ct_out, int num_cts, int l,
+                                    const uint64_t *relin_key, void *ws, size_t ws_bytes,
+                                    void *stream, const uint64_t *sub, int sub_limbs,
+                                    const EpiPostOp *post) {
   int rc = check_level(ctx, l, "b2f_relinearize_rescale");
   if (rc) return rc;
   B2F_CHECK_ARG(l >= 2, "b2f_relinearize_rescale: needs at least 2 limbs, got %d", l);
@@ -881,8 +916,12 @@ int b2f_relinearize_rescale(b2f_context *ctx, const uint64_t *ct3_in,
                        T.mdr_scale, s)))
     return rc;
   if ((rc = launch_moddown_rescale_conv(ctx, acc, conv, l, num_cts, s))) return rc;
-  return ntt_moddown(ctx, conv, num_cts, l - 1, lk, acc, nullptr, nullptr, 0, ct_out,
-                     2LL * (l - 1) * kN, T.rescale_inv, it, s);
+  // the subtrahend of the post-operation enters as the epilogue's add input
+  // (its first l-1 limbs, each ciphertext 2 sub_limbs limbs apart)
+  const uint64_t *s0 = sub, *s1 = sub ? sub + (size_t)sub_limbs * kN : nullptr;
+  return ntt_moddown(ctx, conv, num_cts, l - 1, lk, acc, s0, s1,
+                     sub ? 2LL * sub_limbs * kN : 0, ct_out, 2LL * (l - 1) * kN,
+                     T.rescale_inv, it, s, nullptr, post);
 }
 
 size_t b2f_modup_batch_workspace(const b2f_context *ctx, int num_cts, int l) {

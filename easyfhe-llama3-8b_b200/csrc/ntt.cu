@@ -371,6 +371,9 @@ struct ModDownOut {
   const uint64_t *qlast_mod;  // [q_last]_{q_i}
   uint64_t q_last;
   const Mod *mods;
+  // post-operation (EpiPostOp): x2, subtract add_b, add cadd[i] to poly 0
+  int dbl, add_neg;
+  const uint64_t *cadd;
 };
 
 // The forward transform that finishes a ModDown runs on clusters of 8 CTAs
@@ -619,6 +622,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   const uint64_t q = epi.primes[i];
   const ulonglong2 pi = epi.pinv[i];
   const ulonglong2 qi = epi.qinv ? epi.qinv[i] : make_ulonglong2(0, 0);
+  // the constant of the post-operation (poly 0 only; all ones: none)
+  const uint64_t cadd_i = (epi.cadd && b == 0) ? epi.cadd[i] : ~0ull;
   const uint64_t *accl = epi.acc + (((size_t)it * 2 + b) * epi.lk + i) * kN;
   const uint64_t *addl = b ? epi.add1 : epi.add0;
   if (addl) addl += epi.items.ct(it) * epi.add_stride + (size_t)i * kN;
@@ -645,9 +650,17 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
         w0 = shoup(w0, qi.x, qi.y, q);
         w1 = shoup(w1, qi.x, qi.y, q);
       }
+      if (epi.dbl) {
+        w0 = add_mod(w0, w0, q);
+        w1 = add_mod(w1, w1, q);
+      }
       if (addl) {
-        w0 = add_mod(w0, dv[u].x, q);
-        w1 = add_mod(w1, dv[u].y, q);
+        w0 = epi.add_neg ? sub_mod(w0, dv[u].x, q) : add_mod(w0, dv[u].x, q);
+        w1 = epi.add_neg ? sub_mod(w1, dv[u].y, q) : add_mod(w1, dv[u].y, q);
+      }
+      if (cadd_i != ~0ull) {
+        w0 = add_mod(w0, cadd_i, q);
+        w1 = add_mod(w1, cadd_i, q);
       }
       if (ginv == 1) {
         *reinterpret_cast<ulonglong2 *>(outl + j) = make_ulonglong2(w0, w1);
@@ -752,7 +765,7 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
                 const uint64_t *acc, const uint64_t *add0, const uint64_t *add1,
                 long long add_stride, uint64_t *out, long long out_stride,
                 const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s,
-                const uint64_t *z) {
+                const uint64_t *z, const EpiPostOp *post) {
   std::vector<int> key = {0, q_limbs, 0};
   std::vector<LimbJob> jobs(q_limbs);
   for (int i = 0; i < q_limbs; ++i)
@@ -780,6 +793,9 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
   E.qlast_mod = nullptr;
   E.q_last = 0;
   E.mods = ctx->d_mod;
+  E.dbl = post ? post->dbl : 0;
+  E.add_neg = post ? post->add_neg : 0;
+  E.cadd = post ? post->cadd : nullptr;
   if (E.zK > 0 && !(ctx->fp64 && ctx->K <= 4 && ctx->d_md_conv_f64)) {
     set_error("ntt_moddown: the in-transform conversion needs binary64 and K <= 4");
     return B2F_ERR_UNSUPPORTED;
@@ -822,6 +838,9 @@ int ntt_rescale_jobs(b2f_context *ctx, const uint64_t *last, const uint64_t *in,
   E.qlast_mod = T.rescale_qlast;
   E.q_last = ctx->primes[l - 1];
   E.mods = ctx->d_mod;
+  E.dbl = 0;
+  E.add_neg = 0;
+  E.cadd = nullptr;
   return launch_ntt_impl(ctx, last, 0, out, 0, d, lo, num_polys, 0, nullptr, &E, s);
 }
 

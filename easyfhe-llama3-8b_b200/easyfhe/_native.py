@@ -50,6 +50,8 @@ _SIGS = {
     "b2f_relinearize": (_int, [_vp, _vp, _vp, _int, _int, _vp, _vp, _size, _vp]),
     "b2f_relinearize_rescale_workspace": (_size, [_vp, _int, _int]),
     "b2f_relinearize_rescale": (_int, [_vp, _vp, _vp, _int, _int, _vp, _vp, _size, _vp]),
+    "b2f_relinearize_rescale_postop": (_int, [_vp, _vp, _vp, _int, _int, _vp, _int, _vp, _int,
+                                              _vp, _vp, _size, _vp]),
     "b2f_modup_workspace": (_size, [_vp, _int]),
     "b2f_modup": (_int, [_vp, _vp, _int, _vp, _vp, _size, _vp]),
     "b2f_rotate_hoisted_workspace": (_size, [_vp, _int, _int]),

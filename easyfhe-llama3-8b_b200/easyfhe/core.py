@@ -220,14 +220,30 @@ class NativeContext:
              _ptr(ws), ws.numel(), _stream())
         return out
 
-    def relinearize_rescale(self, ct3: torch.Tensor, l: int, key: torch.Tensor) -> torch.Tensor:
-        """Relinearise and rescale in one pass: [.., 3, l, N] -> [.., 2, l-1, N]."""
+    def relinearize_rescale(self, ct3: torch.Tensor, l: int, key: torch.Tensor,
+                            apply_double: bool = False, sub: torch.Tensor | None = None,
+                            sub_limbs: int = 0, scalar=None) -> torch.Tensor:
+        """Relinearise and rescale in one pass: [.., 3, l, N] -> [.., 2, l-1, N];
+        with a post-operation (x2, minus sub's first l-1 limbs, plus the scalar
+        residues on poly 0) folded into the final transform's epilogue."""
 
         num = ct3.numel() // (3 * l * self.n)
         out = self.empty(num, 2, l - 1) if ct3.dim() == 4 else self.empty(2, l - 1)
         ws = self.workspace(lib.b2f_relinearize_rescale_workspace(self.handle, num, l))
-        call("b2f_relinearize_rescale", self.handle, _ptr(ct3), _ptr(out), num, l,
-             _ptr(key), _ptr(ws), ws.numel(), _stream())
+        if not apply_double and sub is None and scalar is None:
+            call("b2f_relinearize_rescale", self.handle, _ptr(ct3), _ptr(out), num, l,
+                 _ptr(key), _ptr(ws), ws.numel(), _stream())
+            return out
+        res = None
+        if scalar is not None:  # the l-1 residues, uploaded for the epilogue
+            host = np.array([int(v) for v in scalar][: l - 1], dtype=np.uint64)
+            if host.size != l - 1:
+                raise ValueError(f"scalar has {host.size} residues, the result {l - 1} limbs")
+            res = torch.from_numpy(host.view(np.int64)).to(self.device)
+        call("b2f_relinearize_rescale_postop", self.handle, _ptr(ct3), _ptr(out), num, l,
+             _ptr(key), int(bool(apply_double)), _ptr(sub) if sub is not None else None,
+             int(sub_limbs), _ptr(res) if res is not None else None, _ptr(ws), ws.numel(),
+             _stream())
         return out
 
     def modup(self, ct: torch.Tensor, l: int, num_cts: int = 1) -> torch.Tensor:

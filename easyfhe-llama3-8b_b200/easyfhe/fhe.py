@@ -734,16 +734,52 @@ def homo_mul_relin_rescale_postop(left: Ciphertext, right: Ciphertext, context,
                                   apply_double: bool = False, sub=None,
                                   scalar: EncodedScalar | None = None) -> Ciphertext:
     """rescale(relin(l * r)), then optionally times 2, minus `sub`, plus `scalar`
-    (llama3fhe/operators/nonlinear/polynomial.py:108-159)."""
+    (llama3fhe/operators/nonlinear/polynomial.py:108-159): the Chebyshev step
+    T_{a+b} = 2 T_a T_b - T_{a-b}.  The post-operation runs in the epilogue of
+    the relinearise-rescale's last transform (b2f_relinearize_rescale_postop):
+    no extra launch, and sub is read at its own level (no alignment copy).
+    The residues equal relinearise-rescale followed by homo_add(out, out),
+    homo_sub(out, align_to(sub)) and homo_add_scalar."""
 
-    out = _relinearize_rescale(homo_mul_no_relin(left, right, context), context)
-    if apply_double:
-        out = homo_add(out, out, context)
+    ctx = _ctx_of(context)
+    prod = homo_mul_no_relin(left, right, context)
+    if prod.polys == 2 or not (apply_double or sub is not None or scalar is not None):
+        out = _relinearize_rescale(prod, context)
+        if apply_double:
+            out = homo_add(out, out, context)
+        if sub is not None:
+            out = homo_sub(out, align_to(sub, out.state, context), context)
+        if scalar is not None:
+            out = homo_add_scalar(out, scalar, context)
+        return out
+    if ctx.relin_key is None:
+        raise ValueError("context has no relinearisation key")
+    l = _limbs(prod)
+    if l < 2:
+        raise ValueError("rescale needs at least two limbs")
+    state = _rescaled_state(prod, ctx)
+    sub_data, sub_limbs = None, 0
     if sub is not None:
-        out = homo_sub(out, align_to(sub, out.state, context), context)
+        if sub.is_ext or sub.polys != 2 or sub.batch_size != prod.batch_size:
+            raise ValueError("homo_mul_relin_rescale_postop: sub must be a relinearised "
+                             "ciphertext of the product's batch")
+        if int(sub.state.scale_degree) != int(state.scale_degree):
+            raise ValueError("homo_sub: scale degrees differ "
+                             f"({state.scale_degree} vs {sub.state.scale_degree})")
+        sub_limbs = _limbs(sub)
+        if sub_limbs < l - 1:
+            raise ValueError(f"cannot align {sub_limbs} limbs to {l - 1}")
+        sub_data = sub.data.contiguous()
+    residues = None
     if scalar is not None:
-        out = homo_add_scalar(out, scalar, context)
-    return out
+        if len(scalar.residues) < l - 1:
+            raise ValueError(f"scalar encoded for {len(scalar.residues)} limbs, the result "
+                             f"has {l - 1}")
+        residues = scalar.residues[: l - 1]
+    out = ctx.native.relinearize_rescale(prod.data, l, ctx.relin_key,
+                                         apply_double=bool(apply_double), sub=sub_data,
+                                         sub_limbs=sub_limbs, scalar=residues)
+    return _new(out, prod, state)
 
 
 # ---------------------------------------------------------------------------

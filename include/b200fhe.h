@@ -132,6 +132,21 @@ int b2f_relinearize_rescale(b2f_context *ctx, const uint64_t *ct3_in,
                             uint64_t *ct_out, int num_cts, int l,
                             const uint64_t *relin_key, void *ws,
                             size_t ws_bytes, void *stream);
+/* b2f_relinearize_rescale with the post-operation of
+ * fhe.homo_mul_relin_rescale_postop (llama3fhe/operators/nonlinear/
+ * polynomial.py:108-159: the Chebyshev basis step T_{a+b} = 2 T_a T_b -
+ * T_{a-b}) folded into the same final transform's epilogue:
+ *   out = r * (apply_double ? 2 : 1) - sub + scalar
+ * with r the relinearised, rescaled product (l-1 limbs).  sub (optional):
+ * num_cts ciphertexts of sub_limbs >= l-1 limbs, of which the first l-1 are
+ * read (no alignment copy); scalar_residues (optional): l-1 residues in
+ * device memory added to poly 0.  Same launches as without the post-op. */
+int b2f_relinearize_rescale_postop(b2f_context *ctx, const uint64_t *ct3_in,
+                                   uint64_t *ct_out, int num_cts, int l,
+                                   const uint64_t *relin_key, int apply_double,
+                                   const uint64_t *sub, int sub_limbs,
+                                   const uint64_t *scalar_residues, void *ws,
+                                   size_t ws_bytes, void *stream);
 
 /* Hoisting: ModUp of c1 once into the extended digits
  * ext[digit][l+K][N] (NTT form) ...
