@@ -52,7 +52,7 @@ def parse():
                     help="ciphertexts per rank (hrotate 32, bootstrap 16, linear 16)")
     ap.add_argument("--rotation", type=int, default=1)
     ap.add_argument("--workload", default="linear",
-                    choices=["linear", "hrotate", "ntt", "bootstrap", "layer0"],
+                    choices=["linear", "hrotate", "ntt", "bootstrap", "layer0", "mac"],
                     help="linear (default): the encrypted 4096x4096 linear block sharded "
                          "over the ranks with an all-gather; hrotate: the key-switching "
                          "microbench; ntt: only the NTT kernel loop (for profiling); "
@@ -61,6 +61,11 @@ def parse():
     ap.add_argument("--layer-params", action="store_true",
                     help="hrotate/ntt: the layer's chain (depth 37, dnum 5, 59/60-bit "
                          "primes, K = 8) instead of 50-bit primes; --limbs picks the level")
+    ap.add_argument("--linear-chunks", type=int, default=0,
+                    help="linear: only the plan's first N chunks of 512 rows (a smaller "
+                         "linear block, for profiling captures; 0 = all 8)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="linear at N = 1: skip the HRotate, Layer-0 and CPU attachments")
     ap.add_argument("--no-layer", action="store_true",
                     help="skip the Layer-0 run the default line carries at N = 1")
     ap.add_argument("--no-clocks", action="store_true")
@@ -75,7 +80,7 @@ def parse():
     a = ap.parse_args()
     if a.batch is None:
         a.batch = {"hrotate": 32, "ntt": 32, "bootstrap": 16, "linear": 16,
-                   "layer0": 16}[a.workload]
+                   "layer0": 16, "mac": 16}[a.workload]
     return a
 
 
@@ -420,6 +425,8 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
         raise SystemExit(f"{total} ciphertexts do not split over {world} ranks")
     per = total // world
     chunks, offsets, giant_offset = linear_plan()
+    if a.linear_chunks:
+        chunks = chunks[: a.linear_chunks]
     rotations = set(offsets[1:]) | {giant_offset} | {b * giant_offset for b, _ in chunks if b}
     client, ctx = fhe.generate_client_context(
         fhe.CKKSContextSpec(depth=37, log_n=16, dnum=5, dcrt_bits=59, first_mod=60,
@@ -506,7 +513,7 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
     gather_ms = max_over_ranks(sum(x.elapsed_time(y) for x, y in gather_ev) / a.steps
                                if gather_ev else 0.0)
     err = None
-    if rank == 0:  # the first and the last ciphertext of the whole (gathered) set
+    if rank == 0 and not a.linear_chunks:  # first and last ciphertext of the gathered set
         Wn = W.cpu().numpy()
         err = max(float(np.max(np.abs(
             client.decrypt(fhe.Ciphertext(outs[j], out_state["state"], slots, ctx))
@@ -526,6 +533,7 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
     m1.record(stream)
     torch.cuda.synchronize()
     mac_ms = m0.elapsed_time(m1) / mac_reps
+    mac_peak = ctx.native.mac_peak()
     del babies, batch
 
     # ---- end to end: pinned host ciphertexts in, outputs out ----
@@ -583,10 +591,12 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
                                 "all-gathered over NCCL in every step; logN 16 depth 37 dnum 5 "
                                 "59/60-bit primes"),
                    "ciphertexts_total": total, "ciphertexts_per_rank": per,
+                   "chunks": (len(chunks) if not a.linear_chunks else
+                              f"{len(chunks)} of 8 (a smaller linear: --linear-chunks)"),
                    "parallelism": f"output-ciphertext sharding x{world} + all-gather",
                    "l2": "plaintexts 3.3 GB per chunk, babies 13.6 GB per 16 ciphertexts: "
                          "inputs far larger than L2; no flush"},
-        "pt_x_ct_per_s": total * D / (ms / 1e3),
+        "pt_x_ct_per_s": total * B * sum(c for _, c in chunks) / (ms / 1e3),
         "encode_rows_per_s": D / encode_s,
         "max_abs_error": err,
         "gather_ms_per_step": gather_ms,
@@ -599,6 +609,12 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
                      "launch": (f"one chunk: {G0} giants x {B} babies x {per} ciphertexts "
                                 f"at l={level}; {mac_ms:.3f} ms per launch"),
                      "mac128_per_s": G0 * B * per * 2 * level * N / (mac_ms / 1e3)},
+        "compute_roofline": {"bound": "imad", "kernel": "mac_kernel",
+                             "achieved": G0 * B * per * 2 * level * N / (mac_ms / 1e3),
+                             "peak": mac_peak, "unit": "128-bit multiply-adds/s",
+                             "frac": G0 * B * per * 2 * level * N / (mac_ms / 1e3) / mac_peak,
+                             "peak_source": ("measured live: b2f_mac_peak (mac_kernel's "
+                                             "inner step from registers, every SM full)")},
         "gpu_launches": launches,
         "e2e": {"value": total / (e2e_ms / 1e3), "unit": unit,
                 "h2d_bytes_per_step": sum(h.numel() * 8 for h in host_in) * world,
@@ -800,6 +816,69 @@ def run_hrotate(a, dev, rank: int, world: int, barrier, max_over_ranks,
 
 
 
+def run_mac(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict | None:
+    """mac_kernel alone at the production chunk shape: 8 giants x 64 babies at
+    l = 13 over `a.batch` ciphertexts, uniform residues of the layer's primes
+    (the kernel is data-independent): one step = one chunk's launch.  For
+    kernel profiling and the MAC's two rooflines."""
+
+    import torch
+
+    from easyfhe import _native, core
+
+    params = core.Params.from_depth(37, 16, 5, 59, 60)
+    ctx = core.NativeContext(params, dev)
+    l, B, G, C = LINEAR_LEVEL, LINEAR_B, LINEAR_ROWS // LINEAR_B, a.batch
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7 + rank)
+    babies = torch.empty(C * B, 2, l, N, dtype=torch.int64, device=dev)
+    pts = torch.empty(G * B, l, N, dtype=torch.int64, device=dev)
+    for i, q in enumerate(params.q[:l]):
+        babies[:, :, i].random_(0, q, generator=gen)
+        pts[:, i].random_(0, q, generator=gen)
+    stream = torch.cuda.current_stream()
+    for _ in range(a.warmup):
+        ctx.mac(babies, B, pts, G, l, num_cts=C)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    n0 = _native.lib.b2f_launch_count()
+    e0.record(stream)
+    for _ in range(a.steps):
+        ctx.mac(babies, B, pts, G, l, num_cts=C)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = (_native.lib.b2f_launch_count() - n0) // a.steps
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    peak = ctx.mac_peak()
+    if rank:
+        return None
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    alg = (G * B * l + C * B * 2 * l + C * G * 2 * l) * N * 8
+    macs = G * B * C * 2 * l * N
+    return {"metric": "mac_kernel launches/s (one BSGS chunk: 8 giants x 64 babies, l=13)",
+            "value": world / (ms / 1e3), "unit": "launches/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u64", "data": "synthetic",
+            "config": {"workload": f"mac_kernel, {C} ciphertexts x 64 babies x 8 giants, l={l}",
+                       "l2": "plaintext rows 3.3 GB: larger than L2; no flush"},
+            "roofline": {"bound": "hbm", "kernel": "mac_kernel",
+                         "achieved": alg / (ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": alg / (ms / 1e3) / 1e9 / hbm, "traffic": None,
+                         "algorithmic_bytes_per_launch": alg},
+            "compute_roofline": {"bound": "imad", "kernel": "mac_kernel",
+                                 "achieved": macs / (ms / 1e3), "peak": peak,
+                                 "unit": "128-bit multiply-adds/s",
+                                 "frac": macs / (ms / 1e3) / peak},
+            "gpu_launches": launches}
+
+
 def layer0_result(warmup: int = 1, repetitions: int = 1) -> dict:
     """Layer-0 of encrypted Llama-3-8B through the reference's own llama3fhe
     (its runner's Layer-0 preset, unchanged) on this backend: s/layer from the
@@ -942,13 +1021,17 @@ def main() -> None:
             line = run_layer0(a, world) if rank == 0 else None
             if line:
                 print(json.dumps(line), flush=True)
+        elif a.workload == "mac":
+            line = run_mac(a, dev, rank, world, barrier, max_over_ranks)
+            if line:
+                print(json.dumps(line), flush=True)
         elif a.workload in ("hrotate", "ntt"):
             line = run_hrotate(a, dev, rank, world, barrier, max_over_ranks)
             if line:
                 print(json.dumps(line), flush=True)
         else:
             line = run_linear(a, dev, rank, world, barrier, max_over_ranks)
-            if rank == 0 and world == 1:
+            if rank == 0 and world == 1 and not a.no_extras:
                 line.update(single_gpu_extras(a, dev, barrier, max_over_ranks))
             if line:
                 print(json.dumps(line), flush=True)

@@ -6,6 +6,7 @@
 // by HBM, so bench.py reports their butterfly rate against the rate measured
 // here.
 #include "b2f_internal.h"
+#include "modarith.cuh"
 #include "ntt_arith.cuh"
 
 namespace b2f {
@@ -31,10 +32,81 @@ __global__ void __launch_bounds__(256) butterfly_peak_kernel(uint64_t *out,
   out[(size_t)blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
+// The same for mac_kernel's inner step: 8 giants x 2 polys of 128-bit
+// accumulators, babies taken two at a time (2 x 8 x 2 multiply-adds per
+// step), every accumulator reduced every 16 steps (32 babies), all from
+// registers.
+__global__ void __launch_bounds__(256) mac_peak_kernel(uint64_t *out, const Mod *mods,
+                                                       int iters) {
+  const Mod M = mods[0];
+  U128 acc[8][2];
+  uint64_t w[8], c[4];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    acc[g][0] = acc[g][1] = U128{0, 0};
+    w[g] = (0x9E3779B97F4A7C15ull * (g + 1) + threadIdx.x) % M.q;
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) c[u] = (0xD1B54A32D192ED03ull * (u + 7) + blockIdx.x) % M.q;
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        mac128(acc[g][0], c[2 * u], w[g]);
+        mac128(acc[g][1], c[2 * u + 1], w[g]);
+      }
+    if ((it & 15) == 15) {
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        acc[g][0] = U128{reduce128(acc[g][0].hi, acc[g][0].lo, M), 0};
+        acc[g][1] = U128{reduce128(acc[g][1].hi, acc[g][1].lo, M), 0};
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) c[u] ^= (uint64_t)it;  // keeps the inputs live
+  }
+  uint64_t s = 0;
+#pragma unroll
+  for (int g = 0; g < 8; ++g) s ^= acc[g][0].lo ^ acc[g][1].hi;
+  out[(size_t)blockIdx.x * blockDim.x + threadIdx.x] = s;
+}
+
 }  // namespace
 }  // namespace b2f
 
 using namespace b2f;
+
+extern "C" int b2f_mac_peak(b2f_context *ctx, int iters, double *per_second,
+                            void *stream) {
+  B2F_CHECK_ARG(ctx && per_second && iters > 0, "b2f_mac_peak: bad argument");
+  cudaStream_t s = (cudaStream_t)stream;
+  int sms = 0;
+  B2F_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device));
+  const int blocks = sms * 8, threads = 256;
+  uint64_t *out = nullptr;
+  B2F_CUDA(cudaMallocAsync(&out, sizeof(uint64_t) * blocks * threads, s));
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  float ms = 0.f;
+  cudaError_t err = cudaEventCreate(&e0);
+  if (err == cudaSuccess) err = cudaEventCreate(&e1);
+  if (err == cudaSuccess) {
+    mac_peak_kernel<<<blocks, threads, 0, s>>>(out, ctx->d_mod, iters);  // warm-up
+    note_launch();
+    cudaEventRecord(e0, s);
+    mac_peak_kernel<<<blocks, threads, 0, s>>>(out, ctx->d_mod, iters);
+    note_launch();
+    cudaEventRecord(e1, s);
+    err = cudaEventSynchronize(e1);
+  }
+  if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  cudaFreeAsync(out, s);
+  if (err != cudaSuccess) return cuda_status(err, "b2f_mac_peak");
+  *per_second = (double)blocks * threads * iters * 32 / (ms * 1e-3);
+  return B2F_OK;
+}
 
 extern "C" int b2f_butterfly_peak(b2f_context *ctx, int iters, double *per_second,
                                   void *stream) {

@@ -76,6 +76,7 @@ _SIGS = {
     "b2f_linear_combination": (_int, [_vp, _int, _vp, _vp, _vp, _int, _int, _int, _vp,
                                       _vp]),
     "b2f_butterfly_peak": (_int, [_vp, _int, ctypes.POINTER(ctypes.c_double), _vp]),
+    "b2f_mac_peak": (_int, [_vp, _int, ctypes.POINTER(ctypes.c_double), _vp]),
     "b2f_modup_batch_workspace": (_size, [_vp, _int, _int]),
     "b2f_modup_batch": (_int, [_vp, _vp, _int, _int, _vp, _vp, _size, _vp]),
     "b2f_rotate_hoisted_batch_workspace": (_size, [_vp, _int, _int, _int]),

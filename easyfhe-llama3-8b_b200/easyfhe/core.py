@@ -355,6 +355,14 @@ class NativeContext:
         call("b2f_butterfly_peak", self.handle, int(iters), ctypes.byref(out), _stream())
         return float(out.value)
 
+    def mac_peak(self, iters: int = 2000) -> float:
+        """128-bit multiply-adds per second of mac_kernel's inner step from
+        registers alone (its integer-multiply roofline)."""
+
+        out = ctypes.c_double(0.0)
+        call("b2f_mac_peak", self.handle, int(iters), ctypes.byref(out), _stream())
+        return float(out.value)
+
     def linear_combination(self, terms, term_limbs, weights, num_cts: int, polys: int,
                            l: int) -> torch.Tensor:
         """sum_k weights[k] * terms[k] over num_cts x polys polynomials at l

@@ -330,6 +330,12 @@ int b2f_mac_ext(b2f_context *ctx, const uint64_t *babies, int baby_count,
  * their 64-bit products on CUDA cores bound them before HBM does. */
 int b2f_butterfly_peak(b2f_context *ctx, int iters, double *per_second,
                        void *stream);
+/* Rate of mac_kernel's inner step from registers alone (2 babies x 8 giants
+ * x 2 polys of 128-bit multiply-adds per step, each accumulator reduced every
+ * 32 babies, every SM full), in multiply-adds per second: the integer-multiply
+ * roofline the BSGS multiply-accumulate is measured against.  No reference
+ * counterpart (calibration). */
+int b2f_mac_peak(b2f_context *ctx, int iters, double *per_second, void *stream);
 
 /* ---- encoding ----
  * Slot vectors (complex128 interleaved re/im, device) -> plaintexts at

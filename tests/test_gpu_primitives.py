@@ -188,6 +188,34 @@ def test_rotate_special_prime_counts(L, K, dnum):
             assert np.array_equal(out[c], orc.rotate(cts[c], l, g, hkey)), (arith, c)
 
 
+@pytest.mark.parametrize("K,batch", [(1, 16), (2, 64)])
+def test_rotate_dnum4_small_special_batches(K, batch):
+    """HRotate at dnum 4 with 1 or 2 special primes on batches of 16 and 64
+    ciphertexts sharing one key (the primitive microbench's grid): the first
+    and last ciphertext against the oracle, every ciphertext of the batch
+    against its own single-ciphertext rotation, under both arithmetics."""
+
+    from easyfhe import core
+
+    L, l = 16, 16
+    ctx, orc = pair(L, K, 4)
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(40 + K, 192))
+    g = core.galois_element(5)
+    key = ctx.keygen_rotation(s_ntt, g, seed=90 + K)
+    rng = np.random.default_rng(batch)
+    cts = rand_residues(rng, ctx.primes[:l], 2 * batch).reshape(batch, 2, l, N)
+    dcts = to_dev(cts)
+    hkey = to_host(key)
+    for arith in ("f64", "int64"):
+        with use_arith(ctx, arith):
+            out = to_host(ctx.rotate(dcts, l, g, key))
+            for c in range(0, batch, 7):
+                one = to_host(ctx.rotate(dcts[c:c + 1].contiguous(), l, g, key))
+                assert np.array_equal(out[c], one[0]), (arith, c)
+        for c in (0, batch - 1):
+            assert np.array_equal(out[c], orc.rotate(cts[c], l, g, hkey)), (arith, c)
+
+
 def test_hoisted_rotations_identity_items_and_groups():
     """Identity items (galois 1, no key) anywhere in the list are copies, and
     more than 64 rotations run as several launch groups."""
