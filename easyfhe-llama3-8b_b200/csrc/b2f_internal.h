@@ -194,7 +194,8 @@ struct ItemKeys;
 struct EpiPostOp {
   int dbl = 0;
   int add_neg = 0;
-  const uint64_t *cadd = nullptr;  // [q_limbs] residues, device memory, or null
+  int has_cadd = 0;
+  uint64_t cadd[64] = {};  // [q_limbs] residues, by value in the kernel parameters
 };
 int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk,
                 const uint64_t *acc, const uint64_t *add0, const uint64_t *add1,

@@ -862,10 +862,14 @@ int b2f_relinearize_rescale_postop(b2f_context *ctx, const uint64_t *ct3_in,
                 "%d", sub_limbs, l - 1);
   B2F_CHECK_ARG(!sub || (sub != ct_out && sub != ct3_in),
                 "b2f_relinearize_rescale_postop: the subtrahend overlaps an argument");
+  B2F_CHECK_ARG(l - 1 <= 64, "b2f_relinearize_rescale_postop: at most 65 limbs");
   EpiPostOp post;
   post.dbl = apply_double ? 1 : 0;
   post.add_neg = sub ? 1 : 0;
-  post.cadd = scalar_residues;
+  if (scalar_residues) {  // host residues: into the kernel parameters
+    post.has_cadd = 1;
+    for (int i = 0; i < l - 1; ++i) post.cadd[i] = scalar_residues[i] % ctx->primes[i];
+  }
   return relinearize_rescale_impl(ctx, ct3_in, ct_out, num_cts, l, relin_key, ws, ws_bytes,
                                   stream, sub, sub_limbs, &post);
 }

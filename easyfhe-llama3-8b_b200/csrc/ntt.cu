@@ -372,8 +372,8 @@ struct ModDownOut {
   uint64_t q_last;
   const Mod *mods;
   // post-operation (EpiPostOp): x2, subtract add_b, add cadd[i] to poly 0
-  int dbl, add_neg;
-  const uint64_t *cadd;
+  int dbl, add_neg, has_cadd;
+  uint64_t cadd[64];
 };
 
 // The forward transform that finishes a ModDown runs on clusters of 8 CTAs
@@ -622,8 +622,9 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   const uint64_t q = epi.primes[i];
   const ulonglong2 pi = epi.pinv[i];
   const ulonglong2 qi = epi.qinv ? epi.qinv[i] : make_ulonglong2(0, 0);
-  // the constant of the post-operation (poly 0 only; all ones: none)
-  const uint64_t cadd_i = (epi.cadd && b == 0) ? epi.cadd[i] : ~0ull;
+  // the constant of the post-operation (poly 0 only)
+  const bool with_c = epi.has_cadd && b == 0;
+  const uint64_t cadd_i = with_c ? epi.cadd[i] : 0;
   const uint64_t *accl = epi.acc + (((size_t)it * 2 + b) * epi.lk + i) * kN;
   const uint64_t *addl = b ? epi.add1 : epi.add0;
   if (addl) addl += epi.items.ct(it) * epi.add_stride + (size_t)i * kN;
@@ -658,7 +659,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
         w0 = epi.add_neg ? sub_mod(w0, dv[u].x, q) : add_mod(w0, dv[u].x, q);
         w1 = epi.add_neg ? sub_mod(w1, dv[u].y, q) : add_mod(w1, dv[u].y, q);
       }
-      if (cadd_i != ~0ull) {
+      if (with_c) {
         w0 = add_mod(w0, cadd_i, q);
         w1 = add_mod(w1, cadd_i, q);
       }
@@ -795,7 +796,9 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
   E.mods = ctx->d_mod;
   E.dbl = post ? post->dbl : 0;
   E.add_neg = post ? post->add_neg : 0;
-  E.cadd = post ? post->cadd : nullptr;
+  E.has_cadd = post ? post->has_cadd : 0;
+  if (E.has_cadd)
+    for (int i = 0; i < q_limbs; ++i) E.cadd[i] = post->cadd[i];
   if (E.zK > 0 && !(ctx->fp64 && ctx->K <= 4 && ctx->d_md_conv_f64)) {
     set_error("ntt_moddown: the in-transform conversion needs binary64 and K <= 4");
     return B2F_ERR_UNSUPPORTED;
@@ -840,7 +843,7 @@ int ntt_rescale_jobs(b2f_context *ctx, const uint64_t *last, const uint64_t *in,
   E.mods = ctx->d_mod;
   E.dbl = 0;
   E.add_neg = 0;
-  E.cadd = nullptr;
+  E.has_cadd = 0;
   return launch_ntt_impl(ctx, last, 0, out, 0, d, lo, num_polys, 0, nullptr, &E, s);
 }
 

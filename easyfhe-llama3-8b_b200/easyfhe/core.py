@@ -86,7 +86,10 @@ def _ptr(t: torch.Tensor) -> int:
 
 
 def _stream() -> int:
-    return int(torch.cuda.current_stream().cuda_stream)
+    """The raw cudaStream_t of the current device's current torch stream
+    (torch.cuda.current_stream() costs ~15 us per call in Python)."""
+
+    return torch._C._cuda_getCurrentRawStream(torch._C._cuda_getDevice())
 
 
 class NativeContext:
@@ -235,14 +238,14 @@ class NativeContext:
                  _ptr(key), _ptr(ws), ws.numel(), _stream())
             return out
         res = None
-        if scalar is not None:  # the l-1 residues, uploaded for the epilogue
-            host = np.array([int(v) for v in scalar][: l - 1], dtype=np.uint64)
-            if host.size != l - 1:
-                raise ValueError(f"scalar has {host.size} residues, the result {l - 1} limbs")
-            res = torch.from_numpy(host.view(np.int64)).to(self.device)
+        if scalar is not None:  # the l-1 residues, by value (host array)
+            vals = [int(v) for v in scalar][: l - 1]
+            if len(vals) != l - 1:
+                raise ValueError(f"scalar has {len(vals)} residues, the result {l - 1} limbs")
+            res = (ctypes.c_uint64 * (l - 1))(*vals)
         call("b2f_relinearize_rescale_postop", self.handle, _ptr(ct3), _ptr(out), num, l,
              _ptr(key), int(bool(apply_double)), _ptr(sub) if sub is not None else None,
-             int(sub_limbs), _ptr(res) if res is not None else None, _ptr(ws), ws.numel(),
+             int(sub_limbs), res, _ptr(ws), ws.numel(),
              _stream())
         return out
 

@@ -942,9 +942,14 @@ def hoisted_mac_sum(ct: Ciphertext, baby_offsets, plaintexts: Plaintext, giant_o
     n = inner.shape[-1]
     shape = (2, l, n) if C == 1 else (C, 2, l, n)
 
-    def giant(g: int) -> Ciphertext:  # ModDown of giant g's sum, all ciphertexts
-        d = ctx.native.moddown_ext(inner[:, g].contiguous(), C, l)
-        return Ciphertext(d.view(shape), state, ct.slots, ctx)
+    # one ModDown launch for every giant's sum of every ciphertext
+    first = 0 if s == "ext_normal" else 1
+    down = ctx.native.moddown_ext(inner[:, first:].reshape(-1, 2, l + K, n), C * (G - first), l)
+    down = down.view(C, G - first, 2, l, n)
+
+    def giant(g: int) -> Ciphertext:  # giant g's ModDown'ed sum, all ciphertexts
+        d = down[:, g - first]
+        return Ciphertext(d.reshape(shape) if C > 1 else d[0], state, ct.slots, ctx)
 
     if s == "ext_normal":
         acc = giant(G - 1)
@@ -1069,7 +1074,11 @@ class ConstantBundle:
             values = raw
         t = torch.as_tensor(values)
         if t.device.type != "cuda":
-            t = t.to(context.device)
+            # through pinned memory, without blocking the host on the GPU: a
+            # pageable copy would wait for every kernel queued before it (the
+            # reference builds many mask bundles from NumPy inside a layer);
+            # torch keeps the pinned block until the copy has run
+            t = t.pin_memory().to(context.device, non_blocking=True)
         t = t.to(torch.complex128)
         if t.dim() == 1:
             t = t.unsqueeze(0)

@@ -140,7 +140,8 @@ int b2f_relinearize_rescale(b2f_context *ctx, const uint64_t *ct3_in,
  * with r the relinearised, rescaled product (l-1 limbs).  sub (optional):
  * num_cts ciphertexts of sub_limbs >= l-1 limbs, of which the first l-1 are
  * read (no alignment copy); scalar_residues (optional): l-1 residues in
- * device memory added to poly 0.  Same launches as without the post-op. */
+ * HOST memory, passed to the kernel by value (no copy, no synchronisation),
+ * added to poly 0.  Same launches as without the post-op. */
 int b2f_relinearize_rescale_postop(b2f_context *ctx, const uint64_t *ct3_in,
                                    uint64_t *ct_out, int num_cts, int l,
                                    const uint64_t *relin_key, int apply_double,
