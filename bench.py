@@ -52,7 +52,8 @@ def parse():
                     help="ciphertexts per rank (hrotate 32, bootstrap 16, linear 16)")
     ap.add_argument("--rotation", type=int, default=1)
     ap.add_argument("--workload", default="linear",
-                    choices=["linear", "hrotate", "ntt", "bootstrap", "layer0", "mac"],
+                    choices=["linear", "hrotate", "ntt", "bootstrap", "layer0", "mac",
+                             "prefill"],
                     help="linear (default): the encrypted 4096x4096 linear block sharded "
                          "over the ranks with an all-gather; hrotate: the key-switching "
                          "microbench; ntt: only the NTT kernel loop (for profiling); "
@@ -66,6 +67,10 @@ def parse():
                          "linear block, for profiling captures; 0 = all 8)")
     ap.add_argument("--no-extras", action="store_true",
                     help="linear at N = 1: skip the HRotate, Layer-0 and CPU attachments")
+    ap.add_argument("--num-layers", type=int, default=32,
+                    help="prefill: decoder layers through the reference's model loop")
+    ap.add_argument("--no-check", action="store_true",
+                    help="prefill: skip the fp64 check of the decrypted output")
     ap.add_argument("--no-layer", action="store_true",
                     help="skip the Layer-0 run the default line carries at N = 1")
     ap.add_argument("--no-clocks", action="store_true")
@@ -80,7 +85,7 @@ def parse():
     a = ap.parse_args()
     if a.batch is None:
         a.batch = {"hrotate": 32, "ntt": 32, "bootstrap": 16, "linear": 16,
-                   "layer0": 16, "mac": 16}[a.workload]
+                   "layer0": 16, "mac": 16, "prefill": 16}[a.workload]
     return a
 
 
@@ -232,6 +237,78 @@ def run_reference(a) -> None:
     print(json.dumps(line), flush=True)
 
 
+def count_keyswitches(native, fn) -> dict:
+    """Run fn() once with the context's key-switching entry points counted:
+    {limbs: key switches at that level} (rotations, hoisted rotations,
+    relinearisations, the Horner giants inside a BSGS multiply-accumulate)."""
+
+    import collections
+
+    counts = collections.Counter()
+    orig = {}
+
+    def wrap(name, how):
+        f = getattr(native, name)
+        orig[name] = f
+
+        def w(*args, **kw):
+            l, k = how(args, kw)
+            counts[int(l)] += int(k)
+            return f(*args, **kw)
+        setattr(native, name, w)
+
+    n = native.n
+    wrap("rotate", lambda a, k: (a[1], a[0].numel() // (2 * a[1] * n)))
+    wrap("rotate_hoisted", lambda a, k: (a[1], sum(g != 1 for g in a[3])
+                                         * k.get("num_cts", 1)))
+    wrap("rotate_hoisted_ext", lambda a, k: (a[1], sum(g != 1 for g in a[3])))
+    wrap("relinearize", lambda a, k: (a[1], a[0].numel() // (3 * a[1] * n)))
+    wrap("relinearize_rescale", lambda a, k: (a[1], a[0].numel() // (3 * a[1] * n)))
+    wrap("bsgs_mac", lambda a, k: (a[4], (a[3] - 1) * k.get("num_cts", 1)))
+    try:
+        fn()
+    finally:
+        for name, f in orig.items():
+            setattr(native, name, f)
+    return dict(counts)
+
+
+def keyswitch_cpu_seconds(params, counts: dict, samples: int = 1) -> tuple[float, str]:
+    """CPU seconds of the counted key switches on the oracle: HRotate timed at
+    the lowest, middle and highest level used, interpolated linearly in the
+    limbs for the rest."""
+
+    import numpy as np
+
+    from oracle import oracle as O
+
+    O.build()
+    orc = O.Oracle(16, list(params.q), list(params.p), params.dnum)
+    s_ntt = orc.secret_to_ntt(O.sample_secret(16, 2024, 192))
+    g = O.galois_element(16, 1)
+    key = orc.keygen_rotation(s_ntt, g, 7)
+    rng = np.random.default_rng(3)
+    levels = sorted(counts)
+    probes = sorted({levels[0], levels[len(levels) // 2], levels[-1]})
+    t = {}
+    for l in probes:
+        ct = np.empty((2, l, N), dtype=np.uint64)
+        for i, qi in enumerate(params.q[:l]):
+            ct[:, i] = rng.integers(0, qi, (2, N), dtype=np.uint64)
+        t0 = time.perf_counter()
+        for _ in range(samples):
+            orc.rotate(ct, l, g, key)
+        t[l] = (time.perf_counter() - t0) / samples
+    xs = np.array(probes, dtype=np.float64)
+    ys = np.array([t[l] for l in probes])
+    total = float(sum(c * np.interp(l, xs, ys) for l, c in counts.items()))
+    sample = (f"C oracle HRotate at l = {', '.join(str(l) for l in probes)} "
+              f"({', '.join(f'{t[l]:.2f} s' for l in probes)}), interpolated over the "
+              f"{sum(counts.values())} key switches one bootstrap issues; the rest of the "
+              "bootstrap (NTT-free elementwise work, encoding) is not counted: a lower bound")
+    return total, sample
+
+
 def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) -> None:
     """Full-slot CKKS bootstrapping at the layer parameters
     (logN 16, depth 37, dnum 5, 59/60-bit primes, BootstrapSpec(15, (4, 4),
@@ -301,6 +378,54 @@ def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) ->
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    boot_roofline = boot_cpu = ks_per_boot = None
+    if rank == 0:
+        # the dominant kernel: the NTT of the layer chain (integer arithmetic)
+        # over the batch's polynomials at the full 38 limbs, timed live
+        nat = ctx.native
+        buf = torch.empty(a.batch * 2 * ctx.L, N, dtype=torch.int64, device=dev)
+        for i, q in enumerate(ctx.params.q):
+            buf.view(a.batch * 2, ctx.L, N)[:, i].random_(0, q)
+        nat.ntt(buf, ctx.L)
+        nat.ntt(buf, ctx.L, inverse=True)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 4
+        t0.record(stream)
+        for _ in range(reps):
+            nat.ntt(buf, ctx.L)
+            nat.ntt(buf, ctx.L, inverse=True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        ntt_ms = t0.elapsed_time(t1) / (2 * reps)
+        limbs = a.batch * 2 * ctx.L
+        peaks = {}
+        try:
+            peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        except Exception:
+            pass
+        hbm = float(peaks.get("hbm_gbs", 6650.0))
+        gbs = 16 * N * limbs / (ntt_ms / 1e3) / 1e9
+        bfly = limbs * (N // 2) * 16 / (ntt_ms / 1e3)
+        boot_roofline = {"bound": "hbm", "kernel": f"ntt_fwd_kernel/ntt_inv_kernel ({nat.arith})",
+                         "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "traffic": None, "algorithmic_bytes_per_launch": 16 * N * limbs,
+                         "launch": f"{limbs} limbs of 2^16 words, {ntt_ms:.3f} ms",
+                         "compute_frac": bfly / nat.butterfly_peak()}
+        del buf
+        # CPU: the key switches of one bootstrap, priced on the oracle
+        one = cts[0]
+        counts = count_keyswitches(nat, lambda: bs.bootstrap(one, ctx, program))
+        ks_per_boot = {"total": sum(counts.values()), "by_limbs": counts}
+        try:
+            os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+            sec, sample = keyswitch_cpu_seconds(ctx.params, counts)
+            boot_cpu = {"value": 1.0 / sec, "unit": "bootstraps/s",
+                        "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)),
+                        "kind": "port", "sample": sample}
+        except Exception as exc:  # a reported baseline only
+            boot_cpu = {"value": None, "unit": "bootstraps/s", "cores": 0, "kind": "port",
+                        "sample": f"unavailable: {exc}"}
     if rank == 0:
         unit = "bootstraps/s"
         line = {
@@ -319,10 +444,11 @@ def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) ->
             "precision_bits": -math.log2(err) if err > 0 else None,
             "max_abs_error": err,
             "output_limbs": int(outs[0].state.cur_limbs),
-            "roofline": None,
-            "cpu_baseline": None,
-            "note": "the CPU oracle has no bootstrap; cpu_baseline and the kernel roofline "
-                    "are reported on the hrotate line",
+            "roofline": boot_roofline,
+            "cpu_baseline": boot_cpu,
+            "keyswitches_per_bootstrap": ks_per_boot,
+            "note": ("roofline: the integer NTT (the bootstrap's dominant kernel) timed live "
+                     "on this context over the batch's 38-limb polynomials"),
             "e2e": {"value": world * a.batch / (e2e_ms / 1e3), "unit": unit,
                     "h2d_bytes_per_step": sum(h.numel() * 8 for h in host_in),
                     "d2h_bytes_per_step": sum(h.numel() * 8 for h in host_out)},
@@ -968,6 +1094,36 @@ def single_gpu_extras(a, dev, barrier, max_over_ranks) -> dict:
     return out
 
 
+def run_prefill(a, world: int) -> dict:
+    """An encrypted prefill of --num-layers decoder layers through the
+    reference's own model loop (Llama3Model.forward) on one GPU, seeded
+    synthetic layers kept inside the reference's per-layer polynomial fits."""
+
+    import llama3_layer
+
+    from easyfhe import _native
+
+    if llama3_layer.reference_root() is None:
+        return {"metric": "encrypted Llama-3-8B prefill s/layer at seq128",
+                "unavailable": "the reference llama3fhe tree is not installed (baseline/_ref)"}
+    n0 = _native.lib.b2f_launch_count()
+    r = llama3_layer.run_prefill(a.num_layers, check=not a.no_check)
+    launches = _native.lib.b2f_launch_count() - n0
+    r.pop("decoded", None)
+    steady = r["per_layer_seconds"][1:] or r["per_layer_seconds"]
+    return {"metric": f"encrypted Llama-3-8B prefill s/layer at seq128 ({a.num_layers} layers)",
+            "value": r["s_per_layer"], "unit": "s/layer", "n_gpus": 1, "steps": 1,
+            "warmup": 0, "ms_per_step": r["wall_seconds"] * 1e3,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u64", "data": "synthetic",
+            "config": {"workload": (f"{a.num_layers} Llama-3-8B decoder layers, seq 128, through "
+                                    "the reference's Llama3Model.forward; seeded synthetic "
+                                    "layers; logN 16 depth 37 dnum 5 59/60-bit primes")},
+            "prefill_seconds": r["wall_seconds"],
+            "steady_state_s_per_layer": sum(steady) / len(steady),
+            "prefill": r, "gpu_launches_total": launches}
+
+
 def run_layer0(a, world: int) -> dict:
     """The Layer-0 workload as its own line: seconds per encrypted layer."""
 
@@ -1017,6 +1173,10 @@ def main() -> None:
     try:
         if a.workload == "bootstrap":
             run_bootstrap(a, dev, rank, world, barrier, max_over_ranks)
+        elif a.workload == "prefill":
+            line = run_prefill(a, world) if rank == 0 else None
+            if line:
+                print(json.dumps(line), flush=True)
         elif a.workload == "layer0":
             line = run_layer0(a, world) if rank == 0 else None
             if line:

@@ -98,33 +98,24 @@ def _rope(values: np.ndarray, heads: int, head_dim: int, theta: float) -> np.nda
     return out.reshape(seq, heads * head_dim)
 
 
-def layer_fp64(hidden, weights, *, query_heads: int = 32, kv_heads: int = 8,
-               head_dim: int = 128, rope_theta: float = 500000.0, eps: float = 1e-5,
-               approximations=None) -> np.ndarray:
-    """One Llama-3 decoder layer in fp64.  With ``approximations`` (the
-    layer's LayerApproximations) RMSNorm's rsqrt and SiLU are its Chebyshev
-    series; softmax is always exact."""
+def _rmsnorm64(v, gamma, entry, eps: float = 1e-5):
+    ms = np.mean(v * v, axis=-1, keepdims=True)
+    if entry is None:
+        scale = 1.0 / np.sqrt(ms + eps)
+    else:  # the fitted target is rsqrt(ms + eps) (approx/rmsnorm.py:36-37)
+        lo, hi = (float(t) for t in entry["fit_interval"])
+        scale = chebyshev_fp64(ms, entry["coefficients"], lo, hi)
+    return v * scale * np.asarray(gamma, np.float64)[None, :]
+
+
+def attention_delta_fp64(x, weights, *, query_heads: int = 32, kv_heads: int = 8,
+                         head_dim: int = 128, rope_theta: float = 500000.0,
+                         approximations=None) -> np.ndarray:
+    """The attention block's addition to the residual stream x, in fp64."""
 
     f64 = lambda a: np.asarray(a, dtype=np.float64)  # noqa: E731
-    x = f64(hidden)
-
-    def rmsnorm(v, gamma, entry):
-        ms = np.mean(v * v, axis=-1, keepdims=True)
-        if entry is None:
-            scale = 1.0 / np.sqrt(ms + eps)
-        else:  # the fitted target is rsqrt(ms + eps) (approx/rmsnorm.py:36-37)
-            lo, hi = (float(t) for t in entry["fit_interval"])
-            scale = chebyshev_fp64(ms, entry["coefficients"], lo, hi)
-        return v * scale * f64(gamma)[None, :]
-
-    def silu(v, entry):
-        if entry is None:
-            return v / (1.0 + np.exp(-v))
-        lo, hi = (float(t) for t in entry["fit_interval"])
-        return chebyshev_fp64(v, entry["coefficients"], lo, hi)
-
     ap = approximations
-    h1 = rmsnorm(x, weights.input_layernorm, None if ap is None else ap.input_norm)
+    h1 = _rmsnorm64(x, weights.input_layernorm, None if ap is None else ap.input_norm)
     q = _rope(h1 @ f64(weights.q_proj).T, query_heads, head_dim, rope_theta)
     k = _rope(h1 @ f64(weights.k_proj).T, kv_heads, head_dim, rope_theta)
     v = h1 @ f64(weights.v_proj).T
@@ -140,11 +131,34 @@ def layer_fp64(hidden, weights, *, query_heads: int = 32, kv_heads: int = 8,
     p = np.exp(scores)
     p /= p.sum(axis=-1, keepdims=True)
     attn = np.einsum("hqk,khd->qhd", p, vh).reshape(seq, -1)
-    x2 = x + attn @ f64(weights.o_proj).T
-    h2 = rmsnorm(x2, weights.post_attention_layernorm,
-                 None if ap is None else ap.post_attention_norm)
-    act = silu(h2 @ f64(weights.gate_proj).T, None if ap is None else ap.silu)
-    return x2 + (act * (h2 @ f64(weights.up_proj).T)) @ f64(weights.down_proj).T
+    return attn @ f64(weights.o_proj).T
+
+
+def mlp_delta_fp64(x2, weights, *, approximations=None) -> np.ndarray:
+    """The SwiGLU MLP block's addition to the residual stream x2, in fp64."""
+
+    f64 = lambda a: np.asarray(a, dtype=np.float64)  # noqa: E731
+    ap = approximations
+    h2 = _rmsnorm64(x2, weights.post_attention_layernorm,
+                    None if ap is None else ap.post_attention_norm)
+    g = h2 @ f64(weights.gate_proj).T
+    if ap is None:
+        act = g / (1.0 + np.exp(-g))
+    else:
+        lo, hi = (float(t) for t in ap.silu["fit_interval"])
+        act = chebyshev_fp64(g, ap.silu["coefficients"], lo, hi)
+    return (act * (h2 @ f64(weights.up_proj).T)) @ f64(weights.down_proj).T
+
+
+def layer_fp64(hidden, weights, *, approximations=None, **kw) -> np.ndarray:
+    """One Llama-3 decoder layer in fp64 (causal GQA with rotate-half RoPE,
+    SwiGLU, RMSNorm with its gammas).  With ``approximations`` (the layer's
+    LayerApproximations) RMSNorm's rsqrt and SiLU are its Chebyshev series;
+    softmax is always exact."""
+
+    x = np.asarray(hidden, dtype=np.float64)
+    x2 = x + attention_delta_fp64(x, weights, approximations=approximations, **kw)
+    return x2 + mlp_delta_fp64(x2, weights, approximations=approximations)
 
 
 def diff_stats(got: np.ndarray, want: np.ndarray) -> dict:
@@ -253,8 +267,214 @@ def run_layer0(*, warmup: int = 1, repetitions: int = 1, seed: int = 26081461,
     return result
 
 
+GAINS_PATH = HERE / "prefill_gains.json"
+_GAIN_STEPS = [2.0 ** (k / 2) for k in range(0, 31)]  # 1 .. 32768, by sqrt(2)
+_MARGIN = 1.5
+
+
+def _gains() -> dict:
+    import json
+
+    if GAINS_PATH.is_file():
+        return json.loads(GAINS_PATH.read_text())
+    return {}
+
+
+def layer_weights(index: int, seed: int = 26081461, gains: dict | None = None):
+    """Seeded synthetic weights of layer `index`: the reference's Layer-0
+    preset generator (application/inputs.py:80-113) with seed + index, with
+    the two projections that write the residual stream (o_proj, down_proj)
+    scaled by the layer's gains (tune_prefill_gains), so that a stack of such
+    layers keeps every RMSNorm input inside the reference's per-layer fits."""
+
+    import dataclasses
+
+    import_reference()
+    from llama3fhe.application.inputs import _synthetic_inputs
+    from llama3fhe.layouts import AttentionPairLayout, FeatureMajorPrefillLayout
+
+    w = _synthetic_inputs(int(seed) + int(index), layout=FeatureMajorPrefillLayout(),
+                          attention_layout=AttentionPairLayout())[1]
+    g = (_gains() if gains is None else gains).get(str(int(index)))
+    if g and int(_gains().get("seed", seed)) == int(seed):
+        w = dataclasses.replace(w, o_proj=(w.o_proj * np.float32(g[0])).astype(np.float32),
+                                down_proj=(w.down_proj * np.float32(g[1])).astype(np.float32))
+    return w
+
+
+def _ms_range(x: np.ndarray) -> tuple[float, float]:
+    ms = np.mean(x * x, axis=-1)
+    return float(ms.min()), float(ms.max())
+
+
+def _violation(x: np.ndarray, entry) -> float:
+    """How far the tokens' mean squares are outside [1.5 lo, hi] of a fit
+    (log2 ratio; 0 = inside)."""
+
+    lo, hi = (float(t) for t in entry["fit_interval"])
+    a, b = _ms_range(x)
+    if not (np.isfinite(a) and np.isfinite(b)) or a <= 0:
+        return float("inf")
+    return max(0.0, np.log2(_MARGIN * lo / a)) + max(0.0, np.log2(b / hi))
+
+
+def _pick_gain(x: np.ndarray, delta: np.ndarray, entry) -> float:
+    """The smallest gain g putting x + g delta inside the fit, else the one
+    closest to it."""
+
+    best, best_v = 1.0, float("inf")
+    for g in _GAIN_STEPS:
+        v = _violation(x + g * delta, entry)
+        if v == 0.0:
+            return g
+        if v < best_v:
+            best, best_v = g, v
+    return best
+
+
+def tune_prefill_gains(num_layers: int = 32, seed: int = 26081461, log=print) -> dict:
+    """Per-layer gains for layer_weights, found on the CPU with the fp64
+    polynomial layer: for layer i, the smallest gain (a power of sqrt(2)) on
+    o_proj whose attention output leaves every token's mean square inside the
+    layer's post-attention RMSNorm fit (margin 1.5x at both ends), then the
+    smallest on down_proj leaving it inside layer i+1's input RMSNorm fit.
+    The reference's fits follow the real model's residual stream, whose mean
+    square grows ~5000x over the 32 layers; the Layer-0 preset's weights add
+    too little to it, and from layer 2 on the stack falls below the fits."""
+
+    import_reference()
+    from llama3fhe.application import args as ref_args
+    from llama3fhe.application.approx_config import ApproximationConfig
+    from llama3fhe.application.inputs import _synthetic_inputs
+    from llama3fhe.layouts import AttentionPairLayout, FeatureMajorPrefillLayout
+
+    a = ref_args.resolve_poly_paths(ref_args.build_parser().parse_args([]))
+    approx = ApproximationConfig(rmsnorm_path=a.rms_coeffs, silu_path=a.silu_coeffs,
+                                 softmax_path=a.softmax_coeffs)
+    x = np.asarray(_synthetic_inputs(int(seed), layout=FeatureMajorPrefillLayout(),
+                                     attention_layout=AttentionPairLayout())[0], np.float64)
+    gains = {"seed": int(seed)}
+    for i in range(int(num_layers)):
+        ap = approx.for_layer(i)
+        if _violation(x, ap.input_norm):
+            log(f"layer {i}: input mean squares {_ms_range(x)} outside "
+                f"{ap.input_norm['fit_interval']}")
+        w = layer_weights(i, seed, gains={})
+        d_att = attention_delta_fp64(x, w, approximations=ap)
+        go = _pick_gain(x, d_att, ap.post_attention_norm)
+        x2 = x + go * d_att
+        d_mlp = mlp_delta_fp64(x2, w, approximations=ap)
+        nxt = approx.for_layer(i + 1).input_norm if i + 1 < 32 else None
+        gd = 1.0 if nxt is None else _pick_gain(x2, d_mlp, nxt)
+        x = x2 + gd * d_mlp
+        gains[str(i)] = [go, gd]
+        log(f"layer {i}: gains o {go:.3g} down {gd:.3g}; output mean squares {_ms_range(x)}")
+    return gains
+
+
+def run_prefill(num_layers: int = 32, *, seed: int = 26081461, check: bool = True,
+                progress=None, diagnostic=None) -> dict:
+    """An encrypted prefill of `num_layers` decoder layers through the reference's
+    own model loop, unchanged, on this backend.
+
+    The reference's runner accepts a multi-layer run only with a checkpoint
+    (application/settings.py:89-93: synthetic weights are its one-layer
+    preset), so this resolves the settings and schedule a checkpoint run of
+    `num_layers` layers resolves (resolve_settings / layer_schedule,
+    settings.py:65-231: input at the bootstrap-output level, the pre-exp
+    softmax refresh), builds the context with every rotation those layers
+    declare, encrypts the preset's seeded hidden state and streams seeded
+    synthetic layers (layer_weights) with each layer's own approximations into
+    Llama3Model.forward (model.py:171-364): layer 0 consumes the encrypted
+    input, every later layer refreshes the previous output inside its input
+    RMSNorm, and no boundary is decrypted until the end."""
+
+    import_reference()
+    from llama3fhe import Llama3CKKSConfig
+    from llama3fhe.application import args as ref_args
+    from llama3fhe.application import session, settings
+    from llama3fhe.application.approx_config import ApproximationConfig
+    from llama3fhe.application.client import decrypt_hidden
+    from llama3fhe.application.inputs import _synthetic_inputs
+    from llama3fhe.layouts import AttentionPairLayout, FeatureMajorPrefillLayout
+    from llama3fhe.model import Llama3Model, TransformerLayer, prepare_bootstrap_operator
+
+    import torch
+
+    n = int(num_layers)
+    args = ref_args.resolve_poly_paths(ref_args.build_parser().parse_args(
+        ["--num-layers", str(n), "--weights-source", "real"]))
+    config = Llama3CKKSConfig.from_json(args.config)
+    resolved = settings.resolve_settings(args, config)
+    schedule = settings.layer_schedule(args, resolved)
+    approx = ApproximationConfig(rmsnorm_path=args.rms_coeffs, silu_path=args.silu_coeffs,
+                                 softmax_path=args.softmax_coeffs)
+    approx.validate_layers(n)
+    fl, al = FeatureMajorPrefillLayout(), AttentionPairLayout()
+    model = Llama3Model(config=config, num_layers=n, feature_layout=fl, attention_layout=al)
+    t0 = time.perf_counter()
+    rotations = model.required_rotations(
+        schedule, bootstrap_deep_level_budget=(
+            (3, 3) if schedule.softmax_main_deep_bootstrap else None))
+    context = session._create_context(config, rotations)
+    hidden, _ = _synthetic_inputs(int(seed), layout=fl, attention_layout=al)
+    ciphers = session._encrypt_hidden(hidden, context=context, layout=fl,
+                                      input_level=resolved.input_level)
+    op = prepare_bootstrap_operator(context, schedule)
+    setup = time.perf_counter() - t0
+
+    from concurrent.futures import ThreadPoolExecutor
+
+    def layers():
+        # the next layer's weights are generated on a background thread while
+        # this one runs, as the reference streams checkpoint layers
+        # (application/layer_stream.py:23-186)
+        with ThreadPoolExecutor(1) as pool:
+            nxt = pool.submit(layer_weights, 0, seed)
+            for i in range(n):
+                w = nxt.result()
+                if i + 1 < n:
+                    nxt = pool.submit(layer_weights, i + 1, seed)
+                yield TransformerLayer(index=i, weights=w,
+                                       approximations=approx.for_layer(i), config=config,
+                                       feature_layout=fl, attention_layout=al)
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    diag = None
+    if diagnostic is not None:  # diagnostic(index, decrypted hidden) after every layer
+        def diag(index, cts, layer):
+            diagnostic(int(index), decrypt_hidden(cts, crypto_context=context, layout=fl))
+            return {}
+    result = model.forward(hidden, crypto_context=context, input_ciphers=ciphers,
+                           layers=layers(), bootstrap_operator=op, schedule=schedule,
+                           progress_callback=progress, diagnostic_callback=diag)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    decoded = decrypt_hidden(result.ciphers, crypto_context=context, layout=fl)
+    out = {"num_layers": n, "wall_seconds": wall, "s_per_layer": wall / n,
+           "setup_seconds": setup,
+           "per_layer_seconds": [float(r["wall_seconds"]) for r in result.per_layer],
+           "bootstrap_calls": int(result.bootstrap_calls),
+           "input_level": int(resolved.input_level), "decoded": decoded,
+           "finite": bool(np.all(np.isfinite(decoded)))}
+    if check:
+        exact = poly = np.asarray(hidden, np.float64)
+        for i in range(n):
+            w = layer_weights(i, seed)
+            exact = layer_fp64(exact, w)
+            poly = layer_fp64(poly, w, approximations=approx.for_layer(i))
+        out["checks"] = {"vs_fp64_exact": diff_stats(decoded, exact),
+                         "vs_fp64_poly": diff_stats(decoded, poly)}
+    return out
+
+
 if __name__ == "__main__":
     import json
+
+    if sys.argv[1:2] == ["--tune-gains"]:  # writes prefill_gains.json beside this file
+        GAINS_PATH.write_text(json.dumps(tune_prefill_gains(), indent=1) + "\n")
+        sys.exit(0)
 
     r = run_layer0()
     print(json.dumps({"s_per_layer": r["s_per_layer"], "checks": r.get("checks"),

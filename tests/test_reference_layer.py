@@ -31,6 +31,12 @@ needs_ref = pytest.mark.skipif(llama3_layer.reference_root() is None,
                                reason="reference llama3fhe tree not installed")
 
 
+@pytest.fixture(autouse=True)
+def _reference_on_path():
+    if llama3_layer.reference_root() is not None:
+        llama3_layer.import_reference()
+
+
 @needs_ref
 def test_reference_imports_on_this_backend():
     mod = llama3_layer.import_reference()
