@@ -74,6 +74,9 @@ def parse():
     ap.add_argument("--no-layer", action="store_true",
                     help="skip the Layer-0 run the default line carries at N = 1")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--mac-path", default="auto", choices=["auto", "cuda_cores"],
+                    help="BSGS multiply-accumulate kernel: u8 tensor cores where exact "
+                         "(auto) or the CUDA-core kernel")
     ap.add_argument("--arith", default="auto", choices=["auto", "int64", "f64"],
                     help="butterfly arithmetic of the NTT kernels (auto: binary64 when "
                          "every prime is below 2^50)")
@@ -557,6 +560,7 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
     client, ctx = fhe.generate_client_context(
         fhe.CKKSContextSpec(depth=37, log_n=16, dnum=5, dcrt_bits=59, first_mod=60,
                             rotations=tuple(sorted(rotations)), seed=21), dev)
+    ctx.native.set_mac_path(a.mac_path)
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
     Gm = torch.randn(D, D, dtype=torch.float64, device=dev, generator=gen) / math.sqrt(D)
@@ -659,7 +663,9 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
     m1.record(stream)
     torch.cuda.synchronize()
     mac_ms = m0.elapsed_time(m1) / mac_reps
-    mac_peak = ctx.native.mac_peak()
+    mac_name = ctx.native.mac_kernel(B, level, num_cts=per)
+    on_tc = mac_name == "mac_mma_kernel"
+    mac_peak = ctx.native.mma_u8_peak() if on_tc else ctx.native.mac_peak()
     del babies, batch
 
     # ---- end to end: pinned host ciphertexts in, outputs out ----
@@ -691,11 +697,12 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     lim = N * 8
-    # algorithmic bytes of one mac_kernel launch (one chunk of G0 giants on
-    # `per` ciphertexts): the plaintext rows once, the babies once, outputs
+    # algorithmic bytes of one MAC launch (one chunk of G0 giants on `per`
+    # ciphertexts): the plaintext rows once, the babies once, outputs
     mac_bytes = (G0 * B * level + per * B * 2 * level + per * G0 * 2 * level) * lim
+    macs = G0 * B * per * 2 * level * N  # 64 x 64-bit products per launch
     traffic = None
-    tpath = ROOT / "profiles" / "mac_traffic.json"
+    tpath = ROOT / "profiles" / f"{mac_name}_traffic.json"
     if tpath.exists():
         try:
             t = json.loads(tpath.read_text())
@@ -727,20 +734,15 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
         "max_abs_error": err,
         "gather_ms_per_step": gather_ms,
         "gather_share": gather_ms / ms if ms else None,
-        "roofline": {"bound": "hbm", "kernel": "mac_kernel",
+        "roofline": {"bound": "hbm", "kernel": mac_name,
                      "achieved": mac_bytes / (mac_ms / 1e3) / 1e9, "peak": hbm_peak,
                      "unit": "GB/s", "frac": mac_bytes / (mac_ms / 1e3) / 1e9 / hbm_peak,
                      "traffic": traffic, "peak_source": "measured" if peaks else "fallback",
                      "algorithmic_bytes_per_launch": mac_bytes,
                      "launch": (f"one chunk: {G0} giants x {B} babies x {per} ciphertexts "
                                 f"at l={level}; {mac_ms:.3f} ms per launch"),
-                     "mac128_per_s": G0 * B * per * 2 * level * N / (mac_ms / 1e3)},
-        "compute_roofline": {"bound": "imad", "kernel": "mac_kernel",
-                             "achieved": G0 * B * per * 2 * level * N / (mac_ms / 1e3),
-                             "peak": mac_peak, "unit": "128-bit multiply-adds/s",
-                             "frac": G0 * B * per * 2 * level * N / (mac_ms / 1e3) / mac_peak,
-                             "peak_source": ("measured live: b2f_mac_peak (mac_kernel's "
-                                             "inner step from registers, every SM full)")},
+                     "products_per_s": macs / (mac_ms / 1e3)},
+        "compute_roofline": mac_compute_roofline(mac_name, macs, mac_ms, mac_peak),
         "gpu_launches": launches,
         "e2e": {"value": total / (e2e_ms / 1e3), "unit": unit,
                 "h2d_bytes_per_step": sum(h.numel() * 8 for h in host_in) * world,
@@ -942,6 +944,26 @@ def run_hrotate(a, dev, rank: int, world: int, barrier, max_over_ranks,
 
 
 
+def mac_compute_roofline(kernel: str, macs: int, ms: float, peak: float) -> dict:
+    """The MAC launch against the register-only rate of its own inner step:
+    byte multiply-adds (64 per 64-bit product) against b2f_mma_u8_peak for
+    the tensor-core kernel, 128-bit multiply-adds against b2f_mac_peak for the
+    CUDA-core kernel."""
+
+    if kernel == "mac_mma_kernel":
+        achieved = 64 * macs / (ms / 1e3)
+        return {"bound": "tensor (mma.sync m16n8k32 u8)", "kernel": kernel,
+                "achieved": achieved, "peak": peak, "unit": "u8 multiply-adds/s",
+                "frac": achieved / peak,
+                "peak_source": "measured live: b2f_mma_u8_peak (32 independent u8 tiles "
+                               "per warp from registers, every SM full)"}
+    achieved = macs / (ms / 1e3)
+    return {"bound": "imad", "kernel": kernel, "achieved": achieved, "peak": peak,
+            "unit": "128-bit multiply-adds/s", "frac": achieved / peak,
+            "peak_source": "measured live: b2f_mac_peak (mac_kernel's inner step from "
+                           "registers, every SM full)"}
+
+
 def run_mac(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict | None:
     """mac_kernel alone at the production chunk shape: 8 giants x 64 babies at
     l = 13 over `a.batch` ciphertexts, uniform residues of the layer's primes
@@ -954,6 +976,7 @@ def run_mac(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict | No
 
     params = core.Params.from_depth(37, 16, 5, 59, 60)
     ctx = core.NativeContext(params, dev)
+    ctx.set_mac_path(a.mac_path)
     l, B, G, C = LINEAR_LEVEL, LINEAR_B, LINEAR_ROWS // LINEAR_B, a.batch
     gen = torch.Generator(device=dev)
     gen.manual_seed(7 + rank)
@@ -976,7 +999,8 @@ def run_mac(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict | No
     torch.cuda.synchronize()
     launches = (_native.lib.b2f_launch_count() - n0) // a.steps
     ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
-    peak = ctx.mac_peak()
+    kernel = ctx.mac_kernel(B, l, num_cts=C)
+    peak = ctx.mma_u8_peak() if kernel == "mac_mma_kernel" else ctx.mac_peak()
     if rank:
         return None
     peaks = {}
@@ -987,21 +1011,23 @@ def run_mac(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict | No
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     alg = (G * B * l + C * B * 2 * l + C * G * 2 * l) * N * 8
     macs = G * B * C * 2 * l * N
-    return {"metric": "mac_kernel launches/s (one BSGS chunk: 8 giants x 64 babies, l=13)",
+    traffic = None
+    tpath = ROOT / "profiles" / f"{kernel}_traffic.json"
+    if tpath.exists():
+        t = json.loads(tpath.read_text())
+        traffic = float(t["bytes_fixed"]) + float(t["bytes_per_ct"]) * C
+    return {"metric": "MAC launches/s (one BSGS chunk: 8 giants x 64 babies, l=13)",
             "value": world / (ms / 1e3), "unit": "launches/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "u64", "data": "synthetic",
-            "config": {"workload": f"mac_kernel, {C} ciphertexts x 64 babies x 8 giants, l={l}",
+            "config": {"workload": f"{kernel}, {C} ciphertexts x 64 babies x 8 giants, l={l}",
                        "l2": "plaintext rows 3.3 GB: larger than L2; no flush"},
-            "roofline": {"bound": "hbm", "kernel": "mac_kernel",
+            "roofline": {"bound": "hbm", "kernel": kernel,
                          "achieved": alg / (ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
-                         "frac": alg / (ms / 1e3) / 1e9 / hbm, "traffic": None,
+                         "frac": alg / (ms / 1e3) / 1e9 / hbm, "traffic": traffic,
                          "algorithmic_bytes_per_launch": alg},
-            "compute_roofline": {"bound": "imad", "kernel": "mac_kernel",
-                                 "achieved": macs / (ms / 1e3), "peak": peak,
-                                 "unit": "128-bit multiply-adds/s",
-                                 "frac": macs / (ms / 1e3) / peak},
+            "compute_roofline": mac_compute_roofline(kernel, macs, ms, peak),
             "gpu_launches": launches}
 
 

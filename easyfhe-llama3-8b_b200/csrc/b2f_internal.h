@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <map>
 #include <mutex>
@@ -151,6 +152,9 @@ struct b2f_context {
   // binary64 arithmetic (NTT butterflies, key inner product) when every
   // prime is below 2^50: the same twiddles as doubles, and 1/q per prime
   bool fp64_ok = false, fp64 = false;
+  // BSGS multiply-accumulate: 0 = tensor cores wherever exact (mac_mma.cu),
+  // 1 = CUDA cores only (b2f_set_mac_path)
+  int mac_path = 0;
   double *d_twd_fwd = nullptr, *d_twd_inv = nullptr, *d_qinv = nullptr;
   double *d_md_conv_f64 = nullptr;  // L x K: [Phat_k] mod q_i as doubles
   ulonglong2 *d_ninv = nullptr;       // L+K: N^-1
@@ -170,6 +174,13 @@ struct b2f_context {
 };
 
 namespace b2f {
+// Tensor-core BSGS multiply-accumulate (mac_mma.cu): eligibility for one call
+// and the launch of one chunk of G <= 8 giants starting at giant g0.
+bool mac_mma_eligible(const b2f_context *ctx, int baby_count, int l, int ql, int cts);
+int launch_mac_mma(b2f_context *ctx, const uint64_t *babies, int baby_count,
+                   const uint64_t *pts, int g0, int G, int l, uint64_t *out,
+                   int out_giants, int cts, int giant_major, int ql, cudaStream_t s);
+
 const LimbJob *job_table(b2f_context *ctx, const std::vector<int> &key,
                          const std::vector<LimbJob> &jobs);
 // items x jobs_per_item limb transforms; item i reads in + i*in_stride and

@@ -108,6 +108,73 @@ extern "C" int b2f_mac_peak(b2f_context *ctx, int iters, double *per_second,
   return B2F_OK;
 }
 
+// mac_mma_kernel's tensor-core step from registers alone: each warp issues
+// `iters` rounds of the 32 independent mma.sync m16n8k32 u8 tiles (4 row x
+// 8 column tiles) that one 32-baby step of that kernel issues; the operands
+// change every round so nothing is hoisted.  4096 byte multiply-adds per mma.
+__global__ void __launch_bounds__(256, 1) mma_u8_peak_kernel(uint32_t *out, int iters) {
+  int acc[4][8][4] = {};
+  uint32_t a[4], b[2];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) a[r] = 0x01010101u * (threadIdx.x + r);
+  b[0] = 0x02020202u ^ blockIdx.x;
+  b[1] = 0x03030303u ^ threadIdx.x;
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+            "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+            : "+r"(acc[t][j][0]), "+r"(acc[t][j][1]), "+r"(acc[t][j][2]), "+r"(acc[t][j][3])
+            : "r"(a[t & 3]), "r"(a[(t + 1) & 3]), "r"(a[(t + 2) & 3]), "r"(a[(t + 3) & 3]),
+              "r"(b[j & 1]), "r"(b[(j + 1) & 1]));
+    a[0] += 0x01000001u;
+    a[2] ^= (uint32_t)it;
+    b[1] ^= (uint32_t)it;
+  }
+  uint32_t sum = 0;
+#pragma unroll
+  for (int t = 0; t < 4; ++t)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) sum += (uint32_t)acc[t][j][r] * (r + 1);
+  out[(size_t)blockIdx.x * blockDim.x + threadIdx.x] = sum;
+}
+
+extern "C" int b2f_mma_u8_peak(b2f_context *ctx, int iters, double *per_second,
+                               void *stream) {
+  B2F_CHECK_ARG(ctx && per_second && iters > 0, "b2f_mma_u8_peak: bad argument");
+  cudaStream_t s = (cudaStream_t)stream;
+  int sms = 0;
+  B2F_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device));
+  const int blocks = sms * 4, threads = 256;
+  uint32_t *out = nullptr;
+  B2F_CUDA(cudaMallocAsync(&out, sizeof(uint32_t) * blocks * threads, s));
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  float ms = 0.f;
+  cudaError_t err = cudaEventCreate(&e0);
+  if (err == cudaSuccess) err = cudaEventCreate(&e1);
+  if (err == cudaSuccess) {
+    mma_u8_peak_kernel<<<blocks, threads, 0, s>>>(out, iters);  // warm-up
+    note_launch();
+    cudaEventRecord(e0, s);
+    mma_u8_peak_kernel<<<blocks, threads, 0, s>>>(out, iters);
+    note_launch();
+    cudaEventRecord(e1, s);
+    err = cudaEventSynchronize(e1);
+  }
+  if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  cudaFreeAsync(out, s);
+  if (err != cudaSuccess) return cuda_status(err, "b2f_mma_u8_peak");
+  *per_second = (double)blocks * (threads / 32) * iters * 32 * 4096.0 / (ms * 1e-3);
+  return B2F_OK;
+}
+
 extern "C" int b2f_butterfly_peak(b2f_context *ctx, int iters, double *per_second,
                                   void *stream) {
   B2F_CHECK_ARG(ctx && per_second && iters > 0, "b2f_butterfly_peak: bad argument");

@@ -262,8 +262,15 @@ int launch_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
                const uint64_t *pts, int giant_count, int l, uint64_t *out,
                int cts, cudaStream_t s, int giant_major = 0, int ql = -1) {
   if (ql < 0) ql = l;
+  const bool mma = mac_mma_eligible(ctx, baby_count, l, ql, cts);
   for (int g0 = 0; g0 < giant_count; g0 += GMAX) {
     const int G = std::min(GMAX, giant_count - g0);
+    if (mma) {
+      const int rc = launch_mac_mma(ctx, babies, baby_count, pts, g0, G, l, out,
+                                    giant_count, cts, giant_major, ql, s);
+      if (rc) return rc;
+      continue;
+    }
     mac_kernel<<<dim3(cts, kN / TPB, l), TPB, 0, s>>>(
         babies, baby_count, pts, g0, G, l, out, giant_count, giant_major,
         ctx->d_mod, ql, ctx->L);
@@ -490,6 +497,21 @@ int b2f_mac_ext(b2f_context *ctx, const uint64_t *babies, int baby_count,
   if (!num_cts) return B2F_OK;
   return launch_mac(ctx, babies, baby_count, pts, giant_count, q_limbs + p_limbs, out,
                     num_cts, (cudaStream_t)stream, 0, q_limbs);
+}
+
+int b2f_set_mac_path(b2f_context *ctx, int path) {
+  B2F_CHECK_ARG(ctx, "b2f_set_mac_path: null context");
+  B2F_CHECK_ARG(path == 0 || path == 1, "b2f_set_mac_path: path %d is not 0 or 1", path);
+  ctx->mac_path = path;
+  return B2F_OK;
+}
+
+int b2f_mac_uses_tensor_cores(const b2f_context *ctx, int baby_count, int q_limbs,
+                              int p_limbs, int num_cts) {
+  if (!ctx || baby_count < 1 || q_limbs < 1 || q_limbs > ctx->L || p_limbs < 0 ||
+      p_limbs > ctx->K)
+    return 0;
+  return mac_mma_eligible(ctx, baby_count, q_limbs + p_limbs, q_limbs, num_cts) ? 1 : 0;
 }
 
 int b2f_pairwise_mac(b2f_context *ctx, const uint64_t *cts, const uint64_t *pts,

@@ -77,6 +77,7 @@ _SIGS = {
                                       _vp]),
     "b2f_butterfly_peak": (_int, [_vp, _int, ctypes.POINTER(ctypes.c_double), _vp]),
     "b2f_mac_peak": (_int, [_vp, _int, ctypes.POINTER(ctypes.c_double), _vp]),
+    "b2f_mma_u8_peak": (_int, [_vp, _int, ctypes.POINTER(ctypes.c_double), _vp]),
     "b2f_modup_batch_workspace": (_size, [_vp, _int, _int]),
     "b2f_modup_batch": (_int, [_vp, _vp, _int, _int, _vp, _vp, _size, _vp]),
     "b2f_rotate_hoisted_batch_workspace": (_size, [_vp, _int, _int, _int]),
@@ -90,6 +91,8 @@ _SIGS = {
                             _vp]),
     "b2f_mac": (_int, [_vp, _vp, _int, _vp, _int, _int, _vp, _int, _vp]),
     "b2f_mac_ext": (_int, [_vp, _vp, _int, _vp, _int, _int, _int, _vp, _int, _vp]),
+    "b2f_set_mac_path": (_int, [_vp, _int]),
+    "b2f_mac_uses_tensor_cores": (_int, [_vp, _int, _int, _int, _int]),
     "b2f_encode": (_int, [_vp, _vp, _int, _int, _dbl, _int, _int, _vp, _vp, _size, _vp]),
     "b2f_encode_workspace": (_size, [_vp, _int, _int]),
     "b2f_decode": (_int, [_vp, _vp, _int, _int, _dbl, _vp, _vp, _size, _vp]),

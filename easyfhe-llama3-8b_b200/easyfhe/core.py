@@ -358,12 +358,40 @@ class NativeContext:
         call("b2f_butterfly_peak", self.handle, int(iters), ctypes.byref(out), _stream())
         return float(out.value)
 
+    MAC_PATHS = {"auto": 0, "cuda_cores": 1}
+
+    def set_mac_path(self, path: str) -> None:
+        """'auto': BSGS multiply-accumulates on the u8 tensor cores wherever the
+        byte-split sum is exact, else the CUDA cores; 'cuda_cores': always the
+        CUDA-core kernel.  Both give identical residues."""
+
+        if path not in self.MAC_PATHS:
+            raise ValueError(f"mac path {path!r} not in {sorted(self.MAC_PATHS)}")
+        call("b2f_set_mac_path", self.handle, self.MAC_PATHS[path])
+
+    def mac_kernel(self, baby_count: int, q_limbs: int, p_limbs: int = 0,
+                   num_cts: int = 2) -> str:
+        """The kernel a MAC of this shape runs under the current path:
+        "mac_mma_kernel" (u8 tensor cores) or "mac_kernel" (CUDA cores)."""
+
+        on_tc = lib.b2f_mac_uses_tensor_cores(self.handle, int(baby_count), int(q_limbs),
+                                              int(p_limbs), int(num_cts))
+        return "mac_mma_kernel" if on_tc else "mac_kernel"
+
     def mac_peak(self, iters: int = 2000) -> float:
         """128-bit multiply-adds per second of mac_kernel's inner step from
         registers alone (its integer-multiply roofline)."""
 
         out = ctypes.c_double(0.0)
         call("b2f_mac_peak", self.handle, int(iters), ctypes.byref(out), _stream())
+        return float(out.value)
+
+    def mma_u8_peak(self, iters: int = 2000) -> float:
+        """Byte multiply-adds per second of mma.sync m16n8k32 u8 from registers
+        alone (the tensor-core MAC's compute roofline)."""
+
+        out = ctypes.c_double(0.0)
+        call("b2f_mma_u8_peak", self.handle, int(iters), ctypes.byref(out), _stream())
         return float(out.value)
 
     def linear_combination(self, terms, term_limbs, weights, num_cts: int, polys: int,

@@ -323,6 +323,19 @@ int b2f_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
 int b2f_mac_ext(b2f_context *ctx, const uint64_t *babies, int baby_count,
                 const uint64_t *pts, int giant_count, int q_limbs, int p_limbs,
                 uint64_t *out, int num_cts, void *stream);
+/* Which units run the multiply-accumulate of b2f_mac, b2f_mac_ext and
+ * b2f_bsgs_mac(_batch): path 0 (the default) the u8 tensor cores on the byte
+ * split of the residues for batches of two or more ciphertexts wherever the
+ * sum is exact (baby_count <= 1024 and baby_count * q^2 < 2^128 for every
+ * prime of the call), the CUDA cores otherwise; path 1 the CUDA cores always.
+ * Both give the same residues.  Inputs are canonical residues (below their
+ * prime). */
+int b2f_set_mac_path(b2f_context *ctx, int path);
+/* 1 when a MAC of num_cts ciphertexts x baby_count babies over
+ * Q_{q_limbs} u P_{p_limbs} runs on the tensor cores under the context's
+ * current path, else 0. */
+int b2f_mac_uses_tensor_cores(const b2f_context *ctx, int baby_count, int q_limbs,
+                              int p_limbs, int num_cts);
 
 /* ---- calibration (no reference counterpart) ----
  * Rate of the NTT's lazy Shoup butterfly from registers alone (every SM
@@ -337,6 +350,10 @@ int b2f_butterfly_peak(b2f_context *ctx, int iters, double *per_second,
  * roofline the BSGS multiply-accumulate is measured against.  No reference
  * counterpart (calibration). */
 int b2f_mac_peak(b2f_context *ctx, int iters, double *per_second, void *stream);
+/* Byte multiply-adds per second of mma.sync m16n8k32 u8 from registers alone
+ * (mac_mma_kernel's tensor-core step: 32 independent tiles per warp, every SM
+ * full): the compute roofline of the tensor-core MAC. */
+int b2f_mma_u8_peak(b2f_context *ctx, int iters, double *per_second, void *stream);
 
 /* ---- encoding ----
  * Slot vectors (complex128 interleaved re/im, device) -> plaintexts at
