@@ -1,4 +1,4 @@
-// BSGS multiply-accumulate on the u8 tensor cores.
+// BSGS multiply-accumulate on the u8 tensor cores, operands staged by TMA.
 //
 // The chunk sums of a hoisted BSGS transform,
 //   out[ct][p][g] = sum_b pt[g][b] * baby[ct][b][p]   (mod q, per coefficient)
@@ -21,62 +21,95 @@
 //   D_s = set[s].rows(gid) + set[s - 1].rows(gid + 8) = sum_{i+j=s} P[i][j]
 // (below 8 * 1024 * 255^2 < 2^32 for up to 1024 babies), and
 //   value = sum_s D_s 2^(8s)  (< 2^128 when baby_count * q^2 is, checked on
-// the host) needs one Barrett reduction.  14 sets = 56 registers keep a
-// thread at 125 registers: 16 warps per SM.
+// the host) needs one Barrett reduction.  14 sets = 56 registers: 16 warps
+// per SM.
 //
-// Data path: the words arrive coefficient-major (N contiguous per limb).  A
-// block of 16 warps stages 16 coefficients (one 128-byte line per row) x 32
-// babies of the chunk's plaintext rows and of 4 ciphertexts' babies in shared
-// memory with 8-byte cp.async, baby-contiguous per (coefficient, row): rows
-// padded to 272 bytes so the fragment loads (two 16-byte loads per four
-// babies) are free of bank conflicts, coefficient slices 16 bytes apart
-// modulo 128 so the words of one 32-byte sector land in distinct banks; three
-// stages in flight.  The byte transposition into fragments is a 4 x 4 byte
-// transpose (8 byte permutes per 4 registers).
+// Data path: the words arrive coefficient-major (N contiguous per limb).  Per
+// stage one thread issues two TMA tile loads: 16 coefficients x 8 giants x 32
+// babies of the chunk's plaintext rows and 16 coefficients x 8 (ciphertext,
+// poly) columns x 32 babies, 32 KB each.  The tensor maps order their
+// dimensions (coefficient, limb, giant or column, baby), so a box lands as
+// 128-byte rows (16 coefficients) in the order baby-major, giant/column-minor,
+// and the 128-byte swizzle XORs a word's 16-byte chunk with its giant/column:
+// the 32 lanes' 8-byte fragment loads (giant = group id, baby = 4 thread-in-
+// group values) meet 4 to a bank instead of 32.  Out-of-range giants, babies
+// and ciphertexts arrive as zeros.  Three stages, each with a "full" mbarrier
+// (the two loads landed) and an "empty" one (all 16 warps have their fragments
+// in registers): warps run unsynchronised, up to two stages apart, and the
+// issuing thread waits only before it refills a buffer.  Every wait is bounded
+// and a timeout ends the block with an error count.  The byte
+// transposition into fragments is a 4 x 4 byte transpose (8 byte permutes per
+// 4 registers).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "b2f_internal.h"
 
 namespace b2f {
 namespace {
 
-constexpr int MM_KC = 32;          // babies per pipeline stage (one k-step)
-constexpr int MM_ROW = MM_KC + 2;  // words per staged row
-constexpr int MM_TILES = 16;       // coefficient tiles per block
+constexpr int MM_T = 16;                       // coefficients per tile (one 128-byte row)
+constexpr int MM_KC = 32;                      // babies per stage (one k-step)
+constexpr int MM_TILES = 16;                   // coefficient tiles per block
+constexpr int MM_STAGES = 3;
+constexpr int MM_THREADS = 512;                // one warp per coefficient of the tile
+constexpr int MM_BOX = MM_T * 8 * MM_KC * 8;   // bytes of one box (32 KB)
+constexpr int MM_STAGE = 2 * MM_BOX;           // plaintext box, then baby box
+constexpr int MM_WARPS = MM_THREADS / 32;
+constexpr size_t MM_SMEM = (size_t)MM_STAGES * MM_STAGE + 1024 + 64;
+constexpr long long MM_WAIT_LIMIT = 1ll << 24;  // try_wait polls before a stage is declared lost
+static_assert(MM_THREADS == 32 * MM_T, "one warp per coefficient");
+static_assert(MM_SMEM <= 227 * 1024, "stage buffers exceed shared memory");
 
-// T coefficients per tile x NCB column blocks of 8: one warp per pair, 16
-// warps per SM (one block of 16 warps or two of 8), 128 registers a thread.
-template <int T, int NCB>
-struct MmaShape {
-  static constexpr int WARPS = T * NCB;
-  static_assert(WARPS == 8 || WARPS == 16, "8 or 16 warps a block");
-  static constexpr int THREADS = 32 * WARPS;
-  static constexpr int BLOCKS_PER_SM = 16 / WARPS;
-  static constexpr int COLS = 8 * NCB;                  // (ciphertext, poly) columns
-  static constexpr int CTS = 4 * NCB;                   // ciphertexts per block
-  static constexpr int PT_TS = 8 * MM_ROW + 2;          // words per coefficient slice
-  static constexpr int BB_TS = COLS * MM_ROW + 2;
-  static constexpr int STAGE_WORDS = T * (PT_TS + BB_TS);
-  static constexpr int STAGES = 210 * 1024 / BLOCKS_PER_SM / (STAGE_WORDS * 8);
-  static constexpr size_t SMEM = (size_t)STAGES * STAGE_WORDS * 8;
-  static_assert(STAGES >= 2, "stage buffers exceed the shared-memory budget");
-  static_assert((MM_ROW * 8) % 16 == 0 && (PT_TS * 8) % 16 == 0 && (BB_TS * 8) % 16 == 0 &&
-                    (STAGE_WORDS * 8) % 16 == 0,
-                "16-byte fragment loads need 16-byte aligned rows");
-  static_assert((PT_TS * 8) % 128 == 16 && (BB_TS * 8) % 128 == 16,
-                "coefficient slices 16 bytes apart modulo 128");
-};
+__device__ int g_mac_wait_errors;
 
-__device__ __forceinline__ void cp_async8(uint64_t *dst, const uint64_t *src, bool valid) {
-  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
-  // src-size 0 fills the 8 bytes with zeros and reads nothing
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(src),
-               "r"(valid ? 8 : 0));
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
 }
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;\n" ::);
+__device__ __forceinline__ void mbar_init(uint64_t *bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count));
 }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done;
+}
+// bounded wait for the phase of `parity` to complete
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  for (long long it = 0; it < MM_WAIT_LIMIT; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+// TMA tile loads into shared memory, completion counted on `bar`
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(smem_addr(dst)),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_5d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, int c4, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n" ::"r"(smem_addr(dst)),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_addr(bar))
+      : "memory");
 }
 
 // d = a b (fresh accumulators)
@@ -89,7 +122,6 @@ __device__ __forceinline__ void mma_u8_zero(uint32_t (&d)[4], uint32_t a0, uint3
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
-
 // c += a b
 __device__ __forceinline__ void mma_u8_acc(uint32_t (&c)[4], uint32_t a0, uint32_t a1,
                                            uint32_t a2, uint32_t a3, uint32_t b0,
@@ -114,7 +146,7 @@ __device__ __forceinline__ void mma_diagonals(uint32_t (&acc)[14][4], const uint
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int d = 2 * a + j;
-      if (FIRST && a == (d <= 7 ? 0 : (d - 6) / 2))
+      if (FIRST && a == (d <= 7 ? 0 : (d - 6) / 2))  // the first tile of diagonal d
         mma_u8_zero(acc[d], A0[2 * a], A0[2 * a + 1], A1[2 * a], A1[2 * a + 1], B0[j], B1[j]);
       else
         mma_u8_acc(acc[d], A0[2 * a], A0[2 * a + 1], A1[2 * a], A1[2 * a + 1], B0[j], B1[j]);
@@ -134,13 +166,15 @@ __device__ __forceinline__ void byte_transpose4(uint32_t x0, uint32_t x1, uint32
   r[3] = __byte_perm(e1, f1, 0x7632);
 }
 
-// Four consecutive staged words (16-byte aligned) -> R[k] = byte k of each,
-// k = 0..7.
-__device__ __forceinline__ void load_bytes4(const uint64_t *p, uint32_t *R) {
-  const uint4 v0 = *reinterpret_cast<const uint4 *>(p);
-  const uint4 v1 = *reinterpret_cast<const uint4 *>(p + 2);
-  byte_transpose4(v0.x, v0.z, v1.x, v1.z, R);      // low words: bytes 0-3
-  byte_transpose4(v0.y, v0.w, v1.y, v1.w, R + 4);  // high words: bytes 4-7
+// The staged words of four consecutive babies (1024 bytes apart in a box)
+// -> R[k] = byte k of each, k = 0..7.
+__device__ __forceinline__ void load_bytes4(const uint8_t *p, uint32_t *R) {
+  const uint2 w0 = *reinterpret_cast<const uint2 *>(p);
+  const uint2 w1 = *reinterpret_cast<const uint2 *>(p + 1024);
+  const uint2 w2 = *reinterpret_cast<const uint2 *>(p + 2048);
+  const uint2 w3 = *reinterpret_cast<const uint2 *>(p + 3072);
+  byte_transpose4(w0.x, w1.x, w2.x, w3.x, R);      // low words: bytes 0-3
+  byte_transpose4(w0.y, w1.y, w2.y, w3.y, R + 4);  // high words: bytes 4-7
 }
 
 // value = sum_s D[s] 2^(8s) as (hi, lo); the host guarantees value < 2^128
@@ -158,104 +192,107 @@ __device__ __forceinline__ void combine_diagonals(const uint32_t (&D)[15], uint6
   hi = (W[1] >> 32) + W[2] + (W[3] << 32) + (lo < W[0]);
 }
 
-// grid (ceil(cts / (4 NCB)), N / (T * TILES), l), 32 T NCB threads,
-// MmaShape<T, NCB>::SMEM bytes.  Warp w computes coefficient w / NCB of each
-// tile for column block w % NCB.  Limb i reduces modulo prime i for i < ql
-// and prime L + i - ql after it.
-template <int T, int NCB>
-__global__ void __launch_bounds__(32 * T * NCB, 16 / (T * NCB)) mac_mma_kernel(
-    const uint64_t *__restrict__ babies, int baby_count, int cts,
-    const uint64_t *__restrict__ pts, int g0, int G, int l,
-    uint64_t *__restrict__ out, int out_giants, int giant_major,
-    const Mod *__restrict__ mods, int ql, int L) {
-  using S = MmaShape<T, NCB>;
-  extern __shared__ __align__(16) uint64_t smem[];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// grid (ceil(cts / 4), N / (16 * TILES), l), 512 threads, MM_SMEM bytes.
+// Warp w computes coefficient w of each 16-coefficient tile for the block's 4
+// ciphertexts (8 columns).  Limb i reduces modulo prime i for i < ql and
+// prime L + i - ql after it.  tm_pt: the launch's G giants' plaintext rows,
+// dims (coefficient, limb, giant, baby); tm_bb: the babies, dims
+// (coefficient, limb, poly, ciphertext, baby).
+__global__ void __launch_bounds__(MM_THREADS, 1) mac_mma_kernel(
+    const __grid_constant__ CUtensorMap tm_pt, const __grid_constant__ CUtensorMap tm_bb,
+    int baby_count, int cts, int g0, int G, int l, uint64_t *__restrict__ out, int out_giants,
+    int giant_major, const Mod *__restrict__ mods, int ql, int L) {
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzled boxes need 1024-byte aligned destinations
+  uint8_t *const sbase = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *const full = reinterpret_cast<uint64_t *>(sbase + MM_STAGES * MM_STAGE);
+  uint64_t *const empty = full + MM_STAGES;
+  const int tid = threadIdx.x, lane = tid & 31, wt = tid >> 5;
   const int gid = lane >> 2, tq = lane & 3;
-  const int wt = warp / NCB, cb = warp % NCB;
   const int cg = blockIdx.x, limb = blockIdx.z;
   const size_t pw = (size_t)l * kN, cw = 2 * pw;
   const int kchunks = (baby_count + MM_KC - 1) / MM_KC;
   const int stages = MM_TILES * kchunks;
   const int tile0 = blockIdx.y * MM_TILES;
 
-  // copy roles: coefficient lt of the tile; in copy round k the thread
-  // copies baby lb of row group k * RSTEP + lrow (plaintext row groups are
-  // giants, baby row groups (ciphertext, poly) columns, 32 babies each), so
-  // every copy of a stage is a fixed base + the stage's offset + a row stride
-  constexpr int RPR = S::THREADS / T;  // staged rows per copy round
-  static_assert(RPR % 32 == 0, "copy rounds cover whole 32-baby row groups");
-  constexpr int RSTEP = RPR / 32;
-  const int lt = tid % T, lr = tid / T, lb = lr & 31, lrow = lr >> 5;
-  const int valid_cts = min(S::CTS, cts - cg * S::CTS);
-  // rows past the last baby are zero-filled: their source stays at a valid
-  // address (baby min(lb, B - 1) of the first baby chunk) and reads nothing
-  const int lb_c = min(lb, baby_count - 1);
-  const size_t gstride = (size_t)baby_count * pw, cstride = (size_t)baby_count * cw;
-  const uint64_t *pt_base =
-      pts + ((size_t)g0 * baby_count + lb_c) * pw + (size_t)limb * kN + lt;
-  const uint64_t *bb_base =
-      babies + ((size_t)cg * S::CTS * baby_count + lb_c) * cw + (size_t)limb * kN + lt;
-  uint64_t *const pt_dst = smem + lt * S::PT_TS + lb;
-  uint64_t *const bb_dst = smem + T * S::PT_TS + lt * S::BB_TS + lb;
-
-  // issue cursor: tile, baby chunk and buffer of the next stage to load
-  int i_tile = 0, i_kc = 0, i_buf = 0, i_left = stages;
-  auto issue = [&]() {
-    if (i_left > 0) {
-      const int kb = i_kc * MM_KC;
-      const size_t n0 = (size_t)(tile0 + i_tile) * T;
-      const bool ok = kb + lb < baby_count;
-      const size_t poff = (ok ? (size_t)kb * pw : 0) + n0;
-      const size_t boff = (ok ? (size_t)kb * cw : 0) + n0;
-      const size_t so = (size_t)i_buf * S::STAGE_WORDS;
-#pragma unroll
-      for (int k = 0; k < 8 / RSTEP; ++k) {  // plaintext rows: 8 giants x 32 babies
-        const int g = k * RSTEP + lrow;
-        if (g < G) cp_async8(pt_dst + so + g * MM_ROW, pt_base + g * gstride + poff, ok);
-      }
-#pragma unroll
-      for (int k = 0; k < S::COLS / RSTEP; ++k) {  // baby rows: COLS x 32 babies
-        const int c = k * RSTEP + lrow, ct = c >> 1;
-        if (ct < valid_cts)
-          cp_async8(bb_dst + so + c * MM_ROW, bb_base + ct * cstride + (c & 1) * pw + boff, ok);
-      }
-      --i_left;
-      if (++i_kc == kchunks) i_kc = 0, ++i_tile;
-      if (++i_buf == S::STAGES) i_buf = 0;
+  if (tid == 0) {
+    for (int i = 0; i < MM_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], MM_WARPS);
     }
-    cp_async_commit();
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+
+  // issue cursor, used by thread 0 alone; false when the buffer never came
+  // free (a bounded wait on its empty barrier timed out)
+  int i_tile = 0, i_kc = 0, i_buf = 0, issued = 0;
+  auto issue = [&]() -> bool {
+    if (tid == 0 && issued < stages) {
+      // the previous use of this buffer (stage issued - STAGES) must be read
+      if (issued >= MM_STAGES &&
+          !mbar_wait(&empty[i_buf], (uint32_t)(issued / MM_STAGES - 1) & 1))
+        return false;
+      uint8_t *st = sbase + i_buf * MM_STAGE;
+      const int n0 = (tile0 + i_tile) * MM_T, kb = i_kc * MM_KC;
+      mbar_expect_tx(&full[i_buf], MM_STAGE);
+      tma_load_4d(st, &tm_pt, n0, limb, 0, kb, &full[i_buf]);
+      tma_load_5d(st + MM_BOX, &tm_bb, n0, limb, 0, cg * 4, kb, &full[i_buf]);
+      ++issued;
+      if (++i_kc == kchunks) i_kc = 0, ++i_tile;
+      if (++i_buf == MM_STAGES) i_buf = 0;
+    }
+    return true;
   };
+  for (int k = 0; k < MM_STAGES - 1; ++k) issue();
 
   const Mod M = mods[limb < ql ? limb : L + limb - ql];
-  // acc[s]: the tiles (a, j) with 2a + j = s summed by the tensor cores over
-  // babies and stages; c0, c1 (rows gid: byte 2a) add to diagonal s,
-  // c2, c3 (rows gid + 8: byte 2a + 1) to diagonal s + 1
+  // word (coefficient wt, giant or column gid, baby b) of a box: row b * 8 +
+  // gid of 128 bytes, its 16-byte chunk XORed with gid; this lane's four
+  // babies tq*4 .. tq*4 + 3 (and + 16) are 1024 bytes apart
+  const uint32_t frag =
+      gid * 128 + (((((uint32_t)wt >> 1) ^ gid) << 4) | ((wt & 1) << 3)) + tq * 4096;
   uint32_t acc[14][4];
-
-  for (int k = 0; k < S::STAGES - 1; ++k) issue();
   int c_tile = 0, c_kc = 0, c_buf = 0;
+  uint32_t parity = 0;
+  // a lost stage (bounded wait timed out) at stage s: count it; the issuing
+  // thread lets its loads still in flight (stages s .. issued - 1, one per
+  // buffer, so their parities are exact) land before the block's shared
+  // memory is released
+  auto give_up = [&](int s) {
+    if (lane == 0) atomicAdd(&g_mac_wait_errors, 1);
+    if (tid == 0)
+      for (int k = s; k < issued; ++k)
+        mbar_wait(&full[k % MM_STAGES], (uint32_t)(k / MM_STAGES) & 1);
+  };
   for (int s = 0; s < stages; ++s) {
-    cp_async_wait<S::STAGES - 2>();
-    __syncthreads();
-    issue();
-    const uint64_t *st = smem + (size_t)c_buf * S::STAGE_WORDS;
-    const uint64_t *prow = st + wt * S::PT_TS + gid * MM_ROW + tq * 4;
-    const uint64_t *brow =
-        st + T * S::PT_TS + wt * S::BB_TS + (cb * 8 + gid) * MM_ROW + tq * 4;
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[c_buf], parity))) {  // warp-uniform
+      give_up(s);
+      return;
+    }
+    const uint8_t *st = sbase + c_buf * MM_STAGE;
     uint32_t A0[8], A1[8], B0[8], B1[8];
-    load_bytes4(prow, A0);
-    load_bytes4(prow + 16, A1);
-    load_bytes4(brow, B0);
-    load_bytes4(brow + 16, B1);
+    load_bytes4(st + frag, A0);
+    load_bytes4(st + frag + 16 * 1024, A1);
+    load_bytes4(st + MM_BOX + frag, B0);
+    load_bytes4(st + MM_BOX + frag + 16 * 1024, B1);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[c_buf]);  // this warp is done with the buffer
+    // stage s + 2 into the buffer of stage s - 1; warp 0 reconverges on
+    // thread 0's outcome before its mma.sync
+    const bool issued_ok = __shfl_sync(0xffffffffu, issue(), 0);
+    if (!issued_ok) {
+      give_up(s + 1);
+      return;
+    }
     if (c_kc == 0)
       mma_diagonals<true>(acc, A0, A1, B0, B1);
     else
       mma_diagonals<false>(acc, A0, A1, B0, B1);
     if (c_kc == kchunks - 1) {
-      // this thread's outputs: giant gid, ciphertext cg*CTS + cb*4 + tq, polys 0, 1
-      const int ct = cg * S::CTS + cb * 4 + tq;
-      const size_t n = (size_t)(tile0 + c_tile) * T + wt;
+      // this thread's outputs: giant gid, ciphertext cg*4 + tq, polys 0, 1
+      const int ct = cg * 4 + tq;
+      const size_t n = (size_t)(tile0 + c_tile) * MM_T + wt;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t D[15];
@@ -273,9 +310,8 @@ __global__ void __launch_bounds__(32 * T * NCB, 16 / (T * NCB)) mac_mma_kernel(
       }
     }
     if (++c_kc == kchunks) c_kc = 0, ++c_tile;
-    if (++c_buf == S::STAGES) c_buf = 0;
+    if (++c_buf == MM_STAGES) c_buf = 0, parity ^= 1;
   }
-  cp_async_wait<0>();
 }
 
 int ceil_log2(int x) {
@@ -284,14 +320,30 @@ int ceil_log2(int x) {
   return b;
 }
 
+using TensorMapEncoder = PFN_cuTensorMapEncodeTiled_v12000;
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library); null when the driver does not provide it
+TensorMapEncoder tensor_map_encoder() {
+  static const TensorMapEncoder fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (TensorMapEncoder) nullptr;
+    return reinterpret_cast<TensorMapEncoder>(p);
+  }();
+  return fn;
+}
+
 }  // namespace
 
 // True when the tensor-core MAC runs this call: it is exact (every limb's
 // prime q has baby_count * (q - 1)^2 < 2^128, so the recombined byte sums fit
 // the 128-bit Barrett input, and baby_count <= 1024, so the diagonal sums fit
 // 32 bits) and the batch has at least two ciphertexts (one ciphertext fills
-// a quarter of the 8 columns of a tile: the CUDA-core kernel is faster there,
-// 1.2 against 1.7 ms at the linear block's chunk on B200).
+// a quarter of the 8 columns of a tile: the CUDA-core kernel is faster there).
 bool mac_mma_eligible(const b2f_context *ctx, int baby_count, int l, int ql, int cts) {
   if (ctx->mac_path == 1 || baby_count > 1024 || cts < 2) return false;
   int bits = 0;
@@ -302,31 +354,54 @@ bool mac_mma_eligible(const b2f_context *ctx, int baby_count, int l, int ql, int
   return 2 * bits + ceil_log2(baby_count) <= 128;
 }
 
-template <int T, int NCB>
-static int launch_shape(b2f_context *ctx, const uint64_t *babies, int baby_count,
-                        const uint64_t *pts, int g0, int G, int l, uint64_t *out,
-                        int out_giants, int cts, int giant_major, int ql, cudaStream_t s) {
-  using S = MmaShape<T, NCB>;
-  static_assert(kN % (T * MM_TILES) == 0, "tiles must cover N");
+// Launches the G <= 8 giants from g0 on; -1 (nothing launched) when the
+// operands cannot be described as tensor maps (a base address that is not
+// 16-byte aligned, or no tensor-map encoder), so the caller takes the
+// CUDA-core kernel.
+int launch_mac_mma(b2f_context *ctx, const uint64_t *babies, int baby_count,
+                   const uint64_t *pts, int g0, int G, int l, uint64_t *out,
+                   int out_giants, int cts, int giant_major, int ql, cudaStream_t s) {
+  static_assert(kN % (MM_T * MM_TILES) == 0, "tiles must cover N");
+  const TensorMapEncoder enc = tensor_map_encoder();
+  if (!enc) return -1;
+  const cuuint64_t pw = (cuuint64_t)l * kN, B = (cuuint64_t)baby_count;
+  const cuuint32_t unit[5] = {1, 1, 1, 1, 1};
+  CUtensorMap tm_pt, tm_bb;
+  // plaintext rows [giant][baby][limb][N] from giant g0: dims (n, limb, giant, baby)
+  const cuuint64_t pdim[4] = {(cuuint64_t)kN, (cuuint64_t)l, (cuuint64_t)G, B};
+  const cuuint64_t pstride[3] = {kN * 8ull, B * pw * 8, pw * 8};
+  const cuuint32_t pbox[4] = {MM_T, 1, 8, MM_KC};
+  if (enc(&tm_pt, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4,
+          const_cast<uint64_t *>(pts) + (size_t)g0 * baby_count * pw, pdim, pstride, pbox, unit,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return -1;
+  // babies [ct][baby][poly][limb][N]: dims (n, limb, poly, ct, baby)
+  const cuuint64_t bdim[5] = {(cuuint64_t)kN, (cuuint64_t)l, 2, (cuuint64_t)cts, B};
+  const cuuint64_t bstride[4] = {kN * 8ull, pw * 8, B * 2 * pw * 8, 2 * pw * 8};
+  const cuuint32_t bbox[5] = {MM_T, 1, 2, 4, MM_KC};
+  if (enc(&tm_bb, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5, const_cast<uint64_t *>(babies), bdim,
+          bstride, bbox, unit, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return -1;
   static bool attr_set[64] = {};
   if (!attr_set[ctx->device & 63]) {
-    B2F_CUDA(cudaFuncSetAttribute(mac_mma_kernel<T, NCB>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM));
+    B2F_CUDA(cudaFuncSetAttribute(mac_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)MM_SMEM));
     attr_set[ctx->device & 63] = true;
   }
-  const dim3 grid((cts + S::CTS - 1) / S::CTS, kN / (T * MM_TILES), l);
-  mac_mma_kernel<T, NCB><<<grid, S::THREADS, S::SMEM, s>>>(babies, baby_count, cts, pts, g0, G, l,
-                                                    out, out_giants, giant_major, ctx->d_mod,
-                                                    ql, ctx->L);
+  const dim3 grid((cts + 3) / 4, kN / (MM_T * MM_TILES), l);
+  mac_mma_kernel<<<grid, MM_THREADS, MM_SMEM, s>>>(tm_pt, tm_bb, baby_count, cts, g0, G, l, out,
+                                                   out_giants, giant_major, ctx->d_mod, ql,
+                                                   ctx->L);
   B2F_LAUNCHED("mac_mma_kernel");
   return B2F_OK;
 }
 
-int launch_mac_mma(b2f_context *ctx, const uint64_t *babies, int baby_count,
-                   const uint64_t *pts, int g0, int G, int l, uint64_t *out,
-                   int out_giants, int cts, int giant_major, int ql, cudaStream_t s) {
-  return launch_shape<16, 1>(ctx, babies, baby_count, pts, g0, G, l, out, out_giants, cts,
-                             giant_major, ql, s);
-}
-
 }  // namespace b2f
+
+extern "C" int b2f_mac_wait_errors(void) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, b2f::g_mac_wait_errors, sizeof(int)) != cudaSuccess) return -1;
+  return v;
+}

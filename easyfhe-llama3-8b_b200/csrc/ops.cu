@@ -268,8 +268,8 @@ int launch_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
     if (mma) {
       const int rc = launch_mac_mma(ctx, babies, baby_count, pts, g0, G, l, out,
                                     giant_count, cts, giant_major, ql, s);
-      if (rc) return rc;
-      continue;
+      if (rc > 0) return rc;
+      if (rc == 0) continue;
     }
     mac_kernel<<<dim3(cts, kN / TPB, l), TPB, 0, s>>>(
         babies, baby_count, pts, g0, G, l, out, giant_count, giant_major,

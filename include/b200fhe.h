@@ -336,6 +336,11 @@ int b2f_set_mac_path(b2f_context *ctx, int path);
  * current path, else 0. */
 int b2f_mac_uses_tensor_cores(const b2f_context *ctx, int baby_count, int q_limbs,
                               int p_limbs, int num_cts);
+/* Stages the tensor-core MAC gave up waiting for (its bounded waits on the
+ * TMA loads timed out; the block ended and its outputs are not written) since
+ * the library loaded, on the current device; 0 on a healthy run, -1 when the
+ * counter cannot be read. */
+int b2f_mac_wait_errors(void);
 
 /* ---- calibration (no reference counterpart) ----
  * Rate of the NTT's lazy Shoup butterfly from registers alone (every SM

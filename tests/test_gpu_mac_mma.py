@@ -20,6 +20,21 @@ from _ckks import N, pair, rand_residues, to_dev, to_host
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, scope="module")
+def _release_cached_blocks():
+    """These tests hold several GB of torch-allocated operands; hand the
+    cached blocks back so later tests' own allocations (the library's stream
+    -ordered pool) find the memory."""
+
+    yield
+    import gc
+
+    import torch
+
+    gc.collect()
+    torch.cuda.empty_cache()
+
+
 @pytest.mark.parametrize("bits,C,B,G,l", [
     (60, 7, 37, 5, 1),    # ragged: fewer than 64 babies, 8 giants, 8 ciphertexts
     (60, 9, 70, 9, 1),    # two column groups, two baby stages, two giant launches
@@ -120,6 +135,25 @@ def test_single_ciphertext_takes_cuda_cores():
     ctx.set_mac_path("cuda_cores")
     assert ctx.mac_kernel(64, 3, num_cts=16) == "mac_kernel"
     ctx.set_mac_path("auto")
+
+
+def test_tensor_core_mac_waits_never_time_out():
+    """Every stage the tensor-core MAC waited for in this process arrived (its
+    bounded TMA waits count a timeout instead of hanging)."""
+
+    from easyfhe import _native
+
+    ctx, _ = pair(4, 1, 2, 60)
+    ctx.set_mac_path("auto")
+    C, B, G, l = 5, 40, 3, 2
+    rng = np.random.default_rng(9)
+    babies = rand_residues(rng, ctx.primes[:l], C * B * 2)
+    pts = rand_residues(rng, ctx.primes[:l], G * B)
+    ctx.mac(to_dev(babies), B, to_dev(pts), G, l, num_cts=C)
+    import torch
+
+    torch.cuda.synchronize()
+    assert _native.lib.b2f_mac_wait_errors() == 0
 
 
 def test_set_mac_path_rejects_unknown():
