@@ -663,7 +663,7 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
     m1.record(stream)
     torch.cuda.synchronize()
     mac_ms = m0.elapsed_time(m1) / mac_reps
-    mac_name = ctx.native.mac_kernel(B, level, num_cts=per)
+    mac_name = ctx.native.mac_kernel(B, level, num_cts=per, giant_count=G0)
     on_tc = mac_name == "mac_mma_kernel"
     mac_peak = ctx.native.mma_u8_peak() if on_tc else ctx.native.mac_peak()
     del babies, batch
@@ -999,7 +999,7 @@ def run_mac(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict | No
     torch.cuda.synchronize()
     launches = (_native.lib.b2f_launch_count() - n0) // a.steps
     ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
-    kernel = ctx.mac_kernel(B, l, num_cts=C)
+    kernel = ctx.mac_kernel(B, l, num_cts=C, giant_count=G)
     peak = ctx.mma_u8_peak() if kernel == "mac_mma_kernel" else ctx.mac_peak()
     if rank:
         return None

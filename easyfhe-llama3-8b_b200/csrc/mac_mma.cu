@@ -339,13 +339,15 @@ TensorMapEncoder tensor_map_encoder() {
 
 }  // namespace
 
-// True when the tensor-core MAC runs this call: it is exact (every limb's
-// prime q has baby_count * (q - 1)^2 < 2^128, so the recombined byte sums fit
-// the 128-bit Barrett input, and baby_count <= 1024, so the diagonal sums fit
-// 32 bits) and the batch has at least two ciphertexts (one ciphertext fills
-// a quarter of the 8 columns of a tile: the CUDA-core kernel is faster there).
+// True when the tensor-core MAC runs this call's launches of 4 or more
+// giants: it is exact (every limb's prime q has baby_count * (q - 1)^2 <
+// 2^128, so the recombined byte sums fit the 128-bit Barrett input, and
+// baby_count <= 1024, so the diagonal sums fit 32 bits) and the tiles are
+// full enough to beat the CUDA cores: at least two ciphertexts (of a tile's
+// 4), 16 babies (of a 32-baby step) and, per launch, 4 giants (of 8).  The
+// bootstrap's transforms (4-8 babies, 4 giants) stay on the CUDA cores.
 bool mac_mma_eligible(const b2f_context *ctx, int baby_count, int l, int ql, int cts) {
-  if (ctx->mac_path == 1 || baby_count > 1024 || cts < 2) return false;
+  if (ctx->mac_path == 1 || baby_count > 1024 || baby_count < 16 || cts < 2) return false;
   int bits = 0;
   for (int i = 0; i < l; ++i) {
     const uint64_t q = ctx->primes[i < ql ? i : ctx->L + i - ql];

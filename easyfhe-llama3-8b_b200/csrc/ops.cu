@@ -265,7 +265,7 @@ int launch_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
   const bool mma = mac_mma_eligible(ctx, baby_count, l, ql, cts);
   for (int g0 = 0; g0 < giant_count; g0 += GMAX) {
     const int G = std::min(GMAX, giant_count - g0);
-    if (mma) {
+    if (mma && G >= 4) {
       const int rc = launch_mac_mma(ctx, babies, baby_count, pts, g0, G, l, out,
                                     giant_count, cts, giant_major, ql, s);
       if (rc > 0) return rc;
@@ -506,12 +506,15 @@ int b2f_set_mac_path(b2f_context *ctx, int path) {
   return B2F_OK;
 }
 
-int b2f_mac_uses_tensor_cores(const b2f_context *ctx, int baby_count, int q_limbs,
-                              int p_limbs, int num_cts) {
-  if (!ctx || baby_count < 1 || q_limbs < 1 || q_limbs > ctx->L || p_limbs < 0 ||
-      p_limbs > ctx->K)
+int b2f_mac_uses_tensor_cores(const b2f_context *ctx, int baby_count, int giant_count,
+                              int q_limbs, int p_limbs, int num_cts) {
+  if (!ctx || baby_count < 1 || giant_count < 1 || q_limbs < 1 || q_limbs > ctx->L ||
+      p_limbs < 0 || p_limbs > ctx->K)
     return 0;
-  return mac_mma_eligible(ctx, baby_count, q_limbs + p_limbs, q_limbs, num_cts) ? 1 : 0;
+  return mac_mma_eligible(ctx, baby_count, q_limbs + p_limbs, q_limbs, num_cts) &&
+                 std::min(GMAX, giant_count) >= 4
+             ? 1
+             : 0;
 }
 
 int b2f_pairwise_mac(b2f_context *ctx, const uint64_t *cts, const uint64_t *pts,

@@ -370,12 +370,13 @@ class NativeContext:
         call("b2f_set_mac_path", self.handle, self.MAC_PATHS[path])
 
     def mac_kernel(self, baby_count: int, q_limbs: int, p_limbs: int = 0,
-                   num_cts: int = 2) -> str:
-        """The kernel a MAC of this shape runs under the current path:
-        "mac_mma_kernel" (u8 tensor cores) or "mac_kernel" (CUDA cores)."""
+                   num_cts: int = 2, giant_count: int = 8) -> str:
+        """The kernel a MAC of this shape runs (its first launch of up to 8
+        giants) under the current path: "mac_mma_kernel" (u8 tensor cores) or
+        "mac_kernel" (CUDA cores)."""
 
-        on_tc = lib.b2f_mac_uses_tensor_cores(self.handle, int(baby_count), int(q_limbs),
-                                              int(p_limbs), int(num_cts))
+        on_tc = lib.b2f_mac_uses_tensor_cores(self.handle, int(baby_count), int(giant_count),
+                                              int(q_limbs), int(p_limbs), int(num_cts))
         return "mac_mma_kernel" if on_tc else "mac_kernel"
 
     def mac_peak(self, iters: int = 2000) -> float:

@@ -325,17 +325,17 @@ int b2f_mac_ext(b2f_context *ctx, const uint64_t *babies, int baby_count,
                 uint64_t *out, int num_cts, void *stream);
 /* Which units run the multiply-accumulate of b2f_mac, b2f_mac_ext and
  * b2f_bsgs_mac(_batch): path 0 (the default) the u8 tensor cores on the byte
- * split of the residues for batches of two or more ciphertexts wherever the
- * sum is exact (baby_count <= 1024 and baby_count * q^2 < 2^128 for every
- * prime of the call), the CUDA cores otherwise; path 1 the CUDA cores always.
- * Both give the same residues.  Inputs are canonical residues (below their
- * prime). */
+ * split of the residues for launches of 4-8 giants over 16-1024 babies and
+ * two or more ciphertexts wherever the sum is exact (baby_count * q^2 <
+ * 2^128 for every prime of the call), the CUDA cores otherwise; path 1 the
+ * CUDA cores always.  Both give the same residues.  Inputs are canonical
+ * residues (below their prime). */
 int b2f_set_mac_path(b2f_context *ctx, int path);
-/* 1 when a MAC of num_cts ciphertexts x baby_count babies over
- * Q_{q_limbs} u P_{p_limbs} runs on the tensor cores under the context's
- * current path, else 0. */
-int b2f_mac_uses_tensor_cores(const b2f_context *ctx, int baby_count, int q_limbs,
-                              int p_limbs, int num_cts);
+/* 1 when a MAC of num_cts ciphertexts x baby_count babies x giant_count
+ * giants over Q_{q_limbs} u P_{p_limbs} runs (its first launch of up to 8
+ * giants) on the tensor cores under the context's current path, else 0. */
+int b2f_mac_uses_tensor_cores(const b2f_context *ctx, int baby_count, int giant_count,
+                              int q_limbs, int p_limbs, int num_cts);
 /* Stages the tensor-core MAC gave up waiting for (its bounded waits on the
  * TMA loads timed out; the block ended and its outputs are not written) since
  * the library loaded, on the current device; 0 on a healthy run, -1 when the

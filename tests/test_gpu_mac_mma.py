@@ -37,10 +37,12 @@ def _release_cached_blocks():
 
 @pytest.mark.parametrize("bits,C,B,G,l", [
     (60, 7, 37, 5, 1),    # ragged: fewer than 64 babies, 8 giants, 8 ciphertexts
-    (60, 9, 70, 9, 1),    # two column groups, two baby stages, two giant launches
-    (50, 2, 130, 3, 2),   # binary64-path primes, three baby stages
-    (61, 3, 64, 2, 1),    # 61-bit primes at the 128-bit bound
-    (60, 2, 1, 1, 1),     # two ciphertexts, one baby, one giant
+    (60, 9, 70, 9, 1),    # three column groups, three baby stages, 8 giants on the
+                          # tensor cores and the ninth on the CUDA cores
+    (50, 2, 130, 4, 2),   # binary64-path primes, five baby stages
+    (61, 3, 64, 4, 1),    # 61-bit primes at the 128-bit bound
+    (60, 2, 16, 4, 1),    # the smallest shape the tensor cores take
+    (60, 2, 1, 1, 1),     # one baby, one giant: the CUDA-core kernel
     (60, 1, 40, 3, 1),    # one ciphertext: the CUDA-core kernel
 ])
 def test_mac_mma_matches_oracle(bits, C, B, G, l):
@@ -60,7 +62,7 @@ def test_mac_mma_extended_basis_matches_oracle():
 
     ctx, orc = pair(4, 2, 2, 60)
     ctx.set_mac_path("auto")
-    ql, K, C, B, G = 2, ctx.K, 3, 20, 3
+    ql, K, C, B, G = 2, ctx.K, 3, 20, 4
     primes = ctx.primes[:ql] + ctx.primes[4:4 + K]
     rng = np.random.default_rng(77)
     babies = rand_residues(rng, primes, C * B * 2).reshape(C, B, 2, ql + K, N)
@@ -85,12 +87,12 @@ def test_mac_extreme_residues_and_bound(bits, B, kernel):
 
     ctx, _ = pair(4, 1, 2, bits)
     ctx.set_mac_path("auto")
-    C, G, l = 3, 2, 2
+    C, G, l = 3, 4, 2
     q = np.array(ctx.primes[:l], dtype=np.uint64)
     top = torch.tensor([int(v) - 1 for v in q], dtype=torch.int64, device="cuda:0")
     db = top[None, None, :, None].expand(C * B, 2, l, N).contiguous()
     dp = top[None, :, None].expand(G * B, l, N).contiguous()
-    assert ctx.mac_kernel(B, l, num_cts=C) == kernel
+    assert ctx.mac_kernel(B, l, num_cts=C, giant_count=G) == kernel
     got = to_host(ctx.mac(db, B, dp, G, l, num_cts=C))
     want = np.broadcast_to((np.uint64(B) % q)[None, None, None, :, None], got.shape)
     assert np.array_equal(got, want)
@@ -118,20 +120,25 @@ def test_mac_mma_matches_cuda_cores_at_linear_block_shape():
     for path in ("cuda_cores", "auto"):
         ctx.set_mac_path(path)
         want = "mac_mma_kernel" if path == "auto" else "mac_kernel"
-        assert ctx.mac_kernel(B, l, num_cts=C) == want
+        assert ctx.mac_kernel(B, l, num_cts=C, giant_count=G) == want
         outs[path] = ctx.mac(babies, B, pts, G, l, num_cts=C)
     ctx.set_mac_path("auto")
     assert torch.equal(outs["auto"], outs["cuda_cores"])
 
 
-def test_single_ciphertext_takes_cuda_cores():
-    """One ciphertext fills a quarter of a tensor tile's columns: auto routes
-    it to the CUDA-core kernel, two or more to the tensor cores."""
+def test_sparse_tiles_take_cuda_cores():
+    """Auto routes a MAC to the tensor cores only where its tiles are full
+    enough: two or more ciphertexts (of 4 columns pairs), 16 or more babies
+    (of a 32-baby step), 4 or more giants in the launch (of 8); the
+    bootstrap's transforms (4-8 babies, 4 giants) stay on the CUDA cores."""
 
     ctx, _ = pair(4, 1, 2, 60)
     ctx.set_mac_path("auto")
     assert ctx.mac_kernel(64, 3, num_cts=1) == "mac_kernel"
     assert ctx.mac_kernel(64, 3, num_cts=2) == "mac_mma_kernel"
+    assert ctx.mac_kernel(8, 3, num_cts=16, giant_count=4) == "mac_kernel"
+    assert ctx.mac_kernel(16, 3, num_cts=16, giant_count=4) == "mac_mma_kernel"
+    assert ctx.mac_kernel(64, 3, num_cts=16, giant_count=3) == "mac_kernel"
     ctx.set_mac_path("cuda_cores")
     assert ctx.mac_kernel(64, 3, num_cts=16) == "mac_kernel"
     ctx.set_mac_path("auto")
@@ -145,7 +152,8 @@ def test_tensor_core_mac_waits_never_time_out():
 
     ctx, _ = pair(4, 1, 2, 60)
     ctx.set_mac_path("auto")
-    C, B, G, l = 5, 40, 3, 2
+    C, B, G, l = 5, 40, 4, 2
+    assert ctx.mac_kernel(B, l, num_cts=C, giant_count=G) == "mac_mma_kernel"
     rng = np.random.default_rng(9)
     babies = rand_residues(rng, ctx.primes[:l], C * B * 2)
     pts = rand_residues(rng, ctx.primes[:l], G * B)
