@@ -100,7 +100,8 @@ static Mod make_mod(uint64_t q) {
   M.q = q;
   M.m_lo = (uint64_t)m;
   M.m_hi = (uint64_t)(m >> 64);
-  M.pad = 0;
+  const int k = 63 - __builtin_clzll(q);
+  M.mu = (uint64_t)(((u128)1 << (64 + k)) / q);
   return M;
 }
 

@@ -318,7 +318,11 @@ int launch_moddown_rescale_conv(b2f_context *ctx, const uint64_t *acc,
 // Step 3: key inner product.  grid (N/TPB, items, l+K): the slowest grid
 // axis is the target limb, so a key limb shared by a batch, or an ext limb
 // shared by the hoisted rotations of one ciphertext (ext_stride = 0, c1_stride
-// = 0), is reused across the items in L2.
+// = 0), is reused across the items in L2.  BK: the sums (beta products, one
+// more with pre0) stay below 2^(64+k) for every prime of the launch, so the
+// one-word Barrett reduce_bk replaces the 128-bit one (the kernel is
+// issue-bound; the reduction was half its instructions).
+template <bool BK>
 __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
     const uint64_t *__restrict__ c1, long long c1_stride,
     const uint64_t *__restrict__ ext, long long ext_stride, const ItemKeys items,
@@ -367,8 +371,26 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
     mac128(s1, pre1[at], pm);
   }
   uint64_t *o = acc + ((size_t)it * 2 * lk + t) * kN + n;
-  o[0] = reduce128(s0.hi, s0.lo, M);
-  o[(size_t)lk * kN] = reduce128(s1.hi, s1.lo, M);
+  if (BK) {
+    o[0] = reduce_bk(s0.hi, s0.lo, M);
+    o[(size_t)lk * kN] = reduce_bk(s1.hi, s1.lo, M);
+  } else {
+    o[0] = reduce128(s0.hi, s0.lo, M);
+    o[(size_t)lk * kN] = reduce128(s1.hi, s1.lo, M);
+  }
+}
+
+// terms * (q - 1)^2 < 2^(64+k) for every prime of Q_l u P: sums of `terms`
+// products of residues may take reduce_bk
+bool sums_fit_reduce_bk(const b2f_context *ctx, int l, int terms) {
+  using u128 = unsigned __int128;
+  for (int t = 0; t < l + ctx->K; ++t) {
+    const uint64_t q = ctx->primes[t < l ? t : ctx->L + t - l];
+    const int k = 63 - __builtin_clzll(q);
+    if (k < 1 || k > 62 || (u128)(q - 1) * (q - 1) * (u128)terms >= (u128)1 << (64 + k))
+      return false;
+  }
+  return true;
 }
 
 // Step 3 in binary64 (every prime below 2^50): each product is an exact
@@ -554,8 +576,12 @@ int launch_key_inner_product(b2f_context *ctx, int items_n, const uint64_t *c1,
     key_inner_product_f64_kernel<<<dim3(kN / TPB / 2, items_n, l + K), TPB, 0, s>>>(
         c1, c1_stride, ext, ext_stride, items, acc, ctx->d_primes, ctx->d_qinv, l, K,
         ctx->L, ctx->alpha, beta, pre0, pre1, pre_stride, ctx->d_pmod);
+  else if (sums_fit_reduce_bk(ctx, l, beta + (pre0 != nullptr)))
+    key_inner_product_kernel<true><<<grid, TPB, 0, s>>>(
+        c1, c1_stride, ext, ext_stride, items, acc, ctx->d_mod, l, K, ctx->L,
+        ctx->alpha, beta, pre0, pre1, pre_stride, ctx->d_pmod);
   else
-    key_inner_product_kernel<<<grid, TPB, 0, s>>>(
+    key_inner_product_kernel<false><<<grid, TPB, 0, s>>>(
         c1, c1_stride, ext, ext_stride, items, acc, ctx->d_mod, l, K, ctx->L,
         ctx->alpha, beta, pre0, pre1, pre_stride, ctx->d_pmod);
   B2F_LAUNCHED("key_inner_product_kernel");

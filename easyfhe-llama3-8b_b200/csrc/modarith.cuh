@@ -16,7 +16,7 @@ struct Mod {
   uint64_t q;     // the prime
   uint64_t m_lo;  // floor(2^128 / q), low word
   uint64_t m_hi;  // floor(2^128 / q), high word
-  uint64_t pad;
+  uint64_t mu;    // floor(2^(64+k) / q), k = bitlen(q) - 1 (reduce_bk)
 };
 
 __host__ __device__ __forceinline__ uint64_t mulhi64(uint64_t a, uint64_t b) {
@@ -108,6 +108,23 @@ __host__ __device__ __forceinline__ uint64_t reduce128(uint64_t hi, uint64_t lo,
   const uint64_t qe = hi * M.m_hi + a.hi + b.hi + carry;
   const uint64_t r = lo - qe * M.q;
   return csub(r, M.q);
+}
+// (hi*2^64 + lo) mod q for a value s below 2^(64+k), k = bitlen(q) - 1 (a
+// sum of a few products of residues: terms * (q-1)^2 < 2^(64+k), checked by
+// the caller).  Barrett with a one-word quotient estimate:
+// qe = floor(floor(s / 2^k) * mu / 2^64), mu = floor(2^(64+k) / q), never
+// above floor(s/q) and at most 2 below it, so s - qe q < 3q < 2^64 comes from
+// the low words and two conditional subtractions finish it.
+__host__ __device__ __forceinline__ uint64_t reduce_bk(uint64_t hi, uint64_t lo,
+                                                       const Mod &M) {
+#ifdef __CUDA_ARCH__
+  const int k = 63 - __clzll((long long)M.q);
+#else
+  const int k = 63 - __builtin_clzll(M.q);
+#endif
+  const uint64_t x = (hi << (64 - k)) | (lo >> k);
+  const uint64_t r = lo - mulhi64(x, M.mu) * M.q;
+  return csub(csub(r, 2 * M.q), M.q);
 }
 __host__ __device__ __forceinline__ uint64_t mul_mod(uint64_t a, uint64_t b,
                                                      const Mod &M) {
