@@ -74,6 +74,9 @@ def parse():
     ap.add_argument("--no-layer", action="store_true",
                     help="skip the Layer-0 run the default line carries at N = 1")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--conv-path", default="auto", choices=["auto", "tcgen05", "mma_sync"],
+                    help="key-switch base conversions: the faster kernel of each (auto), "
+                         "tcgen05 or mma.sync for both")
     ap.add_argument("--mac-path", default="auto", choices=["auto", "cuda_cores"],
                     help="BSGS multiply-accumulate kernel: u8 tensor cores where exact "
                          "(auto) or the CUDA-core kernel")
@@ -561,6 +564,7 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
         fhe.CKKSContextSpec(depth=37, log_n=16, dnum=5, dcrt_bits=59, first_mod=60,
                             rotations=tuple(sorted(rotations)), seed=21), dev)
     ctx.native.set_mac_path(a.mac_path)
+    ctx.native.set_conv_path(a.conv_path)
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
     Gm = torch.randn(D, D, dtype=torch.float64, device=dev, generator=gen) / math.sqrt(D)
@@ -768,6 +772,7 @@ def run_hrotate(a, dev, rank: int, world: int, barrier, max_over_ranks,
         params = core.Params.uniform(a.limbs, a.special, a.dnum, bits=50)
     ctx = core.NativeContext(params, dev)
     ctx.set_arith(a.arith)
+    ctx.set_conv_path(a.conv_path)
     l, C = a.limbs, a.batch
     if not 1 <= l <= params.L:
         raise SystemExit(f"--limbs {l} outside the chain's 1..{params.L}")

@@ -155,6 +155,10 @@ struct b2f_context {
   // BSGS multiply-accumulate: 0 = tensor cores wherever exact (mac_mma.cu),
   // 1 = CUDA cores only (b2f_set_mac_path)
   int mac_path = 0;
+  // fast base conversions of the key switch (b2f_set_conv_path): 0 = the
+  // faster kernel of each, measured on B200 (ModDown on tcgen05, ModUp on
+  // mma.sync), 1 = mma.sync for both, 2 = tcgen05 (conv_umma.cu) for both
+  int conv_path = 0;
   double *d_twd_fwd = nullptr, *d_twd_inv = nullptr, *d_qinv = nullptr;
   double *d_md_conv_f64 = nullptr;  // L x K: [Phat_k] mod q_i as doubles
   ulonglong2 *d_ninv = nullptr;       // L+K: N^-1
@@ -180,6 +184,12 @@ bool mac_mma_eligible(const b2f_context *ctx, int baby_count, int l, int ql, int
 int launch_mac_mma(b2f_context *ctx, const uint64_t *babies, int baby_count,
                    const uint64_t *pts, int g0, int G, int l, uint64_t *out,
                    int out_giants, int cts, int giant_major, int ql, cudaStream_t s);
+
+// tcgen05 base conversions (conv_umma.cu); -1 when the shape is not taken
+int launch_modup_conv_umma(b2f_context *ctx, const uint64_t *xt, uint64_t *ext, int l,
+                           int cts, cudaStream_t s);
+int launch_moddown_conv_umma(b2f_context *ctx, const uint64_t *acc, uint64_t *conv, int l,
+                             int cts, cudaStream_t s);
 
 const LimbJob *job_table(b2f_context *ctx, const std::vector<int> &key,
                          const std::vector<LimbJob> &jobs);

@@ -248,6 +248,10 @@ int set_smem(Kern k, size_t bytes) {
 
 int launch_modup_conv(b2f_context *ctx, const uint64_t *xt, uint64_t *ext, int l,
                       int cts, cudaStream_t s) {
+  if (ctx->conv_path == 2) {
+    const int rc = launch_modup_conv_umma(ctx, xt, ext, l, cts, s);
+    if (rc >= 0) return rc;
+  }
   const LevelTables &T = ctx->levels[l];
   const int K = ctx->K, lk = l + K, kp = conv_kpad(ctx->alpha);
   const size_t sm = conv_mma_smem(kp, lk);
@@ -272,6 +276,10 @@ int launch_modup_conv(b2f_context *ctx, const uint64_t *xt, uint64_t *ext, int l
 
 int launch_moddown_conv(b2f_context *ctx, const uint64_t *acc, uint64_t *conv,
                         int l, int cts, cudaStream_t s) {
+  if (ctx->conv_path == 0 || ctx->conv_path == 2) {
+    const int rc = launch_moddown_conv_umma(ctx, acc, conv, l, cts, s);
+    if (rc >= 0) return rc;
+  }
   const int K = ctx->K, kp = conv_kpad(K);
   const size_t sm = conv_mma_smem(kp, l);
   const dim3 grid(kN / CNB, 2, cts);

@@ -94,6 +94,8 @@ _SIGS = {
     "b2f_set_mac_path": (_int, [_vp, _int]),
     "b2f_mac_uses_tensor_cores": (_int, [_vp, _int, _int, _int, _int, _int]),
     "b2f_mac_wait_errors": (_int, []),
+    "b2f_set_conv_path": (_int, [_vp, _int]),
+    "b2f_conv_wait_errors": (_int, []),
     "b2f_encode": (_int, [_vp, _vp, _int, _int, _dbl, _int, _int, _vp, _vp, _size, _vp]),
     "b2f_encode_workspace": (_size, [_vp, _int, _int]),
     "b2f_decode": (_int, [_vp, _vp, _int, _int, _dbl, _vp, _vp, _size, _vp]),

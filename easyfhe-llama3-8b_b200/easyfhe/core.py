@@ -358,6 +358,18 @@ class NativeContext:
         call("b2f_butterfly_peak", self.handle, int(iters), ctypes.byref(out), _stream())
         return float(out.value)
 
+    CONV_PATHS = {"auto": 0, "mma_sync": 1, "tcgen05": 2}
+
+    def set_conv_path(self, path: str) -> None:
+        """Kernels of the key switch's fast base conversions (ModUp, ModDown):
+        'auto' (the default: the faster of each, ModDown on tcgen05 with the
+        accumulators in tensor memory, ModUp on mma.sync), 'mma_sync' or
+        'tcgen05' for both.  All give identical residues."""
+
+        if path not in self.CONV_PATHS:
+            raise ValueError(f"conv path {path!r} not in {sorted(self.CONV_PATHS)}")
+        call("b2f_set_conv_path", self.handle, self.CONV_PATHS[path])
+
     MAC_PATHS = {"auto": 0, "cuda_cores": 1}
 
     def set_mac_path(self, path: str) -> None:

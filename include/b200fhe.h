@@ -341,6 +341,18 @@ int b2f_mac_uses_tensor_cores(const b2f_context *ctx, int baby_count, int giant_
  * the library loaded, on the current device; 0 on a healthy run, -1 when the
  * counter cannot be read. */
 int b2f_mac_wait_errors(void);
+/* Which tensor-core kernels run the fast base conversions of the key switch
+ * (ModUp step 2, ModDown's P-to-Q step): tcgen05.mma kind::i8 with the
+ * accumulators in tensor memory (up to 64 targets, else mma.sync) or the
+ * warp-level mma.sync kernel.  Path 0 (the default): the faster of the two
+ * for each, measured on B200 (ModDown on tcgen05, ModUp on mma.sync); path 1:
+ * mma.sync for both; path 2: tcgen05 for both.  All give the same residues. */
+int b2f_set_conv_path(b2f_context *ctx, int path);
+/* Tiles the tcgen05 conversion gave up waiting for (its bounded wait on the
+ * MMAs' completion timed out; the block's outputs are not written) since the
+ * library loaded, on the current device; 0 on a healthy run, -1 when the
+ * counter cannot be read. */
+int b2f_conv_wait_errors(void);
 
 /* ---- calibration (no reference counterpart) ----
  * Rate of the NTT's lazy Shoup butterfly from registers alone (every SM
