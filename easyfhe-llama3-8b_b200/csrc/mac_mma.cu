@@ -34,12 +34,13 @@
 // the 32 lanes' 8-byte fragment loads (giant = group id, baby = 4 thread-in-
 // group values) meet 4 to a bank instead of 32.  Out-of-range giants, babies
 // and ciphertexts arrive as zeros.  Three stages, each with a "full" mbarrier
-// (the two loads landed) and an "empty" one (all 16 warps have their fragments
-// in registers): warps run unsynchronised, up to two stages apart, and the
-// issuing thread waits only before it refills a buffer.  Every wait is bounded
-// and a timeout ends the block with an error count.  The byte
-// transposition into fragments is a 4 x 4 byte transpose (8 byte permutes per
-// 4 registers).
+// (the two loads landed) and an "empty" one (all 16 warps have their
+// fragments in registers): warps run unsynchronised, up to two stages apart,
+// and the issuing thread waits only before it refills a buffer.  A tile's
+// outputs are staged in shared memory and stored as 128-byte rows (for 4+
+// ciphertexts).  Every wait is bounded and a timeout ends the block with an
+// error count.  The byte transposition into fragments is a 4 x 4 byte
+// transpose (8 byte permutes per 4 registers).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -56,7 +57,9 @@ constexpr int MM_THREADS = 512;                // one warp per coefficient of th
 constexpr int MM_BOX = MM_T * 8 * MM_KC * 8;   // bytes of one box (32 KB)
 constexpr int MM_STAGE = 2 * MM_BOX;           // plaintext box, then baby box
 constexpr int MM_WARPS = MM_THREADS / 32;
-constexpr size_t MM_SMEM = (size_t)MM_STAGES * MM_STAGE + 1024 + 64;
+constexpr int MM_OUT_ROWS = 8 * 4 * 2;               // (giant, ciphertext, poly) of a block
+constexpr int MM_OUT = MM_OUT_ROWS * MM_T * 8;       // bytes of one staged output tile
+constexpr size_t MM_SMEM = (size_t)MM_STAGES * MM_STAGE + 128 + 2 * MM_OUT + 1024;
 constexpr long long MM_WAIT_LIMIT = 1ll << 24;  // try_wait polls before a stage is declared lost
 static_assert(MM_THREADS == 32 * MM_T, "one warp per coefficient");
 static_assert(MM_SMEM <= 227 * 1024, "stage buffers exceed shared memory");
@@ -198,6 +201,7 @@ __device__ __forceinline__ void combine_diagonals(const uint32_t (&D)[15], uint6
 // prime L + i - ql after it.  tm_pt: the launch's G giants' plaintext rows,
 // dims (coefficient, limb, giant, baby); tm_bb: the babies, dims
 // (coefficient, limb, poly, ciphertext, baby).
+template <bool STAGE_OUT>
 __global__ void __launch_bounds__(MM_THREADS, 1) mac_mma_kernel(
     const __grid_constant__ CUtensorMap tm_pt, const __grid_constant__ CUtensorMap tm_bb,
     int baby_count, int cts, int g0, int G, int l, uint64_t *__restrict__ out, int out_giants,
@@ -207,6 +211,9 @@ __global__ void __launch_bounds__(MM_THREADS, 1) mac_mma_kernel(
   uint8_t *const sbase = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *const full = reinterpret_cast<uint64_t *>(sbase + MM_STAGES * MM_STAGE);
   uint64_t *const empty = full + MM_STAGES;
+  uint64_t *const staged = empty + MM_STAGES;  // two: a tile's outputs all staged
+  // two output tiles [row = (giant * 4 + ciphertext) * 2 + poly][16 coefficients]
+  uint64_t *const obuf = reinterpret_cast<uint64_t *>(sbase + MM_STAGES * MM_STAGE + 128);
   const int tid = threadIdx.x, lane = tid & 31, wt = tid >> 5;
   const int gid = lane >> 2, tq = lane & 3;
   const int cg = blockIdx.x, limb = blockIdx.z;
@@ -220,6 +227,8 @@ __global__ void __launch_bounds__(MM_THREADS, 1) mac_mma_kernel(
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], MM_WARPS);
     }
+    mbar_init(&staged[0], MM_WARPS);
+    mbar_init(&staged[1], MM_WARPS);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   __syncthreads();
@@ -290,9 +299,14 @@ __global__ void __launch_bounds__(MM_THREADS, 1) mac_mma_kernel(
     else
       mma_diagonals<false>(acc, A0, A1, B0, B1);
     if (c_kc == kchunks - 1) {
-      // this thread's outputs: giant gid, ciphertext cg*4 + tq, polys 0, 1
-      const int ct = cg * 4 + tq;
-      const size_t n = (size_t)(tile0 + c_tile) * MM_T + wt;
+      // this thread's outputs: giant gid, ciphertext cg*4 + tq, polys 0, 1 at
+      // coefficient wt.  STAGE_OUT (4+ ciphertexts): into the tile's staging
+      // buffer; once all 16 warps have staged theirs, each warp stores 4 rows
+      // of 16 coefficients (128 bytes), 16x fewer store transactions than a
+      // word per row.  Below 4 ciphertexts the rendezvous costs more than it
+      // saves (it holds back the warp that issues the loads): direct stores.
+      uint64_t *ob = obuf + (c_tile & 1) * (MM_OUT_ROWS * MM_T);
+      const int my_ct = cg * 4 + tq;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t D[15];
@@ -302,10 +316,34 @@ __global__ void __launch_bounds__(MM_THREADS, 1) mac_mma_kernel(
         D[14] = acc[13][h + 2];
         uint64_t hi, lo;
         combine_diagonals(D, hi, lo);
-        if (gid < G && ct < cts) {
-          const size_t slot = giant_major ? (size_t)(g0 + gid) * cts + ct
-                                          : (size_t)ct * out_giants + g0 + gid;
-          out[slot * cw + h * pw + (size_t)limb * kN + n] = reduce128(hi, lo, M);
+        const uint64_t v = reduce128(hi, lo, M);
+        if (STAGE_OUT) {
+          ob[((gid * 4 + tq) * 2 + h) * MM_T + wt] = v;
+        } else if (gid < G && my_ct < cts) {  // fewer than 4 ciphertexts: store directly
+          const size_t slot = giant_major ? (size_t)(g0 + gid) * cts + my_ct
+                                          : (size_t)my_ct * out_giants + g0 + gid;
+          out[slot * cw + h * pw + (size_t)limb * kN + (size_t)(tile0 + c_tile) * MM_T + wt] =
+              v;
+        }
+      }
+    }
+    if (STAGE_OUT && c_kc == kchunks - 1) {
+      uint64_t *ob = obuf + (c_tile & 1) * (MM_OUT_ROWS * MM_T);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&staged[c_tile & 1]);
+      if (!__all_sync(0xffffffffu, mbar_wait(&staged[c_tile & 1], (c_tile >> 1) & 1))) {
+        give_up(s + 1);
+        return;
+      }
+      const size_t n0 = (size_t)(tile0 + c_tile) * MM_T;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int row = 4 * wt + 2 * k + (lane >> 4), t = lane & 15;
+        const int g = row >> 3, ct = cg * 4 + ((row >> 1) & 3), h = row & 1;
+        if (g < G && ct < cts) {
+          const size_t slot = giant_major ? (size_t)(g0 + g) * cts + ct
+                                          : (size_t)ct * out_giants + g0 + g;
+          out[slot * cw + h * pw + (size_t)limb * kN + n0 + t] = ob[row * MM_T + t];
         }
       }
     }
@@ -388,14 +426,21 @@ int launch_mac_mma(b2f_context *ctx, const uint64_t *babies, int baby_count,
     return -1;
   static bool attr_set[64] = {};
   if (!attr_set[ctx->device & 63]) {
-    B2F_CUDA(cudaFuncSetAttribute(mac_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)MM_SMEM));
+    B2F_CUDA(cudaFuncSetAttribute(mac_mma_kernel<true>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MM_SMEM));
+    B2F_CUDA(cudaFuncSetAttribute(mac_mma_kernel<false>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MM_SMEM));
     attr_set[ctx->device & 63] = true;
   }
   const dim3 grid((cts + 3) / 4, kN / (MM_T * MM_TILES), l);
-  mac_mma_kernel<<<grid, MM_THREADS, MM_SMEM, s>>>(tm_pt, tm_bb, baby_count, cts, g0, G, l, out,
-                                                   out_giants, giant_major, ctx->d_mod, ql,
-                                                   ctx->L);
+  if (cts >= 4)
+    mac_mma_kernel<true><<<grid, MM_THREADS, MM_SMEM, s>>>(tm_pt, tm_bb, baby_count, cts, g0,
+                                                           G, l, out, out_giants, giant_major,
+                                                           ctx->d_mod, ql, ctx->L);
+  else
+    mac_mma_kernel<false><<<grid, MM_THREADS, MM_SMEM, s>>>(tm_pt, tm_bb, baby_count, cts, g0,
+                                                            G, l, out, out_giants, giant_major,
+                                                            ctx->d_mod, ql, ctx->L);
   B2F_LAUNCHED("mac_mma_kernel");
   return B2F_OK;
 }
