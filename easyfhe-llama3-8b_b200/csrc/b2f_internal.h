@@ -156,8 +156,8 @@ struct b2f_context {
   // 1 = CUDA cores only (b2f_set_mac_path)
   int mac_path = 0;
   // fast base conversions of the key switch (b2f_set_conv_path): 0 = the
-  // faster kernel of each, measured on B200 (ModDown on tcgen05, ModUp on
-  // mma.sync), 1 = mma.sync for both, 2 = tcgen05 (conv_umma.cu) for both
+  // faster kernel, measured on B200 (ModDown of 16+ ciphertexts on tcgen05,
+  // the rest on mma.sync), 1 = mma.sync always, 2 = tcgen05 (conv_umma.cu)
   int conv_path = 0;
   double *d_twd_fwd = nullptr, *d_twd_inv = nullptr, *d_qinv = nullptr;
   double *d_md_conv_f64 = nullptr;  // L x K: [Phat_k] mod q_i as doubles

@@ -362,9 +362,10 @@ class NativeContext:
 
     def set_conv_path(self, path: str) -> None:
         """Kernels of the key switch's fast base conversions (ModUp, ModDown):
-        'auto' (the default: the faster of each, ModDown on tcgen05 with the
-        accumulators in tensor memory, ModUp on mma.sync), 'mma_sync' or
-        'tcgen05' for both.  All give identical residues."""
+        'auto' (the default: the faster, the ModDown conversion of 16+
+        ciphertexts on tcgen05 with the accumulators in tensor memory, the
+        rest on mma.sync), 'mma_sync' or 'tcgen05' for both.  All give
+        identical residues."""
 
         if path not in self.CONV_PATHS:
             raise ValueError(f"conv path {path!r} not in {sorted(self.CONV_PATHS)}")

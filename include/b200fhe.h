@@ -344,9 +344,10 @@ int b2f_mac_wait_errors(void);
 /* Which tensor-core kernels run the fast base conversions of the key switch
  * (ModUp step 2, ModDown's P-to-Q step): tcgen05.mma kind::i8 with the
  * accumulators in tensor memory (up to 64 targets, else mma.sync) or the
- * warp-level mma.sync kernel.  Path 0 (the default): the faster of the two
- * for each, measured on B200 (ModDown on tcgen05, ModUp on mma.sync); path 1:
- * mma.sync for both; path 2: tcgen05 for both.  All give the same residues. */
+ * warp-level mma.sync kernel.  Path 0 (the default): the faster of the two,
+ * measured on B200 (the ModDown conversion of 16 or more ciphertexts on
+ * tcgen05, everything else on mma.sync); path 1: mma.sync always; path 2:
+ * tcgen05 for both conversions.  All give the same residues. */
 int b2f_set_conv_path(b2f_context *ctx, int path);
 /* Tiles the tcgen05 conversion gave up waiting for (its bounded wait on the
  * MMAs' completion timed out; the block's outputs are not written) since the

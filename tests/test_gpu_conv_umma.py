@@ -2,7 +2,8 @@
 
 Every key switch converts digits to the other primes (ModUp) and the special
 primes back to Q (ModDown).  On the tcgen05 path both conversions run on
-tcgen05.mma with the accumulators in tensor memory (by default ModDown does);
+tcgen05.mma with the accumulators in tensor memory (by default the ModDown
+conversion of 16+ ciphertexts does);
 the rotations below must be bit-identical on every path (tcgen05, mma.sync,
 the default mix) and to the CPU oracle, at the layer's parameters (59/60-bit primes, dnum 5, K = 8:
 ModUp digits of 13/16 targets at l = 13 and 38 targets at l = 38, which takes
