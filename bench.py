@@ -77,6 +77,9 @@ def parse():
     ap.add_argument("--conv-path", default="auto", choices=["auto", "tcgen05", "mma_sync"],
                     help="key-switch base conversions: the faster kernel of each (auto), "
                          "tcgen05 or mma.sync for both")
+    ap.add_argument("--giant-chain", default="extended", choices=["extended", "rotations"],
+                    help="BSGS Horner chain over the giants: kept in Q_l u P with one "
+                         "ModDown per chain (extended) or a full HRotate per giant")
     ap.add_argument("--mac-path", default="auto", choices=["auto", "cuda_cores"],
                     help="BSGS multiply-accumulate kernel: u8 tensor cores where exact "
                          "(auto) or the CUDA-core kernel")
@@ -333,6 +336,7 @@ def run_bootstrap(a, ctx_dev, rank: int, world: int, barrier, max_over_ranks) ->
     client, ctx = fhe.generate_client_context(
         fhe.CKKSContextSpec(depth=37, log_n=16, dnum=5, dcrt_bits=59, first_mod=60,
                             rotations=rots, seed=11 + rank), dev)
+    ctx.native.set_giant_chain(a.giant_chain)
     program = bs.generate(ctx, spec)
     rng = np.random.default_rng(77 + rank)
     n = ctx.max_slots
@@ -565,6 +569,7 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
                             rotations=tuple(sorted(rotations)), seed=21), dev)
     ctx.native.set_mac_path(a.mac_path)
     ctx.native.set_conv_path(a.conv_path)
+    ctx.native.set_giant_chain(a.giant_chain)
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
     Gm = torch.randn(D, D, dtype=torch.float64, device=dev, generator=gen) / math.sqrt(D)

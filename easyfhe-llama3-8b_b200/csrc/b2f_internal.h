@@ -159,6 +159,9 @@ struct b2f_context {
   // faster kernel, measured on B200 (ModDown of 16+ ciphertexts on tcgen05,
   // the rest on mma.sync), 1 = mma.sync always, 2 = tcgen05 (conv_umma.cu)
   int conv_path = 0;
+  // the BSGS giant chain (b2f_set_giant_chain): 0 = kept in Q_l u P with one
+  // ModDown per chain, 1 = a full rotation (ModDown of both polys) per giant
+  int giant_chain = 0;
   double *d_twd_fwd = nullptr, *d_twd_inv = nullptr, *d_qinv = nullptr;
   double *d_md_conv_f64 = nullptr;  // L x K: [Phat_k] mod q_i as doubles
   ulonglong2 *d_ninv = nullptr;       // L+K: N^-1
@@ -188,8 +191,18 @@ int launch_mac_mma(b2f_context *ctx, const uint64_t *babies, int baby_count,
 // tcgen05 base conversions (conv_umma.cu); -1 when the shape is not taken
 int launch_modup_conv_umma(b2f_context *ctx, const uint64_t *xt, uint64_t *ext, int l,
                            int cts, cudaStream_t s);
+// polys: 2, or 1 for the first poly of each ciphertext at the pointers given
+// (pass both pointers offset by one poly to convert the second polys only)
 int launch_moddown_conv_umma(b2f_context *ctx, const uint64_t *acc, uint64_t *conv, int l,
-                             int cts, cudaStream_t s);
+                             int cts, cudaStream_t s, int polys = 2);
+
+// BSGS giant chain in Q_l u P (keyswitch.cu): giant j of ciphertext c at
+// sums + j gs + c cs (2 x l limbs, or 2 x (l+K) with ext) -> out
+// [cts][2][l][N] = Horner over the giants with the one giant key; G >= 2
+size_t giant_chain_workspace(const b2f_context *ctx, int cts, int l);
+int giant_chain_ext(b2f_context *ctx, const uint64_t *sums, int ext, long long gs,
+                    long long cs, int cts, int G, int l, uint64_t galois, const uint64_t *key,
+                    uint64_t *out, void *ws, size_t ws_bytes, cudaStream_t s);
 
 const LimbJob *job_table(b2f_context *ctx, const std::vector<int> &key,
                          const std::vector<LimbJob> &jobs);
@@ -212,6 +225,9 @@ struct ItemKeys;
 // A post-operation folded into that epilogue (the Paterson-Stockmeyer step
 // of homo_mul_relin_rescale_postop): the result times 2 (dbl), add_b
 // subtracted instead of added (add_neg), and cadd[i] added to poly 0.
+// second_only: only the second poly of each item (b = 1; conv's and acc's
+// layouts unchanged), written as one poly at out + keys.out(it, out_stride) +
+// i N; the conversion must come from conv (no z).
 struct EpiPostOp {
   int dbl = 0;
   int add_neg = 0;
@@ -222,7 +238,8 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
                 const uint64_t *acc, const uint64_t *add0, const uint64_t *add1,
                 long long add_stride, uint64_t *out, long long out_stride,
                 const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s,
-                const uint64_t *z = nullptr, const EpiPostOp *post = nullptr);
+                const uint64_t *z = nullptr, const EpiPostOp *post = nullptr,
+                bool second_only = false);
 // Rescale of num_polys polys [poly][l][N] (NTT form) to out [poly][l-1][N]:
 // last [poly][N] holds each poly's last limb in coefficient form; one forward
 // NTT launch lifts it to every q_i in its input stage and finishes

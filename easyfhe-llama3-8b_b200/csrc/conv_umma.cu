@@ -321,13 +321,13 @@ int launch_modup_conv_umma(b2f_context *ctx, const uint64_t *xt, uint64_t *ext, 
 
 // ModDown conversion (P to Q_l) on tcgen05; -1 when l > 64 or K > 16.
 int launch_moddown_conv_umma(b2f_context *ctx, const uint64_t *acc, uint64_t *conv, int l,
-                             int cts, cudaStream_t s) {
+                             int cts, cudaStream_t s, int polys) {
   const int K = ctx->K, kp = conv_kpad(K);
   if (l > 64 || kp > 128) return -1;
   const size_t sm = conv_umma_smem(kp, 8 * ((l + 1) & ~1));
   int rc;
   if ((rc = set_umma_smem((const void *)moddown_conv_umma_kernel, sm))) return rc;
-  const dim3 grid(kN / (UC_M * UC_TILES), 2, cts);
+  const dim3 grid(kN / (UC_M * UC_TILES), polys, cts);
   moddown_conv_umma_kernel<<<grid, UC_THREADS, sm, s>>>(acc, conv, ctx->d_moddown_bytes,
                                                         ctx->d_red79, l, K, kp);
   B2F_LAUNCHED("moddown_conv_umma_kernel");

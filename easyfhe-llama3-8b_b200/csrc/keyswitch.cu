@@ -274,19 +274,21 @@ int launch_modup_conv(b2f_context *ctx, const uint64_t *xt, uint64_t *ext, int l
   return B2F_OK;
 }
 
+// polys 1: the first poly of each ciphertext only (offset both pointers by
+// one poly for the second)
 int launch_moddown_conv(b2f_context *ctx, const uint64_t *acc, uint64_t *conv,
-                        int l, int cts, cudaStream_t s) {
+                        int l, int cts, cudaStream_t s, int polys = 2) {
   // tcgen05 by default only from 16 ciphertexts: per ModDown conversion at
   // l = 13 it takes 149 against 152.5 us there, but 83.5 / 79.5 us at 8,
   // 52.4 / 41.9 at 4 and 23.7 / 15.1 at 1 (64 coefficient tiles a launch
   // cannot fill the GPU)
   if (ctx->conv_path == 2 || (ctx->conv_path == 0 && cts >= 16)) {
-    const int rc = launch_moddown_conv_umma(ctx, acc, conv, l, cts, s);
+    const int rc = launch_moddown_conv_umma(ctx, acc, conv, l, cts, s, polys);
     if (rc >= 0) return rc;
   }
   const int K = ctx->K, kp = conv_kpad(K);
   const size_t sm = conv_mma_smem(kp, l);
-  const dim3 grid(kN / CNB, 2, cts);
+  const dim3 grid(kN / CNB, polys, cts);
   int rc;
 #define B2F_MODDOWN(KWV)                                                \
   if ((rc = set_smem(moddown_conv_mma_kernel<KWV>, sm))) return rc;     \
@@ -638,6 +640,40 @@ __global__ void __launch_bounds__(TPB) ext_combine_kernel(
   out[(((size_t)r * 2 + b) * lk + t) * kN + k] = v;
 }
 
+// One step of the BSGS giant chain kept in Q_l u P (Horner over the giants,
+// one ModDown at the end): for ciphertext c, limb t < l+K and poly b,
+//   out_b[t][k] = x_b[t][src] + acc_b[t][src] + s_b[t][k],  src = pi_g(k),
+// x_1 = 0 (the key switch replaced the second poly); x_0 the previous state's
+// first poly over Q_l u P ([c][2][l+K][N]) or, x_q, P times the first poly of
+// a Q_l ciphertext (zero on the P limbs); s the next giant's sum over
+// Q_l u P or, s_q, P times a Q_l ciphertext.  x and s at their ciphertext
+// strides (words).  grid (N/TPB, l+K, 2 C).
+__global__ void __launch_bounds__(TPB) giant_step_kernel(
+    const uint64_t *__restrict__ x, int x_q, long long x_cs, const uint64_t *__restrict__ acc,
+    const uint64_t *__restrict__ sg, int s_q, long long s_cs, uint64_t *__restrict__ out,
+    const Mod *__restrict__ mods, const uint64_t *__restrict__ pmod, int l, int K, int L,
+    uint32_t g) {
+  const int k = blockIdx.x * TPB + threadIdx.x;
+  const int t = blockIdx.y, b = blockIdx.z & 1, c = blockIdx.z >> 1;
+  const int lk = l + K;
+  const uint32_t src = auto_src(k, g);
+  const Mod M = mods[t < l ? t : L + (t - l)];
+  uint64_t v = acc[(((size_t)c * 2 + b) * lk + t) * kN + src];
+  if (b == 0) {
+    const uint64_t *x0 = x + c * x_cs + (size_t)t * kN + src;
+    if (!x_q)
+      v = add_mod(v, *x0, M.q);
+    else if (t < l)
+      v = add_mod(v, mul_mod(pmod[t], *x0, M), M.q);
+  }
+  const uint64_t *sb = sg + c * s_cs + ((size_t)b * (s_q ? l : lk) + t) * kN + k;
+  if (!s_q)
+    v = add_mod(v, *sb, M.q);
+  else if (t < l)
+    v = add_mod(v, mul_mod(pmod[t], *sb, M), M.q);
+  out[(((size_t)c * 2 + b) * lk + t) * kN + k] = v;
+}
+
 // ---------------------------------------------------------------------
 // host orchestration
 // ---------------------------------------------------------------------
@@ -783,6 +819,107 @@ bool valid_galois(uint64_t g) { return (g & 1) && g < 2ull * kN; }
 
 size_t rotate_workspace(const b2f_context *ctx, int cts, int l) {
   return modup_bytes(ctx, cts, l) + moddown_bytes(ctx, cts, l);
+}
+
+size_t giant_chain_workspace(const b2f_context *ctx, int cts, int l) {
+  const size_t lk = l + ctx->K, beta = ctx->levels[l].beta, c = cts;
+  return 3 * rnd(c * 2 * lk * kN) + 2 * rnd(c * l * kN) + rnd(c * beta * lk * kN) +
+         rnd(c * 2 * l * kN);
+}
+
+// Horner over the giants with the one giant key (acc = sum_{G-1}; acc =
+// rot(acc) + sum_j), the chain kept in Q_l u P: a rotation's key switch leaves
+// P times its result there (no ModDown), the next rotation ModDowns only the
+// state's second poly (the one it key-switches) and carries the first poly's
+// automorphism over in Q_l u P, and the next giant's sum joins (P times a Q_l
+// sum on the Q limbs, or an extended sum as it is).  One ModDown of both
+// polys ends the chain: per giant step a ModDown of one poly (K inverse, l
+// forward limb transforms) instead of two, and extended sums need no ModDown
+// of their own.  Giant j of ciphertext c: sums + j gs + c cs (words), 2 x l
+// limbs, or 2 x (l+K) with ext; out [cts][2][l][N]; G >= 2.
+int giant_chain_ext(b2f_context *ctx, const uint64_t *sums, int ext, long long gs,
+                    long long cs, int cts, int G, int l, uint64_t galois, const uint64_t *key,
+                    uint64_t *out, void *ws, size_t ws_bytes, cudaStream_t s) {
+  int rc = check_level(ctx, l, "b2f_giant_chain");
+  if (rc) return rc;
+  B2F_CHECK_ARG(valid_galois(galois), "b2f_giant_chain: giant galois element %llu is not "
+                "an odd residue below 2N", (unsigned long long)galois);
+  B2F_CHECK_ARG(G >= 2 && cts >= 1, "b2f_giant_chain: chain of %d giants, %d ciphertexts",
+                G, cts);
+  Scratch sc{ctx, s};
+  if ((rc = sc.init(ws, ws_bytes, giant_chain_workspace(ctx, cts, l)))) return rc;
+  const int K = ctx->K, lk = l + K, beta = ctx->levels[l].beta;
+  uint64_t *state[2] = {sc.take((size_t)cts * 2 * lk * kN),
+                        sc.take((size_t)cts * 2 * lk * kN)};
+  uint64_t *acc = sc.take((size_t)cts * 2 * lk * kN);
+  uint64_t *c1p = sc.take((size_t)cts * l * kN);
+  uint64_t *xt = sc.take((size_t)cts * l * kN);
+  uint64_t *extd = sc.take((size_t)cts * beta * lk * kN);
+  uint64_t *conv = sc.take((size_t)cts * 2 * l * kN);
+  const long long as = 2LL * lk * kN;
+  ItemKeys it{};
+  it.key[0] = key;
+  it.g[0] = (uint32_t)galois;
+  it.shared = 1;
+  const ItemKeys plain{{}, {1u}, {}, 1};
+  // inverse transforms of the P limbs of the second poly (in place), and of
+  // both polys for the last ModDown
+  std::vector<LimbJob> p1, p2;
+  for (int b = 0; b < 2; ++b)
+    for (int k = 0; k < K; ++k) {
+      const uint32_t off = (uint32_t)(b * lk + l + k);
+      const LimbJob j{off, off, (uint16_t)(ctx->L + k), (uint16_t)k, 0};
+      if (b) p1.push_back(j);
+      p2.push_back(j);
+    }
+  const LimbJob *d1 = job_table(ctx, {13, l}, p1);
+  const LimbJob *d2 = job_table(ctx, {3, l}, p2);
+  if (!d1 || !d2) return B2F_ERR_NOMEM;
+
+  uint64_t *x = nullptr;  // the state in Q_l u P, [cts][2][l+K][N]
+  const uint64_t *top = sums + (G - 1) * gs;
+  if (ext) {  // the last giant's extended sum is the first state (its own copy:
+              // the second poly's P limbs are transformed in place)
+    x = state[1];
+    B2F_CUDA(cudaMemcpy2DAsync(x, as * 8, top, cs * 8, as * 8, cts,
+                               cudaMemcpyDeviceToDevice, s));
+  }
+  for (int j = G - 2, cur = 0; j >= 0; --j, cur ^= 1) {
+    const uint64_t *c1 = top + (size_t)l * kN;
+    long long c1s = cs;
+    if (x) {  // ModDown of the state's second poly: c1p = (x_1 - C(x_1[P])) P^-1
+      if ((rc = launch_ntt(ctx, x, as, x, as, d1, K, cts, 1, ctx->d_moddown_scale, s)))
+        return rc;
+      if ((rc = launch_moddown_conv(ctx, x + (size_t)lk * kN, conv + (size_t)l * kN, l, cts,
+                                    s, 1)))
+        return rc;
+      if ((rc = ntt_moddown(ctx, conv, cts, l, lk, x, nullptr, nullptr, 0, c1p,
+                            (long long)l * kN, nullptr, plain, s, nullptr, nullptr, true)))
+        return rc;
+      c1 = c1p;
+      c1s = (long long)l * kN;
+    }
+    if ((rc = modup(ctx, c1, c1s, cts, l, xt, extd, s))) return rc;
+    if ((rc = launch_key_inner_product(ctx, cts, c1, c1s, extd, (long long)beta * lk * kN, it,
+                                       acc, l, s)))
+      return rc;
+    uint64_t *next = state[cur];
+    if (next == x) next = state[cur ^ 1];
+    giant_step_kernel<<<dim3(kN / TPB, lk, 2 * cts), TPB, 0, s>>>(
+        x ? x : top, x ? 0 : 1, x ? as : cs, acc, sums + j * gs, ext ? 0 : 1, cs, next,
+        ctx->d_mod, ctx->d_pmod, l, K, ctx->L, (uint32_t)galois);
+    B2F_LAUNCHED("giant_step_kernel");
+    x = next;
+  }
+  // the one ModDown of both polys
+  if ((rc = launch_ntt(ctx, x, as, x, as, d2, 2 * K, cts, 1, ctx->d_moddown_scale, s)))
+    return rc;
+  if (ctx->fp64 && ctx->d_md_conv_f64)
+    return ntt_moddown(ctx, conv, cts, l, lk, x, nullptr, nullptr, 0, out, 2LL * l * kN,
+                       nullptr, plain, s, x);
+  if ((rc = launch_moddown_conv(ctx, x, conv, l, cts, s))) return rc;
+  return ntt_moddown(ctx, conv, cts, l, lk, x, nullptr, nullptr, 0, out, 2LL * l * kN, nullptr,
+                     plain, s);
 }
 
 }  // namespace b2f
@@ -1182,6 +1319,34 @@ int b2f_moddown_ext(b2f_context *ctx, const uint64_t *in, int num_cts, int l,
   if ((rc = launch_moddown_conv(ctx, pcoef, conv, l, num_cts, s))) return rc;
   return ntt_moddown(ctx, conv, num_cts, l, lk, in, nullptr, nullptr, 0, out, 2LL * l * kN,
                      nullptr, ItemKeys{{}, {1u}, {}, 1}, s);
+}
+
+size_t b2f_giant_chain_workspace(const b2f_context *ctx, int num_cts, int l) {
+  if (!ctx || l < 1 || l > ctx->L || num_cts < 0) return 0;
+  return giant_chain_workspace(ctx, std::max(num_cts, 1), l);
+}
+
+int b2f_giant_chain(b2f_context *ctx, const uint64_t *sums, int extended, int num_cts,
+                    int giant_count, int l, uint64_t giant_galois, const uint64_t *giant_key,
+                    uint64_t *out, void *ws, size_t ws_bytes, void *stream) {
+  B2F_RANGE("b2f_giant_chain");
+  int rc = check_level(ctx, l, "b2f_giant_chain");
+  if (rc) return rc;
+  B2F_CHECK_ARG(sums && out && num_cts >= 0 && giant_count >= 1 &&
+                    (extended == 0 || extended == 1),
+                "b2f_giant_chain: bad argument");
+  B2F_CHECK_ARG(giant_count == 1 || giant_key,
+                "b2f_giant_chain: giant_count > 1 needs the giant rotation key");
+  if (!num_cts) return B2F_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const long long limbs = extended ? l + ctx->K : l, gs = 2 * limbs * kN;
+  if (giant_count == 1) {
+    if (extended) return b2f_moddown_ext(ctx, sums, num_cts, l, out, ws, ws_bytes, stream);
+    B2F_CUDA(cudaMemcpyAsync(out, sums, (size_t)num_cts * gs * 8, cudaMemcpyDeviceToDevice, s));
+    return B2F_OK;
+  }
+  return giant_chain_ext(ctx, sums, extended, gs, gs * giant_count, num_cts, giant_count, l,
+                         giant_galois, giant_key, out, ws, ws_bytes, s);
 }
 
 int b2f_automorphism(b2f_context *ctx, const uint64_t *in, uint64_t *out,

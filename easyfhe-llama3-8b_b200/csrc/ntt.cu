@@ -374,6 +374,9 @@ struct ModDownOut {
   // post-operation (EpiPostOp): x2, subtract add_b, add cadd[i] to poly 0
   int dbl, add_neg, has_cadd;
   uint64_t cadd[64];
+  // 1: the transform's items are the second polys of acc's items only (item
+  // it = transform item, b = 1), written as single polys: out(it) + i N
+  int one_poly = 0;
 };
 
 // The forward transform that finishes a ModDown runs on clusters of 8 CTAs
@@ -449,7 +452,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     // the epilogue's inputs for this CTA's block: into L2 while the
     // transform runs (bulk prefetch, 64 KiB per array)
     if (tid == 0) {
-      const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
+      const int it = epi.one_poly ? (int)item : (int)(item >> 1);
+      const int b = epi.one_poly ? 1 : (int)(item & 1), i = (int)job.out_off;
       const uint64_t *accl =
           epi.acc + (((size_t)it * 2 + b) * epi.lk + i) * kN + (size_t)rank * BLK;
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(accl), "r"(BLK * 8)
@@ -505,7 +509,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     if (!converted && epi.zK > 0) {
       // x = sum_k z_k c_{i,k}: K exact products (|.| <= q each, sum below
       // 2^52 for K <= 4), reduced to |x| <= q/2 before the first stage
-      const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
+      const int it = epi.one_poly ? (int)item : (int)(item >> 1);
+      const int b = epi.one_poly ? 1 : (int)(item & 1), i = (int)job.out_off;
       const uint64_t *zb = epi.z + (((size_t)it * 2 + b) * epi.lk + epi.l_out) * kN + c0;
 #pragma unroll
       for (int k = 0; k < 16; ++k) x[k] = 0.0;
@@ -617,7 +622,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
     for (int k = 0; k < 16; ++k) p[pad_step<2>() * k] = A::to_word(x[k]);
   }
   __syncwarp();
-  const int it = (int)(item >> 1), b = (int)(item & 1), i = (int)job.out_off;
+  const int it = epi.one_poly ? (int)item : (int)(item >> 1);
+  const int b = epi.one_poly ? 1 : (int)(item & 1), i = (int)job.out_off;
   const uint32_t ginv = galois_inverse(epi.items.g[epi.items.at(it)]);
   const uint64_t q = epi.primes[i];
   const ulonglong2 pi = epi.pinv[i];
@@ -629,7 +635,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NT, 2)
   const uint64_t *addl = b ? epi.add1 : epi.add0;
   if (addl) addl += epi.items.ct(it) * epi.add_stride + (size_t)i * kN;
   uint64_t *outl =
-      epi.out + epi.items.out(it, epi.out_stride) + ((size_t)b * epi.l_out + i) * kN;
+      epi.out + epi.items.out(it, epi.out_stride) +
+      ((size_t)(epi.one_poly ? 0 : b) * epi.l_out + i) * kN;
   // pairs of evaluations per lane, four pairs' loads issued together
 #pragma unroll
   for (int r0 = 0; r0 < SEG / 64; r0 += 4) {
@@ -766,7 +773,7 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
                 const uint64_t *acc, const uint64_t *add0, const uint64_t *add1,
                 long long add_stride, uint64_t *out, long long out_stride,
                 const ulonglong2 *qinv, const ItemKeys &keys, cudaStream_t s,
-                const uint64_t *z, const EpiPostOp *post) {
+                const uint64_t *z, const EpiPostOp *post, bool second_only) {
   std::vector<int> key = {0, q_limbs, 0};
   std::vector<LimbJob> jobs(q_limbs);
   for (int i = 0; i < q_limbs; ++i)
@@ -804,6 +811,15 @@ int ntt_moddown(b2f_context *ctx, uint64_t *conv, int items, int q_limbs, int lk
     return B2F_ERR_UNSUPPORTED;
   }
   const long long st = (long long)q_limbs * kN;
+  if (second_only) {  // the second poly of every item: conv [item][2][q_limbs]
+    if (z) {
+      set_error("ntt_moddown: one-poly ModDown takes its conversion from conv");
+      return B2F_ERR_UNSUPPORTED;
+    }
+    E.one_poly = 1;
+    return launch_ntt_impl(ctx, conv + st, 2 * st, conv + st, 2 * st, d, q_limbs, items, 0,
+                           nullptr, &E, s);
+  }
   return launch_ntt_impl(ctx, conv, st, conv, st, d, q_limbs, 2 * items, 0, nullptr, &E, s);
 }
 

@@ -499,6 +499,13 @@ int b2f_mac_ext(b2f_context *ctx, const uint64_t *babies, int baby_count,
                     num_cts, (cudaStream_t)stream, 0, q_limbs);
 }
 
+int b2f_set_giant_chain(b2f_context *ctx, int mode) {
+  B2F_CHECK_ARG(ctx, "b2f_set_giant_chain: null context");
+  B2F_CHECK_ARG(mode == 0 || mode == 1, "b2f_set_giant_chain: mode %d is not 0 or 1", mode);
+  ctx->giant_chain = mode;
+  return B2F_OK;
+}
+
 int b2f_set_mac_path(b2f_context *ctx, int path) {
   B2F_CHECK_ARG(ctx, "b2f_set_mac_path: null context");
   B2F_CHECK_ARG(path == 0 || path == 1, "b2f_set_mac_path: path %d is not 0 or 1", path);
@@ -539,7 +546,9 @@ size_t b2f_bsgs_mac_batch_workspace(const b2f_context *ctx, int num_cts,
                                     int giant_count, int l) {
   if (!ctx || l < 1 || l > ctx->L || num_cts < 0 || giant_count < 1) return 0;
   const size_t ct_words = 2 * (size_t)l * kN * std::max(num_cts, 1);
-  return (giant_count + 1) * ct_words * 8 + rotate_workspace(ctx, num_cts, l) + 512;
+  const size_t horner = ct_words * 8 + rotate_workspace(ctx, num_cts, l);
+  const size_t chain = giant_chain_workspace(ctx, std::max(num_cts, 1), l);
+  return giant_count * ct_words * 8 + std::max(horner, chain) + 512;
 }
 
 size_t b2f_bsgs_mac_workspace(const b2f_context *ctx, int l) {
@@ -582,6 +591,14 @@ int b2f_bsgs_mac_batch(b2f_context *ctx, const uint64_t *babies, int num_cts,
     cudaError_t e = cudaMemcpyAsync(out, inner, batch_words * 8,
                                     cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) rc = cuda_status(e, "b2f_bsgs_mac copy");
+  }
+  if (!rc && giant_count > 1 && ctx->giant_chain == 0) {
+    // Horner kept in Q_l u P: one ModDown per chain
+    rc = giant_chain_ext(ctx, inner, 0, (long long)batch_words, (long long)ct_words, num_cts,
+                         giant_count, l, giant_galois, giant_key, out, rot,
+                         need - giant_count * batch_words * 8, s);
+    if (owned) cudaFreeAsync(owned, s);
+    return rc;
   }
   // Horner over the giants: acc = inner[G-1]; acc = rot(acc) + inner[g]
   const uint64_t *acc = inner + (size_t)(giant_count - 1) * batch_words;

@@ -62,6 +62,9 @@ _SIGS = {
                                       _size, _vp]),
     "b2f_moddown_ext_workspace": (_size, [_vp, _int, _int]),
     "b2f_moddown_ext": (_int, [_vp, _vp, _int, _int, _vp, _vp, _size, _vp]),
+    "b2f_giant_chain_workspace": (_size, [_vp, _int, _int]),
+    "b2f_giant_chain": (_int, [_vp, _vp, _int, _int, _int, _int, _u64, _vp, _vp, _vp, _size,
+                               _vp]),
     "b2f_pairwise_mac": (_int, [_vp, _vp, _vp, _int, _int, _int, _int, _int, _vp, _vp]),
     "b2f_rescale_workspace": (_size, [_vp, _int, _int]),
     "b2f_rescale": (_int, [_vp, _vp, _vp, _int, _int, _vp, _size, _vp]),
@@ -96,6 +99,7 @@ _SIGS = {
     "b2f_mac_wait_errors": (_int, []),
     "b2f_set_conv_path": (_int, [_vp, _int]),
     "b2f_conv_wait_errors": (_int, []),
+    "b2f_set_giant_chain": (_int, [_vp, _int]),
     "b2f_encode": (_int, [_vp, _vp, _int, _int, _dbl, _int, _int, _vp, _vp, _size, _vp]),
     "b2f_encode_workspace": (_size, [_vp, _int, _int]),
     "b2f_decode": (_int, [_vp, _vp, _int, _int, _dbl, _vp, _vp, _size, _vp]),

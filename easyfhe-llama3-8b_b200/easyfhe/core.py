@@ -300,6 +300,19 @@ class NativeContext:
              ws.numel(), _stream())
         return out
 
+    def giant_chain(self, sums: torch.Tensor, extended: bool, num_cts: int, giant_count: int,
+                    l: int, giant_galois: int, giant_key: torch.Tensor | None) -> torch.Tensor:
+        """Horner over the giant sums [num_cts, G, 2, l (+K if extended), N]
+        with the giant rotation, kept in Q_l u P: [num_cts, 2, l, N]."""
+
+        out = self.empty(num_cts, 2, l)
+        ws = self.workspace(lib.b2f_giant_chain_workspace(self.handle, num_cts, l))
+        call("b2f_giant_chain", self.handle, _ptr(sums), int(bool(extended)), num_cts,
+             giant_count, l, int(giant_galois),
+             _ptr(giant_key) if giant_key is not None else None, _ptr(out), _ptr(ws),
+             ws.numel(), _stream())
+        return out
+
     def pairwise_mac(self, cts: torch.Tensor, pts: torch.Tensor, count: int, groups: int,
                      q_limbs: int, p_limbs: int, pt_limb_stride: int) -> torch.Tensor:
         out = self.empty(groups, 2, q_limbs + p_limbs)
@@ -370,6 +383,24 @@ class NativeContext:
         if path not in self.CONV_PATHS:
             raise ValueError(f"conv path {path!r} not in {sorted(self.CONV_PATHS)}")
         call("b2f_set_conv_path", self.handle, self.CONV_PATHS[path])
+
+    GIANT_CHAINS = {"extended": 0, "rotations": 1}
+
+    def set_giant_chain(self, mode: str) -> None:
+        """How bsgs_mac runs its Horner chain over the giants: 'extended'
+        (the default: the chain stays in Q_l u P, each step ModDowns only
+        the poly its key switch reads, one ModDown of both polys at the end)
+        or 'rotations' (a full HRotate per giant).  Both decrypt to the same
+        values; residues differ by the ModDown rounding."""
+
+        if mode not in self.GIANT_CHAINS:
+            raise ValueError(f"giant chain {mode!r} not in {sorted(self.GIANT_CHAINS)}")
+        call("b2f_set_giant_chain", self.handle, self.GIANT_CHAINS[mode])
+        self._giant_chain = mode
+
+    @property
+    def giant_chain_mode(self) -> str:
+        return getattr(self, "_giant_chain", "extended")
 
     MAC_PATHS = {"auto": 0, "cuda_cores": 1}
 

@@ -894,10 +894,11 @@ def hoisted_mac_sum(ct: Ciphertext, baby_offsets, plaintexts: Plaintext, giant_o
 
     strategy (llama3fhe/operators/linear/config.py:9, 286-305):
       normal           babies and MAC in Q_l; Horner over the giants with the
-                       one giant key;
+                       one giant key (by default the chain stays in Q_l u P
+                       and ModDowns once; NativeContext.set_giant_chain);
       ext_normal       babies left in Q_l u P, plaintexts encoded there
-                       (is_ext), MAC over Q_l u P, one ModDown per giant, then
-                       the same Horner chain;
+                       (is_ext), MAC over Q_l u P, then the same Horner chain
+                       over the extended sums;
       ext_double_hoist as ext_normal, but every giant sum but the first is
                        ModDown'ed, rotated by g * giant_offset with its own
                        key into Q_l u P, and the sum is ModDown'ed once."""
@@ -941,6 +942,12 @@ def hoisted_mac_sum(ct: Ciphertext, baby_offsets, plaintexts: Plaintext, giant_o
     inner = ctx.native.mac_ext(block.data, B, pts, G, l, num_cts=C)  # [C, G, 2, l+K, N]
     n = inner.shape[-1]
     shape = (2, l, n) if C == 1 else (C, 2, l, n)
+    if s == "ext_normal" and G > 1 and ctx.native.giant_chain_mode == "extended":
+        # the Horner chain straight from the extended sums, kept in Q_l u P:
+        # one ModDown per chain
+        gg, gkey = ctx.rotation_key(int(giant_offset), l)
+        out = ctx.native.giant_chain(inner, True, C, G, l, gg, gkey)
+        return Ciphertext(out.view(shape), state, ct.slots, ctx)
 
     # one ModDown launch for every giant's sum of every ciphertext
     first = 0 if s == "ext_normal" else 1

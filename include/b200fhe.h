@@ -284,7 +284,9 @@ int b2f_scalar_op(b2f_context *ctx, const uint64_t *a, uint64_t *out,
  * inner_g = sum_b pt[g*B + b] * babies[b]; out = Horner over the giants with
  * the rotation by giant_offset (key giant_key):
  *   acc = inner_{G-1}; acc = rot(acc) + inner_g for g = G-2..0.
- * babies: B ciphertexts at l limbs; pts: G*B plaintexts at l limbs. */
+ * babies: B ciphertexts at l limbs; pts: G*B plaintexts at l limbs.
+ * The chain runs as b2f_set_giant_chain selects (by default in Q_l u P,
+ * one ModDown per chain). */
 size_t b2f_bsgs_mac_workspace(const b2f_context *ctx, int l);
 int b2f_bsgs_mac(b2f_context *ctx, const uint64_t *babies, int baby_count,
                  const uint64_t *pts, int giant_count, int l,
@@ -354,6 +356,31 @@ int b2f_set_conv_path(b2f_context *ctx, int path);
  * library loaded, on the current device; 0 on a healthy run, -1 when the
  * counter cannot be read. */
 int b2f_conv_wait_errors(void);
+/* How b2f_bsgs_mac(_batch) runs its Horner chain over the giants (the one
+ * giant key, as llama3fhe/operators/linear/config.py:292-305 plans it for
+ * the `normal` strategy).  Mode 0 (the default): the chain stays in Q_l u P;
+ * each rotation's key switch leaves P times its result there, the next
+ * rotation ModDowns only the second poly (the one it key-switches), and one
+ * ModDown of both polys ends the chain.  Mode 1: each giant rotation is a
+ * full HRotate (ModDown of both polys) followed by the addition.  The
+ * results decrypt to the same values; mode 0 rounds once per step where
+ * mode 1 rounds twice, so residues differ. */
+int b2f_set_giant_chain(b2f_context *ctx, int mode);
+/* The Horner chain over the giants of fhe.hoisted_mac_sum by itself, kept in
+ * Q_l u P as b2f_set_giant_chain's mode 0 describes: sums [num_cts]
+ * [giant_count][2][limbs][N] as b2f_mac leaves them (limbs = l, extended =
+ * 0) or as b2f_mac_ext does (limbs = l + K, extended = 1: P times the giant
+ * sums, which then need no ModDown of their own) -> out [num_cts][2][l][N]
+ * = acc, acc = sum_{G-1}; acc = rot(acc) + sum_g for g = G-2..0 with the
+ * rotation by the giant offset (giant_galois, giant_key).  The `ext_normal`
+ * strategy's chain (llama3fhe/operators/transform.py:108-116,
+ * operators/linear/config.py:292-305): one ModDown per chain instead of one
+ * per giant sum and one per rotation.  giant_count 1: the ModDown of the
+ * extended sum, or a copy. */
+size_t b2f_giant_chain_workspace(const b2f_context *ctx, int num_cts, int l);
+int b2f_giant_chain(b2f_context *ctx, const uint64_t *sums, int extended, int num_cts,
+                    int giant_count, int l, uint64_t giant_galois, const uint64_t *giant_key,
+                    uint64_t *out, void *ws, size_t ws_bytes, void *stream);
 
 /* ---- calibration (no reference counterpart) ----
  * Rate of the NTT's lazy Shoup butterfly from registers alone (every SM

@@ -315,3 +315,47 @@ class Oracle:
         lib().orc_bsgs_mac(self._h, _p(_u64(babies)), num_cts, baby_count, _p(_u64(pts)),
                            giant_count, l, p_limbs, _p(out))
         return out
+
+    def giant_chain_ext(self, inner, giant_count: int, l: int, g: int, key,
+                        extended: bool = False) -> np.ndarray:
+        """The BSGS giant sum sum_j rot_{j G}(inner[j]) by Horner with the one
+        giant key (llama3fhe/operators/linear/config.py:292-305: `normal` and
+        `ext_normal` repeat one giant rotation key within a chunk), the chain
+        kept in Q_l u P.  Each step ModDowns only the state's second poly,
+        key-switches that with the giant key into Q_l u P (P times the
+        result, no ModDown) and adds the automorphism of the state's first
+        poly; the next giant's sum joins (P times a Q_l sum on the Q limbs, or
+        an extended sum as it is); one ModDown of both polys ends the chain.
+        A Q_l top sum is its own second poly after the ModDown, so its first
+        step is rotate_hoisted_ext itself.
+        inner [G, 2, l, N] (extended: [G, 2, l+K, N], P times the sums) ->
+        [2, l, N]."""
+
+        G, n = int(giant_count), self.n
+        primes = self.q[:l] + self.p
+        q = np.array(primes, dtype=object)[:, None]
+        pm = np.array([int(np.prod([p % qi for p in self.p], dtype=object) % qi)
+                       for qi in self.q[:l]], dtype=object)[:, None]
+        perm = automorphism_perm(self.log_n, g)
+        key = _u64(key)
+
+        def plus(state, ct):  # + the next giant's sum
+            out = state.astype(object)
+            if extended:
+                out = (out + ct.astype(object)) % q[None]
+            else:  # P ct on the Q limbs (P = 0 mod p_k)
+                out[:, :l] = (out[:, :l] + pm[None] * ct.astype(object)) % q[None, :l]
+            return out.astype(np.uint64)
+
+        if extended:
+            state, first = _u64(inner[G - 1]).copy(), G - 2
+        else:
+            state = plus(self.rotate_hoisted_ext(inner[G - 1], l, [g], [key])[0], inner[G - 2])
+            first = G - 3
+        for j in range(first, -1, -1):
+            c1 = self.moddown(state[1][None], 1, l)[0]
+            zero_c0 = np.stack([np.zeros((l, n), dtype=np.uint64), c1])
+            r = self.rotate_hoisted_ext(zero_c0, l, [g], [key])[0]
+            r0 = (r[0].astype(object) + state[0][:, perm].astype(object)) % q
+            state = plus(np.stack([r0.astype(np.uint64), r[1]]), inner[j])
+        return self.moddown(state, 2, l)

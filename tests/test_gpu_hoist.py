@@ -5,8 +5,10 @@ config.py:9, 286-305; operators/transform.py:108-116 always passes
 "ext_normal"):
 
 * ext_normal: babies left in Q_l u P by their key switch, plaintexts encoded
-  there, the multiply-accumulate over Q_l u P, one ModDown per giant, then
-  the Horner chain with the one giant key;
+  there, the multiply-accumulate over Q_l u P, then the Horner chain with the
+  one giant key (by default straight from the extended sums and kept in
+  Q_l u P; with set_giant_chain("rotations") one ModDown per giant and full
+  rotations);
 * ext_double_hoist: the same sums, each giant's ModDown'ed and rotated with
   its own key back into Q_l u P, summed there, one ModDown at the end.
 
@@ -71,6 +73,9 @@ def test_hoisted_mac_sum_extended_strategies_bit_exact():
     normal = fhe.hoisted_mac_sum(ct, OFFSETS, pt_q, GIANT, G, ctx, strategy="normal")
     ext = fhe.hoisted_mac_sum(ct, OFFSETS, pt_x, GIANT, G, ctx, strategy="ext_normal")
     dh = fhe.hoisted_mac_sum(ct, OFFSETS, pt_x, GIANT, G, ctx, strategy="ext_double_hoist")
+    ctx.native.set_giant_chain("rotations")
+    ext_rot = fhe.hoisted_mac_sum(ct, OFFSETS, pt_x, GIANT, G, ctx, strategy="ext_normal")
+    ctx.native.set_giant_chain("extended")
 
     # the oracle's restatement of the two extended strategies
     ct_h = to_host(ct.data)
@@ -86,7 +91,10 @@ def test_hoisted_mac_sum_extended_strategies_bit_exact():
     acc = giants[G - 1]
     for g in range(G - 2, -1, -1):
         acc = _add(orc.rotate(acc, l, gg, gkey), giants[g], qs)
-    assert np.array_equal(to_host(ext.data), acc)
+    assert np.array_equal(to_host(ext_rot.data), acc)  # a ModDown per giant and rotation
+    # the default: the chain straight from the extended sums, one ModDown
+    assert np.array_equal(to_host(ext.data),
+                          orc.giant_chain_ext(inner, G, l, gg, gkey, extended=True))
     acc_x = inner[0]
     for g in range(1, G):
         gk = fhe.galois_element(g * GIANT, 16)
@@ -97,7 +105,7 @@ def test_hoisted_mac_sum_extended_strategies_bit_exact():
 
     # the same linear map: every strategy decrypts to the normal result
     want = client.decrypt_complex(fhe.rescale(normal, ctx))
-    for r in (ext, dh):
+    for r in (ext, ext_rot, dh):
         got = client.decrypt_complex(fhe.rescale(r, ctx))
         assert np.max(np.abs(got - want)) < 1e-6 * max(1.0, np.max(np.abs(want)))
 
@@ -124,3 +132,29 @@ def test_baby_anchor_blocks_and_strategy_errors():
     with pytest.raises(ValueError, match="strategy"):
         fhe.hoisted_mac_sum(ct, OFFSETS, _encode(fhe, ctx, rows, l, True), GIANT, G, ctx,
                             strategy="ext_normal", baby_rotations=babies)
+
+
+def test_normal_strategy_giant_chains_decrypt_alike():
+    """The normal strategy's Horner chain, kept in Q_l u P (the default) or
+    run as full HRotates: the same linear map after the rescale, within the
+    key-switch noise, and the default is the chain the library takes."""
+
+    fhe, client, ctx, _ = _setup()
+    l = 4
+    rng = np.random.default_rng(44)
+    z = rng.uniform(-1, 1, ctx.max_slots)
+    ct = client.encrypt(z, slots=ctx.max_slots, cur_limbs=l, scaling_factor=ctx.scale_at(l))
+    rows = rng.uniform(-1, 1, (G * B, ctx.max_slots)).astype(np.complex128)
+    pt = _encode(fhe, ctx, rows, l, False)
+    outs = {}
+    for chain in ("rotations", "extended"):
+        ctx.native.set_giant_chain(chain)
+        outs[chain] = fhe.hoisted_mac_sum(ct, OFFSETS, pt, GIANT, G, ctx)
+    default = fhe.hoisted_mac_sum(ct, OFFSETS, pt, GIANT, G, ctx)
+    assert np.array_equal(to_host(default.data), to_host(outs["extended"].data))
+    assert not np.array_equal(to_host(outs["rotations"].data), to_host(outs["extended"].data))
+    want = client.decrypt_complex(fhe.rescale(outs["rotations"], ctx))
+    got = client.decrypt_complex(fhe.rescale(outs["extended"], ctx))
+    assert np.max(np.abs(got - want)) < 1e-6 * max(1.0, np.max(np.abs(want)))
+    with pytest.raises(ValueError):
+        ctx.native.set_giant_chain("ext")

@@ -60,7 +60,12 @@ def test_batched_mac_bit_exact(C, B, G):
             assert np.array_equal(got[c, g], want), (c, g)
 
 
-def test_bsgs_mac_horner_bit_exact():
+@pytest.mark.parametrize("chain", ["extended", "rotations"])
+def test_bsgs_mac_horner_bit_exact(chain):
+    """The Horner chain over the giants, both ways the library runs it: kept
+    in Q_l u P (the default) against the oracle's giant_chain_ext, a full
+    HRotate per giant against the oracle's rotations."""
+
     from easyfhe import core
 
     ctx, orc = pair(8, 2, 3)
@@ -71,15 +76,51 @@ def test_bsgs_mac_horner_bit_exact():
     rng = np.random.default_rng(32)
     babies = rand_residues(rng, ctx.primes[:l], 2 * B).reshape(B, 2, l, N)
     pts = rand_residues(rng, ctx.primes[:l], G * B)
-    got = to_host(ctx.bsgs_mac(to_dev(babies), B, to_dev(pts), G, l, gg, key))
+    ctx.set_giant_chain(chain)
+    try:
+        got = to_host(ctx.bsgs_mac(to_dev(babies), B, to_dev(pts), G, l, gg, key))
+    finally:
+        ctx.set_giant_chain("extended")
     inner = _mac_ref(babies, pts, G, B, ctx.primes[:l])
     hkey = to_host(key)
+    if chain == "extended":
+        assert np.array_equal(got, orc.giant_chain_ext(inner, G, l, gg, hkey))
+        return
     q = np.array(ctx.primes[:l], dtype=object)[None, :, None]
     acc = inner[G - 1]
     for g in range(G - 2, -1, -1):
         acc = ((orc.rotate(acc, l, gg, hkey).astype(object) + inner[g].astype(object)) % q)
         acc = acc.astype(np.uint64)
     assert np.array_equal(got, acc)
+
+
+@pytest.mark.parametrize("conv", ["auto", "tcgen05"])
+def test_giant_chain_layer_primes_batch(conv):
+    """The extended-basis chain at the layer's prime sizes (59/60-bit: the
+    integer kernels) on a batch of 3 ciphertexts with 8 giants, both base
+    conversion kernels (tcgen05 takes the one-poly ModDown conversions too):
+    every ciphertext bit-exact against the oracle's chain."""
+
+    from easyfhe import core
+
+    ctx, orc = pair(6, 3, 3, 60)
+    l, B, G, C = 5, 2, 8, 3
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(13, 192))
+    gg = core.galois_element(40)
+    key = ctx.keygen_rotation(s_ntt, gg, seed=6)
+    rng = np.random.default_rng(36)
+    babies = rand_residues(rng, ctx.primes[:l], C * B * 2).reshape(C, B, 2, l, N)
+    pts = rand_residues(rng, ctx.primes[:l], G * B)
+    ctx.set_conv_path(conv)
+    try:
+        got = to_host(ctx.bsgs_mac(to_dev(babies.reshape(C * B, 2, l, N)), B, to_dev(pts), G,
+                                   l, gg, key, num_cts=C))
+    finally:
+        ctx.set_conv_path("auto")
+    hkey = to_host(key)
+    for c in range(C):
+        inner = _mac_ref(babies[c], pts, G, B, ctx.primes[:l])
+        assert np.array_equal(got[c], orc.giant_chain_ext(inner, G, l, gg, hkey)), c
 
 
 def test_batched_hoisting_and_bsgs_match_single_ciphertext():

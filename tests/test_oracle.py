@@ -231,3 +231,37 @@ def test_oracle_bsgs_mac_equals_exact_sum(oracle_mod):
             want = sum(babies[c, b].astype(object) * pts[g * B + b].astype(object)[None]
                        for b in range(B)) % qs[None, :, None]
             assert np.array_equal(got[c, g], want.astype(np.uint64))
+
+
+def test_giant_chain_ext_decrypts_like_rotations(oracle_mod):
+    """The oracle's Horner chain kept in Q_l u P (one poly ModDown'ed per
+    step, both at the end; what the library's bsgs_mac runs by default), the
+    same chain from extended sums, and the chain of full HRotates decrypt to
+    the same giant sum, the exact sum_j rot_{j G}(m_j) of the messages."""
+
+    O = oracle_mod
+    log_n = 8
+    o, s, s_ntt = _small_setup(O, log_n=log_n, L=5, K=2, dnum=3)
+    slots = 1 << (log_n - 1)
+    rng = np.random.default_rng(8)
+    scale, l, G, step = 2.0 ** 40, 4, 4, 3
+    msgs = [rng.uniform(-1, 1, slots) + 1j * rng.uniform(-1, 1, slots) for _ in range(G)]
+    inner = np.stack([o.encrypt(o.encode(m, scale, l), l, s_ntt, 1, 10 + j)
+                      for j, m in enumerate(msgs)])
+    g = O.galois_element(log_n, step)
+    key = o.keygen_rotation(s_ntt, g, 5)
+    q = np.array(o.q[:l], dtype=object)[:, None]
+    acc = inner[G - 1]
+    for j in range(G - 2, -1, -1):
+        acc = ((o.rotate(acc, l, g, key).astype(object) + inner[j].astype(object)) % q)
+        acc = acc.astype(np.uint64)
+    ext = o.giant_chain_ext(inner, G, l, g, key)
+    # extended sums (P times each ciphertext in Q_l u P, as the ext_normal
+    # MAC leaves them) through the same chain
+    ext_sums = np.stack([o.rotate_hoisted_ext(c, l, [1], [None])[0] for c in inner])
+    ext2 = o.giant_chain_ext(ext_sums, G, l, g, key, extended=True)
+    want = sum(np.roll(m, -j * step) for j, m in enumerate(msgs))
+    for ct in (acc, ext, ext2):
+        dec = o.decode(o.decrypt(ct, l, s_ntt), l, slots, scale)
+        assert np.max(np.abs(dec - want)) < 1e-5
+    assert not np.array_equal(acc, ext)  # different roundings, same message
