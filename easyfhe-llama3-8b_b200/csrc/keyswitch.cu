@@ -336,14 +336,31 @@ int launch_moddown_rescale_conv(b2f_context *ctx, const uint64_t *acc,
 // more with pre0) stay below 2^(64+k) for every prime of the launch, so the
 // one-word Barrett reduce_bk replaces the 128-bit one (the kernel is
 // issue-bound; the reduction was half its instructions).
-template <bool BK>
+// CHAIN: a rotation left in Q_l u P finishes here, the automorphism folded
+// into the store: the sums at evaluation n get x_0[n] (the first poly of the
+// ciphertext of item it, ct = items.ct(it), over Q_l u P, or with x_q P times
+// a Q_l poly on the Q limbs: one more product term before the reduction) and,
+// after the reduction, s_b[k] (optional: the next giant's sum of a giant
+// chain step, as giant_step_kernel adds it), and go to out +
+// items.out(it, 2 (l+K) N) at k = pi_g^-1(n), g = items.g[items.at(it)]; acc
+// is never written and the automorphism costs no pass of its own.
+struct ChainStep {
+  const uint64_t *x = nullptr;  // [ct][2][l+K][N], or (x_q) [ct][2][l][N], at x_cs
+  long long x_cs = 0;
+  int x_q = 0;
+  const uint64_t *s = nullptr;  // null, or [ct][2][l+K or (s_q) l][N] at s_cs
+  long long s_cs = 0;
+  int s_q = 0;
+  uint64_t *out = nullptr;      // [..][2][l+K][N] at items.out
+};
+template <bool BK, bool CHAIN = false>
 __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
     const uint64_t *__restrict__ c1, long long c1_stride,
     const uint64_t *__restrict__ ext, long long ext_stride, const ItemKeys items,
     uint64_t *__restrict__ acc, const Mod *__restrict__ mods, int l, int K,
     int L, int alpha, int beta, const uint64_t *__restrict__ pre0 = nullptr,
     const uint64_t *__restrict__ pre1 = nullptr, long long pre_stride = 0,
-    const uint64_t *__restrict__ pmod = nullptr) {
+    const uint64_t *__restrict__ pmod = nullptr, const ChainStep chain = ChainStep{}) {
   const int n = blockIdx.x * TPB + threadIdx.x;
   const int it = blockIdx.y, t = blockIdx.z, ct = items.ct(it);
   const int lk = l + K, np = L + K;
@@ -384,6 +401,31 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
     mac128(s0, pre0[at], pm);
     mac128(s1, pre1[at], pm);
   }
+  if constexpr (CHAIN) {
+    const uint64_t *x0 = chain.x + ct * chain.x_cs + (size_t)t * kN + n;
+    if (!chain.x_q)
+      mac128(s0, *x0, 1);
+    else if (t < l)  // a Q_l poly has no limb t >= l
+      mac128(s0, *x0, pmod[t]);
+    uint64_t w0 = BK ? reduce_bk(s0.hi, s0.lo, M) : reduce128(s0.hi, s0.lo, M);
+    uint64_t w1 = BK ? reduce_bk(s1.hi, s1.lo, M) : reduce128(s1.hi, s1.lo, M);
+    const uint32_t k = auto_src((uint32_t)n, galois_inverse(items.g[items.at(it)]));
+    if (chain.s) {
+      const uint64_t *sb = chain.s + ct * chain.s_cs + (size_t)t * kN + k;
+      const size_t sp = (size_t)(chain.s_q ? l : lk) * kN;  // poly stride of s
+      if (!chain.s_q) {
+        w0 = add_mod(w0, sb[0], M.q);
+        w1 = add_mod(w1, sb[sp], M.q);
+      } else if (t < l) {
+        w0 = add_mod(w0, mul_mod(pmod[t], sb[0], M), M.q);
+        w1 = add_mod(w1, mul_mod(pmod[t], sb[sp], M), M.q);
+      }
+    }
+    uint64_t *o = chain.out + items.out(it, 2LL * lk * kN) + (size_t)t * kN + k;
+    o[0] = w0;
+    o[(size_t)lk * kN] = w1;
+    return;
+  }
   uint64_t *o = acc + ((size_t)it * 2 * lk + t) * kN + n;
   if (BK) {
     o[0] = reduce_bk(s0.hi, s0.lo, M);
@@ -392,6 +434,28 @@ __global__ void __launch_bounds__(TPB) key_inner_product_kernel(
     o[0] = reduce128(s0.hi, s0.lo, M);
     o[(size_t)lk * kN] = reduce128(s1.hi, s1.lo, M);
   }
+}
+
+bool sums_fit_reduce_bk(const b2f_context *ctx, int l, int terms);
+
+// The key inner product of rotations left in Q_l u P with the automorphism
+// and the additions of CHAIN above folded in (integer contexts).
+int launch_key_inner_product_chain(b2f_context *ctx, int cts, const uint64_t *c1,
+                                   long long c1_stride, const uint64_t *ext,
+                                   long long ext_stride, const ItemKeys &items, int l,
+                                   const ChainStep &chain, cudaStream_t s) {
+  const int K = ctx->K, beta = ctx->levels[l].beta;
+  const dim3 grid(kN / TPB, cts, l + K);
+  if (sums_fit_reduce_bk(ctx, l, beta + 1))
+    key_inner_product_kernel<true, true><<<grid, TPB, 0, s>>>(
+        c1, c1_stride, ext, ext_stride, items, nullptr, ctx->d_mod, l, K, ctx->L, ctx->alpha,
+        beta, nullptr, nullptr, 0, ctx->d_pmod, chain);
+  else
+    key_inner_product_kernel<false, true><<<grid, TPB, 0, s>>>(
+        c1, c1_stride, ext, ext_stride, items, nullptr, ctx->d_mod, l, K, ctx->L, ctx->alpha,
+        beta, nullptr, nullptr, 0, ctx->d_pmod, chain);
+  B2F_LAUNCHED("key_inner_product_kernel");
+  return B2F_OK;
 }
 
 // terms * (q - 1)^2 < 2^(64+k) for every prime of Q_l u P: sums of `terms`
@@ -624,12 +688,14 @@ struct ExtItems {
 __global__ void __launch_bounds__(TPB) ext_combine_kernel(
     const uint64_t *__restrict__ acc, const uint64_t *__restrict__ ct,
     uint64_t *__restrict__ out, const Mod *__restrict__ mods,
-    const uint64_t *__restrict__ pmod, int l, int K, int L, const ExtItems items) {
+    const uint64_t *__restrict__ pmod, int l, int K, int L, const ExtItems items,
+    int identity_only = 0) {
   const int k = blockIdx.x * TPB + threadIdx.x;
   const int t = blockIdx.y, b = blockIdx.z & 1, r = blockIdx.z >> 1;
   const int lk = l + K;
   const uint32_t g = items.g[r];
   const int slot = items.slot[r];
+  if (identity_only && slot >= 0) return;  // written by the key inner product
   const uint32_t src = g == 1 ? (uint32_t)k : auto_src(k, g);
   const Mod M = mods[t < l ? t : L + (t - l)];
   const uint64_t *a = slot >= 0 ? acc + (size_t)slot * 2 * lk * kN : nullptr;
@@ -900,15 +966,29 @@ int giant_chain_ext(b2f_context *ctx, const uint64_t *sums, int ext, long long g
       c1s = (long long)l * kN;
     }
     if ((rc = modup(ctx, c1, c1s, cts, l, xt, extd, s))) return rc;
-    if ((rc = launch_key_inner_product(ctx, cts, c1, c1s, extd, (long long)beta * lk * kN, it,
-                                       acc, l, s)))
-      return rc;
     uint64_t *next = state[cur];
     if (next == x) next = state[cur ^ 1];
-    giant_step_kernel<<<dim3(kN / TPB, lk, 2 * cts), TPB, 0, s>>>(
-        x ? x : top, x ? 0 : 1, x ? as : cs, acc, sums + j * gs, ext ? 0 : 1, cs, next,
-        ctx->d_mod, ctx->d_pmod, l, K, ctx->L, (uint32_t)galois);
-    B2F_LAUNCHED("giant_step_kernel");
+    if (!ctx->fp64) {  // the step inside the key inner product
+      ChainStep cs_{};
+      cs_.x = x ? x : top;
+      cs_.x_cs = x ? as : cs;
+      cs_.x_q = x ? 0 : 1;
+      cs_.s = sums + j * gs;
+      cs_.s_cs = cs;
+      cs_.s_q = ext ? 0 : 1;
+      cs_.out = next;
+      if ((rc = launch_key_inner_product_chain(ctx, cts, c1, c1s, extd,
+                                               (long long)beta * lk * kN, it, l, cs_, s)))
+        return rc;
+    } else {
+      if ((rc = launch_key_inner_product(ctx, cts, c1, c1s, extd, (long long)beta * lk * kN,
+                                         it, acc, l, s)))
+        return rc;
+      giant_step_kernel<<<dim3(kN / TPB, lk, 2 * cts), TPB, 0, s>>>(
+          x ? x : top, x ? 0 : 1, x ? as : cs, acc, sums + j * gs, ext ? 0 : 1, cs, next,
+          ctx->d_mod, ctx->d_pmod, l, K, ctx->L, (uint32_t)galois);
+      B2F_LAUNCHED("giant_step_kernel");
+    }
     x = next;
   }
   // the one ModDown of both polys
@@ -1191,8 +1271,17 @@ int b2f_rotate_hoisted_batch(b2f_context *ctx, const uint64_t *ct, int num_cts,
       keyed.push_back(r);
     }
   }
-  for (size_t p = 0; p < keyed.size(); p += kMaxItems) {
-    const int R = (int)std::min<size_t>(kMaxItems, keyed.size() - p);
+  // A launch group takes up to 16 ciphertexts and as many rotations as fit
+  // in kMaxItems items (ciphertext-major: the items of one ciphertext share
+  // its digits, and the same rotation of the group's ciphertexts follows
+  // within kMaxItems items, while its key limbs are still in L2): each
+  // rotation key streams from HBM once per group of ciphertexts, not once per
+  // ciphertext (at l = 13, 16 ciphertexts x 63 rotations: 2.6 GB of key
+  // limbs instead of 42 GB).
+  const int cgroup = std::min(num_cts, 16);
+  const int rblock = std::max(1, kMaxItems / std::max(cgroup, 1));
+  for (size_t p = 0; p < keyed.size(); p += rblock) {
+    const int R = (int)std::min<size_t>(rblock, keyed.size() - p);
     ItemKeys it{};
     it.shared = 0;
     it.per = R;
@@ -1265,20 +1354,35 @@ int b2f_rotate_hoisted_ext(b2f_context *ctx, const uint64_t *ct, int l,
       ex.slot[i] = -1;
       if (galois[p + i] != 1) {
         it.key[keyed] = keys[p + i];
+        it.g[keyed] = (uint32_t)galois[p + i];
+        it.pos[keyed] = (int16_t)i;
         ex.slot[i] = (int16_t)keyed++;
       }
     }
+    uint64_t *outp = out + (size_t)p * 2 * lk * kN;
+    const bool fold = !ctx->fp64;  // the automorphism and P c0 in the key IP's store
     if (keyed) {
       it.shared = 0;
       it.per = keyed;  // one ciphertext: item i is keyed rotation i
-      if ((rc = launch_key_inner_product(ctx, keyed, ct + (size_t)l * kN, 0, ext, 0, it,
-                                         acc, l, s)))
+      it.out_ct_stride = 0;
+      if (fold) {
+        ChainStep cs_{};
+        cs_.x = ct;  // P c0 on the Q limbs
+        cs_.x_q = 1;
+        cs_.out = outp;
+        if ((rc = launch_key_inner_product_chain(ctx, keyed, ct + (size_t)l * kN, 0, ext, 0,
+                                                 it, l, cs_, s)))
+          return rc;
+      } else if ((rc = launch_key_inner_product(ctx, keyed, ct + (size_t)l * kN, 0, ext, 0,
+                                                it, acc, l, s))) {
         return rc;
+      }
     }
-    ext_combine_kernel<<<dim3(kN / TPB, lk, 2 * n), TPB, 0, s>>>(
-        acc, ct, out + (size_t)p * 2 * lk * kN, ctx->d_mod, ctx->d_pmod, l, K,
-        ctx->L, ex);
-    B2F_LAUNCHED("ext_combine_kernel");
+    if (!fold || keyed < n) {
+      ext_combine_kernel<<<dim3(kN / TPB, lk, 2 * n), TPB, 0, s>>>(
+          acc, ct, outp, ctx->d_mod, ctx->d_pmod, l, K, ctx->L, ex, fold ? 1 : 0);
+      B2F_LAUNCHED("ext_combine_kernel");
+    }
   }
   return B2F_OK;
 }

@@ -13,20 +13,23 @@ from _ckks import N, pair, rand_residues, to_dev, to_host
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("arith", ["f64", "int64"])
-def test_ext_rotations_and_moddown_bit_exact(arith):
+@pytest.mark.parametrize("arith,l", [("f64", 7), ("int64", 7), ("int64", 1)])
+def test_ext_rotations_and_moddown_bit_exact(arith, l):
+    """Hoisted rotations left in Q_l u P, an identity among them (the integer
+    kernels store the keyed ones from the key inner product, the automorphism
+    folded in; l = 1 has fewer Q limbs than special primes), and ModDown."""
+
     from easyfhe import core
 
     ctx, orc = pair(8, 2, 3)
     ctx.set_arith(arith)
     try:
-        _ext_rotations_and_moddown(ctx, orc, core)
+        _ext_rotations_and_moddown(ctx, orc, core, l)
     finally:
         ctx.set_arith("auto")
 
 
-def _ext_rotations_and_moddown(ctx, orc, core):
-    l = 7
+def _ext_rotations_and_moddown(ctx, orc, core, l):
     s_ntt = ctx.secret_to_ntt(core.sample_secret(41, 192))
     gs = [1, core.galois_element(5), core.galois_element(131071)]
     keys = [None] + [ctx.keygen_rotation(s_ntt, g, seed=50 + i) for i, g in enumerate(gs[1:])]

@@ -94,17 +94,19 @@ def test_bsgs_mac_horner_bit_exact(chain):
     assert np.array_equal(got, acc)
 
 
-@pytest.mark.parametrize("conv", ["auto", "tcgen05"])
-def test_giant_chain_layer_primes_batch(conv):
+@pytest.mark.parametrize("conv,l", [("auto", 5), ("tcgen05", 5), ("auto", 1)])
+def test_giant_chain_layer_primes_batch(conv, l):
     """The extended-basis chain at the layer's prime sizes (59/60-bit: the
-    integer kernels) on a batch of 3 ciphertexts with 8 giants, both base
-    conversion kernels (tcgen05 takes the one-poly ModDown conversions too):
-    every ciphertext bit-exact against the oracle's chain."""
+    integer kernels, the chain's steps stored by the key inner product) on a
+    batch of 3 ciphertexts with 8 giants, both base conversion kernels
+    (tcgen05 takes the one-poly ModDown conversions too), and one Q limb
+    under three special primes: every ciphertext bit-exact against the
+    oracle's chain."""
 
     from easyfhe import core
 
     ctx, orc = pair(6, 3, 3, 60)
-    l, B, G, C = 5, 2, 8, 3
+    B, G, C = 2, 8, 3
     s_ntt = ctx.secret_to_ntt(core.sample_secret(13, 192))
     gg = core.galois_element(40)
     key = ctx.keygen_rotation(s_ntt, gg, seed=6)
@@ -153,6 +155,33 @@ def test_batched_hoisting_and_bsgs_match_single_ciphertext():
         assert np.array_equal(to_host(babies[c]), to_host(b1)), f"babies of ct {c}"
         o1 = to_host(ctx.bsgs_mac(b1, B, pts, G, l, gg, gkey))
         assert np.array_equal(out[c], o1), f"bsgs of ct {c}"
+
+
+def test_hoisted_rotation_groups_match_single_ciphertext():
+    """20 keyed rotations of 5 ciphertexts: the batch runs in launch groups
+    of 5 ciphertexts x 12 rotations (each key read once per group), a single
+    ciphertext in one group of all 20; every rotation of every ciphertext
+    bit-exact between the two, the first against the oracle."""
+
+    from easyfhe import core
+
+    ctx, orc = pair(8, 2, 3)
+    l, C = 3, 5
+    s_ntt = ctx.secret_to_ntt(core.sample_secret(16, 192))
+    offsets = list(range(1, 21))
+    gal = [core.galois_element(o) for o in offsets]
+    keys = [ctx.keygen_rotation(s_ntt, g, seed=70 + i) for i, g in enumerate(gal)]
+    rng = np.random.default_rng(35)
+    cts = rand_residues(rng, ctx.primes[:l], 2 * C).reshape(C, 2, l, N)
+    dcts = to_dev(cts)
+    ext = ctx.modup(dcts, l, C)
+    out = to_host(ctx.rotate_hoisted(dcts, l, ext, gal, keys, num_cts=C))
+    for c in range(C):
+        one = to_dev(cts[c])
+        single = to_host(ctx.rotate_hoisted(one, l, ctx.modup(one, l), gal, keys))
+        assert np.array_equal(out[c], single), c
+    want = orc.rotate_hoisted(cts[0], l, gal[:2], [to_host(k) for k in keys[:2]])
+    assert np.array_equal(out[0][:2], want)
 
 
 def test_dense_packer_matches_reference_formula():
