@@ -278,11 +278,11 @@ int launch_modup_conv(b2f_context *ctx, const uint64_t *xt, uint64_t *ext, int l
 // one poly for the second)
 int launch_moddown_conv(b2f_context *ctx, const uint64_t *acc, uint64_t *conv,
                         int l, int cts, cudaStream_t s, int polys = 2) {
-  // tcgen05 by default only from 16 ciphertexts: per ModDown conversion at
-  // l = 13 it takes 149 against 152.5 us there, but 83.5 / 79.5 us at 8,
-  // 52.4 / 41.9 at 4 and 23.7 / 15.1 at 1 (64 coefficient tiles a launch
-  // cannot fill the GPU)
-  if (ctx->conv_path == 2 || (ctx->conv_path == 0 && cts >= 16)) {
+  // tcgen05 by default only from 32 polys (16 ciphertexts): per ModDown
+  // conversion at l = 13 it takes 149 against 152.5 us there, but 83.5 / 79.5
+  // us at 8 ciphertexts, 52.4 / 41.9 at 4 and 23.7 / 15.1 at 1 (64 coefficient
+  // tiles a launch cannot fill the GPU)
+  if (ctx->conv_path == 2 || (ctx->conv_path == 0 && cts * polys >= 32)) {
     const int rc = launch_moddown_conv_umma(ctx, acc, conv, l, cts, s, polys);
     if (rc >= 0) return rc;
   }
