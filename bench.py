@@ -80,6 +80,11 @@ def parse():
     ap.add_argument("--giant-chain", default="extended", choices=["extended", "rotations"],
                     help="BSGS Horner chain over the giants: kept in Q_l u P with one "
                          "ModDown per chain (extended) or a full HRotate per giant")
+    ap.add_argument("--hoist-strategy", default="normal",
+                    choices=["normal", "ext_normal", "ext_double_hoist"],
+                    help="linear and layer0: the hoisted-MAC schedule, as the reference's "
+                         "--linear-hoist-strategy (normal: its production schedule; the "
+                         "extended ones leave the babies in Q_l u P)")
     ap.add_argument("--mac-path", default="auto", choices=["auto", "cuda_cores"],
                     help="BSGS multiply-accumulate kernel: u8 tensor cores where exact "
                          "(auto) or the CUDA-core kernel")
@@ -557,6 +562,8 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
     D, lanes, B, level = LINEAR_D, LINEAR_LANES, LINEAR_B, LINEAR_LEVEL
     slots = 32768
     total = a.batch
+    strategy = a.hoist_strategy
+    ext = strategy != "normal"
     if total % world:
         raise SystemExit(f"{total} ciphertexts do not split over {world} ranks")
     per = total // world
@@ -585,8 +592,8 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
     pts = []
     for base, count in chunks:
         vals = ctx.native.pack_diagonals(W, D, lanes, B, base, count, slots)
-        data = ctx.native.encode(vals, scale, level)
-        pts.append(fhe.Plaintext(data, fhe.CipherState(level, 1, scale), slots, False))
+        data = ctx.native.encode(vals, scale, level, ctx.K if ext else 0)
+        pts.append(fhe.Plaintext(data, fhe.CipherState(level, 1, scale), slots, ext))
         del vals
     torch.cuda.synchronize()
     encode_s = time.perf_counter() - t0
@@ -605,11 +612,11 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
 
     def apply(ct):
         # LinearOperator.apply's call sequence; ct is this rank's batch
-        babies = fhe.prepare_hoisted_baby_rotations(ct, offsets, ctx)
+        babies = fhe.prepare_hoisted_baby_rotations(ct, offsets, ctx, strategy=strategy)
         acc = None
         for (base, count), pt in zip(chunks, pts):
             r = fhe.hoisted_mac_sum(ct, offsets, pt, giant_offset, count, ctx,
-                                    baby_rotations=babies)
+                                    strategy=strategy, baby_rotations=babies)
             if base:
                 r = fhe.homo_rotate(r, base * giant_offset, ctx)
             acc = r if acc is None else fhe.homo_add(acc, r, ctx)
@@ -660,19 +667,28 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
 
     # ---- the MAC kernel alone: one chunk's launch on this rank's batch ----
     batch = fhe.pack_cipher_batch(cts)
-    babies = tuple(fhe.prepare_hoisted_baby_rotations(batch, offsets, ctx))[0]
+    babies = tuple(fhe.prepare_hoisted_baby_rotations(batch, offsets, ctx,
+                                                      strategy=strategy))[0]
     G0 = chunks[0][1]
     mac_reps = max(3, min(a.steps, 10))
-    ctx.native.mac(babies.data, B, pts[0].data, G0, level, num_cts=per)
+
+    def mac_launch():
+        if ext:  # over Q_l u P
+            ctx.native.mac_ext(babies.data, B, pts[0].data, G0, level, num_cts=per)
+        else:
+            ctx.native.mac(babies.data, B, pts[0].data, G0, level, num_cts=per)
+
+    mac_launch()
     torch.cuda.synchronize()
     m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     m0.record(stream)
     for _ in range(mac_reps):
-        ctx.native.mac(babies.data, B, pts[0].data, G0, level, num_cts=per)
+        mac_launch()
     m1.record(stream)
     torch.cuda.synchronize()
     mac_ms = m0.elapsed_time(m1) / mac_reps
-    mac_name = ctx.native.mac_kernel(B, level, num_cts=per, giant_count=G0)
+    mac_name = ctx.native.mac_kernel(B, level, ctx.K if ext else 0, num_cts=per,
+                                     giant_count=G0)
     on_tc = mac_name == "mac_mma_kernel"
     mac_peak = ctx.native.mma_u8_peak() if on_tc else ctx.native.mac_peak()
     del babies, batch
@@ -708,11 +724,12 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
     lim = N * 8
     # algorithmic bytes of one MAC launch (one chunk of G0 giants on `per`
     # ciphertexts): the plaintext rows once, the babies once, outputs
-    mac_bytes = (G0 * B * level + per * B * 2 * level + per * G0 * 2 * level) * lim
-    macs = G0 * B * per * 2 * level * N  # 64 x 64-bit products per launch
+    lk = level + (ctx.K if ext else 0)  # limbs the MAC runs over
+    mac_bytes = (G0 * B * lk + per * B * 2 * lk + per * G0 * 2 * lk) * lim
+    macs = G0 * B * per * 2 * lk * N  # 64 x 64-bit products per launch
     traffic = None
     tpath = ROOT / "profiles" / f"{mac_name}_traffic.json"
-    if tpath.exists():
+    if tpath.exists() and not ext:  # captured over Q_l at l = 13
         try:
             t = json.loads(tpath.read_text())
             # DRAM bytes per launch scale with the ciphertexts of the launch
@@ -728,11 +745,13 @@ def run_linear(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict |
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "u64", "data": "synthetic",
         "config": {"workload": (f"linear 4096->4096 D=4096 l={level} B=64 babies, 64 giants in "
-                                f"8 chunks of 512 rows (the reference's production plan), "
+                                f"8 chunks of 512 rows (the reference's production plan"
+                                f"{'' if not ext else ', hoist strategy ' + strategy}), "
                                 f"{total} token-shard ciphertexts sharded {per}/rank, outputs "
                                 "all-gathered over NCCL in every step; logN 16 depth 37 dnum 5 "
                                 "59/60-bit primes"),
                    "ciphertexts_total": total, "ciphertexts_per_rank": per,
+                   "hoist_strategy": strategy,
                    "chunks": (len(chunks) if not a.linear_chunks else
                               f"{len(chunks)} of 8 (a smaller linear: --linear-chunks)"),
                    "parallelism": f"output-ciphertext sharding x{world} + all-gather",
@@ -1041,7 +1060,7 @@ def run_mac(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict | No
             "gpu_launches": launches}
 
 
-def layer0_result(warmup: int = 1, repetitions: int = 1) -> dict:
+def layer0_result(warmup: int = 1, repetitions: int = 1, extra_args=()) -> dict:
     """Layer-0 of encrypted Llama-3-8B through the reference's own llama3fhe
     (its runner's Layer-0 preset, unchanged) on this backend: s/layer from the
     runner's timed repetition, and the decrypted output against the fp64
@@ -1054,7 +1073,8 @@ def layer0_result(warmup: int = 1, repetitions: int = 1) -> dict:
     if llama3_layer.reference_root() is None:
         return {"unavailable": "the reference llama3fhe tree is not installed (baseline/_ref)"}
     n0 = _native.lib.b2f_launch_count()
-    r = llama3_layer.run_layer0(warmup=warmup, repetitions=repetitions)
+    r = llama3_layer.run_layer0(warmup=warmup, repetitions=repetitions,
+                                extra_args=extra_args)
     launches = _native.lib.b2f_launch_count() - n0
     perf = r["payload"]["performance"]
     return {
@@ -1073,6 +1093,7 @@ def layer0_result(warmup: int = 1, repetitions: int = 1) -> dict:
         "gpu_launches_total": launches,
         "source": ("llama3fhe.application.runner.run, Layer-0 synthetic preset "
                    "(seed 26081461), unchanged, on this backend"),
+        "runner_extra_args": list(extra_args),
     }
 
 
@@ -1163,7 +1184,10 @@ def run_prefill(a, world: int) -> dict:
 def run_layer0(a, world: int) -> dict:
     """The Layer-0 workload as its own line: seconds per encrypted layer."""
 
-    r = layer0_result(warmup=max(1, min(a.warmup, 2)), repetitions=max(1, min(a.steps, 3)))
+    extra = (() if a.hoist_strategy == "normal"
+             else ("--linear-hoist-strategy", a.hoist_strategy))
+    r = layer0_result(warmup=max(1, min(a.warmup, 2)), repetitions=max(1, min(a.steps, 3)),
+                      extra_args=extra)
     if "s_per_layer" not in r:
         return {"metric": "encrypted Llama-3-8B prefill s/layer at seq128", **r}
     return {"metric": "encrypted Llama-3-8B prefill s/layer at seq128 (Layer-0 preset)",
@@ -1173,7 +1197,8 @@ def run_layer0(a, world: int) -> dict:
             "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
             "config": {"workload": ("one Llama-3-8B decoder layer, seq 128, hidden 4096, "
                                     "32/8 heads, SwiGLU 14336; logN 16 depth 37 dnum 5 "
-                                    "59/60-bit primes; the reference's graph")},
+                                    "59/60-bit primes; the reference's graph"),
+                       "hoist_strategy": a.hoist_strategy},
             "layer0": r}
 
 
