@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--rotation", type=int, default=1)
     ap.add_argument("--workload", default="linear",
                     choices=["linear", "hrotate", "ntt", "bootstrap", "layer0", "mac",
-                             "prefill"],
+                             "prefill", "mlp"],
                     help="linear (default): the encrypted 4096x4096 linear block sharded "
                          "over the ranks with an all-gather; hrotate: the key-switching "
                          "microbench; ntt: only the NTT kernel loop (for profiling); "
@@ -99,7 +99,7 @@ def parse():
     a = ap.parse_args()
     if a.batch is None:
         a.batch = {"hrotate": 32, "ntt": 32, "bootstrap": 16, "linear": 16,
-                   "layer0": 16, "mac": 16, "prefill": 16}[a.workload]
+                   "layer0": 16, "mac": 16, "prefill": 16, "mlp": 16}[a.workload]
     return a
 
 
@@ -1181,6 +1181,125 @@ def run_prefill(a, world: int) -> dict:
             "prefill": r, "gpu_launches_total": launches}
 
 
+def run_mlp(a, dev, rank: int, world: int, barrier, max_over_ranks) -> dict | None:
+    """The reference's own feature-major SwiGLU MLP block on this backend,
+    sharded by token-shard ciphertext: ``mlp_fhe``
+    (llama3fhe/operators/linear/mlp.py:524-1126: gate/up 4096 -> 14336 in
+    four feature pages sharing one set of baby rotations, SiLU by the
+    reference's Chebyshev PS evaluator, down 14336 -> 4096 over the four
+    pages) with its production schedule, on a layout of 128/N tokens per rank
+    (feature-major, 8 tokens per ciphertext: 16/N ciphertexts), then the
+    outputs are all-gathered over NCCL inside the step.  Inputs: the Layer-0
+    preset's weights and N(0, 1) activations encrypted at the MLP's entry
+    level (11 limbs); the first step's outputs are decrypted against the
+    reference's own NumPy MLP (mlp_packed_numpy) through its verify path."""
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import llama3_layer
+
+    from easyfhe import _native
+
+    if llama3_layer.reference_root() is None:
+        return ({"metric": "encrypted MLP block ciphertexts/s", "impl": "b200",
+                 "unavailable": "the reference llama3fhe tree is not installed (baseline/_ref)"}
+                if rank == 0 else None)
+    llama3_layer.import_reference()
+    from llama3fhe.application import session
+    from llama3fhe.layouts import FeatureMajorPrefillLayout
+    from llama3fhe.operators.linear.mlp import mlp_fhe
+
+    total = a.batch
+    if total % world or (total // world) % 2:
+        raise SystemExit(f"{total} ciphertexts do not split over {world} ranks in pairs")
+    per = total // world
+    full = FeatureMajorPrefillLayout()
+    tokens = per * full.tokens_per_cipher
+    layout = FeatureMajorPrefillLayout(seq_len=tokens)
+    s = llama3_layer.ReferenceSession()
+    _, w, approx = llama3_layer.synthetic_layer()
+    x = np.random.default_rng(6).normal(size=(total * full.tokens_per_cipher,
+                                              full.hidden_dim)).astype(np.float32)
+    x_r = x[rank * tokens:(rank + 1) * tokens]
+    level = 11  # the MLP's entry level at Layer 0 (graph.py:1252-1259)
+    cts = session._encrypt_hidden(x_r, context=s.context, layout=layout,
+                                  input_level=int(s.context.context.L) - level)
+    stream = torch.cuda.current_stream()
+    gathered = None
+    gather_ev = []
+    info = {}
+
+    def step(verify=False, record=False):
+        nonlocal gathered
+        r = mlp_fhe(x_r, w.gate_proj, w.up_proj, w.down_proj, silu_entry=approx.silu,
+                    layout=layout, config=s.config, crypto_context=s.context,
+                    input_ciphers=cts, verify=verify)
+        out = torch.stack([c.data for c in r.ciphers])
+        info["stages"] = r.stage_seconds
+        if verify:
+            info["check"] = {"max_abs": r.max_abs_diff, "mean_abs": r.mean_abs_diff,
+                             "ref_max_abs": float(np.max(np.abs(r.expected)))}
+        if world > 1:  # the stage-boundary exchange: every rank gets every output
+            if gathered is None:
+                gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype,
+                                       device=out.device)
+            if record:
+                e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                e[0].record(stream)
+            dist.all_gather_into_tensor(gathered, out.contiguous())
+            if record:
+                e[1].record(stream)
+                gather_ev.append(e)
+        return out
+
+    step(verify=True)  # warm-up 1: keys generated on first use, outputs checked
+    for _ in range(max(0, a.warmup - 1)):
+        step()
+    torch.cuda.synchronize()
+    clocks = Clocks(dev.index or 0, not a.no_clocks)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    n0 = _native.lib.b2f_launch_count()
+    e0.record(stream)
+    for _ in range(a.steps):
+        step(record=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = (_native.lib.b2f_launch_count() - n0) // a.steps
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    gather_ms = max_over_ranks(sum(x.elapsed_time(y) for x, y in gather_ev) / a.steps
+                               if gather_ev else 0.0)
+    if rank != 0:
+        return None
+    return {
+        "metric": ("encrypted MLP block ciphertexts/s (the reference's feature-major SwiGLU "
+                   "mlp_fhe: gate/up 4096->14336, SiLU, down 14336->4096)"),
+        "value": total / (ms / 1e3), "unit": "ciphertexts/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "u64", "data": "synthetic",
+        "config": {"workload": (f"llama3fhe mlp_fhe, unchanged, production schedule; "
+                                f"{total} token-shard ciphertexts (8 tokens each) sharded "
+                                f"{per}/rank, entry level {level} limbs, outputs all-gathered "
+                                "over NCCL in every step; Layer-0 preset weights; logN 16 "
+                                "depth 37 dnum 5 59/60-bit primes"),
+                   "ciphertexts_total": total, "ciphertexts_per_rank": per,
+                   "parallelism": f"token-shard sharding x{world} + all-gather",
+                   "l2": "plaintexts of 512 rows per chunk (GBs): larger than L2; no flush"},
+        "stage_seconds_rank0": info.get("stages"),
+        "check_rank0": info.get("check"),
+        "gather_ms_per_step": gather_ms,
+        "gather_share": gather_ms / ms if ms else None,
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+
+
 def run_layer0(a, world: int) -> dict:
     """The Layer-0 workload as its own line: seconds per encrypted layer."""
 
@@ -1240,6 +1359,10 @@ def main() -> None:
                 print(json.dumps(line), flush=True)
         elif a.workload == "layer0":
             line = run_layer0(a, world) if rank == 0 else None
+            if line:
+                print(json.dumps(line), flush=True)
+        elif a.workload == "mlp":
+            line = run_mlp(a, dev, rank, world, barrier, max_over_ranks)
             if line:
                 print(json.dumps(line), flush=True)
         elif a.workload == "mac":
