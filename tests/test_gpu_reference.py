@@ -7,7 +7,8 @@ and its code drives every ciphertext operation:
 * ``qkv_fhe`` (``operators/linear/qkv.py:144-273``; ``LinearOperator.apply`` at
   the production plan, ``operators/linear/operator.py:195-405``) and
   ``mlp_fhe`` (``operators/linear/mlp.py:524-1126``) decrypt, through their own
-  ``verify`` paths, to their NumPy restatements;
+  ``verify`` paths, to their NumPy restatements, ``mlp_fhe`` also on one
+  rank's shard at 8 GPUs (16 tokens, 2 ciphertexts);
 * ``eval_chebyshev_series_cipher`` (``operators/nonlinear/polynomial.py:331-412``)
   at the layer's SiLU degree and at degree 384 matches
   ``eval_chebyshev_series_direct`` (``approx/chebyshev.py:136-163``);
@@ -85,6 +86,31 @@ def test_reference_mlp_decrypts_to_swiglu():
     r = mlp_fhe(x, w.gate_proj, w.up_proj, w.down_proj, silu_entry=approx.silu,
                 layout=s.feature_layout, config=s.config, crypto_context=s.context,
                 input_ciphers=cts, verify=True)
+    ref = np.abs(r.expected).max()
+    assert r.max_abs_diff < 1e-3 * ref, (r.max_abs_diff, ref)
+    _no_triton()
+
+
+def test_reference_mlp_on_one_rank_shard():
+    """One rank's share of the MLP at 8 GPUs: ``mlp_fhe`` unchanged on the
+    layout's smallest sharded shape (16 tokens, 2 ciphertexts: one complex
+    pair), as ``bench.py --workload mlp`` runs it on every rank."""
+
+    from llama3fhe.application import session
+    from llama3fhe.layouts import FeatureMajorPrefillLayout
+    from llama3fhe.operators.linear.mlp import mlp_fhe
+
+    s = _session()
+    _, w, approx = llama3_layer.synthetic_layer()
+    layout = FeatureMajorPrefillLayout(seq_len=16)
+    x = np.random.default_rng(8).normal(size=(16, 4096)).astype(np.float32)
+    cts = session._encrypt_hidden(x, context=s.context, layout=layout,
+                                  input_level=int(s.context.context.L) - 11)
+    assert len(cts) == 2
+    r = mlp_fhe(x, w.gate_proj, w.up_proj, w.down_proj, silu_entry=approx.silu,
+                layout=layout, config=s.config, crypto_context=s.context,
+                input_ciphers=cts, verify=True)
+    assert len(r.ciphers) == 2
     ref = np.abs(r.expected).max()
     assert r.max_abs_diff < 1e-3 * ref, (r.max_abs_diff, ref)
     _no_triton()
